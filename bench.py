@@ -1,0 +1,416 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 integer W4A8 decode path (Qwen3.5-9B shapes).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload step|projections]
+
+Workloads (seeded synthetic int4 weights with the 9B shapes):
+  step         one full 32-layer fixed-point decode step + LM head + argmax
+               (the reference's FxRunner.step, ref/fidelity_check.py:423-448)
+               at a context of --context tokens, replayed as one CUDA graph.
+  projections  all 249 projection matvecs of one step (4,091,805,696 B of
+               W4 weights) with their fused epilogues.
+
+A step streams the whole 4.09 GB weight set, so its inputs are larger than
+the 126 MB L2 and no flush is needed between steps.  Rank 0 prints one JSON
+line.  Under torchrun each rank holds a row shard of every matrix
+(ref/seq_format.py:1177-1189 split_rows) and outputs are all-gathered.
+
+``--impl reference`` times the CPU oracle port (oracle/, the restatement of
+the reference's numpy law) on this host's cores over the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+WEIGHT_BYTES_9B = 4091805696
+FPGA_TOKS = 8.182   # published best 9B decode (evidence/qwen9b/sr/SR17_ROUND_CLOSE.md:36)
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d.get("hbm_gbs", 6650.0)), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.f = None
+
+    def start(self):
+        try:
+            self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.flush()
+        rows = [l.strip().split(", ") for l in open(self.f.name) if l.strip()]
+        os.unlink(self.f.name)
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows if len(r) >= 9
+                          for i in range(4) if r[5 + i].strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def cpu_sample_projections(seconds=12.0, threads=0):
+    """Time the oracle C matvec over the projection matrices of the model
+    until ``seconds`` elapse (whole matrices only); returns tok/s-equivalent."""
+    import oracle as O
+    from fable5_llm_b200 import synth
+    geom = O.GEOM_9B
+    specs = synth.matrix_specs(geom)
+    rng = np.random.default_rng(5)
+    x8 = {4096: rng.integers(-127, 128, 4096).astype(np.int8),
+          12288: rng.integers(-127, 128, 12288).astype(np.int8)}
+    done_bytes, spent, nmat = 0, 0.0, 0
+    cache = {}
+    for s in specs:
+        if spent >= seconds:
+            break
+        key = (s.N, s.K)
+        if key not in cache:     # same shape -> same bytes to stream; synthesis not timed
+            cache[key] = s.image(2026)
+        img = cache[key]
+        t0 = time.perf_counter()
+        O.matvec_img(img, s.N, s.K, s.sh, x8[s.K], threads=threads)
+        spent += time.perf_counter() - t0
+        done_bytes += s.nbytes
+        nmat += 1
+    frac = done_bytes / WEIGHT_BYTES_9B
+    toks = frac / spent
+    return {"value": round(toks, 4), "unit": "tok/s", "cores": O.oracle_threads() if threads <= 0 else threads,
+            "kind": "port",
+            "sample": f"{nmat} of 249 matrices ({done_bytes / 1e9:.2f} GB of W4 rows) through the C "
+                      f"oracle matvec in {spent:.1f} s, scaled to one token"}
+
+
+def cpu_sample_step(seconds=20.0):
+    """Time the oracle's full decode step (numpy law + C matvec) on a bounded
+    number of layers of the 9B model; scaled to one token."""
+    import oracle as O
+    from oracle.model import OracleModel
+    t_build = time.time()
+    nl = 4
+    geom = O.Geometry(n_layers=nl, vocab=8192)
+    m = OracleModel(2026, geom)
+    r = O.OracleRunner(m, max_T=16)
+    build_s = time.time() - t_build
+    steps, spent = 0, 0.0
+    while spent < seconds and steps < 8:
+        t0 = time.perf_counter()
+        r.step(17 + steps, steps)
+        spent += time.perf_counter() - t0
+        steps += 1
+    per_layer_step = spent / steps / nl
+    # full step = 32 layers + a 248,320-row head (time the head matvec share)
+    head_bytes = 248320 * 2112
+    s_head = (m.head.N * 2112) / (spent / steps)   # crude; refined below
+    t0 = time.perf_counter()
+    O.matvec_img(m.head.img, m.head.N, 4096, m.head.sh, np.zeros(4096, np.int8))
+    head_s = (time.perf_counter() - t0) * (248320 / m.head.N)
+    full = per_layer_step * 32 + head_s
+    del s_head, head_bytes
+    return {"value": round(1.0 / full, 5), "unit": "tok/s", "cores": O.oracle_threads(), "kind": "port",
+            "sample": f"{steps} decode steps of the first {nl} layers (3 DeltaNet + 1 attention) of the "
+                      f"synthetic 9B model through the oracle ({spent:.1f} s; model build {build_s:.0f} s "
+                      f"untimed), scaled to 32 layers + the 248,320-row head"}
+
+
+# ---------------------------------------------------------------------------
+def split_rows(nrows, nch):
+    """Contiguous row split, first nrows % nch channels +1 row
+    (ref/seq_format.py:1177-1189)."""
+    base, rem = divmod(nrows, nch)
+    out, r = [], 0
+    for c in range(nch):
+        n = base + (1 if c < rem else 0)
+        out.append((r, n))
+        r += n
+    return out
+
+
+class ProjectionsWork:
+    """All 249 projection matvecs of one decode step, grouped and fused the
+    way the decode step issues them (shared-x8 groups, fused epilogues)."""
+
+    def __init__(self, args, ws, rank):
+        import torch
+        from fable5_llm_b200 import _lib as L
+        from fable5_llm_b200 import ops, synth
+        from fable5_llm_b200.config import Geometry
+        self.torch, self.ops, self.L = torch, ops, L
+        self.ws, self.rank = ws, rank
+        geom = Geometry()
+        specs = synth.matrix_specs(geom)
+        self.bytes_per_step = sum(s.nbytes for s in specs)
+        self.local_bytes = 0
+        dev = torch.device("cuda")
+        self.w, self.rows = {}, {}
+        for s in specs:
+            r0, n = split_rows(s.N, ws)[rank]
+            buf = torch.empty(max(n, 1) * s.stride, dtype=torch.uint8, device=dev)
+            ops.synth_w4(buf, n, s.K, s.g, r0, synth.stream_key(args.seed, s.mid, synth.STREAM_W),
+                         synth.stream_key(args.seed, s.mid, synth.STREAM_M), s.symmetric)
+            self.w[(s.layer, s.name)] = (buf, n, s)
+            self.local_bytes += n * s.stride
+        torch.cuda.synchronize()
+        rng = np.random.default_rng(args.seed)
+        self.x8 = {K: ops.to_dev(rng.integers(-127, 128, K).astype(np.int8)) for K in (4096, 12288)}
+        self.meta = ops.to_dev(np.array([3, 7], dtype=np.int32))
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.key = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.resid = torch.zeros(4096, dtype=torch.int16, device=dev)
+        self.scratch = torch.zeros(1 << 16, dtype=torch.int16, device=dev)
+        self.groups = []     # (segs, K, sh, bytes, is_head)
+        for i, lt in enumerate(geom.layer_types):
+            if lt == "full_attention":
+                a = [("q_proj", L.GM_TO16, 8), ("k_proj", L.GM_TO16, 8), ("v_proj", L.GM_TO16, 8)]
+                b = "o_proj"
+            else:
+                a = [("in_qkv", L.GM_TO16, 7), ("in_z", L.GM_TO16, 8), ("in_b", L.GM_TO16, 12),
+                     ("in_a", L.GM_TO16, 12)]
+                b = "out"
+            segs, nb, off = [], 0, 0
+            for nm, mode, of in a:
+                buf, n, s = self.w[(i, nm)]
+                segs.append(ops.seg(buf, self.scratch, n, mode, e=s.e, out_f=of, out_row0=off))
+                off += n
+                nb += n * s.stride
+            self.groups.append((segs, 4096, 7, nb, False))
+            buf, n, s = self.w[(i, b)]
+            self.groups.append(([ops.seg(buf, self.resid, n, L.GM_RESID, e=s.e, out_f=7)], s.K, s.sh,
+                                n * s.stride, False))
+            g_, n, sg = self.w[(i, "gate")]
+            u_, _, su = self.w[(i, "up")]
+            self.groups.append(([ops.seg(g_, self.scratch, n, L.GM_SILU_MUL, e=sg.e, out_f=12, w2=u_,
+                                         e2=su.e, out_f2=7)], 4096, 7, 2 * n * sg.stride, False))
+            buf, n, s = self.w[(i, "down")]
+            self.groups.append(([ops.seg(buf, self.resid, n, L.GM_RESID, e=s.e, out_f=7)], s.K, s.sh,
+                                n * s.stride, False))
+        buf, n, s = self.w[(-1, "head")]
+        self.groups.append(([ops.seg(buf, None, n, L.GM_ARGMAX, out_row0=split_rows(s.N, ws)[rank][0])],
+                            4096, 7, n * s.stride, True))
+        self.launches_per_step = len(self.groups)
+
+    def step(self, events=None):
+        ops = self.ops
+        self.key.zero_()
+        for j, (segs, K, sh, nb, head) in enumerate(self.groups):
+            if events is not None:
+                events[j][0].record()
+            ops.gemv(segs, K, 128, sh, self.x8[K], self.meta, argmax=self.key if head else None,
+                     err=self.err)
+            if events is not None:
+                events[j][1].record()
+
+
+def run_ours(args):
+    import torch
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    work = ProjectionsWork(args, ws, rank)
+    hbm_peak, peak_kind = peaks()
+
+    def barrier_sync():
+        torch.cuda.synchronize()
+        if ws > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    graph = None
+    if ws == 1:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                work.step()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            work.step()
+
+    def one():
+        if graph is not None:
+            graph.replay()
+        else:
+            work.step()
+
+    for _ in range(args.warmup):
+        one()
+    barrier_sync()
+    clocks = ClockSampler(local)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        one()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    ck = clocks.stop()
+    if ws > 1:
+        tt = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        ms = float(tt.item())
+    barrier_sync()
+    err = int(work.err.item())
+
+    # e2e: host x8 -> device, replay, argmax key -> host (pinned buffers)
+    hx = torch.empty(4096, dtype=torch.int8, pin_memory=True)
+    hx.copy_(work.x8[4096].cpu())
+    hk = torch.empty(1, dtype=torch.int64, pin_memory=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier_sync()
+    e0.record()
+    for _ in range(args.steps):
+        work.x8[4096].copy_(hx, non_blocking=True)
+        one()
+        hk.copy_(work.key, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if ws > 1:
+        tt = torch.tensor([e2e_ms], device="cuda")
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+
+    # per-kernel pass: events around every GEMV launch (dominant kernel)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in work.groups]
+    kt = []
+    for _ in range(3):
+        work.step(events=evs)
+        torch.cuda.synchronize()
+        kt.append(sum(a.elapsed_time(b) for a, b in evs))
+    k_ms = min(kt)
+    gemv_bytes = sum(g[3] for g in work.groups)
+    achieved = gemv_bytes / (k_ms * 1e-3) / 1e9
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu = cpu_sample_projections(seconds=12.0)
+    if rank == 0:
+        toks = 1000.0 / ms
+        line = {
+            "metric": "9B W4A8 projection matvecs per token (token-equivalents/s)",
+            "value": round(toks, 2), "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int4xint8->int32/int64",
+            "data": "synthetic (seeded int4 W4 images, 9B shapes)",
+            "config": {"workload": "projections: 249 W4A8 matvecs (4,091,805,696 B) per step, fused "
+                                   "epilogues, 129 grouped launches, CUDA graph",
+                       "model": "Qwen3.5-9B geometry, synthetic", "weight_bytes": work.bytes_per_step,
+                       "l2": "inputs larger than L2 (4.09 GB of weights streamed per step)",
+                       "parallelism": f"row-shard x{ws}" if ws > 1 else "single GPU"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved / hbm_peak, 4), "traffic": None,
+                         "kernel": "k_gemv (all groups, CUDA events per launch)",
+                         "peak_kind": peak_kind, "step_frac": round(work.local_bytes / (ms * 1e-3) / 1e9 / hbm_peak, 4)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 4096,
+                    "d2h_bytes_per_step": 8},
+            "gpu_launches": work.launches_per_step * args.steps,
+            "clocks": ck, "device_err": err,
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def run_reference(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    if args.workload == "projections":
+        cb = cpu_sample_projections(seconds=max(10.0, 3.0 * args.steps))
+        metric = "9B W4A8 projection matvecs per token (token-equivalents/s)"
+    else:
+        cb = cpu_sample_step(seconds=max(15.0, 4.0 * args.steps))
+        metric = "9B W4A8 decode tok/s"
+    line = {"impl": "reference", "metric": metric, "value": cb["value"], "unit": "tok/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1000.0 / cb["value"], 3) if cb["value"] else None,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int64", "data": "synthetic (seeded int4 weights, 9B shapes)",
+            "config": {"workload": args.workload, "context": args.context},
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="projections", choices=["step", "projections"])
+    ap.add_argument("--context", type=int, default=2048)
+    ap.add_argument("--seed", type=int, default=2026)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,80 @@
+"""ctypes binding of ``libf5b200.so`` (the C ABI declared in include/f5b200.h).
+
+The library is the only compute path: if it is missing the import of the
+ops fails loudly -- there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_lib", "libf5b200.so")
+
+c_int, c_ll, c_u64, c_vp, c_size = (ctypes.c_int, ctypes.c_longlong, ctypes.c_uint64,
+                                    ctypes.c_void_p, ctypes.c_size_t)
+
+F5_OK, F5_EINVAL, F5_ECUDA, F5_ENOMEM, F5_ETIMEOUT, F5_EOVERFLOW, F5_ESTATE, F5_ENCCL = \
+    0, -1, -2, -3, -4, -5, -6, -7
+
+GM_Y32, GM_TO16, GM_TO64, GM_RESID, GM_SILU_MUL, GM_ARGMAX = range(6)
+(PR_RSHR, PR_SIGMOID, PR_SOFTPLUS, PR_SILU, PR_EXP_NEG, PR_RSQRT, PR_RECIP,
+ PR_BF_SHIFT, PR_DYNQ8_E, PR_DN_NORM_SCALE, PR_EPS_NORM_SCALE, PR_EXP2_FRAC) = range(12)
+
+
+class F5Error(RuntimeError):
+    def __init__(self, status, msg):
+        super().__init__(f"f5b200 status {status}: {msg}")
+        self.status = status
+
+
+class GemvSeg(ctypes.Structure):
+    _fields_ = [("w", c_vp), ("w2", c_vp), ("out", c_vp), ("p_out", c_vp),
+                ("rows", c_int), ("e", c_int), ("e2", c_int), ("out_f", c_int),
+                ("out_f2", c_int), ("mode", c_int), ("out_row0", c_int)]
+
+
+# (name, restype, argtypes) of every exported symbol, in header order
+SIGNATURES = [
+    ("f5_abi_version", c_int, []),
+    ("f5_status_string", ctypes.c_char_p, [c_int]),
+    ("f5_last_error", c_int, [ctypes.c_char_p, c_size]),
+    ("f5_gemv_dev", c_int, [ctypes.POINTER(GemvSeg), c_int, c_int, c_int, c_int, c_vp, c_vp,
+                            c_vp, c_vp, c_int, c_int, c_vp]),
+    ("f5_rmsnorm_dynq8_dev", c_int, [c_vp, c_vp, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp]),
+    ("f5_dynq8_dev", c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
+    ("f5_prim_dev", c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp]),
+    ("f5_synth_w4_dev", c_int, [c_vp, c_ll, c_int, c_int, c_ll, c_u64, c_u64, c_int, c_vp]),
+    ("f5_synth_emb_dev", c_int, [c_vp, c_ll, c_int, c_ll, c_u64, c_vp]),
+    ("f5_matvec_y32_host", c_int, [c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp]),
+]
+
+_LIB = None
+
+
+def lib():
+    """Load the library once (raises if it has not been built)."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"CUDA library {LIB_PATH} is not built "
+                               "(python -m fable5_llm_b200.build); there is no CPU fallback")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, res, args in SIGNATURES:
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = L
+    return _LIB
+
+
+def last_error():
+    buf = ctypes.create_string_buffer(512)
+    lib().f5_last_error(buf, 512)
+    return buf.value.decode(errors="replace")
+
+
+def check(status, what=""):
+    if status != F5_OK:
+        raise F5Error(status, f"{what}: {last_error()}")
+    return status

@@ -1,0 +1,94 @@
+// Kernel argument structs and host-side launchers of the sm_100a decode path.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace f5 {
+
+// ---- device error word bits (set by kernels, read by the host) ----
+enum : uint32_t {
+  DERR_Y32_OVERFLOW = 1u << 0,   // |y32| >= 2^31 (ref/w4a8_ref.py:288 assert)
+  DERR_TIMEOUT = 1u << 1,        // a bounded device wait gave up
+  DERR_KV_FULL = 1u << 2,        // KV append beyond max_T
+  DERR_RANGE = 1u << 3,          // an input outside a documented range
+};
+
+// ---- quantized activation vector (DYNQ8 output, ref/fixedpoint.py:24-33) ----
+// x8 lives in its own buffer; meta[0] = e_x, meta[1] = in_f (fraction bits
+// of the int16 vector that was quantized; consumed by matvec_to's shift).
+struct XQ {
+  int8_t *x8;
+  int *meta;
+};
+
+// ---- GEMV (batch-1 W4A8 matvec over packed DDR rows) ----
+enum GemvMode : int {
+  GM_Y32 = 0,       // out int32[row] = y32
+  GM_TO16 = 1,      // out int16[row] = clip16(matvec_to shift)
+  GM_TO64 = 2,      // out int64[row] = matvec_to shift
+  GM_RESID = 3,     // out int16[row] = clip16(out[row] + clip16(shift))
+  GM_SILU_MUL = 4,  // paired gate/up rows -> clip16(rshr(silu(g) * u, 12))
+  GM_ARGMAX = 5,    // running (max y32, lowest row) key
+};
+
+constexpr int GEMV_MAX_SEG = 4;
+
+struct GemvSeg {
+  const uint8_t *w;    // packed image row 0
+  const uint8_t *w2;   // paired image (GM_SILU_MUL: up), else null
+  void *out;           // output base (indexed by out_row0 + row)
+  int64_t *p_out;      // optional int64 p per row (debug / API), nullable
+  int rows;            // rows of this segment
+  int unit_begin;      // first unit index (units: row pairs, or paired rows)
+  int e, e2;           // weight exponents
+  int out_f, out_f2;   // output fraction bits (TO16/TO64/RESID/SILU_MUL)
+  int mode;
+  int out_row0;
+};
+
+struct GemvArgs {
+  GemvSeg seg[GEMV_MAX_SEG];
+  int nseg;
+  int total_units;
+  int K;
+  int stride;          // bytes per packed row (ref/w4a8_ref.py:111-114)
+  int g;               // group size 128 or 64
+  int sh;              // final shift (same for all segments: same K)
+  const int8_t *x8;
+  const int *xmeta;    // {e_x, in_f}, nullable (then 0, 0)
+  unsigned long long *argmax_key;
+  uint32_t *err;
+};
+
+cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t st, bool pdl, int max_blocks);
+
+// ---- vector kernels ----
+struct NormArgs {
+  const int16_t *x16;       // input vector (n = 4096)
+  int16_t *x16_store;       // when tok is given: embedding row copied here
+  const int16_t *emb;       // embedding table [vocab][n] or null
+  const int *tok;           // device token id (with emb), nullable
+  const int32_t *w;         // norm weight (Q14, or Q12 pre-folded)
+  int n, in_f, one_plus;
+  int16_t *xn_out;          // optional normalised vector
+  XQ out;                   // DYNQ8 of the normalised vector
+};
+cudaError_t launch_rmsnorm_dynq8(const NormArgs &a, cudaStream_t st, bool pdl);
+
+struct Dynq8Args {
+  const int16_t *x16;
+  int n, in_f;
+  XQ out;
+};
+cudaError_t launch_dynq8(const Dynq8Args &a, cudaStream_t st, bool pdl);
+
+// elementwise primitive evaluation (parity tests of the integer law)
+enum PrimOp : int {
+  PR_RSHR = 0, PR_SIGMOID = 1, PR_SOFTPLUS = 2, PR_SILU = 3, PR_EXP_NEG = 4,
+  PR_RSQRT = 5, PR_RECIP = 6, PR_BF_SHIFT = 7, PR_DYNQ8_E = 8,
+  PR_DN_NORM_SCALE = 9, PR_EPS_NORM_SCALE = 10, PR_EXP2_FRAC = 11,
+};
+cudaError_t launch_prim(int op, const int64_t *in, const int64_t *in2, int64_t *out,
+                        int64_t *out2, int n, int arg0, int arg1, cudaStream_t st);
+
+}  // namespace f5
