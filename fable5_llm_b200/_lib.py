@@ -47,7 +47,44 @@ SIGNATURES = [
     ("f5_synth_w4_dev", c_int, [c_vp, c_ll, c_int, c_int, c_ll, c_u64, c_u64, c_int, c_vp]),
     ("f5_synth_emb_dev", c_int, [c_vp, c_ll, c_int, c_ll, c_u64, c_vp]),
     ("f5_matvec_y32_host", c_int, [c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp]),
+    ("f5_ctx_create", c_int, [c_vp, c_int, c_vp]),
+    ("f5_ctx_destroy", c_int, [c_vp]),
+    ("f5_ctx_upload_matrix", c_int, [c_vp, c_int, c_int, c_vp, c_int, c_int, c_int, c_int, c_int]),
+    ("f5_ctx_synth_matrix", c_int, [c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_u64, c_u64,
+                                    c_int]),
+    ("f5_ctx_upload_vector", c_int, [c_vp, c_int, c_int, c_vp, c_int]),
+    ("f5_ctx_upload_embedding", c_int, [c_vp, c_vp, c_int, c_int]),
+    ("f5_ctx_synth_embedding", c_int, [c_vp, c_u64]),
+    ("f5_ctx_upload_rope", c_int, [c_vp, c_vp, c_int]),
+    ("f5_ctx_reset", c_int, [c_vp]),
+    ("f5_ctx_set_position", c_int, [c_vp, c_int, c_int]),
+    ("f5_ctx_get_position", c_int, [c_vp, c_vp, c_vp]),
+    ("f5_ctx_set_logits", c_int, [c_vp, c_int]),
+    ("f5_ctx_stream", c_int, [c_vp, c_vp]),
+    ("f5_ctx_prepare", c_int, [c_vp]),
+    ("f5_decode_step", c_int, [c_vp, c_int, c_int, c_vp, c_vp]),
+    ("f5_decode_launch", c_int, [c_vp, c_int, c_vp]),
+    ("f5_ctx_sync", c_int, [c_vp, c_vp, c_vp]),
+    ("f5_ctx_time_step", c_int, [c_vp, c_int, c_vp, c_int]),
+    ("f5_layer_step", c_int, [c_vp, c_int, c_vp, c_int, c_int]),
+    ("f5_ctx_read", c_int, [c_vp, c_int, c_int, c_vp, c_size]),
+    ("f5_ctx_write", c_int, [c_vp, c_int, c_int, c_vp, c_size]),
 ]
+
+# f5_config (include/f5b200.h)
+class Config(ctypes.Structure):
+    _fields_ = [("abi_version", c_int), ("n_layers", c_int), ("vocab", c_int), ("max_T", c_int),
+                ("norm_mode", c_int), ("world_size", c_int), ("rank", c_int),
+                ("layer_types", ctypes.c_char_p)]
+
+
+S_IN_QKV, S_IN_Z, S_IN_B, S_IN_A, S_OUT = 0, 1, 2, 3, 4
+S_Q, S_K, S_V, S_O = 0, 1, 2, 3
+S_GATE, S_UP, S_DOWN, S_HEAD = 8, 9, 10, 0
+VEC_LN1, VEC_LN2, VEC_Q_NORM, VEC_K_NORM, VEC_CONV_W, VEC_DT_BIAS, VEC_A, VEC_NORM_W, VEC_LN_F = range(9)
+(BUF_X16, BUF_QKV16, BUF_Z16, BUF_B16, BUF_A16, BUF_ON16, BUF_QG16, BUF_K16, BUF_V16, BUF_PROD64,
+ BUF_PROD16, BUF_STATS, BUF_DN_S, BUF_DN_CONV, BUF_DN_KH, BUF_K8, BUF_KE, BUF_V8, BUF_VE, BUF_KA,
+ BUF_LOGITS) = range(21)
 
 _LIB = None
 

@@ -18,6 +18,18 @@ F5_DEV long long block_sum_ll(long long v, long long *red) {
   return t;
 }
 
+F5_DEV unsigned long long block_sum_ull(unsigned long long v, unsigned long long *red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  unsigned long long t = 0;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  return t;
+}
+
 F5_DEV unsigned long long block_max_ull(unsigned long long v, unsigned long long *red) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) {

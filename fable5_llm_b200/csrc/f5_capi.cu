@@ -99,6 +99,8 @@ int f5_gemv_dev(const f5_gemv_seg *segs, int nseg, int K, int g, int sh, const i
     int st = check_matrix_shape(s.rows, K, g);
     if (st) return st;
     if (!s.w || (!s.out && s.mode != F5_GM_ARGMAX)) return set_error(F5_EINVAL, "f5_gemv_dev: null segment pointer");
+    if ((reinterpret_cast<uintptr_t>(s.w) & 15) || (reinterpret_cast<uintptr_t>(s.w2) & 15))
+      return set_error(F5_EINVAL, "f5_gemv_dev: weight images must be 16-byte aligned (bulk copies)");
     if (s.mode < 0 || s.mode > F5_GM_ARGMAX) return set_error(F5_EINVAL, "f5_gemv_dev: bad mode %d", s.mode);
     if (s.mode == F5_GM_SILU_MUL && !s.w2) return set_error(F5_EINVAL, "f5_gemv_dev: SILU_MUL needs w2");
     if (s.mode == F5_GM_ARGMAX && !d_argmax) return set_error(F5_EINVAL, "f5_gemv_dev: ARGMAX needs d_argmax");
@@ -115,10 +117,10 @@ int f5_gemv_dev(const f5_gemv_seg *segs, int nseg, int K, int g, int sh, const i
     d.out_f2 = s.out_f2;
     d.mode = s.mode;
     d.out_row0 = s.out_row0;
-    units += s.mode == F5_GM_SILU_MUL ? s.rows : (s.rows + 1) / 2;
+    units += s.rows;   // a unit is one row (SILU_MUL: one gate/up row pair)
   }
   a.total_units = units;
-  if (max_blocks <= 0) max_blocks = 2 * sm_count();
+  if (max_blocks <= 0) max_blocks = sm_count();
   return cuda_status(launch_gemv(a, (cudaStream_t)stream, pdl != 0, max_blocks), "f5_gemv_dev");
 }
 

@@ -1,0 +1,857 @@
+// Model context: one GPU's resident 9B integer model, its decode state and
+// the decode step captured as one CUDA graph.
+//
+// Replaces the reference's model-level step (ref/fidelity_check.py:404-448
+// FxRunner.step; ref/gen_model_script.py:602-650 token loop) and, for one
+// layer, ref/layer_fixed.py:1669-1677 layer_decode_fx.  The 39k-record SEQ
+// program the FPGA sequencer runs per token is replaced by a fixed chain of
+// 163 kernel launches (step begin, 5 per layer, LM head, step end) recorded
+// once into a CUDA graph with programmatic dependent launch edges.
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/f5b200.h"
+#include "f5_attn.cuh"
+#include "f5_capi_util.h"
+#include "f5_dn.cuh"
+#include "f5_int.cuh"
+#include "f5_kernels.cuh"
+
+namespace f5 {
+cudaError_t launch_synth_w4(uint8_t *, long long, int, int, long long, uint64_t, uint64_t, int, cudaStream_t);
+cudaError_t launch_synth_emb(int16_t *, long long, int, long long, uint64_t, cudaStream_t);
+
+// device-resident step parameters (read by the graph's kernels)
+struct StepParams {
+  int tok;        // input token of this step
+  int pos;        // RoPE position of this step
+  int T;          // tokens already in every layer's cache / conv window
+  int next_tok;   // argmax of this step (first max wins)
+  int max_val;    // its y32 logit
+  uint32_t err;   // device error bits (DERR_*)
+  int steps;      // steps completed since reset
+  int pad;
+};
+
+// step begin: x16 = emb[tok] (ref/fidelity_check.py:428), reset argmax key
+__global__ void k_step_begin(StepParams *p, const int16_t *emb, int vocab, int H, int16_t *x16,
+                             unsigned long long *key) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  int tok = p->tok;
+  if (tok < 0 || tok >= vocab) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(&p->err, DERR_RANGE);
+    tok = 0;
+  }
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < H; i += gridDim.x * blockDim.x)
+    x16[i] = emb[(size_t)tok * H + i];
+  if (blockIdx.x == 0 && threadIdx.x == 0) *key = 0ull;
+}
+
+// step end: decode the argmax key; feed the token back for a greedy loop
+__global__ void k_step_end(StepParams *p, const unsigned long long *key, const uint32_t *err, int advance) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const unsigned long long k = *key;
+  const int row = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+  const int val = (int)((uint32_t)(k >> 32) ^ 0x80000000u);
+  p->next_tok = row;
+  p->max_val = val;
+  p->err |= *err;
+  if (advance) {
+    p->tok = row;
+    p->pos += 1;
+    p->T += 1;
+    p->steps += 1;
+  }
+}
+
+__global__ void k_collect_err(StepParams *p, const uint32_t *err) { p->err |= *err; }
+
+static cudaError_t launch_pdl(const void *fn, void **args, dim3 grid, dim3 block, cudaStream_t st, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+// ---------------------------------------------------------------------------
+constexpr int H = 4096, FFN = 12288, NQ = 16, NKV = 4, HD = 256, ROT = 64;
+constexpr int LNH = 32, LNKH = 16, LDK = 128, LDV = 128;
+constexpr int LKD = LNKH * LDK, LVD = LNH * LDV, CONV_DIM = 2 * LKD + LVD;
+constexpr int NSLOT = 11;
+
+struct DevMat {
+  uint8_t *w = nullptr;
+  int N = 0, K = 0, g = 128, e = 0, sh = 0, stride = 0;
+  int row0 = 0, rows = 0;   // this rank's rows (split_rows law)
+};
+
+struct Layer {
+  bool attn = false;
+  DevMat m[NSLOT];
+  int32_t *ln1 = nullptr, *ln2 = nullptr;
+  int32_t *q_norm = nullptr, *k_norm = nullptr;
+  int32_t *conv_w = nullptr, *dt_bias = nullptr, *A = nullptr, *norm_w = nullptr;
+  // state
+  int16_t *conv = nullptr;   // [CONV_DIM][4] ring
+  int16_t *S = nullptr;      // [LNH][LDK][LDV]
+  int8_t *k8 = nullptr, *ke = nullptr, *v8 = nullptr, *ve = nullptr;
+  int *kh = nullptr;         // [LNH] last block-float shifts
+  int *ka = nullptr;         // last attention k_a
+};
+
+}  // namespace f5
+
+struct f5_ctx {
+  f5_config cfg;
+  int device = 0;
+  cudaStream_t st = nullptr;
+  std::vector<f5::Layer> L;
+  f5::DevMat head;
+  int32_t *ln_f = nullptr;
+  int16_t *emb = nullptr;
+  int16_t *rope = nullptr;
+  int rope_npos = 0;
+  // activations
+  int16_t *x16 = nullptr, *qkv16 = nullptr, *z16 = nullptr, *b16 = nullptr, *a16 = nullptr;
+  int16_t *on16 = nullptr, *qg16 = nullptr, *k16 = nullptr, *v16 = nullptr, *prod16 = nullptr;
+  int64_t *prod64 = nullptr;
+  int8_t *x8 = nullptr;
+  int *xmeta = nullptr;
+  unsigned long long *key = nullptr, *stats = nullptr;
+  uint32_t *err = nullptr;
+  f5::StepParams *params = nullptr;    // device
+  f5::StepParams *h_params = nullptr;  // pinned host mirror
+  struct Timed {
+    cudaEvent_t a, b;
+    int kind;
+    double bytes;
+  };
+  bool timing = false;         // bracket every launch with events (f5_ctx_time_step)
+  std::vector<Timed> timed;
+  int32_t *logits = nullptr;   // [vocab] y32 of the LM head when enabled
+  bool want_logits = false;
+  cudaGraphExec_t step_exec = nullptr;
+  bool graph_dirty = true;
+  std::vector<void *> allocs;
+};
+
+namespace f5 {
+
+static int alloc(f5_ctx *c, void **p, size_t bytes) {
+  cudaError_t e = cudaMalloc(p, bytes);
+  if (e != cudaSuccess) return cuda_status(e, "cudaMalloc");
+  c->allocs.push_back(*p);
+  e = cudaMemsetAsync(*p, 0, bytes, c->st);
+  return cuda_status(e, "cudaMemset");
+}
+#define F5_ALLOC(c, p, bytes)                                          \
+  do {                                                                 \
+    int _rc = alloc((c), reinterpret_cast<void **>(&(p)), (bytes));    \
+    if (_rc) return _rc;                                               \
+  } while (0)
+#define F5_CU(x, what)                        \
+  do {                                        \
+    int _rc = cuda_status((x), (what));       \
+    if (_rc) return _rc;                      \
+  } while (0)
+
+struct DevGuard {
+  int prev = 0;
+  explicit DevGuard(int d) { cudaGetDevice(&prev); cudaSetDevice(d); }
+  ~DevGuard() { cudaSetDevice(prev); }
+};
+
+enum { TK_GEMV = 0, TK_DN = 1, TK_ATTN = 2, TK_OTHER = 3 };
+static void tl_begin(f5_ctx *c) {
+  if (!c->timing) return;
+  f5_ctx::Timed t = {};
+  cudaEventCreate(&t.a);
+  cudaEventCreate(&t.b);
+  cudaEventRecord(t.a, c->st);
+  c->timed.push_back(t);
+}
+static void tl_end(f5_ctx *c, int kind, double bytes) {
+  if (!c->timing) return;
+  f5_ctx::Timed &t = c->timed.back();
+  t.kind = kind;
+  t.bytes = bytes;
+  cudaEventRecord(t.b, c->st);
+}
+
+static void split_rows(int n, int ws, int rank, int &r0, int &cnt) {
+  const int base = n / ws, rem = n % ws;
+  r0 = rank * base + (rank < rem ? rank : rem);
+  cnt = base + (rank < rem ? 1 : 0);
+}
+
+static DevMat *find_mat(f5_ctx *c, int layer, int slot) {
+  if (layer == -1) return slot == 0 ? &c->head : nullptr;
+  if (layer < 0 || layer >= (int)c->L.size() || slot < 0 || slot >= NSLOT) return nullptr;
+  return &c->L[layer].m[slot];
+}
+
+static bool slot_valid(const Layer &l, int slot) {
+  if (slot >= 8 && slot <= 10) return true;
+  return l.attn ? slot <= 3 : slot <= 4;
+}
+
+static void expected_shape(const f5_ctx *c, int layer, int slot, int &N, int &K) {
+  N = K = 0;
+  if (layer == -1) { N = c->cfg.vocab; K = H; return; }
+  const bool attn = c->L[layer].attn;
+  switch (slot) {
+    case 8: case 9: N = FFN; K = H; return;
+    case 10: N = H; K = FFN; return;
+    default: break;
+  }
+  if (attn) {
+    const int n[4] = {NQ * HD * 2, NKV * HD, NKV * HD, H}, k[4] = {H, H, H, NQ * HD};
+    N = n[slot]; K = k[slot];
+  } else {
+    const int n[5] = {CONV_DIM, LVD, LNH, LNH, H}, k[5] = {H, H, H, H, LVD};
+    N = n[slot]; K = k[slot];
+  }
+}
+
+static int prep_matrix(f5_ctx *c, int layer, int slot, int N, int K, int g, int e, int sh, DevMat *&m) {
+  m = find_mat(c, layer, slot);
+  if (!m || (layer >= 0 && !slot_valid(c->L[layer], slot)))
+    return set_error(F5_EINVAL, "no matrix slot %d in layer %d", slot, layer);
+  int eN, eK;
+  expected_shape(c, layer, slot, eN, eK);
+  if (N != eN || K != eK) return set_error(F5_EINVAL, "layer %d slot %d: shape %dx%d, expected %dx%d", layer, slot, N, K, eN, eK);
+  int st = check_matrix_shape(N, K, g);
+  if (st) return st;
+  if (g != 128) return set_error(F5_EINVAL, "the decode step uses g=128 images");
+  if (sh != (int)(64 - __builtin_clzll((unsigned long long)(K / g) * 65535ull * (unsigned long long)(g * 8 * 127))) - 31)
+    return set_error(F5_EINVAL, "sh=%d is not the final shift of K=%d (ref/w4a8_ref.py:177-179)", sh, K);
+  m->N = N; m->K = K; m->g = g; m->e = e; m->sh = sh; m->stride = row_stride(K, g);
+  split_rows(N, c->cfg.world_size, c->cfg.rank, m->row0, m->rows);
+  if (!m->w) F5_ALLOC(c, m->w, (size_t)m->rows * m->stride + 64);
+  c->graph_dirty = true;
+  return F5_OK;
+}
+
+static int check_ctx(f5_ctx *c) {
+  if (!c) return set_error(F5_EINVAL, "null context");
+  return F5_OK;
+}
+
+static GemvSeg mkseg(const DevMat &m, void *out, int mode, int out_f, const DevMat *m2 = nullptr, int out_f2 = 0) {
+  GemvSeg s = {};
+  s.w = m.w;
+  s.w2 = m2 ? m2->w : nullptr;
+  s.out = out;
+  s.rows = m.rows;
+  s.e = m.e;
+  s.e2 = m2 ? m2->e : 0;
+  s.out_f = out_f;
+  s.out_f2 = out_f2;
+  s.mode = mode;
+  s.out_row0 = m.row0;
+  return s;
+}
+
+static cudaError_t gemv(f5_ctx *c, const GemvSeg *segs, int nseg, int K, const GemvPrologue &pro,
+                        unsigned long long *key, bool pdl) {
+  GemvArgs a = {};
+  int units = 0;
+  for (int i = 0; i < nseg; ++i) {
+    a.seg[i] = segs[i];
+    a.seg[i].unit_begin = units;
+    units += segs[i].rows;
+  }
+  a.nseg = nseg;
+  a.total_units = units;
+  a.K = K;
+  a.g = 128;
+  a.stride = row_stride(K, 128);
+  a.sh = (int)(64 - __builtin_clzll((unsigned long long)(K / 128) * 65535ull * 130048ull)) - 31;
+  a.pro = pro;
+  a.argmax_key = key;
+  a.err = c->err;
+  double bytes = 0;
+  for (int i = 0; i < nseg; ++i) bytes += (double)segs[i].rows * a.stride * (segs[i].mode == GM_SILU_MUL ? 2 : 1);
+  tl_begin(c);
+  cudaError_t e = launch_gemv(a, c->st, pdl, sm_count());
+  tl_end(c, TK_GEMV, bytes);
+  return e;
+}
+
+// the five launches of one layer (ref/layer_fixed.py:1669-1677)
+static cudaError_t enqueue_layer(f5_ctx *c, int li, bool pdl) {
+  Layer &l = c->L[li];
+  cudaError_t e;
+  GemvPrologue pro = {};
+  pro.mode = PRO_RMSNORM;
+  pro.src = c->x16;
+  pro.w = l.ln1;
+  pro.in_f = RS_F;
+  pro.one_plus = 1;
+  if (!l.attn) {
+    // in-projection: qkv16 (Q.RS_F), z16 (Q.QKV_F), b, a (Q12), ref/layer_fixed.py:1503-1509
+    GemvSeg s[4] = {mkseg(l.m[0], c->qkv16, GM_TO16, RS_F), mkseg(l.m[1], c->z16, GM_TO16, QKV_F),
+                    mkseg(l.m[2], c->b16, GM_TO16, 12), mkseg(l.m[3], c->a16, GM_TO16, 12)};
+    if ((e = gemv(c, s, 4, H, pro, nullptr, pdl))) return e;
+    DnArgs d = {};
+    d.qkv16 = c->qkv16; d.z16 = c->z16; d.b16 = c->b16; d.a16 = c->a16;
+    d.conv = l.conv; d.conv_w = l.conv_w; d.dt_bias = l.dt_bias; d.A = l.A; d.norm_w = l.norm_w;
+    d.S = l.S; d.on16 = c->on16; d.T = &c->params->T; d.kh_out = l.kh; d.stats = c->stats;
+    d.lkd = LKD; d.vrep = LNH / LNKH; d.norm_mode = c->cfg.norm_mode;
+    tl_begin(c);
+    e = launch_dn_step(d, LNH, c->st, pdl);
+    tl_end(c, TK_DN, 0);
+    if (e) return e;
+    GemvPrologue p2 = {};
+    p2.mode = PRO_DYNQ8;
+    p2.src = c->on16;
+    p2.in_f = DN_NORM_F;
+    GemvSeg so = mkseg(l.m[4], c->x16, GM_RESID, RS_F);
+    if ((e = gemv(c, &so, 1, LVD, p2, nullptr, pdl))) return e;
+  } else {
+    GemvSeg s[3] = {mkseg(l.m[0], c->qg16, GM_TO16, QKV_F), mkseg(l.m[1], c->k16, GM_TO16, QKV_F),
+                    mkseg(l.m[2], c->v16, GM_TO16, QKV_F)};
+    if ((e = gemv(c, s, 3, H, pro, nullptr, pdl))) return e;
+    AttnArgs at = {};
+    at.qg16 = c->qg16; at.k16 = c->k16; at.v16 = c->v16; at.q_norm = l.q_norm; at.k_norm = l.k_norm;
+    at.rope = c->rope; at.k8 = l.k8; at.ke = l.ke; at.v8 = l.v8; at.ve = l.ve; at.prod = c->prod64;
+    at.T = &c->params->T; at.pos = &c->params->pos; at.err = c->err;
+    at.max_T = c->cfg.max_T; at.max_pos = c->rope_npos; at.nq = NQ; at.nkv = NKV; at.rot = ROT;
+    tl_begin(c);
+    e = launch_attn(at, c->st, pdl);
+    tl_end(c, TK_ATTN, 0);
+    if (e) return e;
+    GemvPrologue p2 = {};
+    p2.mode = PRO_ATTN_GATE;
+    p2.src = c->prod64;
+    p2.dbg = l.ka;
+    GemvSeg so = mkseg(l.m[3], c->x16, GM_RESID, RS_F);
+    if ((e = gemv(c, &so, 1, NQ * HD, p2, nullptr, pdl))) return e;
+  }
+  // MLP (ref/layer_fixed.py:1597-1604) with both residual adds fused
+  GemvPrologue p3 = {};
+  p3.mode = PRO_RMSNORM;
+  p3.src = c->x16;
+  p3.w = l.ln2;
+  p3.in_f = RS_F;
+  p3.one_plus = 1;
+  GemvSeg sgu = mkseg(l.m[8], c->prod16, GM_SILU_MUL, 12, &l.m[9], RS_F);
+  if ((e = gemv(c, &sgu, 1, H, p3, nullptr, pdl))) return e;
+  GemvPrologue p4 = {};
+  p4.mode = PRO_DYNQ8;
+  p4.src = c->prod16;
+  p4.in_f = RS_F;
+  GemvSeg sd = mkseg(l.m[10], c->x16, GM_RESID, RS_F);
+  return gemv(c, &sd, 1, FFN, p4, nullptr, pdl);
+}
+
+static cudaError_t enqueue_step(f5_ctx *c, bool pdl) {
+  cudaError_t e;
+  {
+    StepParams *p = c->params;
+    const int16_t *emb = c->emb;
+    int vocab = c->cfg.vocab, h = H;
+    int16_t *x = c->x16;
+    unsigned long long *k = c->key;
+    void *args[] = {&p, &emb, &vocab, &h, &x, &k};
+    tl_begin(c);
+    e = launch_pdl((const void *)k_step_begin, args, dim3(4), dim3(256), c->st, pdl);
+    tl_end(c, TK_OTHER, 0);
+    if (e) return e;
+  }
+  for (int li = 0; li < (int)c->L.size(); ++li)
+    if ((e = enqueue_layer(c, li, pdl))) return e;
+  GemvPrologue pf = {};
+  pf.mode = PRO_RMSNORM;
+  pf.src = c->x16;
+  pf.w = c->ln_f;
+  pf.in_f = RS_F;
+  pf.one_plus = 0;   // ln_f pre-folded (1+w) at Q3.12 (ref/gen_model_script.py:502-504)
+  GemvSeg sh = mkseg(c->head, c->want_logits ? c->logits : nullptr, GM_ARGMAX, 0);
+  if ((e = gemv(c, &sh, 1, H, pf, c->key, pdl))) return e;
+  {
+    StepParams *p = c->params;
+    const unsigned long long *k = c->key;
+    const uint32_t *er = c->err;
+    int adv = 1;
+    void *args[] = {&p, &k, &er, &adv};
+    tl_begin(c);
+    e = launch_pdl((const void *)k_step_end, args, dim3(1), dim3(1), c->st, pdl);
+    tl_end(c, TK_OTHER, 0);
+    if (e) return e;
+  }
+  return cudaSuccess;
+}
+
+static int layer_ready(f5_ctx *c, int li) {
+  for (int s = 0; s < NSLOT; ++s)
+    if (slot_valid(c->L[li], s) && !c->L[li].m[s].w)
+      return set_error(F5_ESTATE, "layer %d slot %d not uploaded", li, s);
+  if (!c->rope) return set_error(F5_ESTATE, "RoPE table not uploaded");
+  return F5_OK;
+}
+
+static int ready(f5_ctx *c) {
+  for (size_t i = 0; i < c->L.size(); ++i)
+    for (int s = 0; s < NSLOT; ++s)
+      if (slot_valid(c->L[i], s) && !c->L[i].m[s].w)
+        return set_error(F5_ESTATE, "layer %zu slot %d not uploaded", i, s);
+  if (!c->head.w) return set_error(F5_ESTATE, "LM head not uploaded");
+  if (!c->emb) return set_error(F5_ESTATE, "embedding not uploaded");
+  if (!c->rope) return set_error(F5_ESTATE, "RoPE table not uploaded");
+  return F5_OK;
+}
+
+static int build_graph(f5_ctx *c) {
+  if (!c->graph_dirty && c->step_exec) return F5_OK;
+  int rc = ready(c);
+  if (rc) return rc;
+  if (c->cfg.world_size > 1)
+    return set_error(F5_ESTATE, "row-sharded contexts need an output all-gather (f5_ctx_attach_comm) before decoding");
+  if (c->step_exec) {
+    cudaGraphExecDestroy(c->step_exec);
+    c->step_exec = nullptr;
+  }
+  F5_CU(cudaStreamSynchronize(c->st), "sync before capture");
+  cudaGraph_t g = nullptr;
+  F5_CU(cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal), "begin capture");
+  cudaError_t e = enqueue_step(c, true);
+  cudaError_t e2 = cudaStreamEndCapture(c->st, &g);
+  if (e != cudaSuccess) { if (g) cudaGraphDestroy(g); return cuda_status(e, "capture decode step"); }
+  F5_CU(e2, "end capture");
+  e = cudaGraphInstantiate(&c->step_exec, g, 0);
+  cudaGraphDestroy(g);
+  F5_CU(e, "instantiate decode graph");
+  c->graph_dirty = false;
+  return F5_OK;
+}
+
+static int finish_host(f5_ctx *c, const char *what) {
+  F5_CU(cudaMemcpyAsync(c->h_params, c->params, sizeof(StepParams), cudaMemcpyDeviceToHost, c->st), what);
+  F5_CU(cudaStreamSynchronize(c->st), what);
+  if (c->h_params->err & DERR_Y32_OVERFLOW) return set_error(F5_EOVERFLOW, "%s: y32 overflow (ref/w4a8_ref.py:288)", what);
+  if (c->h_params->err & DERR_TIMEOUT) return set_error(F5_ETIMEOUT, "%s: a bounded device wait gave up", what);
+  if (c->h_params->err & DERR_KV_FULL) return set_error(F5_ESTATE, "%s: KV cache full or position outside the RoPE table", what);
+  if (c->h_params->err & DERR_RANGE) return set_error(F5_EINVAL, "%s: token id outside the vocabulary", what);
+  return F5_OK;
+}
+
+}  // namespace f5
+
+using namespace f5;
+
+extern "C" {
+
+int f5_ctx_create(const f5_config *cfg, int device, f5_ctx **out) {
+  if (!cfg || !out) return set_error(F5_EINVAL, "f5_ctx_create: null argument");
+  if (cfg->abi_version != F5_ABI_VERSION) return set_error(F5_EINVAL, "ABI version %d != %d", cfg->abi_version, F5_ABI_VERSION);
+  if (cfg->n_layers <= 0 || cfg->vocab <= 0 || cfg->max_T <= 0 || cfg->world_size < 1 || cfg->rank < 0 ||
+      cfg->rank >= cfg->world_size || (cfg->norm_mode != 0 && cfg->norm_mode != 1))
+    return set_error(F5_EINVAL, "f5_ctx_create: bad config");
+  if (!cfg->layer_types || (int)strlen(cfg->layer_types) != cfg->n_layers)
+    return set_error(F5_EINVAL, "layer_types must hold n_layers chars of 'D' / 'A'");
+  DevGuard dg(device);
+  f5_ctx *c = new f5_ctx();
+  c->cfg = *cfg;
+  c->device = device;
+  std::string types(cfg->layer_types);
+  c->cfg.layer_types = nullptr;
+  int rc = F5_OK;
+  auto fail = [&](int r) { f5_ctx_destroy(c); return r; };
+  if ((rc = cuda_status(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking), "stream"))) return fail(rc);
+  c->L.resize(cfg->n_layers);
+  for (int i = 0; i < cfg->n_layers; ++i) {
+    Layer &l = c->L[i];
+    if (types[i] != 'A' && types[i] != 'D') return fail(set_error(F5_EINVAL, "layer_types[%d] = '%c'", i, types[i]));
+    l.attn = types[i] == 'A';
+    if ((rc = alloc(c, (void **)&l.ln1, H * 4)) || (rc = alloc(c, (void **)&l.ln2, H * 4))) return fail(rc);
+    if (l.attn) {
+      const size_t kv = (size_t)NKV * cfg->max_T;
+      if ((rc = alloc(c, (void **)&l.q_norm, HD * 4)) || (rc = alloc(c, (void **)&l.k_norm, HD * 4)) ||
+          (rc = alloc(c, (void **)&l.k8, kv * HD)) || (rc = alloc(c, (void **)&l.v8, kv * HD)) ||
+          (rc = alloc(c, (void **)&l.ke, kv)) || (rc = alloc(c, (void **)&l.ve, kv)) ||
+          (rc = alloc(c, (void **)&l.ka, 16)))
+        return fail(rc);
+    } else {
+      if ((rc = alloc(c, (void **)&l.conv_w, (size_t)CONV_DIM * 4 * 4)) || (rc = alloc(c, (void **)&l.dt_bias, LNH * 4)) ||
+          (rc = alloc(c, (void **)&l.A, LNH * 4)) || (rc = alloc(c, (void **)&l.norm_w, LDV * 4)) ||
+          (rc = alloc(c, (void **)&l.conv, (size_t)CONV_DIM * 4 * 2)) ||
+          (rc = alloc(c, (void **)&l.S, (size_t)LNH * LDK * LDV * 2)) || (rc = alloc(c, (void **)&l.kh, LNH * 4)))
+        return fail(rc);
+    }
+  }
+  if ((rc = alloc(c, (void **)&c->ln_f, H * 4)) || (rc = alloc(c, (void **)&c->x16, H * 2)) ||
+      (rc = alloc(c, (void **)&c->qkv16, CONV_DIM * 2)) || (rc = alloc(c, (void **)&c->z16, LVD * 2)) ||
+      (rc = alloc(c, (void **)&c->b16, 64 * 2)) || (rc = alloc(c, (void **)&c->a16, 64 * 2)) ||
+      (rc = alloc(c, (void **)&c->on16, LVD * 2)) || (rc = alloc(c, (void **)&c->qg16, NQ * HD * 2 * 2)) ||
+      (rc = alloc(c, (void **)&c->k16, NKV * HD * 2)) || (rc = alloc(c, (void **)&c->v16, NKV * HD * 2)) ||
+      (rc = alloc(c, (void **)&c->prod16, FFN * 2)) || (rc = alloc(c, (void **)&c->prod64, NQ * HD * 8)) ||
+      (rc = alloc(c, (void **)&c->x8, FFN)) || (rc = alloc(c, (void **)&c->xmeta, 16)) ||
+      (rc = alloc(c, (void **)&c->key, 8)) || (rc = alloc(c, (void **)&c->stats, 8)) ||
+      (rc = alloc(c, (void **)&c->err, 4)) || (rc = alloc(c, (void **)&c->params, sizeof(StepParams))))
+    return fail(rc);
+  if ((rc = cuda_status(cudaMallocHost(&c->h_params, sizeof(StepParams)), "cudaMallocHost"))) return fail(rc);
+  memset(c->h_params, 0, sizeof(StepParams));
+  if ((rc = cuda_status(cudaStreamSynchronize(c->st), "create sync"))) return fail(rc);
+  *out = c;
+  return F5_OK;
+}
+
+int f5_ctx_destroy(f5_ctx *c) {
+  if (!c) return F5_OK;
+  DevGuard dg(c->device);
+  if (c->st) cudaStreamSynchronize(c->st);
+  if (c->step_exec) cudaGraphExecDestroy(c->step_exec);
+  for (void *p : c->allocs) cudaFree(p);
+  if (c->h_params) cudaFreeHost(c->h_params);
+  if (c->st) cudaStreamDestroy(c->st);
+  delete c;
+  return F5_OK;
+}
+
+int f5_ctx_upload_matrix(f5_ctx *c, int layer, int slot, const uint8_t *img, int N, int K, int g, int e, int sh) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  if (!img) return set_error(F5_EINVAL, "f5_ctx_upload_matrix: null image");
+  DevGuard dg(c->device);
+  DevMat *m;
+  if ((rc = prep_matrix(c, layer, slot, N, K, g, e, sh, m))) return rc;
+  F5_CU(cudaMemcpyAsync(m->w, img + (size_t)m->row0 * m->stride, (size_t)m->rows * m->stride,
+                        cudaMemcpyHostToDevice, c->st), "upload matrix");
+  F5_CU(cudaStreamSynchronize(c->st), "upload matrix");
+  return F5_OK;
+}
+
+int f5_ctx_synth_matrix(f5_ctx *c, int layer, int slot, int N, int K, int g, int e, int sh, uint64_t key_w,
+                        uint64_t key_m, int symmetric) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  DevGuard dg(c->device);
+  DevMat *m;
+  if ((rc = prep_matrix(c, layer, slot, N, K, g, e, sh, m))) return rc;
+  F5_CU(launch_synth_w4(m->w, m->rows, K, g, m->row0, key_w, key_m, symmetric, c->st), "synth matrix");
+  return F5_OK;
+}
+
+int f5_ctx_upload_vector(f5_ctx *c, int layer, int kind, const int64_t *v, int n) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  if (!v) return set_error(F5_EINVAL, "f5_ctx_upload_vector: null data");
+  DevGuard dg(c->device);
+  int32_t *dst = nullptr;
+  int want = 0;
+  if (layer == -1) {
+    if (kind == F5_VEC_LN_F) { dst = c->ln_f; want = H; }
+  } else if (layer >= 0 && layer < (int)c->L.size()) {
+    Layer &l = c->L[layer];
+    switch (kind) {
+      case F5_VEC_LN1: dst = l.ln1; want = H; break;
+      case F5_VEC_LN2: dst = l.ln2; want = H; break;
+      case F5_VEC_Q_NORM: dst = l.q_norm; want = HD; break;
+      case F5_VEC_K_NORM: dst = l.k_norm; want = HD; break;
+      case F5_VEC_CONV_W: dst = l.conv_w; want = CONV_DIM * 4; break;
+      case F5_VEC_DT_BIAS: dst = l.dt_bias; want = LNH; break;
+      case F5_VEC_A: dst = l.A; want = LNH; break;
+      case F5_VEC_NORM_W: dst = l.norm_w; want = LDV; break;
+      default: break;
+    }
+  }
+  if (!dst) return set_error(F5_EINVAL, "no vector kind %d in layer %d", kind, layer);
+  if (n != want) return set_error(F5_EINVAL, "vector kind %d: %d values, expected %d", kind, n, want);
+  std::vector<int32_t> tmp(n);
+  for (int i = 0; i < n; ++i) {
+    if (v[i] < INT32_MIN || v[i] > INT32_MAX) return set_error(F5_EINVAL, "vector kind %d: value outside int32", kind);
+    tmp[i] = (int32_t)v[i];
+  }
+  F5_CU(cudaMemcpyAsync(dst, tmp.data(), n * 4, cudaMemcpyHostToDevice, c->st), "upload vector");
+  F5_CU(cudaStreamSynchronize(c->st), "upload vector");
+  return F5_OK;
+}
+
+static int ensure_emb(f5_ctx *c) {
+  if (!c->emb) {
+    F5_ALLOC(c, c->emb, (size_t)c->cfg.vocab * H * 2);
+    c->graph_dirty = true;
+  }
+  return F5_OK;
+}
+
+int f5_ctx_upload_embedding(f5_ctx *c, const int16_t *emb, int vocab, int h) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  if (!emb || vocab != c->cfg.vocab || h != H) return set_error(F5_EINVAL, "embedding must be [vocab][4096] int16");
+  DevGuard dg(c->device);
+  if ((rc = ensure_emb(c))) return rc;
+  F5_CU(cudaMemcpyAsync(c->emb, emb, (size_t)vocab * H * 2, cudaMemcpyHostToDevice, c->st), "upload embedding");
+  F5_CU(cudaStreamSynchronize(c->st), "upload embedding");
+  return F5_OK;
+}
+
+int f5_ctx_synth_embedding(f5_ctx *c, uint64_t key_e) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  DevGuard dg(c->device);
+  if ((rc = ensure_emb(c))) return rc;
+  F5_CU(launch_synth_emb(c->emb, c->cfg.vocab, H, 0, key_e, c->st), "synth embedding");
+  return F5_OK;
+}
+
+int f5_ctx_upload_rope(f5_ctx *c, const int16_t *tab, int npos) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  if (!tab || npos <= 0) return set_error(F5_EINVAL, "RoPE table must be [npos][128] int16");
+  DevGuard dg(c->device);
+  if (c->rope && npos > c->rope_npos) return set_error(F5_EINVAL, "RoPE table cannot grow");
+  if (!c->rope) F5_ALLOC(c, c->rope, (size_t)npos * 128 * 2);
+  c->rope_npos = npos;
+  F5_CU(cudaMemcpyAsync(c->rope, tab, (size_t)npos * 128 * 2, cudaMemcpyHostToDevice, c->st), "upload rope");
+  F5_CU(cudaStreamSynchronize(c->st), "upload rope");
+  c->graph_dirty = true;
+  return F5_OK;
+}
+
+int f5_ctx_reset(f5_ctx *c) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  DevGuard dg(c->device);
+  for (Layer &l : c->L) {
+    if (l.attn) {
+      const size_t kv = (size_t)NKV * c->cfg.max_T;
+      F5_CU(cudaMemsetAsync(l.k8, 0, kv * HD, c->st), "reset");
+      F5_CU(cudaMemsetAsync(l.v8, 0, kv * HD, c->st), "reset");
+      F5_CU(cudaMemsetAsync(l.ke, 0, kv, c->st), "reset");
+      F5_CU(cudaMemsetAsync(l.ve, 0, kv, c->st), "reset");
+    } else {
+      F5_CU(cudaMemsetAsync(l.conv, 0, (size_t)CONV_DIM * 4 * 2, c->st), "reset");
+      F5_CU(cudaMemsetAsync(l.S, 0, (size_t)LNH * LDK * LDV * 2, c->st), "reset");
+    }
+  }
+  F5_CU(cudaMemsetAsync(c->params, 0, sizeof(StepParams), c->st), "reset");
+  F5_CU(cudaMemsetAsync(c->err, 0, 4, c->st), "reset");
+  F5_CU(cudaMemsetAsync(c->stats, 0, 8, c->st), "reset");
+  F5_CU(cudaStreamSynchronize(c->st), "reset");
+  return F5_OK;
+}
+
+int f5_ctx_set_position(f5_ctx *c, int T, int pos) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  if (T < 0 || T > c->cfg.max_T) return set_error(F5_EINVAL, "T=%d outside [0, max_T]", T);
+  DevGuard dg(c->device);
+  F5_CU(cudaMemcpyAsync(c->h_params, c->params, sizeof(StepParams), cudaMemcpyDeviceToHost, c->st), "set position");
+  F5_CU(cudaStreamSynchronize(c->st), "set position");
+  c->h_params->T = T;
+  c->h_params->pos = pos;
+  F5_CU(cudaMemcpyAsync(c->params, c->h_params, sizeof(StepParams), cudaMemcpyHostToDevice, c->st), "set position");
+  F5_CU(cudaStreamSynchronize(c->st), "set position");
+  return F5_OK;
+}
+
+int f5_ctx_get_position(f5_ctx *c, int *T, int *pos) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  DevGuard dg(c->device);
+  F5_CU(cudaMemcpyAsync(c->h_params, c->params, sizeof(StepParams), cudaMemcpyDeviceToHost, c->st), "get position");
+  F5_CU(cudaStreamSynchronize(c->st), "get position");
+  if (T) *T = c->h_params->T;
+  if (pos) *pos = c->h_params->pos;
+  return F5_OK;
+}
+
+int f5_ctx_set_logits(f5_ctx *c, int on) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  DevGuard dg(c->device);
+  if (on && !c->logits) F5_ALLOC(c, c->logits, (size_t)c->cfg.vocab * 4);
+  if ((bool)on != c->want_logits) {
+    c->want_logits = on != 0;
+    c->graph_dirty = true;
+  }
+  return F5_OK;
+}
+
+int f5_ctx_stream(f5_ctx *c, void **stream) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  if (!stream) return set_error(F5_EINVAL, "f5_ctx_stream: null out");
+  *stream = (void *)c->st;
+  return F5_OK;
+}
+
+int f5_ctx_prepare(f5_ctx *c) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  DevGuard dg(c->device);
+  return build_graph(c);
+}
+
+int f5_decode_step(f5_ctx *c, int32_t tok, int32_t pos, int32_t *next_tok, int32_t *max_logit) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  DevGuard dg(c->device);
+  if ((rc = build_graph(c))) return rc;
+  F5_CU(cudaMemcpyAsync(c->h_params, c->params, sizeof(StepParams), cudaMemcpyDeviceToHost, c->st), "decode step");
+  F5_CU(cudaStreamSynchronize(c->st), "decode step");
+  c->h_params->tok = tok;
+  c->h_params->pos = pos;
+  c->h_params->err = 0;
+  F5_CU(cudaMemcpyAsync(c->params, c->h_params, sizeof(StepParams), cudaMemcpyHostToDevice, c->st), "decode step");
+  F5_CU(cudaMemsetAsync(c->err, 0, 4, c->st), "decode step");
+  F5_CU(cudaGraphLaunch(c->step_exec, c->st), "decode step");
+  if ((rc = finish_host(c, "f5_decode_step"))) return rc;
+  if (next_tok) *next_tok = c->h_params->next_tok;
+  if (max_logit) *max_logit = c->h_params->max_val;
+  return F5_OK;
+}
+
+int f5_decode_launch(f5_ctx *c, int n_steps, void *stream_unused) {
+  (void)stream_unused;
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  DevGuard dg(c->device);
+  if ((rc = build_graph(c))) return rc;
+  for (int i = 0; i < n_steps; ++i) F5_CU(cudaGraphLaunch(c->step_exec, c->st), "decode launch");
+  return F5_OK;
+}
+
+int f5_ctx_sync(f5_ctx *c, int32_t *last_tok, int32_t *max_logit) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  DevGuard dg(c->device);
+  if ((rc = finish_host(c, "f5_ctx_sync"))) return rc;
+  if (last_tok) *last_tok = c->h_params->next_tok;
+  if (max_logit) *max_logit = c->h_params->max_val;
+  return F5_OK;
+}
+
+int f5_ctx_time_step(f5_ctx *c, int reps, double *out, int nout) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  if (!out || nout < 8 || reps < 1) return set_error(F5_EINVAL, "f5_ctx_time_step: out[8] and reps >= 1 required");
+  DevGuard dg(c->device);
+  if ((rc = ready(c))) return rc;
+  for (int i = 0; i < 8; ++i) out[i] = 0;
+  for (int r = 0; r < reps; ++r) {
+    c->timing = true;
+    c->timed.clear();
+    cudaError_t e = enqueue_step(c, false);
+    c->timing = false;
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->st);
+    for (auto &t : c->timed) {
+      float ms = 0;
+      if (e == cudaSuccess) cudaEventElapsedTime(&ms, t.a, t.b);
+      const int slot = t.kind == TK_GEMV ? 0 : (t.kind == TK_DN ? 3 : (t.kind == TK_ATTN ? 4 : 5));
+      out[slot] += ms;
+      if (t.kind == TK_GEMV) { out[1] += t.bytes; out[2] += 1; }
+      out[6] += ms;
+      out[7] += 1;
+      cudaEventDestroy(t.a);
+      cudaEventDestroy(t.b);
+    }
+    c->timed.clear();
+    if (e != cudaSuccess) return cuda_status(e, "f5_ctx_time_step");
+  }
+  for (int i = 0; i < 8; ++i) out[i] /= reps;
+  return finish_host(c, "f5_ctx_time_step");
+}
+
+int f5_layer_step(f5_ctx *c, int layer, int16_t *x16_inout, int T, int pos) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  if (!x16_inout || layer < 0 || layer >= (int)c->L.size()) return set_error(F5_EINVAL, "f5_layer_step: bad layer / buffer");
+  DevGuard dg(c->device);
+  if ((rc = layer_ready(c, layer))) return rc;
+  F5_CU(cudaMemcpyAsync(c->h_params, c->params, sizeof(StepParams), cudaMemcpyDeviceToHost, c->st), "layer step");
+  F5_CU(cudaStreamSynchronize(c->st), "layer step");
+  if (T < 0 || T >= c->cfg.max_T) return set_error(F5_ESTATE, "f5_layer_step: T=%d outside [0, max_T)", T);
+  c->h_params->T = T;
+  c->h_params->pos = pos;
+  c->h_params->err = 0;
+  F5_CU(cudaMemcpyAsync(c->params, c->h_params, sizeof(StepParams), cudaMemcpyHostToDevice, c->st), "layer step");
+  F5_CU(cudaMemsetAsync(c->err, 0, 4, c->st), "layer step");
+  F5_CU(cudaMemcpyAsync(c->x16, x16_inout, H * 2, cudaMemcpyHostToDevice, c->st), "layer step");
+  F5_CU(enqueue_layer(c, layer, false), "layer step");
+  {
+    StepParams *p = c->params;
+    const uint32_t *er = c->err;
+    void *args[] = {&p, &er};
+    F5_CU(launch_pdl((const void *)k_collect_err, args, dim3(1), dim3(1), c->st, false), "layer step");
+  }
+  F5_CU(cudaMemcpyAsync(x16_inout, c->x16, H * 2, cudaMemcpyDeviceToHost, c->st), "layer step");
+  return finish_host(c, "f5_layer_step");
+}
+
+int f5_ctx_read(f5_ctx *c, int what, int layer, void *dst, size_t bytes) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  if (!dst) return set_error(F5_EINVAL, "f5_ctx_read: null destination");
+  DevGuard dg(c->device);
+  const void *src = nullptr;
+  size_t n = 0;
+  Layer *l = (layer >= 0 && layer < (int)c->L.size()) ? &c->L[layer] : nullptr;
+  switch (what) {
+    case F5_BUF_X16: src = c->x16; n = H * 2; break;
+    case F5_BUF_QKV16: src = c->qkv16; n = CONV_DIM * 2; break;
+    case F5_BUF_Z16: src = c->z16; n = LVD * 2; break;
+    case F5_BUF_B16: src = c->b16; n = LNH * 2; break;
+    case F5_BUF_A16: src = c->a16; n = LNH * 2; break;
+    case F5_BUF_ON16: src = c->on16; n = LVD * 2; break;
+    case F5_BUF_QG16: src = c->qg16; n = NQ * HD * 2 * 2; break;
+    case F5_BUF_K16: src = c->k16; n = NKV * HD * 2; break;
+    case F5_BUF_V16: src = c->v16; n = NKV * HD * 2; break;
+    case F5_BUF_PROD64: src = c->prod64; n = NQ * HD * 8; break;
+    case F5_BUF_PROD16: src = c->prod16; n = FFN * 2; break;
+    case F5_BUF_STATS: src = c->stats; n = 8; break;
+    case F5_BUF_DN_S: if (l && !l->attn) { src = l->S; n = (size_t)LNH * LDK * LDV * 2; } break;
+    case F5_BUF_DN_CONV: if (l && !l->attn) { src = l->conv; n = (size_t)CONV_DIM * 4 * 2; } break;
+    case F5_BUF_DN_KH: if (l && !l->attn) { src = l->kh; n = LNH * 4; } break;
+    case F5_BUF_K8: if (l && l->attn) { src = l->k8; n = (size_t)NKV * c->cfg.max_T * HD; } break;
+    case F5_BUF_KE: if (l && l->attn) { src = l->ke; n = (size_t)NKV * c->cfg.max_T; } break;
+    case F5_BUF_V8: if (l && l->attn) { src = l->v8; n = (size_t)NKV * c->cfg.max_T * HD; } break;
+    case F5_BUF_VE: if (l && l->attn) { src = l->ve; n = (size_t)NKV * c->cfg.max_T; } break;
+    case F5_BUF_KA: if (l && l->attn) { src = l->ka; n = 4; } break;
+    case F5_BUF_LOGITS: if (c->logits) { src = c->logits; n = (size_t)c->cfg.vocab * 4; } break;
+    default: break;
+  }
+  if (!src) return set_error(F5_EINVAL, "f5_ctx_read: no buffer %d for layer %d", what, layer);
+  if (bytes != n) return set_error(F5_EINVAL, "f5_ctx_read: buffer %d holds %zu bytes, asked %zu", what, n, bytes);
+  F5_CU(cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToHost, c->st), "f5_ctx_read");
+  F5_CU(cudaStreamSynchronize(c->st), "f5_ctx_read");
+  return F5_OK;
+}
+
+int f5_ctx_write(f5_ctx *c, int what, int layer, const void *src, size_t bytes) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  if (!src) return set_error(F5_EINVAL, "f5_ctx_write: null source");
+  DevGuard dg(c->device);
+  void *dst = nullptr;
+  size_t n = 0;
+  Layer *l = (layer >= 0 && layer < (int)c->L.size()) ? &c->L[layer] : nullptr;
+  switch (what) {
+    case F5_BUF_X16: dst = c->x16; n = H * 2; break;
+    case F5_BUF_DN_S: if (l && !l->attn) { dst = l->S; n = (size_t)LNH * LDK * LDV * 2; } break;
+    case F5_BUF_DN_CONV: if (l && !l->attn) { dst = l->conv; n = (size_t)CONV_DIM * 4 * 2; } break;
+    case F5_BUF_K8: if (l && l->attn) { dst = l->k8; n = (size_t)NKV * c->cfg.max_T * HD; } break;
+    case F5_BUF_KE: if (l && l->attn) { dst = l->ke; n = (size_t)NKV * c->cfg.max_T; } break;
+    case F5_BUF_V8: if (l && l->attn) { dst = l->v8; n = (size_t)NKV * c->cfg.max_T * HD; } break;
+    case F5_BUF_VE: if (l && l->attn) { dst = l->ve; n = (size_t)NKV * c->cfg.max_T; } break;
+    default: break;
+  }
+  if (!dst) return set_error(F5_EINVAL, "f5_ctx_write: buffer %d of layer %d is not writable", what, layer);
+  if (bytes != n) return set_error(F5_EINVAL, "f5_ctx_write: buffer %d holds %zu bytes, got %zu", what, n, bytes);
+  F5_CU(cudaMemcpyAsync(dst, src, n, cudaMemcpyHostToDevice, c->st), "f5_ctx_write");
+  F5_CU(cudaStreamSynchronize(c->st), "f5_ctx_write");
+  return F5_OK;
+}
+
+}  // extern "C"

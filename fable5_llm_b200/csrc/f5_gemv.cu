@@ -25,7 +25,7 @@
 // m_g * acc is applied per lane-chunk (linear, so summing partial group sums
 // times m_g equals m_g times the group sum -- integer arithmetic is exact
 // and order-free).
-#include "f5_int.cuh"
+#include "f5_block.cuh"
 #include "f5_kernels.cuh"
 
 namespace f5 {
@@ -69,119 +69,437 @@ F5_DEV int32_t finish_y32(long long p16, int sh, uint32_t *err, long long *p_exa
   return (int32_t)y;
 }
 
+F5_DEV void load8_i16(const int16_t *p, long long v[8]) {
+  const uint4 u = *reinterpret_cast<const uint4 *>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    v[2 * j] = (int16_t)(w[j] & 0xFFFFu);
+    v[2 * j + 1] = (int16_t)(w[j] >> 16);
+  }
+}
+F5_DEV void load8_i64(const int64_t *p, long long v[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; j += 2) {
+    const longlong2 u = *reinterpret_cast<const longlong2 *>(p + j);
+    v[j] = u.x;
+    v[j + 1] = u.y;
+  }
+}
+F5_DEV void put8(uint2 *xs, int b, const long long x[8]) {
+  uint32_t ev = 0, od = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    ev |= ((uint32_t)(x[2 * j] & 0xFF)) << (8 * j);
+    od |= ((uint32_t)(x[2 * j + 1] & 0xFF)) << (8 * j);
+  }
+  xs[(((b >> 7) << 2) + (b & 3)) * 32 + ((b >> 2) & 31)] = make_uint2(ev, od);
+}
+
+// rmsnorm_fx element (ref/layer_fixed.py:1242-1278): clip33(rshr(x*r, 30-e)) * gain
+F5_DEV long long rms_elem(long long x, long long r, int e, long long gain) {
+  long long y = rshr(x * r, 30 - e);
+  y = clip(y, -(1ll << 32), (1ll << 32) - 1);
+  return clip16(rshr(y * gain, 14));
+}
+
+// Redundant per-CTA computation of the GEMV's quantized input (see GemvPro).
+F5_DEV void prologue(const GemvArgs &a, uint2 *xs, long long *red, long long *s_r, int *s_meta) {
+  const int tid = threadIdx.x, K = a.K, nblk = K >> 3;
+  const GemvPrologue &P = a.pro;
+  const bool store = (P.xq_out.x8 != nullptr) && blockIdx.x == 0;
+  long long v[8];
+  if (P.mode == PRO_RMSNORM) {
+    const int16_t *src = static_cast<const int16_t *>(P.src);
+    long long ss = 0;
+    for (int b = tid; b < nblk; b += blockDim.x) {
+      load8_i16(src + 8 * b, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+    }
+    ss = block_sum_ll(ss, red);
+    if (tid == 0) {
+      int64_t r; int e;
+      rsqrt_q((uint64_t)(ss == 0 ? 1 : ss), 2 * P.in_f + (31 - __clz(K)), r, e);
+      *s_r = r;
+      s_meta[2] = e;
+    }
+    __syncthreads();
+    const long long r = *s_r;
+    const int e = s_meta[2];
+    const long long add1 = P.one_plus ? (1 << 14) : 0;
+    unsigned long long mx = 0;
+    for (int b = tid; b < nblk; b += blockDim.x) {
+      load8_i16(src + 8 * b, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const unsigned long long m = uabs(rms_elem(v[j], r, e, P.w[8 * b + j] + add1));
+        mx = m > mx ? m : mx;
+      }
+    }
+    mx = block_max_ull(mx, reinterpret_cast<unsigned long long *>(red));
+    const int ex = dynq8_e(mx);
+    for (int b = tid; b < nblk; b += blockDim.x) {
+      load8_i16(src + 8 * b, v);
+      long long q[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        q[j] = dynq8_apply(rms_elem(v[j], r, e, P.w[8 * b + j] + add1), ex);
+        if (store) P.xq_out.x8[8 * b + j] = (int8_t)q[j];
+      }
+      put8(xs, b, q);
+    }
+    if (tid == 0) { s_meta[0] = ex; s_meta[1] = P.in_f; }
+  } else if (P.mode == PRO_DYNQ8) {
+    const int16_t *src = static_cast<const int16_t *>(P.src);
+    unsigned long long mx = 0;
+    for (int b = tid; b < nblk; b += blockDim.x) {
+      load8_i16(src + 8 * b, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) { const unsigned long long m = uabs(v[j]); mx = m > mx ? m : mx; }
+    }
+    mx = block_max_ull(mx, reinterpret_cast<unsigned long long *>(red));
+    const int ex = dynq8_e(mx);
+    for (int b = tid; b < nblk; b += blockDim.x) {
+      load8_i16(src + 8 * b, v);
+      long long q[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        q[j] = dynq8_apply(v[j], ex);
+        if (store) P.xq_out.x8[8 * b + j] = (int8_t)q[j];
+      }
+      put8(xs, b, q);
+    }
+    if (tid == 0) { s_meta[0] = ex; s_meta[1] = P.in_f; }
+  } else {  // PRO_ATTN_GATE (ref/layer_fixed.py:1441-1449)
+    const int64_t *src = static_cast<const int64_t *>(P.src);
+    unsigned long long mx = 0;
+    for (int b = tid; b < nblk; b += blockDim.x) {
+      load8_i64(src + 8 * b, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) { const unsigned long long m = uabs(v[j]); mx = m > mx ? m : mx; }
+    }
+    mx = block_max_ull(mx, reinterpret_cast<unsigned long long *>(red));
+    int ka = bf_shift(mx);
+    if (ka < 0) ka = 0;                      // attn_o_shift clamp (ref/layer_fixed.py:489-506)
+    unsigned long long mg = 0;
+    for (int b = tid; b < nblk; b += blockDim.x) {
+      load8_i64(src + 8 * b, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) { const unsigned long long m = uabs(clip16(rshr(v[j], ka))); mg = m > mg ? m : mg; }
+    }
+    mg = block_max_ull(mg, reinterpret_cast<unsigned long long *>(red));
+    const int ex = dynq8_e(mg);
+    for (int b = tid; b < nblk; b += blockDim.x) {
+      load8_i64(src + 8 * b, v);
+      long long q[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        q[j] = dynq8_apply(clip16(rshr(v[j], ka)), ex);
+        if (store) P.xq_out.x8[8 * b + j] = (int8_t)q[j];
+      }
+      put8(xs, b, q);
+    }
+    if (tid == 0) {
+      s_meta[0] = ex;
+      s_meta[1] = QKV_F + GAT_F - ka;
+      if (P.dbg && blockIdx.x == 0) *P.dbg = ka;
+    }
+  }
+  if (store && tid == 0) {
+    P.xq_out.meta[0] = s_meta[0];
+    P.xq_out.meta[1] = s_meta[1];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Epilogues (ref/layer_fixed.py:1224-1236 matvec_to and its call sites)
+// ---------------------------------------------------------------------------
+F5_DEV void epilogue_row(const GemvArgs &a, const GemvSeg &sg, int row, long long acc16, int e_x,
+                         int in_f, unsigned long long &best) {
+  long long pex;
+  const int32_t y = finish_y32(acc16, a.sh, a.err, &pex);
+  const int orow = sg.out_row0 + row;
+  if (sg.mode == GM_ARGMAX) {
+    const unsigned long long k = argmax_key(y, orow);
+    best = k > best ? k : best;
+    if (sg.out) static_cast<int32_t *>(sg.out)[orow] = y;   // optional logits
+    return;
+  }
+  if (sg.p_out) sg.p_out[orow] = pex;
+  const int sh2 = (15 - sg.e - a.sh) - e_x + in_f - sg.out_f;
+  switch (sg.mode) {
+    case GM_Y32: static_cast<int32_t *>(sg.out)[orow] = y; break;
+    case GM_TO16: static_cast<int16_t *>(sg.out)[orow] = (int16_t)clip16(shift_to(y, sh2)); break;
+    case GM_TO64: static_cast<int64_t *>(sg.out)[orow] = shift_to(y, sh2); break;
+    case GM_RESID: {
+      int16_t *o = static_cast<int16_t *>(sg.out) + orow;
+      *o = (int16_t)clip16((int64_t)*o + clip16(shift_to(y, sh2)));
+    } break;
+    default: break;
+  }
+}
+
+// MLP gate/up pair (ref/layer_fixed.py:1597-1602)
+F5_DEV void epilogue_pair(const GemvArgs &a, const GemvSeg &sg, int row, long long accg, long long accu,
+                          int e_x, int in_f) {
+  const int32_t yg = finish_y32(accg, a.sh, a.err, nullptr);
+  const int32_t yu = finish_y32(accu, a.sh, a.err, nullptr);
+  const int64_t gq = shift_to(yg, (15 - sg.e - a.sh) - e_x + in_f - sg.out_f);
+  const int64_t uq = shift_to(yu, (15 - sg.e2 - a.sh) - e_x + in_f - sg.out_f2);
+  const int64_t sgv = clip16(silu_q(clip(gq, -(1 << 20), (1 << 20) - 1)));
+  static_cast<int16_t *>(sg.out)[sg.out_row0 + row] = (int16_t)clip16(rshr(sgv * uq, 12));
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier / bulk-copy helpers (PTX ISA 8.x, sm_90+; no multicast anywhere)
+// ---------------------------------------------------------------------------
+F5_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+F5_DEV void mbar_init(uint64_t *b, int cnt) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(cnt) : "memory");
+}
+F5_DEV void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
+               : "memory");
+}
+F5_DEV void mbar_arrive(uint64_t *b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+F5_DEV unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait on an mbarrier phase: gives up after ~`limit_ns` (the
+// caller then records DERR_TIMEOUT and unwinds; nothing ever spins forever).
+F5_DEV bool mbar_wait(uint64_t *b, uint32_t parity, unsigned long long limit_ns) {
+  const uint32_t addr = smem_u32(b);
+  unsigned long long t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok) : "r"(addr), "r"(parity) : "memory");
+    if (ok) return true;
+    if ((it & 63) == 0) {
+      const unsigned long long t = gtimer();
+      if (t0 == 0) t0 = t;
+      else if (t - t0 > limit_ns) return false;
+    }
+  }
+}
+F5_DEV void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+constexpr int GT_CONS = 8;                      // consumer warps
+constexpr int GT_THREADS = (GT_CONS + 1) * 32;  // + one producer warp
+constexpr int GT_STAGES = 4;
+constexpr unsigned long long GT_WAIT_NS = 2000000000ull;   // 2 s: a safety net only
+
+F5_DEV int seg_of(const GemvArgs &a, int u) {
+  int s = 0;
+#pragma unroll
+  for (int i = 1; i < GEMV_MAX_SEG; ++i)
+    if (i < a.nseg && u >= a.seg[i].unit_begin) s = i;
+  return s;
+}
+
+// Deterministic chunking of this CTA's unit range (same in producer and
+// consumers): a chunk is <= R rows of ONE segment (paired: R/2 row pairs).
+struct Chunk {
+  int seg, r0, n;
+};
+F5_DEV bool next_chunk(const GemvArgs &a, int &u, int u1, Chunk &ch) {
+  if (u >= u1) return false;
+  const int s = seg_of(a, u);
+  const GemvSeg &sg = a.seg[s];
+  const int seg_end = (s + 1 < a.nseg) ? a.seg[s + 1].unit_begin : a.total_units;
+  const int ru = sg.mode == GM_SILU_MUL ? (a.rows_per_stage >> 1) : a.rows_per_stage;
+  const int n = min(min(ru, u1 - u), seg_end - u);
+  ch.seg = s;
+  ch.r0 = u - sg.unit_begin;
+  ch.n = n;
+  u += n;
+  return true;
+}
+
+// 16*sum_k w*x over one row held in shared memory (lane-strided 16 B reads)
 template <int NCH>
-__global__ void __launch_bounds__(256, 2) k_gemv(const __grid_constant__ GemvArgs a) {
-  extern __shared__ uint2 xs[];
-  const int tid = threadIdx.x, lane = tid & 31;
-  const int wpb = blockDim.x >> 5;
-  const int nw = gridDim.x * wpb;
-  const int gw = blockIdx.x * wpb + (tid >> 5);
+F5_DEV long long row_dot(const uint8_t *row, int K2, int gshift, int lane, const uint2 (&xr)[4][4],
+                         const uint2 *xs) {
+  long long acc = 0;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int boff = c * 512 + lane * 16;
+    if (boff < K2) {
+      const uint4 w = *reinterpret_cast<const uint4 *>(row + boff);
+      const uint32_t m = *reinterpret_cast<const uint16_t *>(row + K2 + 2 * (boff >> gshift));
+      int d;
+      if (NCH <= 4) {
+        d = dot32(w, xr[c & 3][0], xr[c & 3][1], xr[c & 3][2], xr[c & 3][3]);
+      } else {
+        const uint2 *x = xs + (c << 2) * 32 + lane;
+        d = dot32(w, x[0], x[32], x[64], x[96]);
+      }
+      acc += (long long)m * d;
+    }
+  }
+  return acc;
+}
+
+F5_DEV long long warp_sum_ll(long long v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Persistent TMA-pipelined GEMV: one CTA per SM, a producer warp streams
+// contiguous blocks of packed rows (cp.async.bulk, 16-byte aligned, no
+// multicast) into GT_STAGES shared-memory stages guarded by full/empty
+// mbarriers; eight consumer warps reduce rows out of shared memory.  The
+// first stages are issued BEFORE griddepcontrol.wait: the weights do not
+// depend on the previous kernel, so under programmatic dependent launch the
+// weight stream overlaps the producer kernel's tail.
+template <int NCH>
+__global__ void __launch_bounds__(GT_THREADS, 1) k_gemv(const __grid_constant__ GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t bar_full[GT_STAGES], bar_empty[GT_STAGES];
+  __shared__ long long red[32];
+  __shared__ long long s_r;
+  __shared__ int s_meta[4];
+  __shared__ volatile int s_abort;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K2 = a.K >> 1;
   const int gshift = (a.g == 128) ? 6 : 5;
+  const uint32_t stage_bytes = (uint32_t)a.rows_per_stage * (uint32_t)a.stride;
+  uint2 *xs = reinterpret_cast<uint2 *>(smem + GT_STAGES * stage_bytes);
+  const int G = gridDim.x, b = blockIdx.x;
+  const int u0 = (int)((long long)a.total_units * b / G);
+  const int u1 = (int)((long long)a.total_units * (b + 1) / G);
+
+  if (tid == 0) {
+    for (int i = 0; i < GT_STAGES; ++i) {
+      mbar_init(&bar_full[i], 1);
+      mbar_init(&bar_empty[i], GT_CONS);
+    }
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  // producer: the first GT_STAGES chunks need no empty-wait -> issue now
+  int pu = u0, pi = 0;
+  if (warp == GT_CONS && lane == 0) {
+    Chunk ch;
+    while (pi < GT_STAGES && next_chunk(a, pu, u1, ch)) {
+      const GemvSeg &sg = a.seg[ch.seg];
+      const uint32_t nb = (uint32_t)ch.n * a.stride;
+      uint8_t *dst = smem + pi * stage_bytes;
+      const bool pair = sg.mode == GM_SILU_MUL;
+      mbar_expect_tx(&bar_full[pi], pair ? 2 * nb : nb);
+      bulk_g2s(dst, sg.w + (size_t)ch.r0 * a.stride, nb, &bar_full[pi]);
+      if (pair) bulk_g2s(dst + nb, sg.w2 + (size_t)ch.r0 * a.stride, nb, &bar_full[pi]);
+      ++pi;
+    }
+  }
 
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
-  // x8 -> lane-major even/odd layout: 8-k block b sits at [(c*4 + j)*32 + l]
+  // ---- prologue (all warps): x8 into the lane-major even/odd layout ----
   const int nblk = a.K >> 3;
-  for (int b = tid; b < nblk; b += blockDim.x) {
-    const uint2 v = *reinterpret_cast<const uint2 *>(a.x8 + 8 * b);
-    uint2 o;
-    o.x = __byte_perm(v.x, v.y, 0x6420);
-    o.y = __byte_perm(v.x, v.y, 0x7531);
-    xs[(((b >> 7) << 2) + (b & 3)) * 32 + ((b >> 2) & 31)] = o;
+  if (a.pro.mode == PRO_X8) {
+    for (int bb = tid; bb < nblk; bb += blockDim.x) {
+      const uint2 v = *reinterpret_cast<const uint2 *>(a.x8 + 8 * bb);
+      uint2 o;
+      o.x = __byte_perm(v.x, v.y, 0x6420);
+      o.y = __byte_perm(v.x, v.y, 0x7531);
+      xs[(((bb >> 7) << 2) + (bb & 3)) * 32 + ((bb >> 2) & 31)] = o;
+    }
+    if (tid == 0) {
+      s_meta[0] = a.xmeta ? a.xmeta[0] : 0;
+      s_meta[1] = a.xmeta ? a.xmeta[1] : 0;
+    }
+  } else {
+    prologue(a, xs, red, &s_r, s_meta);
   }
-  int e_x = 0, in_f = 0;
-  if (a.xmeta) { e_x = a.xmeta[0]; in_f = a.xmeta[1]; }
   __syncthreads();
+  const int e_x = s_meta[0], in_f = s_meta[1];
 
-  unsigned long long best = 0ull;
-  for (int u = gw; u < a.total_units; u += nw) {
-    int s = 0;
-#pragma unroll
-    for (int i = 1; i < GEMV_MAX_SEG; ++i)
-      if (i < a.nseg && u >= a.seg[i].unit_begin) s = i;
-    const GemvSeg &sg = a.seg[s];
-    const int ul = u - sg.unit_begin;
-    const bool paired = sg.mode == GM_SILU_MUL;
-    int rA, rB;
-    const uint8_t *pa, *pb;
-    bool vB;
-    if (paired) {
-      rA = rB = ul;
-      pa = sg.w + (size_t)ul * a.stride;
-      pb = sg.w2 + (size_t)ul * a.stride;
-      vB = true;
-    } else {
-      rA = 2 * ul;
-      rB = rA + 1;
-      vB = rB < sg.rows;
-      pa = sg.w + (size_t)rA * a.stride;
-      pb = vB ? pa + a.stride : pa;
-    }
-    long long accA = 0, accB = 0;
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      const int boff = c * 512 + lane * 16;
-      if (boff < K2) {
-        const uint4 wa = ld_stream16(pa + boff);
-        const uint4 wb = ld_stream16(pb + boff);
-        const int moff = K2 + 2 * (boff >> gshift);
-        const uint32_t ma = ld_u16(pa + moff);
-        const uint32_t mb = ld_u16(pb + moff);
-        const uint2 *xr = xs + (c << 2) * 32 + lane;
-        const uint2 x0 = xr[0], x1 = xr[32], x2 = xr[64], x3 = xr[96];
-        accA += (long long)ma * dot32(wa, x0, x1, x2, x3);
-        accB += (long long)mb * dot32(wb, x0, x1, x2, x3);
-      }
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      accA += __shfl_xor_sync(0xffffffffu, accA, o);
-      accB += __shfl_xor_sync(0xffffffffu, accB, o);
-    }
-    if (sg.mode == GM_ARGMAX) {
-      if (lane == 0) {
-        const int32_t ya = finish_y32(accA, a.sh, a.err, nullptr);
-        unsigned long long k = argmax_key(ya, sg.out_row0 + rA);
-        if (vB) {
-          const int32_t yb = finish_y32(accB, a.sh, a.err, nullptr);
-          const unsigned long long kb = argmax_key(yb, sg.out_row0 + rB);
-          k = kb > k ? kb : k;
+  if (warp == GT_CONS) {
+    // ---- producer: remaining chunks, each after its stage is released ----
+    if (lane == 0) {
+      Chunk ch;
+      int issued = pi;
+      while (!s_abort && next_chunk(a, pu, u1, ch)) {
+        const int s = issued % GT_STAGES;
+        if (!mbar_wait(&bar_empty[s], ((issued / GT_STAGES) - 1) & 1, GT_WAIT_NS)) {
+          s_abort = 1;
+          atomicOr(a.err, DERR_TIMEOUT);
+          break;
         }
-        best = k > best ? k : best;
+        const GemvSeg &sg = a.seg[ch.seg];
+        const uint32_t nb = (uint32_t)ch.n * a.stride;
+        uint8_t *dst = smem + s * stage_bytes;
+        const bool pair = sg.mode == GM_SILU_MUL;
+        mbar_expect_tx(&bar_full[s], pair ? 2 * nb : nb);
+        bulk_g2s(dst, sg.w + (size_t)ch.r0 * a.stride, nb, &bar_full[s]);
+        if (pair) bulk_g2s(dst + nb, sg.w2 + (size_t)ch.r0 * a.stride, nb, &bar_full[s]);
+        ++issued;
       }
-      continue;
-    }
-    if (paired) {
-      if (lane == 0) {
-        const int32_t yg = finish_y32(accA, a.sh, a.err, nullptr);
-        const int32_t yu = finish_y32(accB, a.sh, a.err, nullptr);
-        const int64_t gq = shift_to(yg, (15 - sg.e - a.sh) - e_x + in_f - sg.out_f);
-        const int64_t uq = shift_to(yu, (15 - sg.e2 - a.sh) - e_x + in_f - sg.out_f2);
-        const int64_t sgv = clip16(silu_q(clip(gq, -(1 << 20), (1 << 20) - 1)));
-        static_cast<int16_t *>(sg.out)[sg.out_row0 + rA] = (int16_t)clip16(rshr(sgv * uq, 12));
-      }
-      continue;
-    }
-    if (lane < 2 && (lane == 0 || vB)) {
-      const int row = lane == 0 ? rA : rB;
-      long long pex;
-      const int32_t y = finish_y32(lane == 0 ? accA : accB, a.sh, a.err, &pex);
-      const int orow = sg.out_row0 + row;
-      if (sg.p_out) sg.p_out[orow] = pex;
-      const int sh2 = (15 - sg.e - a.sh) - e_x + in_f - sg.out_f;
-      switch (sg.mode) {
-        case GM_Y32: static_cast<int32_t *>(sg.out)[orow] = y; break;
-        case GM_TO16: static_cast<int16_t *>(sg.out)[orow] = (int16_t)clip16(shift_to(y, sh2)); break;
-        case GM_TO64: static_cast<int64_t *>(sg.out)[orow] = shift_to(y, sh2); break;
-        case GM_RESID: {
-          int16_t *o = static_cast<int16_t *>(sg.out) + orow;
-          *o = (int16_t)clip16((int64_t)*o + clip16(shift_to(y, sh2)));
-        } break;
-        default: break;
+      // never leave the CTA with copies in flight: drain every issued stage
+      // the consumers have not waited on (bounded)
+      if (s_abort) {
+        for (int i = max(0, issued - GT_STAGES); i < issued; ++i)
+          mbar_wait(&bar_full[i % GT_STAGES], (i / GT_STAGES) & 1, GT_WAIT_NS);
       }
     }
+    return;
+  }
+
+  // ---- consumers ----
+  uint2 xr[4][4];
+  if (NCH <= 4) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) xr[c][j] = c < NCH ? xs[((c << 2) + j) * 32 + lane] : make_uint2(0, 0);
+  }
+  unsigned long long best = 0ull;
+  int cu = u0, ci = 0;
+  Chunk ch;
+  while (next_chunk(a, cu, u1, ch)) {
+    const int s = ci % GT_STAGES;
+    if (s_abort || !mbar_wait(&bar_full[s], (ci / GT_STAGES) & 1, GT_WAIT_NS)) {
+      if (!s_abort) { s_abort = 1; atomicOr(a.err, DERR_TIMEOUT); }
+      break;
+    }
+    const uint8_t *st = smem + s * stage_bytes;
+    const GemvSeg &sg = a.seg[ch.seg];
+    if (sg.mode == GM_SILU_MUL) {
+      for (int uu = warp; uu < ch.n; uu += GT_CONS) {
+        const long long ag = warp_sum_ll(row_dot<NCH>(st + (size_t)uu * a.stride, K2, gshift, lane, xr, xs));
+        const long long au =
+            warp_sum_ll(row_dot<NCH>(st + (size_t)(ch.n + uu) * a.stride, K2, gshift, lane, xr, xs));
+        if (lane == 0) epilogue_pair(a, sg, ch.r0 + uu, ag, au, e_x, in_f);
+      }
+    } else {
+      for (int uu = warp; uu < ch.n; uu += 2 * GT_CONS) {
+        const int ub = uu + GT_CONS;
+        long long aa = row_dot<NCH>(st + (size_t)uu * a.stride, K2, gshift, lane, xr, xs);
+        long long ab = ub < ch.n ? row_dot<NCH>(st + (size_t)ub * a.stride, K2, gshift, lane, xr, xs) : 0;
+        aa = warp_sum_ll(aa);
+        ab = warp_sum_ll(ab);
+        if (lane == 0) epilogue_row(a, sg, ch.r0 + uu, aa, e_x, in_f, best);
+        if (lane == 1 && ub < ch.n) epilogue_row(a, sg, ch.r0 + ub, ab, e_x, in_f, best);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bar_empty[s]);
+    ++ci;
   }
   if (a.argmax_key) {
 #pragma unroll
@@ -193,16 +511,35 @@ __global__ void __launch_bounds__(256, 2) k_gemv(const __grid_constant__ GemvArg
   }
 }
 
+int gemv_rows_per_stage(int stride) {
+  int r = 53248 / stride;
+  if (r > 16) r = 16;
+  if (r < 2) r = 2;
+  return r & ~1;
+}
+
+size_t gemv_smem_bytes(int K, int stride) {
+  const int nch = (K + 1023) / 1024;
+  return (size_t)GT_STAGES * gemv_rows_per_stage(stride) * stride + (size_t)nch * 4 * 32 * sizeof(uint2);
+}
+
 template <int NCH>
 static cudaError_t launch_nch(const GemvArgs &a, cudaStream_t st, bool pdl, int max_blocks) {
-  const int threads = 256;
-  int blocks = (a.total_units + 7) / 8;
+  static bool attr_set = false;
+  const size_t smem = gemv_smem_bytes(a.K, a.stride);
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemv<NCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 2048);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  const int ru = a.rows_per_stage;
+  int blocks = (a.total_units + ru - 1) / ru;
   if (blocks > max_blocks) blocks = max_blocks;
   if (blocks < 1) blocks = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(blocks);
-  cfg.blockDim = dim3(threads);
-  cfg.dynamicSmemBytes = NCH * 4 * 32 * sizeof(uint2);
+  cfg.blockDim = dim3(GT_THREADS);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -212,7 +549,9 @@ static cudaError_t launch_nch(const GemvArgs &a, cudaStream_t st, bool pdl, int 
   return cudaLaunchKernelEx(&cfg, k_gemv<NCH>, a);
 }
 
-cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t st, bool pdl, int max_blocks) {
+cudaError_t launch_gemv(const GemvArgs &a_in, cudaStream_t st, bool pdl, int max_blocks) {
+  GemvArgs a = a_in;
+  a.rows_per_stage = gemv_rows_per_stage(a.stride);
   const int nch = (a.K + 1023) / 1024;
   switch (nch) {
     case 1: return launch_nch<1>(a, st, pdl, max_blocks);

@@ -33,6 +33,28 @@ enum GemvMode : int {
 
 constexpr int GEMV_MAX_SEG = 4;
 
+// How a GEMV CTA obtains its quantized input x8 (+ e_x, in_f).  Every CTA
+// computes the prologue redundantly from the producer's vector (<= 32 KB,
+// L2-resident), which removes a separate single-CTA kernel and its
+// dependency hop from the decode step.
+enum GemvPro : int {
+  PRO_X8 = 0,         // x8 / xmeta ready in global memory
+  PRO_RMSNORM = 1,    // src int16[K]: rmsnorm_fx(src, w, in_f, one_plus) -> DYNQ8
+  PRO_DYNQ8 = 2,      // src int16[K]: DYNQ8, in_f given
+  PRO_ATTN_GATE = 3,  // src int64[K] (gated attention product): k_a = attn_o_shift,
+                      // clip16(rshr(src, k_a)) -> DYNQ8, in_f = QKV_F + GAT_F - k_a
+};
+
+struct GemvPrologue {
+  int mode;
+  const void *src;
+  const int32_t *w;   // PRO_RMSNORM gains
+  int in_f;
+  int one_plus;
+  XQ xq_out;          // optional: block 0 stores the computed x8 / meta here
+  int *dbg;           // optional: PRO_ATTN_GATE stores k_a here (block 0)
+};
+
 struct GemvSeg {
   const uint8_t *w;    // packed image row 0
   const uint8_t *w2;   // paired image (GM_SILU_MUL: up), else null
@@ -54,8 +76,10 @@ struct GemvArgs {
   int stride;          // bytes per packed row (ref/w4a8_ref.py:111-114)
   int g;               // group size 128 or 64
   int sh;              // final shift (same for all segments: same K)
+  int rows_per_stage;  // set by launch_gemv
   const int8_t *x8;
   const int *xmeta;    // {e_x, in_f}, nullable (then 0, 0)
+  GemvPrologue pro;    // mode PRO_X8 uses x8 / xmeta
   unsigned long long *argmax_key;
   uint32_t *err;
 };

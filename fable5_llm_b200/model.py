@@ -1,0 +1,291 @@
+"""Host side of the resident decode model (one GPU per context).
+
+``DecodeModel`` owns an ``f5_ctx`` (include/f5b200.h): the integer
+Qwen3.5-9B weights in HBM in the reference's packed row format, the decode
+state (int8 KV caches, DeltaNet conv windows and int16 states) and the
+decode step recorded as one CUDA graph.  All compute is in the CUDA
+library; this module only moves parameters and results.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _lib as L
+from . import synth
+from .config import RS_F, Geometry
+from .rope import rope_table
+
+I64 = np.int64
+
+DN_SLOTS = {"in_qkv": L.S_IN_QKV, "in_z": L.S_IN_Z, "in_b": L.S_IN_B, "in_a": L.S_IN_A, "out": L.S_OUT}
+ATTN_SLOTS = {"q_proj": L.S_Q, "k_proj": L.S_K, "v_proj": L.S_V, "o_proj": L.S_O}
+MLP_SLOTS = {"gate": L.S_GATE, "up": L.S_UP, "down": L.S_DOWN}
+NORM_MODES = {"float": 0, "eps": 1}
+
+
+def _p(a):
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+class DecodeModel:
+    """Resident integer model on one GPU.
+
+    geom: fable5_llm_b200.config.Geometry (9B shapes; n_layers/vocab may be
+    reduced); max_T: KV capacity; norm_mode: "float" (ref/layer_fixed.py
+    default) or "eps" (the seq_model EPS-NORM law)."""
+
+    def __init__(self, geom=None, max_T=4096, norm_mode="float", device=0, world_size=1, rank=0,
+                 max_pos=None):
+        self.geom = geom or Geometry()
+        self.max_T = int(max_T)
+        self.norm_mode = norm_mode
+        self.device = device
+        self.lib = L.lib()
+        types = "".join("A" if t == "full_attention" else "D" for t in self.geom.layer_types)
+        self._types = types.encode()
+        cfg = L.Config(1, self.geom.n_layers, self.geom.vocab, self.max_T, NORM_MODES[norm_mode],
+                       world_size, rank, self._types)
+        h = ctypes.c_void_p()
+        L.check(self.lib.f5_ctx_create(ctypes.byref(cfg), device, ctypes.byref(h)), "f5_ctx_create")
+        self.h = h
+        npos = int(max_pos) if max_pos else self.max_T
+        self.rope = rope_table(npos, self.geom)
+        L.check(self.lib.f5_ctx_upload_rope(self.h, _p(self.rope), npos), "f5_ctx_upload_rope")
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.f5_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- weights ----
+    def upload_matrix(self, layer, slot, img, N, K, e, sh, g=128):
+        img = np.ascontiguousarray(img, dtype=np.uint8)
+        L.check(self.lib.f5_ctx_upload_matrix(self.h, layer, slot, _p(img), N, K, g, e, sh),
+                f"upload_matrix({layer},{slot})")
+
+    def upload_qmat(self, layer, slot, qm):
+        """qm: the reference dict {"w4","m","e","sh","g"} or an object with
+        .img/.N/.K/.e/.sh/.g (packed image)."""
+        if isinstance(qm, dict):
+            from .w4a8_ref import pack_ddr_rows
+            img, _ = pack_ddr_rows(qm["w4"], qm["m"], qm.get("g", 128))
+            N, K = qm["w4"].shape
+            self.upload_matrix(layer, slot, np.frombuffer(img, dtype=np.uint8), N, K, qm["e"], qm["sh"],
+                               qm.get("g", 128))
+        else:
+            self.upload_matrix(layer, slot, qm.img, qm.N, qm.K, qm.e, qm.sh, qm.g)
+
+    def upload_vector(self, layer, kind, v):
+        v = np.ascontiguousarray(np.asarray(v, dtype=I64).reshape(-1))
+        L.check(self.lib.f5_ctx_upload_vector(self.h, layer, kind, _p(v), v.size), f"upload_vector({layer},{kind})")
+
+    def upload_layer(self, i, qw):
+        """One layer in the reference dict layout (ref/layer_fixed.py:1607-1651)."""
+        self.upload_vector(i, L.VEC_LN1, qw["ln1"])
+        self.upload_vector(i, L.VEC_LN2, qw["ln2"])
+        for nm, sl in MLP_SLOTS.items():
+            self.upload_qmat(i, sl, qw["mlp"][nm])
+        if qw["type"] == "full_attention":
+            a = qw["attn"]
+            for nm, sl in ATTN_SLOTS.items():
+                self.upload_qmat(i, sl, a[nm])
+            self.upload_vector(i, L.VEC_Q_NORM, a["q_norm"])
+            self.upload_vector(i, L.VEC_K_NORM, a["k_norm"])
+        else:
+            d = qw["dn"]
+            for nm, sl in DN_SLOTS.items():
+                self.upload_qmat(i, sl, d[nm])
+            self.upload_vector(i, L.VEC_CONV_W, d["conv_w"])
+            self.upload_vector(i, L.VEC_DT_BIAS, d["dt_bias_q12"])
+            self.upload_vector(i, L.VEC_A, d["A_q15"])
+            self.upload_vector(i, L.VEC_NORM_W, d["norm_w_q14"])
+
+    def upload_model(self, layers, emb_q, head, ln_f_q12):
+        for i, qw in enumerate(layers):
+            self.upload_layer(i, qw)
+        self.upload_qmat(-1, L.S_HEAD, head)
+        self.upload_vector(-1, L.VEC_LN_F, ln_f_q12)
+        emb = np.ascontiguousarray(emb_q, dtype=np.int16)
+        L.check(self.lib.f5_ctx_upload_embedding(self.h, _p(emb), emb.shape[0], emb.shape[1]), "upload_embedding")
+
+    def load_synthetic(self, seed):
+        """The seeded synthetic model of fable5_llm_b200.synth, generated on
+        the device (weights) and the host (small vectors)."""
+        g = self.geom
+        for s in synth.matrix_specs(g):
+            slot = L.S_HEAD if s.name == "head" else {**DN_SLOTS, **ATTN_SLOTS, **MLP_SLOTS}[s.name]
+            L.check(self.lib.f5_ctx_synth_matrix(
+                self.h, s.layer, slot, s.N, s.K, s.g, s.e, s.sh,
+                synth.stream_key(seed, s.mid, synth.STREAM_W), synth.stream_key(seed, s.mid, synth.STREAM_M),
+                int(s.symmetric)), f"synth {s.name}@{s.layer}")
+        vec, ln_f = synth.vector_params(seed, g)
+        for i, lt in enumerate(g.layer_types):
+            p = vec[i]
+            self.upload_vector(i, L.VEC_LN1, p["ln1"])
+            self.upload_vector(i, L.VEC_LN2, p["ln2"])
+            if lt == "full_attention":
+                self.upload_vector(i, L.VEC_Q_NORM, p["q_norm"])
+                self.upload_vector(i, L.VEC_K_NORM, p["k_norm"])
+            else:
+                self.upload_vector(i, L.VEC_CONV_W, p["conv_w"])
+                self.upload_vector(i, L.VEC_DT_BIAS, p["dt_bias_q12"])
+                self.upload_vector(i, L.VEC_A, p["A_q15"])
+                self.upload_vector(i, L.VEC_NORM_W, p["norm_w_q14"])
+        self.upload_vector(-1, L.VEC_LN_F, ln_f)
+        L.check(self.lib.f5_ctx_synth_embedding(self.h, synth.stream_key(seed, synth.MID_EMB, synth.STREAM_E)),
+                "synth embedding")
+
+    # ---- state ----
+    def reset(self):
+        L.check(self.lib.f5_ctx_reset(self.h), "reset")
+
+    def set_position(self, T, pos):
+        L.check(self.lib.f5_ctx_set_position(self.h, int(T), int(pos)), "set_position")
+
+    def position(self):
+        T, pos = ctypes.c_int(), ctypes.c_int()
+        L.check(self.lib.f5_ctx_get_position(self.h, ctypes.byref(T), ctypes.byref(pos)), "get_position")
+        return T.value, pos.value
+
+    def set_logits(self, on=True):
+        L.check(self.lib.f5_ctx_set_logits(self.h, int(on)), "set_logits")
+
+    def stream_handle(self):
+        sp = ctypes.c_void_p()
+        L.check(self.lib.f5_ctx_stream(self.h, ctypes.byref(sp)), "f5_ctx_stream")
+        return sp.value
+
+    def prepare(self):
+        L.check(self.lib.f5_ctx_prepare(self.h), "prepare")
+
+    # ---- steps ----
+    def decode_step(self, tok, pos):
+        """One model step (FxRunner.step + argmax) -> (next token, its y32)."""
+        nt, mv = ctypes.c_int(), ctypes.c_int()
+        L.check(self.lib.f5_decode_step(self.h, int(tok), int(pos), ctypes.byref(nt), ctypes.byref(mv)),
+                "f5_decode_step")
+        return nt.value, mv.value
+
+    def decode_launch(self, n):
+        L.check(self.lib.f5_decode_launch(self.h, int(n), None), "f5_decode_launch")
+
+    def sync(self):
+        nt, mv = ctypes.c_int(), ctypes.c_int()
+        L.check(self.lib.f5_ctx_sync(self.h, ctypes.byref(nt), ctypes.byref(mv)), "f5_ctx_sync")
+        return nt.value, mv.value
+
+    def time_step(self, reps=3):
+        """Per-kernel-class device time of one eager step (CUDA events)."""
+        out = np.zeros(8, dtype=np.float64)
+        L.check(self.lib.f5_ctx_time_step(self.h, int(reps), _p(out), 8), "f5_ctx_time_step")
+        keys = ("gemv_ms", "gemv_bytes", "gemv_launches", "dn_ms", "attn_ms", "other_ms", "sum_ms", "launches")
+        return dict(zip(keys, out.tolist()))
+
+    def layer_step(self, layer, x16, T, pos):
+        x = np.ascontiguousarray(np.asarray(x16).astype(np.int16))
+        L.check(self.lib.f5_layer_step(self.h, int(layer), _p(x), int(T), int(pos)), "f5_layer_step")
+        return x.astype(I64)
+
+    # ---- buffers ----
+    _SIZES = None
+
+    def read(self, what, layer=0, dtype=np.int16, count=None):
+        g = self.geom
+        sizes = {L.BUF_X16: (g.H, np.int16), L.BUF_QKV16: (g.CONV_DIM, np.int16), L.BUF_Z16: (g.LVD, np.int16),
+                 L.BUF_B16: (g.LNH, np.int16), L.BUF_A16: (g.LNH, np.int16), L.BUF_ON16: (g.LVD, np.int16),
+                 L.BUF_QG16: (g.NQ * g.HD * 2, np.int16), L.BUF_K16: (g.NKV * g.HD, np.int16),
+                 L.BUF_V16: (g.NKV * g.HD, np.int16), L.BUF_PROD64: (g.NQ * g.HD, I64),
+                 L.BUF_PROD16: (g.FFN, np.int16), L.BUF_STATS: (1, np.uint64),
+                 L.BUF_DN_S: (g.LNH * g.LDK * g.LDV, np.int16), L.BUF_DN_CONV: (g.CONV_DIM * 4, np.int16),
+                 L.BUF_DN_KH: (g.LNH, np.int32), L.BUF_K8: (g.NKV * self.max_T * g.HD, np.int8),
+                 L.BUF_KE: (g.NKV * self.max_T, np.int8), L.BUF_V8: (g.NKV * self.max_T * g.HD, np.int8),
+                 L.BUF_VE: (g.NKV * self.max_T, np.int8), L.BUF_KA: (1, np.int32),
+                 L.BUF_LOGITS: (g.vocab, np.int32)}
+        n, dt = sizes[what]
+        out = np.empty(n, dtype=dt)
+        L.check(self.lib.f5_ctx_read(self.h, what, layer, _p(out), out.nbytes), f"read({what})")
+        return out
+
+    def write(self, what, layer, arr):
+        a = np.ascontiguousarray(arr)
+        L.check(self.lib.f5_ctx_write(self.h, what, layer, _p(a), a.nbytes), f"write({what})")
+
+    def logits(self):
+        return self.read(L.BUF_LOGITS)
+
+    # ---- reference-layout state I/O (ref/layer_fixed.py:1654-1666) ----
+    def get_dn_state(self, layer, T):
+        """-> {"conv": int64[CONV_DIM, 3] oldest first, "S": int16[LNH, LDK, LDV]}"""
+        g = self.geom
+        ring = self.read(L.BUF_DN_CONV, layer).reshape(g.CONV_DIM, 4).astype(I64)
+        conv = np.stack([ring[:, (T - 3 + j) & 3] for j in range(3)], axis=1)
+        S = self.read(L.BUF_DN_S, layer).reshape(g.LNH, g.LDK, g.LDV)
+        return {"conv": conv, "S": S}
+
+    def set_dn_state(self, layer, T, cache):
+        g = self.geom
+        ring = np.zeros((g.CONV_DIM, 4), dtype=np.int16)
+        conv = np.asarray(cache["conv"], dtype=I64)
+        assert (np.abs(conv) <= 32768).all(), "conv window holds clip16 values"
+        for j in range(3):
+            ring[:, (T - 3 + j) & 3] = conv[:, j]
+        self.write(L.BUF_DN_CONV, layer, ring)
+        self.write(L.BUF_DN_S, layer, np.asarray(cache["S"], dtype=np.int16))
+
+    def get_kv(self, layer, T):
+        """-> {"k": [[(k8, ke)] * NKV] * T, "v": ...} (ref/layer_fixed.py:1400-1401)"""
+        g = self.geom
+        k8 = self.read(L.BUF_K8, layer).reshape(g.NKV, self.max_T, g.HD)
+        ke = self.read(L.BUF_KE, layer).reshape(g.NKV, self.max_T)
+        v8 = self.read(L.BUF_V8, layer).reshape(g.NKV, self.max_T, g.HD)
+        ve = self.read(L.BUF_VE, layer).reshape(g.NKV, self.max_T)
+        return {"k": [[(k8[h, t].copy(), int(ke[h, t])) for h in range(g.NKV)] for t in range(T)],
+                "v": [[(v8[h, t].copy(), int(ve[h, t])) for h in range(g.NKV)] for t in range(T)]}
+
+    def set_kv(self, layer, cache):
+        g = self.geom
+        T = len(cache["k"])
+        assert T <= self.max_T
+        k8 = np.zeros((g.NKV, self.max_T, g.HD), dtype=np.int8)
+        v8 = np.zeros_like(k8)
+        ke = np.zeros((g.NKV, self.max_T), dtype=np.int8)
+        ve = np.zeros_like(ke)
+        for t in range(T):
+            for h in range(g.NKV):
+                k8[h, t], ke[h, t] = cache["k"][t][h]
+                v8[h, t], ve[h, t] = cache["v"][t][h]
+        for buf, a in ((L.BUF_K8, k8), (L.BUF_KE, ke), (L.BUF_V8, v8), (L.BUF_VE, ve)):
+            self.write(buf, layer, a)
+        return T
+
+    def save_state(self, path, T):
+        """Per-sequence state (.npz) in the reference's cache layout arrays."""
+        out = {"T": np.array(T)}
+        for i, lt in enumerate(self.geom.layer_types):
+            if lt == "full_attention":
+                for nm, buf in (("k8", L.BUF_K8), ("ke", L.BUF_KE), ("v8", L.BUF_V8), ("ve", L.BUF_VE)):
+                    out[f"l{i}_{nm}"] = self.read(buf, i)
+            else:
+                st = self.get_dn_state(i, T)
+                out[f"l{i}_conv"], out[f"l{i}_S"] = st["conv"], st["S"]
+        np.savez(path, **out)
+
+    def load_state(self, path, pos=None):
+        d = np.load(path)
+        T = int(d["T"])
+        for i, lt in enumerate(self.geom.layer_types):
+            if lt == "full_attention":
+                for nm, buf in (("k8", L.BUF_K8), ("ke", L.BUF_KE), ("v8", L.BUF_V8), ("ve", L.BUF_VE)):
+                    self.write(buf, i, d[f"l{i}_{nm}"])
+            else:
+                self.set_dn_state(i, T, {"conv": d[f"l{i}_conv"], "S": d[f"l{i}_S"]})
+        self.set_position(T, T if pos is None else pos)
+        return T

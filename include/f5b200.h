@@ -132,6 +132,103 @@ int f5_synth_emb_dev(int16_t *d_emb, long long nrows, int H, long long row0,
 int f5_matvec_y32_host(const uint8_t *img, int N, int K, int g, int sh,
                        const int8_t *x8, int32_t *y32, int64_t *p);
 
+/* ---------------------------------------------------------------------------
+ * Model context: one GPU's resident integer Qwen3.5-9B model + decode state
+ * ------------------------------------------------------------------------- */
+
+typedef struct f5_ctx f5_ctx;
+
+typedef struct f5_config {
+  int abi_version;          /* F5_ABI_VERSION                                       */
+  int n_layers;             /* 32 at 9B                                              */
+  int vocab;                /* 248320 at 9B                                          */
+  int max_T;                /* KV-cache capacity per attention layer (tokens)       */
+  int norm_mode;            /* DeltaNet gated norm: 0 float64 host scale (layer_fixed
+                               default, ref/layer_fixed.py:509-546), 1 integer EPS-NORM
+                               (SEQ_NORM / seq_model epsnorm, :694-781)            */
+  int world_size, rank;     /* row sharding (ref/seq_format.py:1177-1189); 1, 0     */
+  const char *layer_types;  /* n_layers chars: 'D' linear_attention, 'A' full_attention
+                               (copied at create)                                   */
+} f5_config;
+
+/* matrix slots (f5_ctx_upload_matrix): DeltaNet 0 in_qkv, 1 in_z, 2 in_b,
+ * 3 in_a, 4 out; attention 0 q_proj, 1 k_proj, 2 v_proj, 3 o_proj; MLP
+ * 8 gate, 9 up, 10 down; LM head: layer -1, slot 0 (ref/layer_fixed.py:
+ * 1360-1375, 1455-1490, 1586-1595) */
+enum f5_slot { F5_S_IN_QKV = 0, F5_S_IN_Z = 1, F5_S_IN_B = 2, F5_S_IN_A = 3, F5_S_OUT = 4,
+               F5_S_Q = 0, F5_S_K = 1, F5_S_V = 2, F5_S_O = 3,
+               F5_S_GATE = 8, F5_S_UP = 9, F5_S_DOWN = 10, F5_S_HEAD = 0 };
+
+/* integer vector parameters (f5_ctx_upload_vector), as the reference's
+ * quantized dicts hold them (ref/layer_fixed.py:1607-1651) */
+enum f5_vec { F5_VEC_LN1 = 0, F5_VEC_LN2 = 1, F5_VEC_Q_NORM = 2, F5_VEC_K_NORM = 3,
+              F5_VEC_CONV_W = 4 /* [CONV_DIM][4] */, F5_VEC_DT_BIAS = 5, F5_VEC_A = 6,
+              F5_VEC_NORM_W = 7, F5_VEC_LN_F = 8 /* layer -1, (1+w) at Q3.12 */ };
+
+/* device buffers readable with f5_ctx_read (debug taps and state) */
+enum f5_buf { F5_BUF_X16 = 0, F5_BUF_QKV16 = 1, F5_BUF_Z16 = 2, F5_BUF_B16 = 3, F5_BUF_A16 = 4,
+              F5_BUF_ON16 = 5, F5_BUF_QG16 = 6, F5_BUF_K16 = 7, F5_BUF_V16 = 8,
+              F5_BUF_PROD64 = 9, F5_BUF_PROD16 = 10, F5_BUF_STATS = 11,
+              F5_BUF_DN_S = 12 /* int16 [32][128][128] */, F5_BUF_DN_CONV = 13 /* int16 [8192][4] ring */,
+              F5_BUF_DN_KH = 14, F5_BUF_K8 = 15, F5_BUF_KE = 16, F5_BUF_V8 = 17, F5_BUF_VE = 18,
+              F5_BUF_KA = 19, F5_BUF_LOGITS = 20 /* int32 [vocab], see f5_ctx_set_logits */ };
+
+/* create / destroy (state zeroed, T = 0) */
+int f5_ctx_create(const f5_config *cfg, int device, f5_ctx **out);
+int f5_ctx_destroy(f5_ctx *ctx);
+
+/* weights: a full pack_ddr_rows image of an N x K matrix (host; this rank's
+ * row share is copied), or the seeded synthetic generator on the device.
+ * Replaces the quantized dict {"w4","m","e","sh","g"} of ref/layer_fixed.py:
+ * 1111 and the DDR images of ref/seq_model.py:305-452 (DDRWeights). */
+int f5_ctx_upload_matrix(f5_ctx *ctx, int layer, int slot, const uint8_t *img, int N, int K, int g,
+                         int e, int sh);
+int f5_ctx_synth_matrix(f5_ctx *ctx, int layer, int slot, int N, int K, int g, int e, int sh,
+                        uint64_t key_w, uint64_t key_m, int symmetric);
+int f5_ctx_upload_vector(f5_ctx *ctx, int layer, int kind, const int64_t *v, int n);
+/* int16 embedding table at Q.RS_F [vocab][4096] (ref/gen_model_script.py:546-552) */
+int f5_ctx_upload_embedding(f5_ctx *ctx, const int16_t *emb, int vocab, int h);
+int f5_ctx_synth_embedding(f5_ctx *ctx, uint64_t key_e);
+/* RoPE tables [npos][128] = rope_tables_q15(pos) cos | sin (ref/layer_fixed.py:1333-1337) */
+int f5_ctx_upload_rope(f5_ctx *ctx, const int16_t *tab, int npos);
+
+/* state: zero every cache (ref/layer_fixed.py:1654-1666 new_cache_fx), T = 0 */
+int f5_ctx_reset(f5_ctx *ctx);
+int f5_ctx_set_position(f5_ctx *ctx, int T, int pos);
+int f5_ctx_get_position(f5_ctx *ctx, int *T, int *pos);
+/* also store the LM head's y32 logits (F5_BUF_LOGITS) each step: the
+ * return value of ref/fidelity_check.py:423-448 FxRunner.step */
+int f5_ctx_set_logits(f5_ctx *ctx, int on);
+/* the context's CUDA stream (cudaStream_t) every launch of the context uses */
+int f5_ctx_stream(f5_ctx *ctx, void **stream);
+/* record the decode-step CUDA graph now (otherwise at the first step) */
+int f5_ctx_prepare(f5_ctx *ctx);
+
+/* One full model step from a host token id: embedding row, every layer,
+ * final RMSNorm, DYNQ8, LM head, argmax (first max wins).  Replaces
+ * ref/fidelity_check.py:423-448 FxRunner.step and the token loop of
+ * ref/gen_model_script.py:602-650.  Caches advance by one token (T += 1). */
+int f5_decode_step(f5_ctx *ctx, int32_t tok, int32_t pos, int32_t *next_tok, int32_t *max_logit);
+/* n greedy steps on the device without host round trips: each step feeds
+ * its argmax to the next (pos and T advance); read the last with f5_ctx_sync */
+int f5_decode_launch(f5_ctx *ctx, int n_steps, void *stream_unused);
+int f5_ctx_sync(f5_ctx *ctx, int32_t *last_tok, int32_t *max_logit);
+
+/* Run `reps` decode steps eagerly with a CUDA event pair around every kernel
+ * launch (measurement only; caches advance).  out[8] per step (averaged):
+ * {GEMV ms, GEMV algorithmic weight bytes, GEMV launches, DeltaNet-step ms,
+ *  attention ms, other ms, sum of launch ms, launches}. */
+int f5_ctx_time_step(f5_ctx *ctx, int reps, double *out, int nout);
+
+/* One decoder layer on a host residual vector at cache length T and RoPE
+ * position pos (ref/layer_fixed.py:1669-1677 layer_decode_fx); the layer's
+ * cache is updated in place (KV slot T / conv window / state). */
+int f5_layer_step(f5_ctx *ctx, int layer, int16_t *x16_inout, int T, int pos);
+
+/* raw device buffer copies (enum f5_buf); bytes must equal the buffer size */
+int f5_ctx_read(f5_ctx *ctx, int what, int layer, void *dst, size_t bytes);
+int f5_ctx_write(f5_ctx *ctx, int what, int layer, const void *src, size_t bytes);
+
 #ifdef __cplusplus
 }
 #endif
