@@ -181,3 +181,48 @@ def test_ref_rope(golden):
         assert np.array_equal(cc, c) and np.array_equal(ss, s)
     for x, p, y in zip(d["ropefx_x"], d["ropefx_pos"], d["ropefx_y"]):
         assert np.array_equal(O.rope_fx(x, *O.rope_tables_q15(int(p))), y)
+
+
+# ---- layer- and model-level law: oracle vs the unmodified reference ----
+@pytest.fixture(scope="module")
+def oracle_model4():
+    from oracle.model import OracleModel
+    return OracleModel(2026, O.Geometry(4, 4096))
+
+
+@pytest.mark.parametrize("mode", ["float", "eps"])
+def test_oracle_dn_layer_vs_reference(golden, oracle_model4, mode):
+    d = golden("ref_layers")
+    qw = oracle_model4.layers[0]
+    st = O.DNCache()
+    for t in range(d["x_in"].shape[0]):
+        y = O.layer_decode_fx(d["x_in"][t], qw, st, t, norm_mode=mode)
+        assert np.array_equal(y, d[f"dn_{mode}_y"][t])
+        assert st.dn_o_shift == list(d[f"dn_{mode}_k"][t])
+    assert digest(st.S) == str(d[f"dn_{mode}_S_digest"])
+    assert np.array_equal(st.conv, d[f"dn_{mode}_conv"])
+
+
+def test_oracle_attn_layer_vs_reference(golden, oracle_model4):
+    d = golden("ref_layers")
+    qw = oracle_model4.layers[3]
+    c = O.AttnCache(16)
+    for t in range(d["x_in"].shape[0]):
+        y = O.layer_decode_fx(d["x_in"][t], qw, c, t + 5)
+        assert np.array_equal(y, d["attn_y"][t])
+        assert c.attn_o_shift == int(d["attn_ka"][t])
+    n = d["x_in"].shape[0]
+    assert np.array_equal(c.k8[:, :n].transpose(1, 0, 2).astype(I64), d["attn_k8"])
+    assert np.array_equal(c.ke[:, :n].T.astype(I64), d["attn_ke"])
+    assert np.array_equal(c.v8[:, :n].transpose(1, 0, 2).astype(I64), d["attn_v8"])
+    assert np.array_equal(c.ve[:, :n].T.astype(I64), d["attn_ve"])
+
+
+def test_oracle_model4_vs_reference(golden, oracle_model4):
+    d = golden("ref_model4")
+    r = O.OracleRunner(oracle_model4, max_T=16)
+    for t, tok in enumerate(d["m4_in"]):
+        nt, y = r.step(int(tok), t)
+        assert nt == int(d["m4_out"][t]) and int(y.max()) == int(d["m4_ymax"][t])
+        for i, x in enumerate(r.layer_out):
+            assert np.array_equal(x, d["m4_layer_x"][t][i].astype(I64)), (t, i)
