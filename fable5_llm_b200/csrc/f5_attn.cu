@@ -20,6 +20,8 @@
 
 #include "f5_attn.cuh"
 #include "f5_block.cuh"
+#include "f5_kernels.cuh"
+#include "f5_tma.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -58,7 +60,7 @@ F5_DEV long long head_norm_rope(long long x, const int32_t *w, const int16_t *cs
 }
 
 __global__ void __launch_bounds__(ATT_THREADS) k_attn(const __grid_constant__ AttnArgs a) {
-  extern __shared__ long long s_sc[];            // [chunk] scores -> exp
+  extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ long long red[32];
   __shared__ long long s_buf[8 + 256];
   __shared__ int s_int[8];
@@ -68,23 +70,48 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(const __grid_constant__ At
   __shared__ int32_t s_acc[8][256];
   __shared__ long long s_part[4];                // [0] local max, [1] local sum
   __shared__ int32_t s_cacc[256];
+  __shared__ __align__(8) uint64_t bar_k, bar_v;
 
   cg::cluster_group cl = cg::this_cluster();
-  asm volatile("griddepcontrol.launch_dependents;");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-
   const int c = (int)cl.block_rank();
   const int nsplit = (int)cl.num_blocks();
   const int h = blockIdx.y;
   const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
   const int group = a.nq / a.nkv;
   const int kv = h / group;
+  // T and pos are only written by the host or by the previous step's last
+  // kernel, so they can be read before the dependency wait.
   const int T = *a.T;
   int pos = *a.pos;
-  bool ok = T < a.max_T;
+  bool ok = T >= 0 && T < a.max_T;
   if (pos < 0 || pos >= a.max_pos) { ok = false; pos = 0; }
-  if (!ok && c == 0 && d == 0 && h == 0) atomicOr(a.err, (uint32_t)0x4u);
   const int Tn = ok ? T + 1 : max(0, min(T, a.max_T));   // tokens attended (incl. the new one)
+  const int chunk = (((Tn + nsplit - 1) / nsplit) + 15) & ~15;
+  const int t0 = c * chunk;
+  const int t1 = min(t0 + chunk, Tn);
+  const int Told = ok ? T : Tn;                  // cached rows (global memory)
+  const int n_old = max(0, min(t1, Told) - t0);  // rows of this chunk already cached
+  const uint32_t row_bytes = (uint32_t)n_old * 256, e_bytes = ((uint32_t)n_old + 15) & ~15u;
+  uint8_t *buf = dsm;                                          // [chunk][256]: K rows, then V rows
+  int8_t *s_e8 = reinterpret_cast<int8_t *>(dsm + (size_t)a.chunk_max * 256);   // [chunk] exponents
+  long long *s_sc = reinterpret_cast<long long *>(dsm + (size_t)a.chunk_max * 258);
+  const size_t kv_row0 = (size_t)kv * a.max_T + t0;
+
+  // cached K rows of this chunk do not depend on the previous kernel: copy
+  // them into shared memory before the dependency wait
+  if (d == 0) {
+    mbar_init(&bar_k, 1);
+    mbar_init(&bar_v, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    if (n_old > 0) {
+      mbar_expect_tx(&bar_k, row_bytes + e_bytes);
+      bulk_g2s(buf, a.k8 + kv_row0 * 256, row_bytes, &bar_k);
+      bulk_g2s(s_e8, a.ke + kv_row0, e_bytes, &bar_k);
+    }
+  }
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (!ok && c == 0 && d == 0 && h == 0) atomicOr(a.err, (uint32_t)DERR_KV_FULL);
   const int16_t *cs = a.rope + (size_t)pos * 128;
 
   // ---- 1. q, k norm + rope; kv_quant(k), kv_quant(v) ----
@@ -107,27 +134,24 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(const __grid_constant__ At
       a.ve[(size_t)kv * a.max_T + T] = (int8_t)ve_new;
     }
   }
-  __syncthreads();
+  bool got = n_old == 0 || mbar_wait(&bar_k, 0, 2000000000ull);
+  const bool kv_ok = !__syncthreads_or(!got);    // block-uniform
+  if (!kv_ok && d == 0) atomicOr(a.err, (uint32_t)DERR_TIMEOUT);
 
-  // ---- 2. scores over this CTA's token chunk ----
-  const int chunk = (Tn + nsplit - 1) / nsplit;
-  const int t0 = c * chunk;
-  const int t1 = min(t0 + chunk, Tn);
+  // ---- 2. scores over this CTA's token chunk (warp per token) ----
   int32_t qr[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) qr[j] = s_q[8 * lane + j];
-  const int8_t *K8 = a.k8 + (size_t)kv * a.max_T * 256;
-  const int8_t *KE = a.ke + (size_t)kv * a.max_T;
   long long lmax = LLONG_MIN;
   for (int t = t0 + warp; t < t1; t += 8) {
-    uint2 kw;
-    int ke;
+    uint2 kw = make_uint2(0, 0);
+    int ke = 0;
     if (ok && t == T) {
       kw = *reinterpret_cast<const uint2 *>(s_k8 + 8 * lane);
       ke = ke_new;
-    } else {
-      kw = *reinterpret_cast<const uint2 *>(K8 + (size_t)t * 256 + 8 * lane);
-      ke = KE[t];
+    } else if (kv_ok) {
+      kw = *reinterpret_cast<const uint2 *>(buf + (size_t)(t - t0) * 256 + 8 * lane);
+      ke = s_e8[t - t0];
     }
     int dot = 0;
 #pragma unroll
@@ -137,12 +161,19 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(const __grid_constant__ At
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-    const long long s = rshr((long long)dot * 2048, 15);   // SCALE_Q15 = round(2^15/sqrt(256))
-    const long long sc = shift_to(s, QKV_F - ke - 16);
+    const long long sv = rshr((long long)dot * 2048, 15);   // SCALE_Q15 = round(2^15/sqrt(256))
+    const long long sc = shift_to(sv, QKV_F - ke - 16);
     if (lane == 0) s_sc[t - t0] = sc;
     lmax = sc > lmax ? sc : lmax;
   }
-  lmax = block_max_ll(lmax, red);
+  lmax = block_max_ll(lmax, red);   // ends with __syncthreads: the K rows are no longer read
+  // V rows reuse the buffer; their copy overlaps the softmax phases
+  if (d == 0 && n_old > 0 && got) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic reads before async writes
+    mbar_expect_tx(&bar_v, row_bytes + e_bytes);
+    bulk_g2s(buf, a.v8 + kv_row0 * 256, row_bytes, &bar_v);
+    bulk_g2s(s_e8, a.ve + kv_row0, e_bytes, &bar_v);
+  }
   if (d == 0) s_part[0] = lmax;
   cl.sync();
   long long mx = LLONG_MIN;
@@ -173,21 +204,21 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(const __grid_constant__ At
   const long long rcp = s_buf[0];
   const int psh = 30 - s_int[0] + 15;
   for (int i = d; i < t1 - t0; i += ATT_THREADS) s_sc[i] = clip(rshr(s_sc[i] * rcp, psh), 0, 1 << 15);
-  __syncthreads();
+  got = n_old == 0 || !kv_ok || mbar_wait(&bar_v, 0, 2000000000ull);
+  const bool v_ok = kv_ok && !__syncthreads_or(!got);
+  if (kv_ok && !v_ok && d == 0) atomicOr(a.err, (uint32_t)DERR_TIMEOUT);
 
   // ---- 4. PV partial sums: warp w takes tokens t0+w, t0+w+8, ...; lane = 8 dims ----
   int32_t acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  const int8_t *V8 = a.v8 + (size_t)kv * a.max_T * 256;
-  const int8_t *VE = a.ve + (size_t)kv * a.max_T;
   for (int t = t0 + warp; t < t1; t += 8) {
-    uint2 vw;
-    int ve;
+    uint2 vw = make_uint2(0, 0);
+    int ve = 0;
     if (ok && t == T) {
       vw = *reinterpret_cast<const uint2 *>(s_v8 + 8 * lane);
       ve = ve_new;
-    } else {
-      vw = *reinterpret_cast<const uint2 *>(V8 + (size_t)t * 256 + 8 * lane);
-      ve = VE[t];
+    } else if (v_ok) {
+      vw = *reinterpret_cast<const uint2 *>(buf + (size_t)(t - t0) * 256 + 8 * lane);
+      ve = s_e8[t - t0];
     }
     const int32_t p = (int32_t)s_sc[t - t0];
     const int sh = 15 - ve - QKV_F;                      // in [6, 15]
@@ -214,16 +245,20 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(const __grid_constant__ At
     const long long og = sigmoid_q((long long)a.qg16[h * 512 + 256 + d] << (12 - QKV_F));
     a.prod[h * 256 + d] = tot * og;
   }
+  // drain: no copy may still target this CTA's shared memory at exit
+  if (d == 0 && n_old > 0 && !got) mbar_wait(&bar_v, 0, 2000000000ull);
   cl.sync();
 }
 
-cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st, bool pdl) {
+cudaError_t launch_attn(const AttnArgs &a_in, cudaStream_t st, bool pdl) {
   const int nsplit = ATT_SPLIT;
-  const int chunk = (a.max_T + nsplit - 1) / nsplit;
+  AttnArgs a = a_in;
+  if (a.max_T % 16) return cudaErrorInvalidValue;
+  a.chunk_max = (((a.max_T + nsplit - 1) / nsplit) + 15) & ~15;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nsplit, a.nq);
   cfg.blockDim = dim3(ATT_THREADS);
-  cfg.dynamicSmemBytes = (size_t)chunk * sizeof(long long);
+  cfg.dynamicSmemBytes = (size_t)a.chunk_max * (256 + 2 + 8);
   cfg.stream = st;
   cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeClusterDimension;

@@ -20,7 +20,8 @@ struct AttnArgs {
   const int *T;           // tokens already cached (new token goes to slot T)
   const int *pos;         // rope position of this token
   uint32_t *err;
-  int max_T, max_pos;
+  int max_T, max_pos;    // max_T a multiple of 16
+  int chunk_max;          // set by launch_attn
   int nq, nkv, rot;
 };
 

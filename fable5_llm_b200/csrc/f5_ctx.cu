@@ -305,7 +305,7 @@ static cudaError_t enqueue_layer(f5_ctx *c, int li, bool pdl) {
     DnArgs d = {};
     d.qkv16 = c->qkv16; d.z16 = c->z16; d.b16 = c->b16; d.a16 = c->a16;
     d.conv = l.conv; d.conv_w = l.conv_w; d.dt_bias = l.dt_bias; d.A = l.A; d.norm_w = l.norm_w;
-    d.S = l.S; d.on16 = c->on16; d.T = &c->params->T; d.kh_out = l.kh; d.stats = c->stats;
+    d.S = l.S; d.on16 = c->on16; d.T = &c->params->T; d.kh_out = l.kh; d.stats = c->stats; d.err = c->err;
     d.lkd = LKD; d.vrep = LNH / LNKH; d.norm_mode = c->cfg.norm_mode;
     tl_begin(c);
     e = launch_dn_step(d, LNH, c->st, pdl);
@@ -459,9 +459,11 @@ int f5_ctx_create(const f5_config *cfg, int device, f5_ctx **out) {
     return set_error(F5_EINVAL, "f5_ctx_create: bad config");
   if (!cfg->layer_types || (int)strlen(cfg->layer_types) != cfg->n_layers)
     return set_error(F5_EINVAL, "layer_types must hold n_layers chars of 'D' / 'A'");
+  if (cfg->max_T > 6144) return set_error(F5_EINVAL, "max_T=%d above the 6144-token KV capacity of a context", cfg->max_T);
   DevGuard dg(device);
   f5_ctx *c = new f5_ctx();
   c->cfg = *cfg;
+  c->cfg.max_T = (cfg->max_T + 15) & ~15;   // KV rows are bulk-copied in 16-row multiples
   c->device = device;
   std::string types(cfg->layer_types);
   c->cfg.layer_types = nullptr;

@@ -15,21 +15,33 @@
 //   clip16(on) for the out-projection's DYNQ8 prologue.
 #include "f5_block.cuh"
 #include "f5_dn.cuh"
+#include "f5_kernels.cuh"
+#include "f5_tma.cuh"
 
 namespace f5 {
 
 constexpr int DN_THREADS = 128;
 
 __global__ void __launch_bounds__(DN_THREADS) k_dn_step(const __grid_constant__ DnArgs a) {
-  __shared__ int16_t s_sd[128 * 128];         // decayed state, [dk][dv]
+  __shared__ __align__(128) int16_t s_sd[128 * 128];   // head state [dk][dv] -> decayed in place
   __shared__ int32_t s_qn[128], s_kn[128];
   __shared__ long long red[32];
   __shared__ long long s_gate[4];             // beta, decay, rq, rk
   __shared__ int s_e[2];
-  asm volatile("griddepcontrol.launch_dependents;");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ __align__(8) uint64_t bar_s;
 
   const int h = blockIdx.x, t = threadIdx.x;
+  int16_t *S = a.S + (size_t)h * 128 * 128;
+  // The head's 32 KB state does not depend on the previous kernel: start its
+  // bulk copy into shared memory before the dependency wait.
+  if (t == 0) {
+    mbar_init(&bar_s, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_expect_tx(&bar_s, 128 * 128 * 2);
+    bulk_g2s(s_sd, S, 128 * 128 * 2, &bar_s);
+  }
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int kh = h / a.vrep;
   const int T = *a.T;
   const int slot_new = T & 3;
@@ -86,12 +98,20 @@ __global__ void __launch_bounds__(DN_THREADS) k_dn_step(const __grid_constant__ 
   __syncthreads();
 
   // ---- recurrence (ref/layer_fixed.py:1545-1571), column dv = t ----
-  int16_t *S = a.S + (size_t)h * 128 * 128;
+  const bool got = mbar_wait(&bar_s, 0, 2000000000ull);
+  if (__syncthreads_or(!got)) {
+    // the state never arrived: flag it, leave S untouched, emit zeros (the
+    // decision is block-uniform, so no thread is left at a barrier)
+    if (t == 0) atomicOr(a.err, DERR_TIMEOUT);
+    a.on16[h * 128 + t] = 0;
+    if (!got) mbar_wait(&bar_s, 0, 2000000000ull);
+    return;
+  }
   const int decay = (int)s_gate[1];
   long long kvm = 0;
 #pragma unroll 8
   for (int dk = 0; dk < 128; ++dk) {
-    const int sd = rshr32p((int32_t)S[dk * 128 + t] * decay, GAT_F);   // |S*decay| < 2^30
+    const int sd = rshr32p((int32_t)s_sd[dk * 128 + t] * decay, GAT_F);   // |S*decay| < 2^30
     s_sd[dk * 128 + t] = (int16_t)sd;
     kvm += (long long)sd * s_kn[dk];
   }

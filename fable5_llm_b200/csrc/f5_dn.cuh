@@ -20,6 +20,7 @@ struct DnArgs {
   const int *T;           // tokens already in the window (ring slot = T % 4)
   int *kh_out;            // optional [LNH] block-float shifts k_h
   unsigned long long *stats;  // optional: state saturation count
+  uint32_t *err;          // device error word (DERR_TIMEOUT)
   int lkd;                // key channels (LNKH * LDK)
   int vrep;               // value heads per key head
   int norm_mode;          // 0 float64 host-scale law, 1 integer EPS-NORM

@@ -27,6 +27,7 @@
 // and order-free).
 #include "f5_block.cuh"
 #include "f5_kernels.cuh"
+#include "f5_tma.cuh"
 
 namespace f5 {
 
@@ -251,53 +252,13 @@ F5_DEV void epilogue_pair(const GemvArgs &a, const GemvSeg &sg, int row, long lo
   static_cast<int16_t *>(sg.out)[sg.out_row0 + row] = (int16_t)clip16(rshr(sgv * uq, 12));
 }
 
-// ---------------------------------------------------------------------------
-// mbarrier / bulk-copy helpers (PTX ISA 8.x, sm_90+; no multicast anywhere)
-// ---------------------------------------------------------------------------
-F5_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-F5_DEV void mbar_init(uint64_t *b, int cnt) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(cnt) : "memory");
-}
-F5_DEV void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
-               : "memory");
-}
-F5_DEV void mbar_arrive(uint64_t *b) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
-}
-F5_DEV unsigned long long gtimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-// Bounded wait on an mbarrier phase: gives up after ~`limit_ns` (the
-// caller then records DERR_TIMEOUT and unwinds; nothing ever spins forever).
-F5_DEV bool mbar_wait(uint64_t *b, uint32_t parity, unsigned long long limit_ns) {
-  const uint32_t addr = smem_u32(b);
-  unsigned long long t0 = 0;
-  for (uint32_t it = 0;; ++it) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok) : "r"(addr), "r"(parity) : "memory");
-    if (ok) return true;
-    if ((it & 63) == 0) {
-      const unsigned long long t = gtimer();
-      if (t0 == 0) t0 = t;
-      else if (t - t0 > limit_ns) return false;
-    }
-  }
-}
-F5_DEV void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
-
-constexpr int GT_CONS = 8;                      // consumer warps
-constexpr int GT_THREADS = (GT_CONS + 1) * 32;  // + one producer warp
-constexpr int GT_STAGES = 4;
+constexpr int GT_CONS = 16;                     // consumer warps
+constexpr int GT_CTHREADS = GT_CONS * 32;
+constexpr int GT_THREADS = GT_CTHREADS + 32;    // + one producer warp
+constexpr int GT_MAX_STAGES = 4;
+constexpr int GT_RES_MAX = 2048;                // deferred row results per CTA
 constexpr unsigned long long GT_WAIT_NS = 2000000000ull;   // 2 s: a safety net only
+constexpr int GT_SMEM_BUDGET = 232448 - 4096;   // dynamic smem budget per CTA
 
 F5_DEV int seg_of(const GemvArgs &a, int u) {
   int s = 0;
@@ -310,7 +271,7 @@ F5_DEV int seg_of(const GemvArgs &a, int u) {
 // Deterministic chunking of this CTA's unit range (same in producer and
 // consumers): a chunk is <= R rows of ONE segment (paired: R/2 row pairs).
 struct Chunk {
-  int seg, r0, n;
+  int seg, r0, n, u;
 };
 F5_DEV bool next_chunk(const GemvArgs &a, int &u, int u1, Chunk &ch) {
   if (u >= u1) return false;
@@ -322,6 +283,7 @@ F5_DEV bool next_chunk(const GemvArgs &a, int &u, int u1, Chunk &ch) {
   ch.seg = s;
   ch.r0 = u - sg.unit_begin;
   ch.n = n;
+  ch.u = u;
   u += n;
   return true;
 }
@@ -356,17 +318,20 @@ F5_DEV long long warp_sum_ll(long long v) {
   return v;
 }
 
-// Persistent TMA-pipelined GEMV: one CTA per SM, a producer warp streams
-// contiguous blocks of packed rows (cp.async.bulk, 16-byte aligned, no
-// multicast) into GT_STAGES shared-memory stages guarded by full/empty
-// mbarriers; eight consumer warps reduce rows out of shared memory.  The
-// first stages are issued BEFORE griddepcontrol.wait: the weights do not
+// Persistent TMA-pipelined GEMV: a producer warp streams contiguous blocks
+// of packed rows (cp.async.bulk, 16-byte aligned, no multicast) into
+// shared-memory stages guarded by full/empty mbarriers; sixteen consumer
+// warps reduce one row per warp out of shared memory, park the row's p16 in
+// shared memory and release the stage at once.  The per-row epilogues run
+// after the CTA's last chunk with every consumer thread taking one row, so
+// the serial int64 epilogue never sits on the weight-stream critical path.
+// The first stages are issued BEFORE griddepcontrol.wait: the weights do not
 // depend on the previous kernel, so under programmatic dependent launch the
 // weight stream overlaps the producer kernel's tail.
 template <int NCH>
 __global__ void __launch_bounds__(GT_THREADS, 1) k_gemv(const __grid_constant__ GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ __align__(8) uint64_t bar_full[GT_STAGES], bar_empty[GT_STAGES];
+  __shared__ __align__(8) uint64_t bar_full[GT_MAX_STAGES], bar_empty[GT_MAX_STAGES];
   __shared__ long long red[32];
   __shared__ long long s_r;
   __shared__ int s_meta[4];
@@ -374,14 +339,16 @@ __global__ void __launch_bounds__(GT_THREADS, 1) k_gemv(const __grid_constant__ 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K2 = a.K >> 1;
   const int gshift = (a.g == 128) ? 6 : 5;
+  const int NS = a.stages;
   const uint32_t stage_bytes = (uint32_t)a.rows_per_stage * (uint32_t)a.stride;
-  uint2 *xs = reinterpret_cast<uint2 *>(smem + GT_STAGES * stage_bytes);
+  uint2 *xs = reinterpret_cast<uint2 *>(smem + NS * stage_bytes);
+  long long *s_res = reinterpret_cast<long long *>(smem + NS * stage_bytes + NCH * 4 * 32 * sizeof(uint2));
   const int G = gridDim.x, b = blockIdx.x;
   const int u0 = (int)((long long)a.total_units * b / G);
   const int u1 = (int)((long long)a.total_units * (b + 1) / G);
 
   if (tid == 0) {
-    for (int i = 0; i < GT_STAGES; ++i) {
+    for (int i = 0; i < NS; ++i) {
       mbar_init(&bar_full[i], 1);
       mbar_init(&bar_empty[i], GT_CONS);
     }
@@ -390,11 +357,11 @@ __global__ void __launch_bounds__(GT_THREADS, 1) k_gemv(const __grid_constant__ 
   }
   __syncthreads();
 
-  // producer: the first GT_STAGES chunks need no empty-wait -> issue now
+  // producer: the first NS chunks need no empty-wait -> issue them now
   int pu = u0, pi = 0;
   if (warp == GT_CONS && lane == 0) {
     Chunk ch;
-    while (pi < GT_STAGES && next_chunk(a, pu, u1, ch)) {
+    while (pi < NS && next_chunk(a, pu, u1, ch)) {
       const GemvSeg &sg = a.seg[ch.seg];
       const uint32_t nb = (uint32_t)ch.n * a.stride;
       uint8_t *dst = smem + pi * stage_bytes;
@@ -435,8 +402,8 @@ __global__ void __launch_bounds__(GT_THREADS, 1) k_gemv(const __grid_constant__ 
       Chunk ch;
       int issued = pi;
       while (!s_abort && next_chunk(a, pu, u1, ch)) {
-        const int s = issued % GT_STAGES;
-        if (!mbar_wait(&bar_empty[s], ((issued / GT_STAGES) - 1) & 1, GT_WAIT_NS)) {
+        const int s = issued % NS;
+        if (!mbar_wait(&bar_empty[s], ((issued / NS) - 1) & 1, GT_WAIT_NS)) {
           s_abort = 1;
           atomicOr(a.err, DERR_TIMEOUT);
           break;
@@ -453,14 +420,14 @@ __global__ void __launch_bounds__(GT_THREADS, 1) k_gemv(const __grid_constant__ 
       // never leave the CTA with copies in flight: drain every issued stage
       // the consumers have not waited on (bounded)
       if (s_abort) {
-        for (int i = max(0, issued - GT_STAGES); i < issued; ++i)
-          mbar_wait(&bar_full[i % GT_STAGES], (i / GT_STAGES) & 1, GT_WAIT_NS);
+        for (int i = max(0, issued - NS); i < issued; ++i)
+          mbar_wait(&bar_full[i % NS], (i / NS) & 1, GT_WAIT_NS);
       }
     }
     return;
   }
 
-  // ---- consumers ----
+  // ---- consumers: one row per warp, results parked in s_res ----
   uint2 xr[4][4];
   if (NCH <= 4) {
 #pragma unroll
@@ -468,38 +435,48 @@ __global__ void __launch_bounds__(GT_THREADS, 1) k_gemv(const __grid_constant__ 
 #pragma unroll
       for (int j = 0; j < 4; ++j) xr[c][j] = c < NCH ? xs[((c << 2) + j) * 32 + lane] : make_uint2(0, 0);
   }
-  unsigned long long best = 0ull;
   int cu = u0, ci = 0;
   Chunk ch;
   while (next_chunk(a, cu, u1, ch)) {
-    const int s = ci % GT_STAGES;
-    if (s_abort || !mbar_wait(&bar_full[s], (ci / GT_STAGES) & 1, GT_WAIT_NS)) {
+    const int s = ci % NS;
+    if (s_abort || !mbar_wait(&bar_full[s], (ci / NS) & 1, GT_WAIT_NS)) {
       if (!s_abort) { s_abort = 1; atomicOr(a.err, DERR_TIMEOUT); }
       break;
     }
     const uint8_t *st = smem + s * stage_bytes;
-    const GemvSeg &sg = a.seg[ch.seg];
-    if (sg.mode == GM_SILU_MUL) {
-      for (int uu = warp; uu < ch.n; uu += GT_CONS) {
-        const long long ag = warp_sum_ll(row_dot<NCH>(st + (size_t)uu * a.stride, K2, gshift, lane, xr, xs));
-        const long long au =
-            warp_sum_ll(row_dot<NCH>(st + (size_t)(ch.n + uu) * a.stride, K2, gshift, lane, xr, xs));
-        if (lane == 0) epilogue_pair(a, sg, ch.r0 + uu, ag, au, e_x, in_f);
-      }
-    } else {
-      for (int uu = warp; uu < ch.n; uu += 2 * GT_CONS) {
-        const int ub = uu + GT_CONS;
-        long long aa = row_dot<NCH>(st + (size_t)uu * a.stride, K2, gshift, lane, xr, xs);
-        long long ab = ub < ch.n ? row_dot<NCH>(st + (size_t)ub * a.stride, K2, gshift, lane, xr, xs) : 0;
-        aa = warp_sum_ll(aa);
-        ab = warp_sum_ll(ab);
-        if (lane == 0) epilogue_row(a, sg, ch.r0 + uu, aa, e_x, in_f, best);
-        if (lane == 1 && ub < ch.n) epilogue_row(a, sg, ch.r0 + ub, ab, e_x, in_f, best);
+    const bool pair = a.seg[ch.seg].mode == GM_SILU_MUL;
+    const int nrows = pair ? 2 * ch.n : ch.n;
+    const int cbase = ch.u - u0;
+    for (int r = warp; r < nrows; r += 2 * GT_CONS) {
+      const int r2 = r + GT_CONS;
+      long long aa = row_dot<NCH>(st + (size_t)r * a.stride, K2, gshift, lane, xr, xs);
+      long long ab = r2 < nrows ? row_dot<NCH>(st + (size_t)r2 * a.stride, K2, gshift, lane, xr, xs) : 0;
+      aa = warp_sum_ll(aa);
+      ab = warp_sum_ll(ab);
+      if (lane == 0) {
+        s_res[pair ? (r < ch.n ? 2 * (cbase + r) : 2 * (cbase + r - ch.n) + 1) : cbase + r] = aa;
+        if (r2 < nrows)
+          s_res[pair ? (r2 < ch.n ? 2 * (cbase + r2) : 2 * (cbase + r2 - ch.n) + 1) : cbase + r2] = ab;
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&bar_empty[s]);
     ++ci;
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(GT_CTHREADS) : "memory");
+  if (s_abort) return;
+
+  // ---- deferred epilogues: one unit per consumer thread ----
+  unsigned long long best = 0ull;
+  for (int i = tid; i < u1 - u0; i += GT_CTHREADS) {
+    const int u = u0 + i;
+    const GemvSeg &sg = a.seg[seg_of(a, u)];
+    const int row = u - sg.unit_begin;
+    if (sg.mode == GM_SILU_MUL) {
+      epilogue_pair(a, sg, row, s_res[2 * i], s_res[2 * i + 1], e_x, in_f);
+    } else {
+      epilogue_row(a, sg, row, s_res[i], e_x, in_f, best);
+    }
   }
   if (a.argmax_key) {
 #pragma unroll
@@ -518,28 +495,34 @@ int gemv_rows_per_stage(int stride) {
   return r & ~1;
 }
 
-size_t gemv_smem_bytes(int K, int stride) {
-  const int nch = (K + 1023) / 1024;
-  return (size_t)GT_STAGES * gemv_rows_per_stage(stride) * stride + (size_t)nch * 4 * 32 * sizeof(uint2);
-}
-
 template <int NCH>
-static cudaError_t launch_nch(const GemvArgs &a, cudaStream_t st, bool pdl, int max_blocks) {
+static cudaError_t launch_nch(GemvArgs a, cudaStream_t st, bool pdl, int max_blocks) {
   static bool attr_set = false;
-  const size_t smem = gemv_smem_bytes(a.K, a.stride);
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemv<NCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 2048);
+    cudaError_t e = cudaFuncSetAttribute(k_gemv<NCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, GT_SMEM_BUDGET);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
   const int ru = a.rows_per_stage;
   int blocks = (a.total_units + ru - 1) / ru;
   if (blocks > max_blocks) blocks = max_blocks;
+  const int min_blocks = (a.total_units + GT_RES_MAX - 1) / GT_RES_MAX;
+  if (blocks < min_blocks) blocks = min_blocks;
   if (blocks < 1) blocks = 1;
+  bool paired = false;
+  for (int i = 0; i < a.nseg; ++i) paired |= a.seg[i].mode == GM_SILU_MUL;
+  const size_t per_cta = (size_t)(a.total_units + blocks - 1) / blocks + 1;
+  const size_t res_bytes = per_cta * (paired ? 2 : 1) * sizeof(long long);
+  const size_t xs_bytes = (size_t)NCH * 4 * 32 * sizeof(uint2);
+  const size_t stage_bytes = (size_t)a.rows_per_stage * a.stride;
+  int stages = (int)((GT_SMEM_BUDGET - xs_bytes - res_bytes) / stage_bytes);
+  if (stages > GT_MAX_STAGES) stages = GT_MAX_STAGES;
+  if (stages < 2) return cudaErrorInvalidValue;
+  a.stages = stages;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(blocks);
   cfg.blockDim = dim3(GT_THREADS);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = stages * stage_bytes + xs_bytes + res_bytes;
   cfg.stream = st;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -77,6 +77,7 @@ struct GemvArgs {
   int g;               // group size 128 or 64
   int sh;              // final shift (same for all segments: same K)
   int rows_per_stage;  // set by launch_gemv
+  int stages;          // set by launch_gemv
   const int8_t *x8;
   const int *xmeta;    // {e_x, in_f}, nullable (then 0, 0)
   GemvPrologue pro;    // mode PRO_X8 uses x8 / xmeta

@@ -1,0 +1,51 @@
+// mbarrier + bulk-copy (TMA, non-tensor) helpers for sm_100a kernels.
+// No load anywhere uses .multicast::cluster.
+#pragma once
+#include "f5_int.cuh"
+
+namespace f5 {
+
+// ---------------------------------------------------------------------------
+// mbarrier / bulk-copy helpers (PTX ISA 8.x, sm_90+; no multicast anywhere)
+// ---------------------------------------------------------------------------
+F5_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+F5_DEV void mbar_init(uint64_t *b, int cnt) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(cnt) : "memory");
+}
+F5_DEV void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
+               : "memory");
+}
+F5_DEV void mbar_arrive(uint64_t *b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+F5_DEV unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait on an mbarrier phase: gives up after ~`limit_ns` (the
+// caller then records DERR_TIMEOUT and unwinds; nothing ever spins forever).
+F5_DEV bool mbar_wait(uint64_t *b, uint32_t parity, unsigned long long limit_ns) {
+  const uint32_t addr = smem_u32(b);
+  unsigned long long t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok) : "r"(addr), "r"(parity) : "memory");
+    if (ok) return true;
+    if ((it & 63) == 0) {
+      const unsigned long long t = gtimer();
+      if (t0 == 0) t0 = t;
+      else if (t - t0 > limit_ns) return false;
+    }
+  }
+}
+F5_DEV void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+}  // namespace f5

@@ -39,7 +39,7 @@ class DecodeModel:
     def __init__(self, geom=None, max_T=4096, norm_mode="float", device=0, world_size=1, rank=0,
                  max_pos=None):
         self.geom = geom or Geometry()
-        self.max_T = int(max_T)
+        self.max_T = (int(max_T) + 15) & ~15      # the context rounds KV capacity to 16 rows
         self.norm_mode = norm_mode
         self.device = device
         self.lib = L.lib()
