@@ -104,108 +104,140 @@ F5_DEV long long rms_elem(long long x, long long r, int e, long long gain) {
   return clip16(rshr(y * gain, 14));
 }
 
+// element j (0..7) of 8 int16 packed in a uint4
+F5_DEV long long get16(const uint4 &u, int j) {
+  const uint32_t w = (j >> 1) == 0 ? u.x : ((j >> 1) == 1 ? u.y : ((j >> 1) == 2 ? u.z : u.w));
+  return (long long)(int16_t)((j & 1) ? (w >> 16) : (w & 0xFFFFu));
+}
+
 // Redundant per-CTA computation of the GEMV's quantized input (see GemvPro).
+// Every value is read from global memory once and held in registers across
+// the reduction passes (MAXB 8-element blocks per thread).
+template <int MAXB>
 F5_DEV void prologue(const GemvArgs &a, uint2 *xs, long long *red, long long *s_r, int *s_meta) {
-  const int tid = threadIdx.x, K = a.K, nblk = K >> 3;
+  const int tid = threadIdx.x, BT = blockDim.x, K = a.K, nblk = K >> 3;
   const GemvPrologue &P = a.pro;
   const bool store = (P.xq_out.x8 != nullptr) && blockIdx.x == 0;
-  long long v[8];
-  if (P.mode == PRO_RMSNORM) {
+  long long q[8];
+  if (P.mode == PRO_RMSNORM || P.mode == PRO_DYNQ8) {
     const int16_t *src = static_cast<const int16_t *>(P.src);
-    long long ss = 0;
-    for (int b = tid; b < nblk; b += blockDim.x) {
-      load8_i16(src + 8 * b, v);
+    uint4 raw[MAXB];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+    for (int j = 0; j < MAXB; ++j) {
+      const int b = tid + j * BT;
+      raw[j] = b < nblk ? *reinterpret_cast<const uint4 *>(src + 8 * b) : make_uint4(0, 0, 0, 0);
     }
-    ss = block_sum_ll(ss, red);
-    if (tid == 0) {
-      int64_t r; int e;
-      rsqrt_q((uint64_t)(ss == 0 ? 1 : ss), 2 * P.in_f + (31 - __clz(K)), r, e);
-      *s_r = r;
-      s_meta[2] = e;
-    }
-    __syncthreads();
-    const long long r = *s_r;
-    const int e = s_meta[2];
-    const long long add1 = P.one_plus ? (1 << 14) : 0;
-    unsigned long long mx = 0;
-    for (int b = tid; b < nblk; b += blockDim.x) {
-      load8_i16(src + 8 * b, v);
+    if constexpr (MAXB <= 2) {
+      if (P.mode == PRO_RMSNORM) {     // ref/layer_fixed.py:1242-1278 (H = 4096)
+        int4 wl[MAXB][2];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const unsigned long long m = uabs(rms_elem(v[j], r, e, P.w[8 * b + j] + add1));
-        mx = m > mx ? m : mx;
+        for (int j = 0; j < MAXB; ++j) {
+          const int b = tid + j * BT;
+          wl[j][0] = b < nblk ? *reinterpret_cast<const int4 *>(P.w + 8 * b) : make_int4(0, 0, 0, 0);
+          wl[j][1] = b < nblk ? *reinterpret_cast<const int4 *>(P.w + 8 * b + 4) : make_int4(0, 0, 0, 0);
+        }
+        long long ss = 0;
+#pragma unroll
+        for (int j = 0; j < MAXB; ++j)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) { const long long v = get16(raw[j], k); ss += v * v; }
+        ss = block_sum_ll(ss, red);
+        if (tid == 0) {
+          int64_t r; int e;
+          rsqrt_q((uint64_t)(ss == 0 ? 1 : ss), 2 * P.in_f + (31 - __clz(K)), r, e);
+          *s_r = r;
+          s_meta[2] = e;
+        }
+        __syncthreads();
+        const long long r = *s_r;
+        const int e = s_meta[2];
+        const long long add1 = P.one_plus ? (1 << 14) : 0;
+#pragma unroll
+        for (int j = 0; j < MAXB; ++j) {
+          const int wv[8] = {wl[j][0].x, wl[j][0].y, wl[j][0].z, wl[j][0].w,
+                             wl[j][1].x, wl[j][1].y, wl[j][1].z, wl[j][1].w};
+          uint32_t pk[4];
+#pragma unroll
+          for (int k = 0; k < 8; k += 2) {
+            const long long x0 = rms_elem(get16(raw[j], k), r, e, wv[k] + add1);
+            const long long x1 = rms_elem(get16(raw[j], k + 1), r, e, wv[k + 1] + add1);
+            pk[k >> 1] = ((uint32_t)x0 & 0xFFFFu) | ((uint32_t)x1 << 16);
+          }
+          raw[j] = make_uint4(pk[0], pk[1], pk[2], pk[3]);   // normalised, int16
+        }
       }
+    } else {
+      if (P.mode == PRO_RMSNORM && tid == 0) atomicOr(a.err, DERR_RANGE);   // RMSNorm is bound to K <= 4096
     }
+    unsigned long long mx = 0;
+#pragma unroll
+    for (int j = 0; j < MAXB; ++j)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) { const unsigned long long m = uabs(get16(raw[j], k)); mx = m > mx ? m : mx; }
     mx = block_max_ull(mx, reinterpret_cast<unsigned long long *>(red));
     const int ex = dynq8_e(mx);
-    for (int b = tid; b < nblk; b += blockDim.x) {
-      load8_i16(src + 8 * b, v);
-      long long q[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        q[j] = dynq8_apply(rms_elem(v[j], r, e, P.w[8 * b + j] + add1), ex);
-        if (store) P.xq_out.x8[8 * b + j] = (int8_t)q[j];
+    for (int j = 0; j < MAXB; ++j) {
+      const int b = tid + j * BT;
+      if (b < nblk) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          q[k] = dynq8_apply(get16(raw[j], k), ex);
+          if (store) P.xq_out.x8[8 * b + k] = (int8_t)q[k];
+        }
+        put8(xs, b, q);
       }
-      put8(xs, b, q);
     }
     if (tid == 0) { s_meta[0] = ex; s_meta[1] = P.in_f; }
-  } else if (P.mode == PRO_DYNQ8) {
-    const int16_t *src = static_cast<const int16_t *>(P.src);
-    unsigned long long mx = 0;
-    for (int b = tid; b < nblk; b += blockDim.x) {
-      load8_i16(src + 8 * b, v);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) { const unsigned long long m = uabs(v[j]); mx = m > mx ? m : mx; }
-    }
-    mx = block_max_ull(mx, reinterpret_cast<unsigned long long *>(red));
-    const int ex = dynq8_e(mx);
-    for (int b = tid; b < nblk; b += blockDim.x) {
-      load8_i16(src + 8 * b, v);
-      long long q[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        q[j] = dynq8_apply(v[j], ex);
-        if (store) P.xq_out.x8[8 * b + j] = (int8_t)q[j];
-      }
-      put8(xs, b, q);
-    }
-    if (tid == 0) { s_meta[0] = ex; s_meta[1] = P.in_f; }
-  } else {  // PRO_ATTN_GATE (ref/layer_fixed.py:1441-1449)
+  } else if constexpr (MAXB <= 2) {  // PRO_ATTN_GATE (ref/layer_fixed.py:1441-1449); K = NQ*HD = 4096
     const int64_t *src = static_cast<const int64_t *>(P.src);
-    unsigned long long mx = 0;
-    for (int b = tid; b < nblk; b += blockDim.x) {
-      load8_i64(src + 8 * b, v);
+    long long v[MAXB][8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) { const unsigned long long m = uabs(v[j]); mx = m > mx ? m : mx; }
+    for (int j = 0; j < MAXB; ++j) {
+      const int b = tid + j * BT;
+      if (b < nblk) load8_i64(src + 8 * b, v[j]);
+      else
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[j][k] = 0;
     }
+    unsigned long long mx = 0;
+#pragma unroll
+    for (int j = 0; j < MAXB; ++j)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) { const unsigned long long m = uabs(v[j][k]); mx = m > mx ? m : mx; }
     mx = block_max_ull(mx, reinterpret_cast<unsigned long long *>(red));
     int ka = bf_shift(mx);
     if (ka < 0) ka = 0;                      // attn_o_shift clamp (ref/layer_fixed.py:489-506)
     unsigned long long mg = 0;
-    for (int b = tid; b < nblk; b += blockDim.x) {
-      load8_i64(src + 8 * b, v);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) { const unsigned long long m = uabs(clip16(rshr(v[j], ka))); mg = m > mg ? m : mg; }
-    }
+    for (int j = 0; j < MAXB; ++j)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        v[j][k] = clip16(rshr(v[j][k], ka));
+        const unsigned long long m = uabs(v[j][k]);
+        mg = m > mg ? m : mg;
+      }
     mg = block_max_ull(mg, reinterpret_cast<unsigned long long *>(red));
     const int ex = dynq8_e(mg);
-    for (int b = tid; b < nblk; b += blockDim.x) {
-      load8_i64(src + 8 * b, v);
-      long long q[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        q[j] = dynq8_apply(clip16(rshr(v[j], ka)), ex);
-        if (store) P.xq_out.x8[8 * b + j] = (int8_t)q[j];
+    for (int j = 0; j < MAXB; ++j) {
+      const int b = tid + j * BT;
+      if (b < nblk) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          q[k] = dynq8_apply(v[j][k], ex);
+          if (store) P.xq_out.x8[8 * b + k] = (int8_t)q[k];
+        }
+        put8(xs, b, q);
       }
-      put8(xs, b, q);
     }
     if (tid == 0) {
       s_meta[0] = ex;
       s_meta[1] = QKV_F + GAT_F - ka;
       if (P.dbg && blockIdx.x == 0) *P.dbg = ka;
     }
+  } else {
+    if (tid == 0) atomicOr(a.err, DERR_RANGE);   // the attention gate prologue is bound to K <= 4096
   }
   if (store && tid == 0) {
     P.xq_out.meta[0] = s_meta[0];
@@ -256,9 +288,9 @@ constexpr int GT_CONS = 16;                     // consumer warps
 constexpr int GT_CTHREADS = GT_CONS * 32;
 constexpr int GT_THREADS = GT_CTHREADS + 32;    // + one producer warp
 constexpr int GT_MAX_STAGES = 4;
+constexpr int GT_CTA_SMEM = 232448 - 6144;      // dynamic smem per CTA (one CTA per SM)
 constexpr int GT_RES_MAX = 2048;                // deferred row results per CTA
 constexpr unsigned long long GT_WAIT_NS = 2000000000ull;   // 2 s: a safety net only
-constexpr int GT_SMEM_BUDGET = 232448 - 4096;   // dynamic smem budget per CTA
 
 F5_DEV int seg_of(const GemvArgs &a, int u) {
   int s = 0;
@@ -391,7 +423,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1) k_gemv(const __grid_constant__ 
       s_meta[1] = a.xmeta ? a.xmeta[1] : 0;
     }
   } else {
-    prologue(a, xs, red, &s_r, s_meta);
+    prologue<(NCH * 128 + GT_THREADS - 1) / GT_THREADS>(a, xs, red, &s_r, s_meta);
   }
   __syncthreads();
   const int e_x = s_meta[0], in_f = s_meta[1];
@@ -447,17 +479,9 @@ __global__ void __launch_bounds__(GT_THREADS, 1) k_gemv(const __grid_constant__ 
     const bool pair = a.seg[ch.seg].mode == GM_SILU_MUL;
     const int nrows = pair ? 2 * ch.n : ch.n;
     const int cbase = ch.u - u0;
-    for (int r = warp; r < nrows; r += 2 * GT_CONS) {
-      const int r2 = r + GT_CONS;
-      long long aa = row_dot<NCH>(st + (size_t)r * a.stride, K2, gshift, lane, xr, xs);
-      long long ab = r2 < nrows ? row_dot<NCH>(st + (size_t)r2 * a.stride, K2, gshift, lane, xr, xs) : 0;
-      aa = warp_sum_ll(aa);
-      ab = warp_sum_ll(ab);
-      if (lane == 0) {
-        s_res[pair ? (r < ch.n ? 2 * (cbase + r) : 2 * (cbase + r - ch.n) + 1) : cbase + r] = aa;
-        if (r2 < nrows)
-          s_res[pair ? (r2 < ch.n ? 2 * (cbase + r2) : 2 * (cbase + r2 - ch.n) + 1) : cbase + r2] = ab;
-      }
+    for (int r = warp; r < nrows; r += GT_CONS) {
+      const long long aa = warp_sum_ll(row_dot<NCH>(st + (size_t)r * a.stride, K2, gshift, lane, xr, xs));
+      if (lane == 0) s_res[pair ? (r < ch.n ? 2 * (cbase + r) : 2 * (cbase + r - ch.n) + 1) : cbase + r] = aa;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&bar_empty[s]);
@@ -489,17 +513,17 @@ __global__ void __launch_bounds__(GT_THREADS, 1) k_gemv(const __grid_constant__ 
 }
 
 int gemv_rows_per_stage(int stride) {
-  int r = 53248 / stride;
+  int r = 53248 / stride;     // <= 52 KB stages: 16 rows at K=4096, 8 at K=12288
   if (r > 16) r = 16;
   if (r < 2) r = 2;
-  return r & ~1;
+  return r;
 }
 
 template <int NCH>
 static cudaError_t launch_nch(GemvArgs a, cudaStream_t st, bool pdl, int max_blocks) {
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemv<NCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, GT_SMEM_BUDGET);
+    cudaError_t e = cudaFuncSetAttribute(k_gemv<NCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, GT_CTA_SMEM);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
@@ -515,7 +539,7 @@ static cudaError_t launch_nch(GemvArgs a, cudaStream_t st, bool pdl, int max_blo
   const size_t res_bytes = per_cta * (paired ? 2 : 1) * sizeof(long long);
   const size_t xs_bytes = (size_t)NCH * 4 * 32 * sizeof(uint2);
   const size_t stage_bytes = (size_t)a.rows_per_stage * a.stride;
-  int stages = (int)((GT_SMEM_BUDGET - xs_bytes - res_bytes) / stage_bytes);
+  int stages = (int)(((long long)GT_CTA_SMEM - (long long)xs_bytes - (long long)res_bytes) / (long long)stage_bytes);
   if (stages > GT_MAX_STAGES) stages = GT_MAX_STAGES;
   if (stages < 2) return cudaErrorInvalidValue;
   a.stages = stages;

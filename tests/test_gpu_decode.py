@@ -158,7 +158,7 @@ def test_attention_long_context_vs_oracle(model4):
     big.decode_step(int(prompt[0]), 0)
     for t in range(1, T):
         big.decode_step(int(prompt[t]), t)
-    r = O.OracleRunner(OracleModel(SEED, O.Geometry(4, 4096)), max_T=T + 8)
+    r = O.OracleRunner(OracleModel(SEED, O.Geometry(4, 4096)), max_T=big.max_T)
     for i, lt in enumerate(big.geom.layer_types):
         if lt == "full_attention":
             c = r.caches[i]
