@@ -132,6 +132,20 @@ int f5_synth_emb_dev(int16_t *d_emb, long long nrows, int H, long long row0,
 int f5_matvec_y32_host(const uint8_t *img, int N, int K, int g, int sh,
                        const int8_t *x8, int32_t *y32, int64_t *p);
 
+/* Allocation-free form of f5_matvec_y32_host, for callers that cannot call
+ * cudaMalloc (a process capturing a stream into a CUDA graph at the time, a
+ * host whose device memory belongs to another allocator, a loop that cannot
+ * take cudaMalloc/cudaFree's device synchronisation).  No counterpart in the
+ * reference: it is an extra deployment form of the matvec_y32 drop-in.
+ * Stages everything in one fixed device array of F5_NOALLOC_SCRATCH_BYTES
+ * that every GPU loading the library holds until exit; larger requests fail
+ * with F5_EINVAL.  The first call on a device resolves the array's address
+ * (make it before any stream capture).  Calls share the array: calls that
+ * overlap on the GPU race.  Synchronous, legacy default stream. */
+#define F5_NOALLOC_SCRATCH_BYTES (16u << 20)
+int f5_matvec_y32_host_noalloc(const uint8_t *img, int N, int K, int g, int sh,
+                               const int8_t *x8, int32_t *y32, int64_t *p);
+
 /* ---------------------------------------------------------------------------
  * Model context: one GPU's resident integer Qwen3.5-9B model + decode state
  * ------------------------------------------------------------------------- */
