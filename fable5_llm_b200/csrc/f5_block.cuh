@@ -60,4 +60,69 @@ F5_DEV long long block_max_ll(long long v, long long *red) {
   return t;
 }
 
+// ---- sync policies: the same reduction code over the whole block
+// (__syncthreads) or over a thread group with a named barrier ----
+struct BlockSync {
+  F5_DEV int tid() const { return threadIdx.x; }
+  F5_DEV int n() const { return blockDim.x; }
+  F5_DEV void sync() const { __syncthreads(); }
+  F5_DEV bool any(bool p) const { return __syncthreads_or(p) != 0; }
+};
+// group = threads [BASE, BASE+N) of the block, barrier id ID (N % 32 == 0)
+template <int ID, int N, int BASE = 0>
+struct NamedSync {
+  F5_DEV int tid() const { return (int)threadIdx.x - BASE; }
+  F5_DEV int n() const { return N; }
+  F5_DEV void sync() const { asm volatile("bar.sync %0, %1;" ::"n"(ID), "n"(N) : "memory"); }
+  // group-uniform OR of a predicate (also a barrier)
+  F5_DEV bool any(bool p) const {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred pi, po;\n setp.ne.u32 pi, %1, 0;\n bar.red.or.pred po, %2, %3, pi;\n"
+        " selp.u32 %0, 1, 0, po;\n}"
+        : "=r"(r) : "r"((uint32_t)p), "n"(ID), "n"(N) : "memory");
+    return r != 0;
+  }
+};
+
+template <class SY>
+F5_DEV long long g_sum_ll(const SY &sy, long long v, long long *red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = sy.tid() >> 5, nw = sy.n() >> 5;
+  sy.sync();
+  if ((sy.tid() & 31) == 0) red[w] = v;
+  sy.sync();
+  long long t = 0;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  return t;
+}
+template <class SY>
+F5_DEV unsigned long long g_sum_ull(const SY &sy, unsigned long long v, unsigned long long *red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = sy.tid() >> 5, nw = sy.n() >> 5;
+  sy.sync();
+  if ((sy.tid() & 31) == 0) red[w] = v;
+  sy.sync();
+  unsigned long long t = 0;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  return t;
+}
+template <class SY>
+F5_DEV unsigned long long g_max_ull(const SY &sy, unsigned long long v, unsigned long long *red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(0xffffffffu, v, o);
+    v = t > v ? t : v;
+  }
+  const int w = sy.tid() >> 5, nw = sy.n() >> 5;
+  sy.sync();
+  if ((sy.tid() & 31) == 0) red[w] = v;
+  sy.sync();
+  unsigned long long t = 0;
+  for (int i = 0; i < nw; ++i) t = red[i] > t ? red[i] : t;
+  return t;
+}
+
 }  // namespace f5

@@ -22,18 +22,6 @@ namespace f5 {
 cudaError_t launch_synth_w4(uint8_t *, long long, int, int, long long, uint64_t, uint64_t, int, cudaStream_t);
 cudaError_t launch_synth_emb(int16_t *, long long, int, long long, uint64_t, cudaStream_t);
 
-// device-resident step parameters (read by the graph's kernels)
-struct StepParams {
-  int tok;        // input token of this step
-  int pos;        // RoPE position of this step
-  int T;          // tokens already in every layer's cache / conv window
-  int next_tok;   // argmax of this step (first max wins)
-  int max_val;    // its y32 logit
-  uint32_t err;   // device error bits (DERR_*)
-  int steps;      // steps completed since reset
-  int pad;
-};
-
 // step begin: x16 = emb[tok] (ref/fidelity_check.py:428), reset argmax key
 __global__ void k_step_begin(StepParams *p, const int16_t *emb, int vocab, int H, int16_t *x16,
                              unsigned long long *key) {

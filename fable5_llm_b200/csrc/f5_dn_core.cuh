@@ -1,0 +1,166 @@
+// Device core of the Gated-DeltaNet decode step for one value head
+// (ref/layer_fixed.py:1493-1580), shared by the per-op kernel k_dn_step and
+// the persistent decode kernel.  A group of NQ*128 threads runs one head:
+// thread t owns value column dv = t & 127 and, in the recurrence, the state
+// rows dk in quarter q = t >> 7 (NQ = 1: all 128 rows).  Integer sums are
+// order-free, so splitting the dk reductions across threads is exact.
+// Activations written by other CTAs of the same kernel are read at L2
+// (__ldcg): the persistent kernel separates producer and consumer CTAs by a
+// grid barrier, and L1 is not coherent across CTAs.
+#pragma once
+#include "f5_block.cuh"
+#include "f5_dn.cuh"
+#include "f5_kernels.cuh"
+
+namespace f5 {
+
+struct DnSmem {
+  int16_t *sd;      // [128*128] head state [dk][dv] (decayed in place)
+  int32_t *qn, *kn; // [128]
+  long long *part;  // [NQ*128] partial sums of the split recurrence
+  long long *red;   // [32]
+  long long *gate;  // [4] beta, decay, rq, rk
+  int *e;           // [2]
+};
+
+// conv4 + SiLU, gates, l2norm of q and k, conv-window ring update
+// (ref/layer_fixed.py:1511-1543).  Needs the in-projection outputs; does not
+// touch the state.  qkv[] holds this column's q, k, v (valid for q == 0).
+template <class SY, int NQ>
+F5_DEV void dn_head_pre(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, long long (&qkv)[3]) {
+  const int t = sy.tid(), dv = t & 127, q = t >> 7;
+  const int kh = h / a.vrep;
+  const int T = *a.T;
+  const int chans[3] = {kh * 128 + dv, a.lkd + kh * 128 + dv, 2 * a.lkd + h * 128 + dv};
+  qkv[0] = qkv[1] = qkv[2] = 0;
+  if (q == 0) {
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      const int c = chans[i];
+      const int16_t *ring = a.conv + (size_t)c * 4;
+      const int32_t *cw = a.conv_w + (size_t)c * 4;
+      const long long xnew = __ldcg(a.qkv16 + c);
+      long long acc = 0;
+#pragma unroll
+      for (int j = 0; j < 3; ++j) acc += (long long)__ldcg(ring + ((T + 1 + j) & 3)) * cw[j];
+      acc += xnew * cw[3];
+      const long long pre = clip(rshr(acc, RS_F + CW_F - 12), -(1 << 20), (1 << 20) - 1);
+      const long long co = clip16(silu_q(pre));
+      qkv[i] = rshr(co, 12 - QKV_F);
+    }
+  }
+  if (t == 0) {   // gates (ref/layer_fixed.py:1531-1538)
+    const long long beta = sigmoid_q(__ldcg(a.b16 + h));
+    const long long sp = softplus_q((long long)__ldcg(a.a16 + h) + a.dt_bias[h]);
+    const long long g = -rshr((long long)a.A[h] * sp, 15 + 12 - 16);
+    long long dec = rshr(exp_neg_q(g < 0 ? g : 0), 15);
+    if (dec > 32767) dec = 32767;
+    sm.gate[0] = beta;
+    sm.gate[1] = dec;
+  }
+  const long long ssq = g_sum_ll(sy, qkv[0] * qkv[0], sm.red);
+  const long long ssk = g_sum_ll(sy, qkv[1] * qkv[1], sm.red);
+  if (t == 0) {   // ref/layer_fixed.py:1322-1330
+    int64_t r; int e;
+    rsqrt_q((uint64_t)(ssq == 0 ? 1 : ssq), 2 * QKV_F, r, e);
+    sm.gate[2] = r; sm.e[0] = e;
+    rsqrt_q((uint64_t)(ssk == 0 ? 1 : ssk), 2 * QKV_F, r, e);
+    sm.gate[3] = r; sm.e[1] = e;
+  }
+  sy.sync();
+  if (q == 0) {
+    const long long qn = clip16(rshr(qkv[0] * sm.gate[2], QKV_F + 30 - sm.e[0] - NRM_F));
+    sm.qn[dv] = (int32_t)rshr(qn * 2896, 15);    // round(2^15 / sqrt(128)) = 2896
+    sm.kn[dv] = (int32_t)clip16(rshr(qkv[1] * sm.gate[3], QKV_F + 30 - sm.e[1] - NRM_F));
+    // conv ring: slot T%4 takes this step's pre-conv input; q/k channels are
+    // shared by the VREP value heads of a key head -> written by the first
+    const int slot_new = T & 3;
+    if ((h % a.vrep) == 0) {
+      a.conv[(size_t)chans[0] * 4 + slot_new] = __ldcg(a.qkv16 + chans[0]);
+      a.conv[(size_t)chans[1] * 4 + slot_new] = __ldcg(a.qkv16 + chans[1]);
+    }
+    a.conv[(size_t)chans[2] * 4 + slot_new] = __ldcg(a.qkv16 + chans[2]);
+  }
+  sy.sync();
+}
+
+// recurrence, block-float shift, gated norm, x silu(z)  (ref/layer_fixed.py:
+// 1545-1580).  sm.sd must hold the head's state.
+template <class SY, int NQ>
+F5_DEV void dn_head_rec(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, const long long (&qkv)[3]) {
+  const int t = sy.tid(), dv = t & 127, q = t >> 7;
+  constexpr int RQ = 128 / NQ;
+  int16_t *S = a.S + (size_t)h * 128 * 128;
+  const int decay = (int)sm.gate[1];
+  long long kvm = 0;
+#pragma unroll 8
+  for (int dk = q * RQ; dk < (q + 1) * RQ; ++dk) {
+    const int sd = rshr32p((int32_t)sm.sd[dk * 128 + dv] * decay, GAT_F);   // |S*decay| < 2^30
+    sm.sd[dk * 128 + dv] = (int16_t)sd;
+    kvm += (long long)sd * sm.kn[dk];
+  }
+  if (NQ > 1) {
+    sm.part[q * 128 + dv] = kvm;
+    sy.sync();
+    kvm = 0;
+#pragma unroll
+    for (int i = 0; i < NQ; ++i) kvm += sm.part[i * 128 + dv];
+    sy.sync();
+  }
+  kvm = rshr(kvm, NRM_F);
+  const long long v_col = NQ > 1 ? 0 : qkv[2];
+  long long delta;
+  if (NQ > 1) {
+    if (q == 0) sm.part[dv] = rshr(((qkv[2] << (S_F - QKV_F)) - kvm) * sm.gate[0], GAT_F);
+    sy.sync();
+    delta = sm.part[dv];
+    sy.sync();
+  } else {
+    delta = rshr(((v_col << (S_F - QKV_F)) - kvm) * sm.gate[0], GAT_F);
+  }
+  long long o = 0;
+  int sat = 0;
+#pragma unroll 8
+  for (int dk = q * RQ; dk < (q + 1) * RQ; ++dk) {
+    long long sn = (long long)sm.sd[dk * 128 + dv] + rshr((long long)sm.kn[dk] * delta, NRM_F);
+    if (sn > 32767 || sn < -32767) ++sat;   // |Sh| > 32767 (ref/layer_fixed.py:1557)
+    sn = clip16(sn);
+    S[dk * 128 + dv] = (int16_t)sn;
+    o += sn * sm.qn[dk];
+  }
+  if (a.stats && sat) atomicAdd(a.stats, (unsigned long long)sat);
+  if (NQ > 1) {
+    sm.part[q * 128 + dv] = o;
+    sy.sync();
+    o = 0;
+#pragma unroll
+    for (int i = 0; i < NQ; ++i) o += sm.part[i * 128 + dv];
+    sy.sync();
+  }
+  o = rshr(o, NRM_F);
+  if (q != 0) o = 0;   // one contribution per column to the head reductions
+  // ---- block floating k_h (ref/layer_fixed.py:470-486) ----
+  const unsigned long long om = g_max_ull(sy, uabs(o), reinterpret_cast<unsigned long long *>(sm.red));
+  const int kh_shift = bf_shift(om);
+  const long long o16 = clip16(kh_shift >= 0 ? rshr(o, kh_shift) : (long long)((unsigned long long)o << (-kh_shift)));
+  // ---- gated RMSNorm scale (ref/layer_fixed.py:509-546 or 694-781) ----
+  long long m;
+  if (a.norm_mode == 0) {
+    // numpy int64 sum of o*o (wrapping modulo 2^64, order-free)
+    const long long ss = (long long)g_sum_ull(sy, (unsigned long long)o * (unsigned long long)o,
+                                              reinterpret_cast<unsigned long long *>(sm.red));
+    m = dn_norm_scale(ss, kh_shift, 128);
+  } else {
+    const long long ss = g_sum_ll(sy, o16 * o16, sm.red);
+    m = eps_norm_scale(ss, kh_shift, 7);
+  }
+  if (q == 0) {
+    const long long tt = clip16(rshr(o16 * m, 15));
+    const long long nh = clip16(rshr(tt * a.norm_w[dv], 14));
+    const long long zg = clip16(silu_q((long long)__ldcg(a.z16 + h * 128 + dv) << (12 - QKV_F)));
+    a.on16[h * 128 + dv] = (int16_t)clip16(rshr(nh * zg, 12));
+    if (dv == 0 && a.kh_out) a.kh_out[h] = kh_shift;
+  }
+}
+
+}  // namespace f5

@@ -13,6 +13,18 @@ enum : uint32_t {
   DERR_RANGE = 1u << 3,          // an input outside a documented range
 };
 
+// ---- device-resident step parameters (read by the decode step's kernels) ----
+struct StepParams {
+  int tok;        // input token of this step
+  int pos;        // RoPE position of this step
+  int T;          // tokens already in every layer's cache / conv window
+  int next_tok;   // argmax of this step (first max wins)
+  int max_val;    // its y32 logit
+  uint32_t err;   // device error bits (DERR_*)
+  int steps;      // steps completed since reset
+  int pad;
+};
+
 // ---- quantized activation vector (DYNQ8 output, ref/fixedpoint.py:24-33) ----
 // x8 lives in its own buffer; meta[0] = e_x, meta[1] = in_f (fraction bits
 // of the int16 vector that was quantized; consumed by matvec_to's shift).
@@ -43,11 +55,14 @@ enum GemvPro : int {
   PRO_DYNQ8 = 2,      // src int16[K]: DYNQ8, in_f given
   PRO_ATTN_GATE = 3,  // src int64[K] (gated attention product): k_a = attn_o_shift,
                       // clip16(rshr(src, k_a)) -> DYNQ8, in_f = QKV_F + GAT_F - k_a
+  PRO_ATTN_ACC = 4,   // src int32[K] attention sums acc, src2 int16 q|gate rows of the
+                      // q projection: product acc * sigmoid(gate), then as PRO_ATTN_GATE
 };
 
 struct GemvPrologue {
   int mode;
   const void *src;
+  const void *src2;   // PRO_ATTN_ACC: q|gate rows ([K/256][512] int16)
   const int32_t *w;   // PRO_RMSNORM gains
   int in_f;
   int one_plus;
