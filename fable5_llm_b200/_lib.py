@@ -18,6 +18,7 @@ F5_OK, F5_EINVAL, F5_ECUDA, F5_ENOMEM, F5_ETIMEOUT, F5_EOVERFLOW, F5_ESTATE, F5_
     0, -1, -2, -3, -4, -5, -6, -7
 
 GM_Y32, GM_TO16, GM_TO64, GM_RESID, GM_SILU_MUL, GM_ARGMAX = range(6)
+ENGINE_GRAPH, ENGINE_PERSISTENT = 0, 1
 (PR_RSHR, PR_SIGMOID, PR_SOFTPLUS, PR_SILU, PR_EXP_NEG, PR_RSQRT, PR_RECIP,
  PR_BF_SHIFT, PR_DYNQ8_E, PR_DN_NORM_SCALE, PR_EPS_NORM_SCALE, PR_EXP2_FRAC) = range(12)
 
@@ -63,6 +64,9 @@ SIGNATURES = [
     ("f5_ctx_set_logits", c_int, [c_vp, c_int]),
     ("f5_ctx_stream", c_int, [c_vp, c_vp]),
     ("f5_ctx_prepare", c_int, [c_vp]),
+    ("f5_ctx_set_engine", c_int, [c_vp, c_int]),
+    ("f5_ctx_get_engine", c_int, [c_vp, c_vp]),
+    ("f5_ctx_trace_step", c_int, [c_vp, c_vp, c_size, c_vp, c_vp]),
     ("f5_decode_step", c_int, [c_vp, c_int, c_int, c_vp, c_vp]),
     ("f5_decode_launch", c_int, [c_vp, c_int, c_vp]),
     ("f5_ctx_sync", c_int, [c_vp, c_vp, c_vp]),

@@ -1,12 +1,18 @@
 // Model context: one GPU's resident 9B integer model, its decode state and
-// the decode step captured as one CUDA graph.
+// the decode step in two engines.
 //
 // Replaces the reference's model-level step (ref/fidelity_check.py:404-448
 // FxRunner.step; ref/gen_model_script.py:602-650 token loop) and, for one
 // layer, ref/layer_fixed.py:1669-1677 layer_decode_fx.  The 39k-record SEQ
-// program the FPGA sequencer runs per token is replaced by a fixed chain of
-// 163 kernel launches (step begin, 5 per layer, LM head, step end) recorded
-// once into a CUDA graph with programmatic dependent launch edges.
+// program the FPGA sequencer runs per token is replaced by
+//  * F5_ENGINE_PERSISTENT: one cooperative launch of the persistent decode
+//    kernel (f5_mega.cu) walking a device-resident list of op descriptors;
+//  * F5_ENGINE_GRAPH: a fixed chain of 163 kernel launches (step begin, 5
+//    per layer, LM head, step end) recorded once into a CUDA graph with
+//    programmatic dependent launch edges.
+// Both are built by the same enqueue_step walk (the persistent program is
+// the walk in "emit" mode), so they run the same descriptors.
+#include <algorithm>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -17,6 +23,7 @@
 #include "f5_dn.cuh"
 #include "f5_int.cuh"
 #include "f5_kernels.cuh"
+#include "f5_mega.cuh"
 
 namespace f5 {
 cudaError_t launch_synth_w4(uint8_t *, long long, int, int, long long, uint64_t, uint64_t, int, cudaStream_t);
@@ -129,6 +136,17 @@ struct f5_ctx {
   bool want_logits = false;
   cudaGraphExec_t step_exec = nullptr;
   bool graph_dirty = true;
+  // persistent engine
+  int engine = -1;                      // -1 auto (persistent when it fits), else F5_ENGINE_*
+  bool mega_dirty = true;
+  f5::MegaOp *d_ops = nullptr;          // device op list
+  unsigned *d_bars = nullptr;           // barrier counters (+ abort flag, final arrivals)
+  uint4 *d_attacc = nullptr;            // per attention layer: score max, exp sum, PV sums
+  f5::MegaArgs margs = {};
+  int mega_grid = 0;
+  size_t mega_smem = 0;
+  std::vector<f5::MegaOp> *emit = nullptr;   // enqueue_step in emit mode
+  int emit_err = 0;
   std::vector<void *> allocs;
 };
 
@@ -225,7 +243,7 @@ static int prep_matrix(f5_ctx *c, int layer, int slot, int N, int K, int g, int 
   m->N = N; m->K = K; m->g = g; m->e = e; m->sh = sh; m->stride = row_stride(K, g);
   split_rows(N, c->cfg.world_size, c->cfg.rank, m->row0, m->rows);
   if (!m->w) F5_ALLOC(c, m->w, (size_t)m->rows * m->stride + 64);
-  c->graph_dirty = true;
+  c->graph_dirty = c->mega_dirty = true;
   return F5_OK;
 }
 
@@ -249,6 +267,13 @@ static GemvSeg mkseg(const DevMat &m, void *out, int mode, int out_f, const DevM
   return s;
 }
 
+static void emit_op(f5_ctx *c, MegaOp &op) {
+  // every op waits for the previous one on grid barrier (index - 1); the
+  // persistent kernel relies on this numbering
+  op.bar = c->emit->empty() ? -1 : (int)c->emit->size() - 1;
+  c->emit->push_back(op);
+}
+
 static cudaError_t gemv(f5_ctx *c, const GemvSeg *segs, int nseg, int K, const GemvPrologue &pro,
                         unsigned long long *key, bool pdl) {
   GemvArgs a = {};
@@ -269,10 +294,41 @@ static cudaError_t gemv(f5_ctx *c, const GemvSeg *segs, int nseg, int K, const G
   a.err = c->err;
   double bytes = 0;
   for (int i = 0; i < nseg; ++i) bytes += (double)segs[i].rows * a.stride * (segs[i].mode == GM_SILU_MUL ? 2 : 1);
+  if (c->emit) {
+    // persistent program: same descriptor, ring-stage chunking, one CTA per SM
+    a.rows_per_stage = mega_rows_per_stage(a.stride);
+    a.stages = 0;
+    bool paired = false, argmax = false;
+    for (int i = 0; i < nseg; ++i) {
+      paired |= segs[i].mode == GM_SILU_MUL;
+      argmax |= segs[i].mode == GM_ARGMAX;
+    }
+    const int per_cta = (units + c->mega_grid - 1) / c->mega_grid;
+    // K = 12288 rows are reduced as 3 K-parts by 15 warps: <= 5 rows per stage
+    if (K == 12288 && a.rows_per_stage > 5) a.rows_per_stage = 5;
+    const int res_per_unit = paired ? 2 : (K == 12288 ? 3 : 1);
+    if ((K != 4096 && K != 12288) || (argmax && (nseg != 1 || K != 4096)) || pro.mode == PRO_X8 ||
+        (K == 12288 && (paired || argmax)) || (!argmax && per_cta * res_per_unit > MEGA_RES) ||
+        a.rows_per_stage < 2)
+      c->emit_err = 1;
+    MegaOp op = {};
+    op.kind = MK_GEMV;
+    op.g = a;
+    emit_op(c, op);
+    return cudaSuccess;
+  }
   tl_begin(c);
   cudaError_t e = launch_gemv(a, c->st, pdl, sm_count());
   tl_end(c, TK_GEMV, bytes);
   return e;
+}
+
+// per attention layer: NQ score-max keys, NQ exp sums (u64), NQ*HD PV sums (i32)
+constexpr size_t ATT_ACC_BYTES = NQ * 8 + NQ * 8 + NQ * HD * 4;
+static size_t n_attn_layers(const f5_ctx *c) {
+  size_t n = 0;
+  for (const Layer &l : c->L) n += l.attn ? 1 : 0;
+  return n;
 }
 
 // the five launches of one layer (ref/layer_fixed.py:1669-1677)
@@ -295,10 +351,17 @@ static cudaError_t enqueue_layer(f5_ctx *c, int li, bool pdl) {
     d.conv = l.conv; d.conv_w = l.conv_w; d.dt_bias = l.dt_bias; d.A = l.A; d.norm_w = l.norm_w;
     d.S = l.S; d.on16 = c->on16; d.T = &c->params->T; d.kh_out = l.kh; d.stats = c->stats; d.err = c->err;
     d.lkd = LKD; d.vrep = LNH / LNKH; d.norm_mode = c->cfg.norm_mode;
-    tl_begin(c);
-    e = launch_dn_step(d, LNH, c->st, pdl);
-    tl_end(c, TK_DN, 0);
-    if (e) return e;
+    if (c->emit) {
+      MegaOp op = {};
+      op.kind = MK_DN;
+      op.d = d;
+      emit_op(c, op);
+    } else {
+      tl_begin(c);
+      e = launch_dn_step(d, LNH, c->st, pdl);
+      tl_end(c, TK_DN, 0);
+      if (e) return e;
+    }
     GemvPrologue p2 = {};
     p2.mode = PRO_DYNQ8;
     p2.src = c->on16;
@@ -314,14 +377,34 @@ static cudaError_t enqueue_layer(f5_ctx *c, int li, bool pdl) {
     at.rope = c->rope; at.k8 = l.k8; at.ke = l.ke; at.v8 = l.v8; at.ve = l.ve; at.prod = c->prod64;
     at.T = &c->params->T; at.pos = &c->params->pos; at.err = c->err;
     at.max_T = c->cfg.max_T; at.max_pos = c->rope_npos; at.nq = NQ; at.nkv = NKV; at.rot = ROT;
-    tl_begin(c);
-    e = launch_attn(at, c->st, pdl);
-    tl_end(c, TK_ATTN, 0);
-    if (e) return e;
     GemvPrologue p2 = {};
     p2.mode = PRO_ATTN_GATE;
     p2.src = c->prod64;
     p2.dbg = l.ka;
+    if (c->emit) {
+      // split-T over G/NKV CTAs per KV head; sums land in this layer's accumulators
+      const int n_attn = (int)std::count_if(c->emit->begin(), c->emit->end(),
+                                            [](const MegaOp &o) { return o.kind == MK_ATTN; });
+      const int cpg = c->mega_grid / NKV;
+      uint8_t *acc = reinterpret_cast<uint8_t *>(c->d_attacc) + (size_t)n_attn * ATT_ACC_BYTES;
+      MegaOp op = {};
+      op.kind = MK_ATTN;
+      op.at.a = at;
+      op.at.a.chunk_max = (((c->cfg.max_T + cpg - 1) / cpg) + 15) & ~15;
+      op.at.gmax = reinterpret_cast<unsigned long long *>(acc);
+      op.at.gsum = reinterpret_cast<unsigned long long *>(acc + NQ * 8);
+      op.at.gacc = reinterpret_cast<int32_t *>(acc + NQ * 16);
+      op.at.gbar = -1;   // assigned after the walk
+      emit_op(c, op);
+      p2.mode = PRO_ATTN_ACC;
+      p2.src = op.at.gacc;
+      p2.src2 = c->qg16;
+    } else {
+      tl_begin(c);
+      e = launch_attn(at, c->st, pdl);
+      tl_end(c, TK_ATTN, 0);
+      if (e) return e;
+    }
     GemvSeg so = mkseg(l.m[3], c->x16, GM_RESID, RS_F);
     if ((e = gemv(c, &so, 1, NQ * HD, p2, nullptr, pdl))) return e;
   }
@@ -344,7 +427,18 @@ static cudaError_t enqueue_layer(f5_ctx *c, int li, bool pdl) {
 
 static cudaError_t enqueue_step(f5_ctx *c, bool pdl) {
   cudaError_t e;
-  {
+  if (c->emit) {
+    MegaOp op = {};
+    op.kind = MK_BEGIN;
+    op.b.emb = c->emb;
+    op.b.x16 = c->x16;
+    op.b.vocab = c->cfg.vocab;
+    op.b.H = H;
+    op.b.key = c->key;
+    op.b.zero = c->d_attacc;
+    op.b.zero_n = (int)(n_attn_layers(c) * ATT_ACC_BYTES / 16);
+    emit_op(c, op);
+  } else {
     StepParams *p = c->params;
     const int16_t *emb = c->emb;
     int vocab = c->cfg.vocab, h = H;
@@ -366,7 +460,7 @@ static cudaError_t enqueue_step(f5_ctx *c, bool pdl) {
   pf.one_plus = 0;   // ln_f pre-folded (1+w) at Q3.12 (ref/gen_model_script.py:502-504)
   GemvSeg sh = mkseg(c->head, c->want_logits ? c->logits : nullptr, GM_ARGMAX, 0);
   if ((e = gemv(c, &sh, 1, H, pf, c->key, pdl))) return e;
-  {
+  if (!c->emit) {
     StepParams *p = c->params;
     const unsigned long long *k = c->key;
     const uint32_t *er = c->err;
@@ -421,6 +515,100 @@ static int build_graph(f5_ctx *c) {
   F5_CU(e, "instantiate decode graph");
   c->graph_dirty = false;
   return F5_OK;
+}
+
+static void free_mega(f5_ctx *c) {
+  if (c->d_ops) cudaFree(c->d_ops);
+  if (c->d_bars) cudaFree(c->d_bars);
+  c->d_ops = nullptr;
+  c->d_bars = nullptr;
+}
+
+// Emit the step as the persistent kernel's op list.  `unsupported` tells a
+// configuration the persistent engine cannot run (auto mode then uses the
+// graph engine) from a context that is not ready.
+static int build_mega(f5_ctx *c, bool &unsupported) {
+  unsupported = false;
+  if (!c->mega_dirty && c->d_ops) return F5_OK;
+  int rc = ready(c);
+  if (rc) return rc;
+  unsupported = true;
+  if (c->cfg.world_size > 1) return set_error(F5_ESTATE, "the persistent engine runs unsharded contexts");
+  const int sms = sm_count();
+  if (sms < NKV) return set_error(F5_ESTATE, "too few SMs for the persistent engine");
+  const int cpg = sms / NKV;
+  const int chunk_max = (((c->cfg.max_T + cpg - 1) / cpg) + 15) & ~15;
+  int grid = 0, ns = 0;
+  size_t smem = 0;
+  cudaError_t e = mega_config(chunk_max, &grid, &smem, &ns);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(F5_ESTATE, "persistent engine not resident on this device: %s", cudaGetErrorString(e));
+  }
+  c->mega_grid = grid;
+  c->mega_smem = smem;
+  const size_t n_attn = n_attn_layers(c);
+  if (!c->d_attacc) {
+    unsupported = false;
+    F5_ALLOC(c, c->d_attacc, (n_attn ? n_attn : 1) * ATT_ACC_BYTES);
+    unsupported = true;
+  }
+  std::vector<MegaOp> ops;
+  c->emit = &ops;
+  c->emit_err = 0;
+  e = enqueue_step(c, false);
+  c->emit = nullptr;
+  if (e != cudaSuccess) return cuda_status(e, "emit persistent program");
+  if (c->emit_err) return set_error(F5_ESTATE, "a GEMV of this model does not fit the persistent engine");
+  const int n_grid = (int)ops.size() - 1;
+  int ai = 0;
+  for (MegaOp &op : ops)
+    if (op.kind == MK_ATTN) op.at.gbar = n_grid + 2 * NKV * ai++;
+  const int nbars = n_grid + 2 * NKV * ai + 2;
+  unsupported = false;
+  free_mega(c);
+  F5_CU(cudaMalloc(&c->d_ops, ops.size() * sizeof(MegaOp)), "persistent program");
+  F5_CU(cudaMalloc(&c->d_bars, (size_t)nbars * 4), "persistent barriers");
+  F5_CU(cudaMemcpyAsync(c->d_ops, ops.data(), ops.size() * sizeof(MegaOp), cudaMemcpyHostToDevice, c->st),
+        "persistent program");
+  F5_CU(cudaMemsetAsync(c->d_bars, 0, (size_t)nbars * 4, c->st), "persistent barriers");
+  F5_CU(cudaStreamSynchronize(c->st), "persistent program");
+  MegaArgs &m = c->margs;
+  m = {};
+  m.ops = c->d_ops;
+  m.nops = (int)ops.size();
+  m.params = c->params;
+  m.bars = c->d_bars;
+  m.nbars = nbars;
+  m.err = c->err;
+  m.advance = 1;
+  m.dn_heads = LNH;
+  m.ns = ns;
+  c->mega_dirty = false;
+  return F5_OK;
+}
+
+// engine of the next step (auto: persistent when it fits, else the graph)
+static int resolve_engine(f5_ctx *c, int &eng) {
+  if (c->engine == F5_ENGINE_GRAPH) {
+    eng = F5_ENGINE_GRAPH;
+    return build_graph(c);
+  }
+  bool unsupported = false;
+  int rc = build_mega(c, unsupported);
+  if (rc == F5_OK) {
+    eng = F5_ENGINE_PERSISTENT;
+    return F5_OK;
+  }
+  if (!unsupported || c->engine == F5_ENGINE_PERSISTENT) return rc;
+  eng = F5_ENGINE_GRAPH;
+  return build_graph(c);
+}
+
+static int launch_step(f5_ctx *c, int eng) {
+  if (eng == F5_ENGINE_PERSISTENT)
+    return cuda_status(launch_mega(c->margs, c->mega_grid, c->mega_smem, c->st), "persistent decode step");
+  return cuda_status(cudaGraphLaunch(c->step_exec, c->st), "decode step");
 }
 
 static int finish_host(f5_ctx *c, const char *what) {
@@ -501,6 +689,7 @@ int f5_ctx_destroy(f5_ctx *c) {
   DevGuard dg(c->device);
   if (c->st) cudaStreamSynchronize(c->st);
   if (c->step_exec) cudaGraphExecDestroy(c->step_exec);
+  free_mega(c);
   for (void *p : c->allocs) cudaFree(p);
   if (c->h_params) cudaFreeHost(c->h_params);
   if (c->st) cudaStreamDestroy(c->st);
@@ -570,7 +759,7 @@ int f5_ctx_upload_vector(f5_ctx *c, int layer, int kind, const int64_t *v, int n
 static int ensure_emb(f5_ctx *c) {
   if (!c->emb) {
     F5_ALLOC(c, c->emb, (size_t)c->cfg.vocab * H * 2);
-    c->graph_dirty = true;
+    c->graph_dirty = c->mega_dirty = true;
   }
   return F5_OK;
 }
@@ -605,7 +794,7 @@ int f5_ctx_upload_rope(f5_ctx *c, const int16_t *tab, int npos) {
   c->rope_npos = npos;
   F5_CU(cudaMemcpyAsync(c->rope, tab, (size_t)npos * 128 * 2, cudaMemcpyHostToDevice, c->st), "upload rope");
   F5_CU(cudaStreamSynchronize(c->st), "upload rope");
-  c->graph_dirty = true;
+  c->graph_dirty = c->mega_dirty = true;
   return F5_OK;
 }
 
@@ -664,7 +853,7 @@ int f5_ctx_set_logits(f5_ctx *c, int on) {
   if (on && !c->logits) F5_ALLOC(c, c->logits, (size_t)c->cfg.vocab * 4);
   if ((bool)on != c->want_logits) {
     c->want_logits = on != 0;
-    c->graph_dirty = true;
+    c->graph_dirty = c->mega_dirty = true;
   }
   return F5_OK;
 }
@@ -681,14 +870,57 @@ int f5_ctx_prepare(f5_ctx *c) {
   int rc = check_ctx(c);
   if (rc) return rc;
   DevGuard dg(c->device);
-  return build_graph(c);
+  int eng;
+  return resolve_engine(c, eng);
+}
+
+int f5_ctx_set_engine(f5_ctx *c, int engine) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  if (engine != F5_ENGINE_GRAPH && engine != F5_ENGINE_PERSISTENT)
+    return set_error(F5_EINVAL, "f5_ctx_set_engine: engine %d", engine);
+  c->engine = engine;
+  return F5_OK;
+}
+
+int f5_ctx_get_engine(f5_ctx *c, int *engine) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  if (!engine) return set_error(F5_EINVAL, "f5_ctx_get_engine: null out");
+  DevGuard dg(c->device);
+  return resolve_engine(c, *engine);
+}
+
+int f5_ctx_trace_step(f5_ctx *c, uint64_t *out, size_t cap, int *grid, int *nops) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  DevGuard dg(c->device);
+  bool unsupported = false;
+  if ((rc = build_mega(c, unsupported))) return rc;
+  if (grid) *grid = c->mega_grid;
+  if (nops) *nops = c->margs.nops;
+  if (!out) return F5_OK;
+  const size_t n = (size_t)c->mega_grid * c->margs.nops * 2;
+  if (cap < n) return set_error(F5_EINVAL, "f5_ctx_trace_step: %zu slots, need %zu", cap, n);
+  unsigned long long *d = nullptr;
+  F5_CU(cudaMalloc(&d, n * 8), "trace buffer");
+  MegaArgs m = c->margs;
+  m.trace = d;
+  cudaError_t e = cudaMemsetAsync(d, 0, n * 8, c->st);
+  if (e == cudaSuccess) e = launch_mega(m, c->mega_grid, c->mega_smem, c->st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(out, d, n * 8, cudaMemcpyDeviceToHost, c->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->st);
+  cudaFree(d);
+  F5_CU(e, "f5_ctx_trace_step");
+  return finish_host(c, "f5_ctx_trace_step");
 }
 
 int f5_decode_step(f5_ctx *c, int32_t tok, int32_t pos, int32_t *next_tok, int32_t *max_logit) {
   int rc = check_ctx(c);
   if (rc) return rc;
   DevGuard dg(c->device);
-  if ((rc = build_graph(c))) return rc;
+  int eng;
+  if ((rc = resolve_engine(c, eng))) return rc;
   F5_CU(cudaMemcpyAsync(c->h_params, c->params, sizeof(StepParams), cudaMemcpyDeviceToHost, c->st), "decode step");
   F5_CU(cudaStreamSynchronize(c->st), "decode step");
   c->h_params->tok = tok;
@@ -696,7 +928,7 @@ int f5_decode_step(f5_ctx *c, int32_t tok, int32_t pos, int32_t *next_tok, int32
   c->h_params->err = 0;
   F5_CU(cudaMemcpyAsync(c->params, c->h_params, sizeof(StepParams), cudaMemcpyHostToDevice, c->st), "decode step");
   F5_CU(cudaMemsetAsync(c->err, 0, 4, c->st), "decode step");
-  F5_CU(cudaGraphLaunch(c->step_exec, c->st), "decode step");
+  if ((rc = launch_step(c, eng))) return rc;
   if ((rc = finish_host(c, "f5_decode_step"))) return rc;
   if (next_tok) *next_tok = c->h_params->next_tok;
   if (max_logit) *max_logit = c->h_params->max_val;
@@ -708,8 +940,10 @@ int f5_decode_launch(f5_ctx *c, int n_steps, void *stream_unused) {
   int rc = check_ctx(c);
   if (rc) return rc;
   DevGuard dg(c->device);
-  if ((rc = build_graph(c))) return rc;
-  for (int i = 0; i < n_steps; ++i) F5_CU(cudaGraphLaunch(c->step_exec, c->st), "decode launch");
+  int eng;
+  if ((rc = resolve_engine(c, eng))) return rc;
+  for (int i = 0; i < n_steps; ++i)
+    if ((rc = launch_step(c, eng))) return rc;
   return F5_OK;
 }
 

@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1) k_gemv(const __grid_constant__ 
     const int nrows = pair ? 2 * ch.n : ch.n;
     const int cbase = ch.u - u0;
     for (int r = warp; r < nrows; r += GT_CONS) {
-      const long long aa = warp_sum_ll(row_dot<NCH>(st + (size_t)r * a.stride, K2, gshift, lane, xr, xs));
+      const long long aa = warp_sum_row(row_dot<NCH>(st + (size_t)r * a.stride, K2, gshift, lane, xr, xs));
       if (lane == 0) s_res[pair ? (r < ch.n ? 2 * (cbase + r) : 2 * (cbase + r - ch.n) + 1) : cbase + r] = aa;
     }
     __syncwarp();

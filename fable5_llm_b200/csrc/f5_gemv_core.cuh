@@ -146,6 +146,34 @@ F5_DEV long long warp_sum_ll(long long v) {
   return v;
 }
 
+// Exact warp sum of a row's per-lane partials p (|p| < 2^39: at most twelve
+// group terms m * d with m < 2^16, |d| < 2^19) with two 32-bit redux.sync
+// adds instead of a 64-bit shuffle tree: p = hi * 2^22 + lo with
+// lo = p mod 2^22 in [0, 2^22) and hi = floor(p / 2^22), |hi| < 2^17, so
+// sum(lo) < 2^27 and |sum(hi)| < 2^22 both fit 32 bits.
+F5_DEV long long warp_sum_row(long long p) {
+  const unsigned lo = (unsigned)p & 0x3FFFFFu;
+  const int hi = (int)(p >> 22);
+  const unsigned slo = __reduce_add_sync(0xffffffffu, lo);
+  const int shi = __reduce_add_sync(0xffffffffu, hi);
+  return ((long long)shi << 22) + (long long)slo;
+}
+
+// 16*sum_k w*x over one K=4096 row held in shared memory, x held in
+// registers (lane l owns bytes [c*512 + 16l, +16) of the weights, c < 4)
+F5_DEV long long row_dot4096(const uint8_t *row, int lane, const uint2 (&xr)[4][4]) {
+  long long acc = 0;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int boff = c * 512 + lane * 16;
+    const uint4 w = *reinterpret_cast<const uint4 *>(row + boff);
+    const uint32_t m = *reinterpret_cast<const uint16_t *>(row + 2048 + 2 * (boff >> 6));
+    acc += (long long)m * dot32(w, xr[c][0], xr[c][1], xr[c][2], xr[c][3]);
+  }
+  return acc;
+}
+
+
 // Redundant per-CTA computation of the GEMV's quantized input (see GemvPro).
 // Every value is read from global memory once and held in registers across
 // the reduction passes (MAXB 8-element blocks per thread).

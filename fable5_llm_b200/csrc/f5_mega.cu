@@ -1,0 +1,910 @@
+// Persistent decode-step kernel (sm_100a): one cooperative launch runs the
+// whole batch-1 decode step of ref/fidelity_check.py:404-448 (FxRunner.step)
+// over every SM, replacing the 163-launch per-op chain and its ~6-8 us of
+// launch / drain / ramp cost per dependent kernel.
+//
+// Roles inside each CTA (one CTA per SM, 544 threads):
+//  * producer (one lane of warp 16) walks the step's op list and streams
+//    EVERY weight row this CTA will ever consume, in consumption order,
+//    through a ring of MEGA_STAGE-byte shared-memory stages (cp.async.bulk,
+//    no multicast, full / empty mbarriers).  Weights do not depend on
+//    activations, so the stream never waits for a grid barrier: while the
+//    consumers sit at a barrier or in a DeltaNet / attention core, the ring
+//    fills and HBM stays busy.  It also prefetches the CTA's DeltaNet head
+//    state and its attention K / V rows into a scratch region, gated by a
+//    scratch-free mbarrier the consumers arrive on after each use.
+//  * consumers (warps 0-15, named barrier 1) run the ops in order, separated
+//    by grid barriers (global counters, bounded spins): GEMV prologue /
+//    row dot products / epilogues (f5_gemv_core.cuh), the DeltaNet head core
+//    (f5_dn_core.cuh, dk rows split over 4 thread quarters) and a split-T
+//    attention core whose three cross-CTA reductions (score max, exp sum,
+//    PV sums) are exact integer atomics in L2 with two group barriers.
+//
+// Every wait is bounded (globaltimer); a CTA that gives up raises a global
+// abort flag that every other wait polls, so the whole grid unwinds, drains
+// its in-flight bulk copies and exits with DERR_TIMEOUT set.  The last CTA
+// to finish decodes the argmax, advances the step parameters and re-zeroes
+// the barrier counters for the next launch.
+#include <climits>
+
+#include "f5_dn_core.cuh"
+#include "f5_gemv_core.cuh"
+#include "f5_mega.cuh"
+
+namespace f5 {
+
+constexpr int MG_CONS = 16;
+constexpr int MG_CT = MG_CONS * 32;
+constexpr int MG_NS_MAX = 6;
+constexpr int MG_XS = 12 * 4 * 32 * 8;          // x8 of K <= 12288 in the lane-major layout
+constexpr int MG_RESB = MEGA_RES * 8;
+constexpr unsigned long long MG_WAIT_NS = 1000000000ull;   // 1 s: a safety net only
+using CSync = NamedSync<1, MG_CT>;
+
+// scratch layout: DeltaNet head
+constexpr int DN_SD = 0, DN_QN = 32768, DN_KN = DN_QN + 512, DN_PART = DN_KN + 512, DN_END = DN_PART + 4096;
+// scratch layout: attention (K / V fills are 16-byte aligned for cp.async.bulk)
+constexpr int AT_K = 0, AT_V = AT_K + MEGA_SUB * 256, AT_KE = AT_V + MEGA_SUB * 256, AT_VE = AT_KE + MEGA_SUB,
+              AT_Q16 = AT_VE + MEGA_SUB, AT_K16 = AT_Q16 + 4 * 256 * 2, AT_K8N = AT_K16 + 4 * 256 * 2,
+              AT_V8N = AT_K8N + 256, AT_XN = AT_V8N + 256, AT_SC = AT_XN + 4 * 256 * 2;
+static_assert(AT_SC % 16 == 0 && AT_KE % 16 == 0 && AT_VE % 16 == 0, "scratch alignment");
+
+// ---------------------------------------------------------------------------
+// bounded waits and barriers
+// ---------------------------------------------------------------------------
+F5_DEV unsigned ld_acquire_u32(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+F5_DEV unsigned ld_relaxed_u32(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+struct Abort {
+  unsigned *flag;
+  uint32_t *err;
+  F5_DEV void raise() const {
+    atomicOr(err, DERR_TIMEOUT);
+    atomicExch(flag, 1u);
+  }
+  F5_DEV bool raised() const { return ld_relaxed_u32(flag) != 0; }
+};
+
+// mbarrier wait that gives up after MG_WAIT_NS or once another CTA aborted.
+// The abort flag lives in L2: under a saturated weight stream one poll costs
+// about a microsecond, so it is read only after MG_POLL_NS of waiting (and
+// then every MG_POLL_NS), never on the normal sub-microsecond waits.
+constexpr unsigned long long MG_POLL_NS = 20000ull;
+F5_DEV bool mwait(uint64_t *b, uint32_t parity, const Abort &ab) {
+  const uint32_t addr = smem_u32(b);
+  unsigned long long t0 = 0, tpoll = 0;
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok) : "r"(addr), "r"(parity) : "memory");
+    if (ok) return true;
+    if ((it & 63) == 63) {
+      const unsigned long long t = gtimer();
+      if (t0 == 0) {
+        t0 = t;
+        tpoll = t + MG_POLL_NS;
+      } else if (t >= tpoll) {
+        if (ab.raised()) return false;
+        if (t - t0 > MG_WAIT_NS) { ab.raise(); return false; }
+        tpoll = t + MG_POLL_NS;
+      }
+    }
+  }
+}
+
+// Counter barrier over `target` CTAs (consumer groups).  The release
+// (fence + add) / acquire (load + fence) pair by one thread, bracketed by
+// the group's named barrier, orders every consumer thread's prior global
+// writes before any later read in the other CTAs.
+F5_DEV bool counter_barrier(const CSync &sy, unsigned *cnt, unsigned target, const Abort &ab) {
+  sy.sync();
+  bool bad = false;
+  if (sy.tid() == 0) {
+    __threadfence();
+    atomicAdd(cnt, 1u);
+    unsigned long long t0 = 0, tpoll = 0;
+    for (uint32_t it = 0;; ++it) {
+      if (ld_acquire_u32(cnt) >= target) break;
+      if ((it & 7) == 7) {
+        const unsigned long long t = gtimer();
+        if (t0 == 0) {
+          t0 = t;
+          tpoll = t + MG_POLL_NS;
+        } else if (t >= tpoll) {
+          if (ab.raised()) { bad = true; break; }
+          if (t - t0 > MG_WAIT_NS) { ab.raise(); bad = true; break; }
+          tpoll = t + MG_POLL_NS;
+        }
+      }
+    }
+    __threadfence();
+  }
+  return !sy.any(bad);
+}
+
+F5_DEV void release_scratch(const CSync &sy, uint64_t *bfree) {
+  sy.sync();
+  if (sy.tid() == 0) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic accesses before the next async fill
+    mbar_arrive(bfree);
+  }
+}
+
+F5_DEV int part_lo(int total, int G, int b) { return (int)((long long)total * b / G); }
+
+// ---------------------------------------------------------------------------
+// attention geometry (identical in producer and consumers)
+// ---------------------------------------------------------------------------
+struct AttGeo {
+  bool ok;
+  int pos, Tn, Told, chunk, t0, t1, kv, j, cpg;
+};
+F5_DEV AttGeo att_geo(const AttnArgs &a, int T, int pos, int G, int b) {
+  AttGeo g;
+  g.cpg = G / a.nkv;
+  g.kv = b / g.cpg;
+  g.j = b % g.cpg;
+  g.ok = T >= 0 && T < a.max_T;
+  g.pos = pos;
+  if (pos < 0 || pos >= a.max_pos) { g.ok = false; g.pos = 0; }
+  g.Tn = g.ok ? T + 1 : max(0, min(T, a.max_T));
+  g.Told = g.ok ? T : g.Tn;
+  g.chunk = (((g.Tn + g.cpg - 1) / g.cpg) + 15) & ~15;
+  g.t0 = g.j * g.chunk;
+  g.t1 = min(g.t0 + g.chunk, g.Tn);
+  return g;
+}
+// cached rows of fill `s` of this CTA's token chunk: [sb, sb + n)
+F5_DEV int att_fill_rows(const AttGeo &g, int s, int &sb) {
+  sb = g.t0 + s * MEGA_SUB;
+  const int se = min(sb + MEGA_SUB, g.t1);
+  return max(0, min(se, g.Told) - sb);
+}
+F5_DEV void att_issue(uint8_t *dst_rows, uint8_t *dst_e, const int8_t *rows, const int8_t *ex, size_t row0, int n,
+                      uint64_t *bar) {
+  const uint32_t rb = (uint32_t)n * 256, eb = ((uint32_t)n + 15) & ~15u;
+  mbar_expect_tx(bar, rb + eb);
+  bulk_g2s(dst_rows, rows + row0 * 256, rb, bar);
+  bulk_g2s(dst_e, ex + row0, eb, bar);
+}
+
+// Shared memory at namespace scope: every address below is a compile-time
+// constant (no pointer kept in registers); the dynamic region's layout
+// depends only on the ring depth ns (a launch parameter):
+//   [ns x MEGA_STAGE ring][MG_XS x8 layout][MG_RESB row results][scratch]
+extern __shared__ __align__(128) uint8_t mg_dyn[];
+__shared__ __align__(8) uint64_t mg_full[MG_NS_MAX], mg_empty[MG_NS_MAX];
+__shared__ __align__(8) uint64_t mg_bsd, mg_bsk, mg_bsv, mg_bfree, mg_bpd[2];
+__shared__ __align__(16) MegaOp mg_cop[2], mg_pop[2];   // op i's descriptor in [i & 1]
+__shared__ long long mg_red[64];
+__shared__ long long mg_r, mg_gate[4], mg_att[8];
+__shared__ int mg_meta[4], mg_e[2];
+__shared__ int mg_cnt[6];   // issued fills: [0] ring, [1] sd, [2] sk, [3] sv (producer), [4] sk, [5] sv (consumers)
+__shared__ volatile int mg_abort;
+__shared__ int mg_last;
+
+struct MegaSmem {
+  int ns;
+  F5_DEV uint8_t *ring() const { return mg_dyn; }
+  F5_DEV uint2 *xs() const { return reinterpret_cast<uint2 *>(mg_dyn + ns * MEGA_STAGE); }
+  F5_DEV long long *res() const { return reinterpret_cast<long long *>(mg_dyn + ns * MEGA_STAGE + MG_XS); }
+  F5_DEV uint8_t *scr() const { return mg_dyn + ns * MEGA_STAGE + MG_XS + MG_RESB; }
+};
+
+// position in the stage ring: stage s, lap parity ph (flips each wrap)
+struct RingPos {
+  int s = 0;
+  uint32_t ph = 0;
+  int lap = 0;   // completed wraps (saturating at 2: only "first lap or not" matters)
+  F5_DEV void next(int ns) {
+    if (++s == ns) {
+      s = 0;
+      ph ^= 1u;
+      lap = lap < 2 ? lap + 1 : 2;
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
+// producer
+// ---------------------------------------------------------------------------
+F5_DEV void issue_desc(const MegaArgs &ma, const MegaSmem &S, int oi) {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // buffer's previous generic reads
+  mbar_expect_tx(&mg_bpd[oi & 1], sizeof(MegaOp));
+  bulk_g2s(&mg_pop[oi & 1], ma.ops + oi, sizeof(MegaOp), &mg_bpd[oi & 1]);
+}
+
+F5_DEV void producer(const MegaArgs &ma, const MegaSmem &S, int T, int pos, const Abort &ab) {
+  const int G = gridDim.x, b = blockIdx.x, ns = S.ns;
+  int issued = 0, n_scr = 0;
+  RingPos rp;
+  bool bad = false;
+  int desc_pending = -1;   // descriptor copy in flight (drained before exit)
+  issue_desc(ma, S, 0);
+  desc_pending = 0;
+  for (int oi = 0; oi < ma.nops && !bad; ++oi) {
+    if (!mwait(&mg_bpd[oi & 1], (oi >> 1) & 1, ab)) { bad = true; break; }
+    desc_pending = -1;
+    if (oi + 1 < ma.nops) {
+      issue_desc(ma, S, oi + 1);
+      desc_pending = oi + 1;
+    }
+    const MegaOp &op = mg_pop[oi & 1];
+    const int kind = op.kind;
+    if (kind == MK_GEMV) {
+      const GemvArgs &a = op.g;
+      int u = part_lo(a.total_units, G, b);
+      const int u1 = part_lo(a.total_units, G, b + 1);
+      Chunk ch;
+      while (next_chunk(a, u, u1, ch)) {
+        const int s = rp.s;
+        if (rp.lap > 0 && !mwait(&mg_empty[s], rp.ph ^ 1u, ab)) { bad = true; break; }
+        const GemvSeg &sg = a.seg[ch.seg];
+        const uint32_t nb = (uint32_t)ch.n * a.stride;
+        const bool pair = sg.mode == GM_SILU_MUL;
+        uint8_t *dst = S.ring() + (size_t)s * MEGA_STAGE;
+        mbar_expect_tx(&mg_full[s], pair ? 2 * nb : nb);
+        bulk_g2s(dst, sg.w + (size_t)ch.r0 * a.stride, nb, &mg_full[s]);
+        if (pair) bulk_g2s(dst + nb, sg.w2 + (size_t)ch.r0 * a.stride, nb, &mg_full[s]);
+        mg_cnt[0] = ++issued;
+        rp.next(ns);
+      }
+    } else if (kind == MK_DN) {
+      if (b < ma.dn_heads) {
+        if (n_scr > 0 && !mwait((&mg_bfree), (n_scr - 1) & 1, ab)) { bad = true; break; }
+        mbar_expect_tx((&mg_bsd), 128 * 128 * 2);
+        bulk_g2s(S.scr() + DN_SD, op.d.S + (size_t)b * 128 * 128, 128 * 128 * 2, (&mg_bsd));
+        mg_cnt[1] += 1;
+        ++n_scr;
+      }
+    } else if (kind == MK_ATTN) {
+      const AttnArgs &a = op.at.a;
+      const AttGeo g = att_geo(a, T, pos, G, b);
+      if (g.kv < a.nkv) {
+        if (n_scr > 0 && !mwait((&mg_bfree), (n_scr - 1) & 1, ab)) { bad = true; break; }
+        int sb;
+        const int n = att_fill_rows(g, 0, sb);
+        if (n > 0) {
+          const size_t row0 = (size_t)g.kv * a.max_T + sb;
+          att_issue(S.scr() + AT_K, S.scr() + AT_KE, a.k8, a.ke, row0, n, (&mg_bsk));
+          att_issue(S.scr() + AT_V, S.scr() + AT_VE, a.v8, a.ve, row0, n, (&mg_bsv));
+          mg_cnt[2] += 1;
+          mg_cnt[3] += 1;
+        }
+        ++n_scr;
+      }
+    }
+  }
+  if (desc_pending >= 0) mbar_wait(&mg_bpd[desc_pending & 1], (desc_pending >> 1) & 1, MG_WAIT_NS);
+}
+
+// ---------------------------------------------------------------------------
+// consumers: GEMV
+// ---------------------------------------------------------------------------
+// K = 4096 (every GEMV of the step but the MLP down projection): one row per
+// consumer warp per 16-row stage.  The consumer loop is issue-bound, so it is
+// kept to the row's own arithmetic: chunks are walked segment by segment
+// (the same split as next_chunk, which the producer uses), K and the group
+// size are compile-time constants (the host admits only g = 128), the row
+// sum uses two redux.sync adds, and the LM head's argmax epilogue is batched
+// -- lane k % 32 of a warp holds the warp's k-th row sum, and every 32 rows
+// all lanes turn their rows into (y32, row) keys at once.
+F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const Abort &ab) {
+  const CSync sy;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = gridDim.x, b = blockIdx.x, ns = S.ns;
+  prologue<1>(sy, a, S.xs(), mg_red, (&mg_r), mg_meta);
+  sy.sync();
+  const int e_x = mg_meta[0], in_f = mg_meta[1];
+  uint2 xr[4][4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) xr[c][j] = S.xs()[((c << 2) + j) * 32 + lane];
+  const int u0 = part_lo(a.total_units, G, b), u1 = part_lo(a.total_units, G, b + 1);
+  const int stride = a.stride, sh = a.sh;
+  const bool argmax = a.seg[0].mode == GM_ARGMAX;
+  long long *res = S.res();
+  int32_t *logits = static_cast<int32_t *>(a.seg[0].out);   // argmax: optional y32 of every row
+  unsigned long long best = 0ull;
+  long long hold = 0;
+  int hold_row = -1, k = 0;
+  auto flush = [&]() {
+    if (hold_row >= 0) {
+      const long long y = rshr(hold >> 4, sh);
+      if (y >= (1ll << 31) || y <= -(1ll << 31)) atomicOr(a.err, DERR_Y32_OVERFLOW);
+      const unsigned long long key = argmax_key((int32_t)y, hold_row);
+      best = key > best ? key : best;
+      if (logits) logits[hold_row] = (int32_t)y;
+    }
+    hold_row = -1;
+  };
+  bool bad = false;
+  int u = u0;
+  while (u < u1 && !bad) {
+    const int si = seg_of(a, u);
+    const GemvSeg &sg = a.seg[si];
+    const int seg_hi = min(u1, si + 1 < a.nseg ? a.seg[si + 1].unit_begin : a.total_units);
+    const bool pair = sg.mode == GM_SILU_MUL;
+    const int ru = pair ? (a.rows_per_stage >> 1) : a.rows_per_stage;
+    const int orow0 = sg.out_row0 - sg.unit_begin;   // output row of unit v: orow0 + v
+    while (u < seg_hi) {
+      const int n = min(ru, seg_hi - u);
+      if (mg_abort || !mwait(&mg_full[rp.s], rp.ph, ab)) {
+        mg_abort = 1;
+        bad = true;
+        break;
+      }
+      const uint8_t *st = S.ring() + rp.s * MEGA_STAGE;
+      const int nrows = pair ? 2 * n : n;
+      const int cbase = u - u0;
+      for (int r = warp; r < nrows; r += MG_CONS) {
+        const long long acc = warp_sum_row(row_dot4096(st + r * stride, lane, xr));
+        if (argmax) {
+          if (lane == (k & 31)) {
+            hold = acc;
+            hold_row = orow0 + u + r;
+          }
+          if ((++k & 31) == 0) flush();
+        } else if (lane == 0) {
+          res[pair ? (r < n ? 2 * (cbase + r) : 2 * (cbase + r - n) + 1) : cbase + r] = acc;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&mg_empty[rp.s]);
+      rp.next(ns);
+      u += n;
+    }
+  }
+  if (sy.any(bad)) return false;
+  if (argmax) {
+    flush();
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+      best = t > best ? t : best;
+    }
+    if (lane == 0 && best) atomicMax(a.argmax_key, best);
+    return true;
+  }
+  unsigned long long unused = 0ull;
+  for (int i = tid; i < u1 - u0; i += MG_CT) {
+    const int uu = u0 + i;
+    const GemvSeg &sg = a.seg[seg_of(a, uu)];
+    const int row = uu - sg.unit_begin;
+    if (sg.mode == GM_SILU_MUL) epilogue_pair(a, sg, row, res[2 * i], res[2 * i + 1], e_x, in_f);
+    else epilogue_row(a, sg, row, res[i], e_x, in_f, unused);
+  }
+  return true;
+}
+
+// K = NP * 4096 (the MLP down projection, NP = 3): a stage holds only
+// MEGA_STAGE / stride rows, so each row is split into NP K-parts of 4096 and
+// warp w reduces part w % NP of row w / NP against its x8 slice held in
+// registers.  The partial sums are exact integers; the deferred epilogue adds
+// the NP partials of a row (order-free) before the group-scale law's shift.
+template <int NP>
+F5_DEV bool c_gemv_split(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const Abort &ab) {
+  const CSync sy;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = gridDim.x, b = blockIdx.x, ns = S.ns;
+  prologue<(NP * 4 * 128 + MG_CT - 1) / MG_CT>(sy, a, S.xs(), mg_red, (&mg_r), mg_meta);
+  sy.sync();
+  const int e_x = mg_meta[0], in_f = mg_meta[1];
+  const int part = warp % NP, wrow = warp / NP;   // warps >= NP * (16 / NP) idle
+  uint2 xr[4][4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) xr[c][j] = S.xs()[(((part * 4 + c) << 2) + j) * 32 + lane];
+  const int K2 = a.K >> 1;
+  const int u0 = part_lo(a.total_units, G, b), u1 = part_lo(a.total_units, G, b + 1);
+  bool bad = false;
+  int u = u0;
+  Chunk ch;
+  while (next_chunk(a, u, u1, ch)) {
+    const int s = rp.s;
+    if (mg_abort || !mwait(&mg_full[s], rp.ph, ab)) {
+      mg_abort = 1;
+      bad = true;
+      break;
+    }
+    if (wrow < ch.n && warp < NP * (MG_CONS / NP)) {
+      const uint8_t *row = S.ring() + (size_t)s * MEGA_STAGE + (size_t)wrow * a.stride;
+      long long acc = 0;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int boff = (part * 4 + c) * 512 + lane * 16;
+        const uint4 w = *reinterpret_cast<const uint4 *>(row + boff);
+        const uint32_t m = *reinterpret_cast<const uint16_t *>(row + K2 + 2 * (boff >> 6));
+        acc += (long long)m * dot32(w, xr[c][0], xr[c][1], xr[c][2], xr[c][3]);
+      }
+      acc = warp_sum_row(acc);
+      if (lane == 0) S.res()[NP * (ch.u - u0 + wrow) + part] = acc;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&mg_empty[s]);
+    rp.next(ns);
+  }
+  if (sy.any(bad)) return false;
+  unsigned long long best = 0ull;
+  for (int i = tid; i < u1 - u0; i += MG_CT) {
+    const int uu = u0 + i;
+    const GemvSeg &sg = a.seg[seg_of(a, uu)];
+    long long acc = 0;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) acc += S.res()[NP * i + p];
+    epilogue_row(a, sg, uu - sg.unit_begin, acc, e_x, in_f, best);
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// consumers: DeltaNet head (ref/layer_fixed.py:1493-1580)
+// ---------------------------------------------------------------------------
+F5_DEV bool c_dn(const MegaArgs &ma, const DnArgs &d, const MegaSmem &S, int &w_sd, const Abort &ab) {
+  const int h = blockIdx.x;
+  if (h >= ma.dn_heads) return true;
+  const CSync sy;
+  const DnSmem sm = {reinterpret_cast<int16_t *>(S.scr() + DN_SD), reinterpret_cast<int32_t *>(S.scr() + DN_QN),
+                     reinterpret_cast<int32_t *>(S.scr() + DN_KN), reinterpret_cast<long long *>(S.scr() + DN_PART),
+                     mg_red, mg_gate, mg_e};
+  long long qkv[3];
+  dn_head_pre<CSync, 4>(sy, d, h, sm, qkv);
+  const bool got = mwait((&mg_bsd), w_sd & 1, ab);
+  ++w_sd;
+  if (sy.any(!got)) return false;
+  dn_head_rec<CSync, 4>(sy, d, h, sm, qkv);
+  release_scratch(sy, (&mg_bfree));
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// consumers: attention (ref/layer_fixed.py:1383-1449)
+// ---------------------------------------------------------------------------
+// RMSNorm(1+w) over a 256-dim head (ref/layer_fixed.py:1242-1278) then
+// rope_fx on the first `rot` dims (ref/layer_fixed.py:1340-1348), for four
+// heads at once: thread t owns dims e and e+128 (e = t & 127) of head t>>7.
+F5_DEV void norm_rope4(const CSync &sy, long long x0, long long x1, const int32_t *w, const int16_t *cs, int rot,
+                       int16_t *xn, int16_t *out, int nslots, long long *red) {
+  const int t = sy.tid(), hs = t >> 7, e = t & 127, warp = t >> 5, lane = t & 31;
+  const long long ss = warp_sum_ll(x0 * x0 + x1 * x1);
+  if (lane == 0) red[warp] = ss;
+  sy.sync();
+  const long long tot = red[4 * hs] + red[4 * hs + 1] + red[4 * hs + 2] + red[4 * hs + 3];
+  int64_t r;
+  int ee;
+  rsqrt_q((uint64_t)(tot == 0 ? 1 : tot), 2 * QKV_F + 8, r, ee);   // n = 256
+  const long long n0 = clip16(rshr(clip(rshr(x0 * r, 30 - ee), -(1ll << 32), (1ll << 32) - 1) * ((long long)w[e] + (1 << 14)), 14));
+  const long long n1 =
+      clip16(rshr(clip(rshr(x1 * r, 30 - ee), -(1ll << 32), (1ll << 32) - 1) * ((long long)w[e + 128] + (1 << 14)), 14));
+  xn[hs * 256 + e] = (int16_t)n0;
+  xn[hs * 256 + e + 128] = (int16_t)n1;
+  sy.sync();
+  long long o0 = n0;
+  if (e < rot) {   // rot <= 128: dims e + 128 are never rotated
+    const int hh = rot >> 1;
+    const long long rr = e < hh ? -(long long)xn[hs * 256 + e + hh] : (long long)xn[hs * 256 + e - hh];
+    o0 = clip16(rshr(n0 * cs[e] + rr * cs[64 + e], ROPE_F));
+  }
+  if (hs < nslots) {
+    out[hs * 256 + e] = (int16_t)o0;
+    out[hs * 256 + e + 128] = (int16_t)n1;
+  }
+  sy.sync();
+}
+
+F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int T, int pos, int &w_sk, int &w_sv,
+                   const Abort &ab) {
+  const AttnArgs &a = m.a;
+  const AttGeo g = att_geo(a, T, pos, gridDim.x, blockIdx.x);
+  if (g.kv >= a.nkv) return true;
+  const CSync sy;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, hs = tid >> 7, e = tid & 127;
+  const int hq = g.kv * 4 + hs;
+  const int cm = a.chunk_max;
+  uint8_t *scr = S.scr();
+  int16_t *q16 = reinterpret_cast<int16_t *>(scr + AT_Q16);
+  int16_t *k16n = reinterpret_cast<int16_t *>(scr + AT_K16);
+  int16_t *xn = reinterpret_cast<int16_t *>(scr + AT_XN);
+  int8_t *k8n = reinterpret_cast<int8_t *>(scr + AT_K8N);
+  int8_t *v8n = reinterpret_cast<int8_t *>(scr + AT_V8N);
+  const uint8_t *kbuf = scr + AT_K, *vbuf = scr + AT_V;
+  const int8_t *kebuf = reinterpret_cast<const int8_t *>(scr + AT_KE);
+  const int8_t *vebuf = reinterpret_cast<const int8_t *>(scr + AT_VE);
+  long long *sc = reinterpret_cast<long long *>(scr + AT_SC);
+  long long *red4 = mg_red;   // [16 warps][4 heads]
+  if (!g.ok && blockIdx.x == 0 && tid == 0) atomicOr(a.err, (uint32_t)DERR_KV_FULL);
+  const int16_t *cs = a.rope + (size_t)g.pos * 128;
+  const size_t kvrow = (size_t)g.kv * a.max_T;
+
+  // ---- 1. q / k norm + rope; kv_quant of the new k and v ----
+  norm_rope4(sy, __ldcg(a.qg16 + hq * 512 + e), __ldcg(a.qg16 + hq * 512 + e + 128), a.q_norm, cs, a.rot, xn, q16,
+             4, mg_red);
+  const bool k_act = hs == 0;
+  norm_rope4(sy, k_act ? __ldcg(a.k16 + g.kv * 256 + e) : 0, k_act ? __ldcg(a.k16 + g.kv * 256 + e + 128) : 0,
+             a.k_norm, cs, a.rot, xn, k16n, 1, mg_red);
+  const long long kn0 = k_act ? k16n[e] : 0, kn1 = k_act ? k16n[e + 128] : 0;
+  const long long v0 = k_act ? __ldcg(a.v16 + g.kv * 256 + e) : 0, v1 = k_act ? __ldcg(a.v16 + g.kv * 256 + e + 128) : 0;
+  const unsigned long long mk0 = uabs(kn0) > uabs(kn1) ? uabs(kn0) : uabs(kn1);
+  const unsigned long long mv0 = uabs(v0) > uabs(v1) ? uabs(v0) : uabs(v1);
+  const int ek = dynq8_e(g_max_ull(sy, mk0, reinterpret_cast<unsigned long long *>(mg_red)));
+  const int ev = dynq8_e(g_max_ull(sy, mv0, reinterpret_cast<unsigned long long *>(mg_red)));
+  if (k_act) {
+    const int8_t k0 = (int8_t)dynq8_apply(kn0, ek), k1 = (int8_t)dynq8_apply(kn1, ek);
+    const int8_t w0 = (int8_t)dynq8_apply(v0, ev), w1 = (int8_t)dynq8_apply(v1, ev);
+    k8n[e] = k0; k8n[e + 128] = k1;
+    v8n[e] = w0; v8n[e + 128] = w1;
+    if (g.ok && g.j == 0) {   // append to the cache at slot T (one CTA per KV head)
+      const size_t row = (kvrow + T) * 256;
+      a.k8[row + e] = k0; a.k8[row + e + 128] = k1;
+      a.v8[row + e] = w0; a.v8[row + e + 128] = w1;
+      if (e == 0) {
+        a.ke[kvrow + T] = (int8_t)(ek - QKV_F);
+        a.ve[kvrow + T] = (int8_t)(ev - QKV_F);
+      }
+    }
+  }
+  const int ke_new = ek - QKV_F, ve_new = ev - QKV_F;
+  sy.sync();
+
+  // ---- 2. scores: warp per token, 4 heads at once; lane = 8 dims ----
+  int32_t qr[4][8];
+#pragma unroll
+  for (int h = 0; h < 4; ++h)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qr[h][i] = q16[h * 256 + 8 * lane + i];
+  long long lmax[4] = {LLONG_MIN, LLONG_MIN, LLONG_MIN, LLONG_MIN};
+  const int len = max(0, g.t1 - g.t0);
+  const int nfill = (len + MEGA_SUB - 1) / MEGA_SUB;
+  bool bad = false;
+  for (int si = 0; si < nfill && !bad; ++si) {
+    int sb;
+    const int n_old = att_fill_rows(g, si, sb);
+    const int se = min(sb + MEGA_SUB, g.t1);
+    if (n_old > 0) {
+      if (si > 0) {
+        sy.sync();   // previous fill fully read
+        if (tid == 0) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          att_issue(scr + AT_K, scr + AT_KE, a.k8, a.ke, kvrow + sb, n_old, (&mg_bsk));
+          mg_cnt[4] += 1;
+        }
+      }
+      const bool got = mwait((&mg_bsk), w_sk & 1, ab);
+      ++w_sk;
+      if (sy.any(!got)) { bad = true; break; }
+    }
+    for (int t = sb + warp; t < se; t += MG_CONS) {
+      uint2 kw;
+      int kex;
+      if (t >= g.Told) {   // the new token (t == T)
+        kw = *reinterpret_cast<const uint2 *>(k8n + 8 * lane);
+        kex = ke_new;
+      } else {
+        kw = *reinterpret_cast<const uint2 *>(kbuf + (size_t)(t - sb) * 256 + 8 * lane);
+        kex = kebuf[t - sb];
+      }
+      int dot[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int b0 = (int)(int8_t)((kw.x >> (8 * j)) & 0xFF), b1 = (int)(int8_t)((kw.y >> (8 * j)) & 0xFF);
+#pragma unroll
+        for (int h = 0; h < 4; ++h) dot[h] += qr[h][j] * b0 + qr[h][4 + j] * b1;
+      }
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], o);
+        const long long sv = rshr((long long)dot[h] * 2048, 15);   // SCALE_Q15 = round(2^15/sqrt(256))
+        const long long s = shift_to(sv, QKV_F - kex - 16);
+        lmax[h] = s > lmax[h] ? s : lmax[h];
+        if (lane == h) sc[h * cm + (t - g.t0)] = s;
+      }
+    }
+  }
+  if (sy.any(bad)) return false;
+  if (lane == 0)
+#pragma unroll
+    for (int h = 0; h < 4; ++h) red4[warp * 4 + h] = lmax[h];
+  sy.sync();
+  if (tid < 4 && len > 0) {
+    long long mx = LLONG_MIN;
+    for (int w = 0; w < MG_CONS; ++w) mx = red4[w * 4 + tid] > mx ? red4[w * 4 + tid] : mx;
+    atomicMax(&m.gmax[g.kv * 4 + tid], (unsigned long long)mx ^ (1ull << 63));
+  }
+  if (!counter_barrier(sy, &ma.bars[m.gbar + 2 * g.kv], (unsigned)g.cpg, ab)) return false;
+  if (tid < 4) mg_att[tid] = (long long)(__ldcg(&m.gmax[g.kv * 4 + tid]) ^ (1ull << 63));
+  sy.sync();
+
+  // ---- 3. exp, group sum, reciprocal, probabilities (Q15) ----
+  long long sum[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    const long long mx = mg_att[h];
+    for (int i = tid; i < len; i += MG_CT) {
+      const long long x = sc[h * cm + i] - mx;
+      const long long es = exp_neg_q(x < 0 ? x : 0);
+      sc[h * cm + i] = es;
+      sum[h] += es;
+    }
+    sum[h] = warp_sum_ll(sum[h]);
+  }
+  if (lane == 0)
+#pragma unroll
+    for (int h = 0; h < 4; ++h) red4[warp * 4 + h] = sum[h];
+  sy.sync();
+  if (tid < 4 && len > 0) {
+    long long tot = 0;
+    for (int w = 0; w < MG_CONS; ++w) tot += red4[w * 4 + tid];
+    atomicAdd(&m.gsum[g.kv * 4 + tid], (unsigned long long)tot);
+  }
+  if (!counter_barrier(sy, &ma.bars[m.gbar + 2 * g.kv + 1], (unsigned)g.cpg, ab)) return false;
+  if (tid < 4) {
+    const long long den = (long long)__ldcg(&m.gsum[g.kv * 4 + tid]);
+    int64_t rr;
+    int re;
+    recip_q((uint64_t)(den > 0 ? den : 1), 30, rr, re);
+    mg_att[tid] = rr;
+    mg_att[4 + tid] = 30 - re + 15;
+  }
+  sy.sync();
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    const long long rcp = mg_att[h];
+    const int psh = (int)mg_att[4 + h];
+    for (int i = tid; i < len; i += MG_CT) sc[h * cm + i] = clip(rshr(sc[h * cm + i] * rcp, psh), 0, 1 << 15);
+  }
+  sy.sync();
+
+  // ---- 4. PV: warp = (token phase, head); lane = 8 dims ----
+  const int ph = warp >> 2, hv = warp & 3;
+  int32_t acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int si = 0; si < nfill && !bad; ++si) {
+    int sb;
+    const int n_old = att_fill_rows(g, si, sb);
+    const int se = min(sb + MEGA_SUB, g.t1);
+    if (n_old > 0) {
+      if (si > 0) {
+        sy.sync();
+        if (tid == 0) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          att_issue(scr + AT_V, scr + AT_VE, a.v8, a.ve, kvrow + sb, n_old, (&mg_bsv));
+          mg_cnt[5] += 1;
+        }
+      }
+      const bool got = mwait((&mg_bsv), w_sv & 1, ab);
+      ++w_sv;
+      if (sy.any(!got)) { bad = true; break; }
+    }
+    for (int t = sb + ph; t < se; t += 4) {
+      uint2 vw;
+      int vex;
+      if (t >= g.Told) {
+        vw = *reinterpret_cast<const uint2 *>(v8n + 8 * lane);
+        vex = ve_new;
+      } else {
+        vw = *reinterpret_cast<const uint2 *>(vbuf + (size_t)(t - sb) * 256 + 8 * lane);
+        vex = vebuf[t - sb];
+      }
+      const int32_t p = (int32_t)sc[hv * cm + (t - g.t0)];
+      const int sh = 15 - vex - QKV_F;   // in [6, 15]
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[j] += rshr32p(p * (int32_t)(int8_t)((vw.x >> (8 * j)) & 0xFF), sh);
+        acc[4 + j] += rshr32p(p * (int32_t)(int8_t)((vw.y >> (8 * j)) & 0xFF), sh);
+      }
+    }
+  }
+  if (bad) return false;
+  int32_t *pv = reinterpret_cast<int32_t *>(scr + AT_K);   // [4 phases][4 heads][256]; K rows are done
+  sy.sync();
+#pragma unroll
+  for (int j = 0; j < 8; ++j) pv[(ph * 4 + hv) * 256 + 8 * lane + j] = acc[j];
+  sy.sync();
+  if (len > 0) {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int idx = tid + k * MG_CT, h = idx >> 8, dd = idx & 255;
+      const int32_t s = pv[h * 256 + dd] + pv[(4 + h) * 256 + dd] + pv[(8 + h) * 256 + dd] + pv[(12 + h) * 256 + dd];
+      if (s) atomicAdd(&m.gacc[(g.kv * 4 + h) * 256 + dd], s);
+    }
+  }
+  release_scratch(sy, (&mg_bfree));
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+F5_DEV void c_begin(const MegaArgs &ma, const MegaBegin &B, int tok) {
+  const int tid = threadIdx.x, G = gridDim.x, b = blockIdx.x;
+  if (tok < 0 || tok >= B.vocab) {
+    if (b == 0 && tid == 0) atomicOr(ma.err, DERR_RANGE);
+    tok = 0;
+  }
+  const uint4 *src = reinterpret_cast<const uint4 *>(B.emb + (size_t)tok * B.H);
+  uint4 *dst = reinterpret_cast<uint4 *>(B.x16);
+  for (int i = b * MG_CT + tid; i < B.H / 8; i += G * MG_CT) dst[i] = src[i];
+  for (int i = b * MG_CT + tid; i < B.zero_n; i += G * MG_CT) B.zero[i] = make_uint4(0, 0, 0, 0);
+  if (b == 0 && tid == 0) *B.key = 0ull;
+}
+
+// descriptor of op `oi` into cop[oi & 1]: cp.async by the first threads,
+// completed (cp.async.wait_all) before the next group barrier publishes it
+constexpr int MG_DESC_V4 = (int)(sizeof(MegaOp) / 16);
+static_assert(MG_DESC_V4 <= MG_CT, "descriptor copy: one 16-byte piece per thread");
+F5_DEV void stage_desc(const MegaArgs &ma, const MegaSmem &S, int oi) {
+  const int t = threadIdx.x;
+  if (t < MG_DESC_V4) {
+    const uint32_t dst = smem_u32(reinterpret_cast<uint4 *>(&mg_cop[oi & 1]) + t);
+    const uint4 *src = reinterpret_cast<const uint4 *>(ma.ops + oi) + t;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+}
+F5_DEV void stage_wait() {
+  if (threadIdx.x < MG_DESC_V4) asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+F5_DEV void consumers(const MegaArgs &ma, const MegaSmem &S, int tok, int T, int pos, const Abort &ab) {
+  const CSync sy;
+  RingPos rp;
+  int w_sd = 0, w_sk = 0, w_sv = 0;
+  unsigned long long *tr = ma.trace ? ma.trace + (size_t)blockIdx.x * ma.nops * 2 : nullptr;
+  stage_desc(ma, S, 0);
+  stage_wait();
+  sy.sync();
+  for (int oi = 0; oi < ma.nops; ++oi) {
+    // Op oi waits for op oi-1 on every CTA (grid barrier oi-1: the emitter
+    // numbers them so).  The barrier's entry sync also publishes the staged
+    // descriptor and retires every reader of the buffer staged next.
+    if (oi > 0) {
+      stage_wait();
+      if (!counter_barrier(sy, &ma.bars[oi - 1], gridDim.x, ab)) return;
+    }
+    if (oi + 1 < ma.nops) stage_desc(ma, S, oi + 1);
+    const MegaOp &op = mg_cop[oi & 1];
+    if (tr && threadIdx.x == 0) tr[2 * oi] = gtimer();
+    bool ok = true;
+    switch (op.kind) {
+      case MK_BEGIN: c_begin(ma, op.b, tok); break;
+      case MK_GEMV: ok = op.g.K > 4096 ? c_gemv_split<3>(op.g, S, rp, ab) : c_gemv4096(op.g, S, rp, ab); break;
+      case MK_DN: ok = c_dn(ma, op.d, S, w_sd, ab); break;
+      case MK_ATTN: ok = c_attn(ma, op.at, S, T, pos, w_sk, w_sv, ab); break;
+      default: break;
+    }
+    if (tr && threadIdx.x == 0) tr[2 * oi + 1] = gtimer();
+    if (!ok) {
+      stage_wait();
+      return;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega(const __grid_constant__ MegaArgs ma) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ns = ma.ns;
+  MegaSmem S;
+  S.ns = ns;
+  const Abort ab = {ma.bars + ma.nbars - 2, ma.err};
+
+  if (tid == 0) {
+    for (int i = 0; i < ns; ++i) {
+      mbar_init(&mg_full[i], 1);
+      mbar_init(&mg_empty[i], MG_CONS);
+    }
+    mbar_init(&mg_bsd, 1);
+    mbar_init(&mg_bsk, 1);
+    mbar_init(&mg_bsv, 1);
+    mbar_init(&mg_bfree, 1);
+    mbar_init(&mg_bpd[0], 1);
+    mbar_init(&mg_bpd[1], 1);
+    for (int i = 0; i < 6; ++i) mg_cnt[i] = 0;
+    mg_abort = 0;
+    mg_last = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // step parameters: written by the host or by the previous launch only
+  const volatile StepParams *vp = ma.params;
+  const int tok = vp->tok, T = vp->T, pos = vp->pos;
+  __syncthreads();
+
+  if (warp == MG_CONS) {
+    if (lane == 0) producer(ma, S, T, pos, ab);
+  } else {
+    consumers(ma, S, tok, T, pos, ab);
+  }
+  __syncwarp();   // reconverge each warp (the producer lane joins its warp) before the CTA barrier
+  __syncthreads();
+
+  if (tid == 0) {
+    // never exit with a bulk copy in flight: wait (bounded) for the last
+    // issued phase of every barrier; a completed phase returns at once
+    const int issued = mg_cnt[0];
+    for (int s = 0; s < ns && s < issued; ++s) {
+      const int last = issued - 1 - ((issued - 1 - s) % ns);   // last chunk that used stage s
+      mbar_wait(&mg_full[s], (last / ns) & 1, MG_WAIT_NS);
+    }
+    if (mg_cnt[1]) mbar_wait(&mg_bsd, (mg_cnt[1] - 1) & 1, MG_WAIT_NS);
+    const int nk = mg_cnt[2] + mg_cnt[4], nv = mg_cnt[3] + mg_cnt[5];
+    if (nk) mbar_wait(&mg_bsk, (nk - 1) & 1, MG_WAIT_NS);
+    if (nv) mbar_wait(&mg_bsv, (nv - 1) & 1, MG_WAIT_NS);
+    __threadfence();
+    mg_last = atomicAdd(&ma.bars[ma.nbars - 1], 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!mg_last) return;
+  __threadfence();
+  if (tid == 0) {
+    // step end (ref/gen_model_script.py:641 argmax, first max wins)
+    StepParams *p = ma.params;
+    const unsigned long long k = __ldcg(ma.ops[ma.nops - 1].g.argmax_key);
+    const bool aborted = __ldcg(ma.bars + ma.nbars - 2) != 0;
+    const int row = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+    p->next_tok = row;
+    p->max_val = (int)((uint32_t)(k >> 32) ^ 0x80000000u);
+    p->err |= __ldcg(ma.err);
+    if (ma.advance && !aborted) {
+      p->tok = row;
+      p->pos += 1;
+      p->T += 1;
+      p->steps += 1;
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < ma.nbars; i += MEGA_THREADS) ma.bars[i] = 0u;
+}
+
+static size_t mega_smem_bytes(int ns, int chunk_max) {
+  size_t scr = (size_t)AT_SC + (size_t)4 * chunk_max * 8;
+  if (scr < (size_t)DN_END) scr = DN_END;
+  return (size_t)ns * MEGA_STAGE + MG_XS + MG_RESB + scr;
+}
+
+cudaError_t mega_config(int chunk_max, int *grid, size_t *smem, int *ns) {
+  int dev = 0, sms = 0, optin = 0, coop = 0;
+  cudaError_t e;
+  if ((e = cudaGetDevice(&dev))) return e;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev))) return e;
+  if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev))) return e;
+  if ((e = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev))) return e;
+  if (!coop) return cudaErrorNotSupported;
+  cudaFuncAttributes fa;
+  if ((e = cudaFuncGetAttributes(&fa, k_mega))) return e;
+  int n = MG_NS_MAX;
+  while (n >= 3 && mega_smem_bytes(n, chunk_max) + fa.sharedSizeBytes > (size_t)optin) --n;
+  if (n < 3) return cudaErrorInvalidValue;
+  const size_t bytes = mega_smem_bytes(n, chunk_max);
+  if ((e = cudaFuncSetAttribute(k_mega, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes))) return e;
+  int per_sm = 0;
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_mega, MEGA_THREADS, bytes))) return e;
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  *grid = sms;   // one CTA per SM (the kernel is written for exactly one)
+  *smem = bytes;
+  *ns = n;
+  return cudaSuccess;
+}
+
+cudaError_t launch_mega(const MegaArgs &a, int grid, size_t smem, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(MEGA_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_mega, a);
+}
+
+}  // namespace f5

@@ -1,0 +1,81 @@
+// Persistent decode-step kernel: the whole 9B decode step (embedding row,
+// every layer's GEMVs, DeltaNet and attention cores, the LM head and its
+// argmax) as ONE cooperative launch over all SMs.  See f5_mega.cu.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "f5_attn.cuh"
+#include "f5_dn.cuh"
+#include "f5_kernels.cuh"
+
+namespace f5 {
+
+enum MegaKind : int {
+  MK_BEGIN = 0,   // x16 = emb[tok]; clear the argmax key and the attention sums
+  MK_GEMV = 1,    // one fused GEMV (same descriptor as k_gemv)
+  MK_DN = 2,      // Gated-DeltaNet core, one value head per CTA
+  MK_ATTN = 3,    // attention core, kv head x token chunk per CTA
+};
+
+struct MegaBegin {
+  const int16_t *emb;         // [vocab][H]
+  int16_t *x16;               // [H]
+  int vocab, H;
+  unsigned long long *key;    // LM-head argmax key
+  uint4 *zero;                // attention accumulators, cleared every step
+  int zero_n;                 // in uint4
+};
+
+struct MegaAttn {
+  AttnArgs a;                 // same operands as the per-op attention kernel
+  unsigned long long *gmax;   // [nq] order-preserving keys of the score max
+  unsigned long long *gsum;   // [nq] sums of exp
+  int32_t *gacc;              // [nq * HD] PV sums
+  int gbar;                   // first of 2 * nkv group counters
+};
+
+// 16-byte aligned and sized: the kernel stages each descriptor in shared
+// memory (bulk copy for the producer, vector loads for the consumers)
+struct alignas(16) MegaOp {
+  int kind;
+  int bar;         // grid-barrier counter taken before the op (-1: none)
+  int pad[2];
+  union {
+    GemvArgs g;
+    DnArgs d;
+    MegaAttn at;
+    MegaBegin b;
+  };
+};
+static_assert(sizeof(MegaOp) % 16 == 0, "MegaOp is copied in 16-byte units");
+
+struct MegaArgs {
+  const MegaOp *ops;
+  int nops;
+  StepParams *params;
+  unsigned *bars;   // [nbars] counters, zero at launch and zero again at exit
+  int nbars;        // bars[nbars-2]: abort flag, bars[nbars-1]: final arrivals
+  uint32_t *err;
+  int advance;      // feed the argmax back as the next token (greedy loop)
+  int dn_heads;     // CTAs [0, dn_heads) run one DeltaNet value head each
+  int ns;           // ring stages (from mega_config)
+  unsigned long long *trace;   // optional [G][nops][2] globaltimer at each op's start / end
+};
+
+constexpr int MEGA_THREADS = 544;       // 16 consumer warps + 1 producer warp
+constexpr int MEGA_STAGE = 33792;       // ring stage: 16 rows of K=4096, 5 of K=12288
+constexpr int MEGA_RES = 256;           // deferred per-CTA row results
+constexpr int MEGA_SUB = 64;            // attention tokens per K/V shared-memory fill
+
+// Rows of one ring stage for a packed row stride.
+inline int mega_rows_per_stage(int stride) {
+  int r = MEGA_STAGE / stride;
+  return r > 16 ? 16 : r;
+}
+// Grid (one CTA per SM) and dynamic shared memory of the persistent kernel
+// for a given attention token chunk bound; error if it cannot be resident.
+cudaError_t mega_config(int chunk_max, int *grid, size_t *smem, int *ns);
+cudaError_t launch_mega(const MegaArgs &a, int grid, size_t smem, cudaStream_t st);
+
+}  // namespace f5

@@ -166,6 +166,36 @@ class DecodeModel:
     def prepare(self):
         L.check(self.lib.f5_ctx_prepare(self.h), "prepare")
 
+    def set_engine(self, engine):
+        """"persistent" (one cooperative launch per step) or "graph" (the
+        per-op kernel chain as a CUDA graph); both are bit-exact."""
+        code = {"graph": L.ENGINE_GRAPH, "persistent": L.ENGINE_PERSISTENT}[engine]
+        L.check(self.lib.f5_ctx_set_engine(self.h, code), "set_engine")
+
+    def trace_step(self):
+        """One persistent greedy step with per-op device timestamps ->
+        (ns int64[grid, nops, 2] start/end relative to the earliest start,
+        op kinds list).  Caches advance by one token."""
+        grid, nops = ctypes.c_int(), ctypes.c_int()
+        L.check(self.lib.f5_ctx_trace_step(self.h, None, 0, ctypes.byref(grid), ctypes.byref(nops)), "trace")
+        out = np.zeros(grid.value * nops.value * 2, dtype=np.uint64)
+        L.check(self.lib.f5_ctx_trace_step(self.h, _p(out), out.size, ctypes.byref(grid), ctypes.byref(nops)),
+                "trace")
+        t = out.astype(np.int64).reshape(grid.value, nops.value, 2)
+        t -= t[:, 0, 0].min()
+        kinds = ["begin"]
+        for lt in self.geom.layer_types:
+            core = "attn" if lt == "full_attention" else "dn"
+            kinds += [f"{core}_in", core, f"{core}_out", "mlp_gate_up", "mlp_down"]
+        kinds.append("head")
+        assert len(kinds) == nops.value
+        return t, kinds
+
+    def engine(self):
+        e = ctypes.c_int()
+        L.check(self.lib.f5_ctx_get_engine(self.h, ctypes.byref(e)), "get_engine")
+        return {L.ENGINE_GRAPH: "graph", L.ENGINE_PERSISTENT: "persistent"}[e.value]
+
     # ---- steps ----
     def decode_step(self, tok, pos):
         """One model step (FxRunner.step + argmax) -> (next token, its y32)."""

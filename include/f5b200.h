@@ -218,6 +218,24 @@ int f5_ctx_stream(f5_ctx *ctx, void **stream);
 /* record the decode-step CUDA graph now (otherwise at the first step) */
 int f5_ctx_prepare(f5_ctx *ctx);
 
+/* Decode engines (no reference counterpart: the reference has one sequencer).
+ * F5_ENGINE_PERSISTENT runs each step as ONE cooperative launch of the
+ * persistent decode kernel (one CTA per SM, weights streamed continuously
+ * across op boundaries); F5_ENGINE_GRAPH replays the per-op kernel chain as a
+ * CUDA graph.  Both compute the same integer law bit-exactly.  Default: the
+ * persistent engine when the device can hold it resident, else the graph. */
+enum f5_engine { F5_ENGINE_GRAPH = 0, F5_ENGINE_PERSISTENT = 1 };
+int f5_ctx_set_engine(f5_ctx *ctx, int engine);
+/* the engine the next step uses (builds its program if needed) */
+int f5_ctx_get_engine(f5_ctx *ctx, int *engine);
+
+/* Timeline of one persistent step (no reference counterpart: profiling aid).
+ * Runs one greedy step (caches advance) with every CTA recording the device
+ * globaltimer (ns) at the start (after its grid barrier) and end of each op:
+ * out[(cta * nops + op) * 2 + {0, 1}].  With out == NULL only *grid and *nops
+ * are returned; otherwise cap must be >= grid * nops * 2. */
+int f5_ctx_trace_step(f5_ctx *ctx, uint64_t *out, size_t cap, int *grid, int *nops);
+
 /* One full model step from a host token id: embedding row, every layer,
  * final RMSNorm, DYNQ8, LM head, argmax (first max wins).  Replaces
  * ref/fidelity_check.py:423-448 FxRunner.step and the token loop of

@@ -28,6 +28,13 @@ def model4():
     return m
 
 
+@pytest.fixture(params=["persistent", "graph"])
+def engine(request):
+    """Both decode engines (one persistent cooperative launch per step, or
+    the per-op kernel chain as a CUDA graph) must be bit-exact."""
+    return request.param
+
+
 @pytest.fixture(scope="module")
 def model4_eps():
     m = DecodeModel(Geometry(4, 4096), max_T=128, norm_mode="eps")
@@ -68,12 +75,17 @@ def test_attn_layer_vs_reference(golden, model4):
             assert kv["v"][t][h][1] == d["attn_ve"][t][h]
 
 
-def test_model4_vs_reference(golden, model4):
+def test_default_engine_is_persistent(model4):
+    assert model4.engine() == "persistent"
+
+
+def test_model4_vs_reference(golden, model4, engine):
     """The reduced model (3 DeltaNet + 1 attention layer, 4096-row head):
     every emitted token, max logit and the final residual equal the
     reference's FxRunner-sequence run."""
     d = golden("ref_model4")
     m = model4
+    m.set_engine(engine)
     m.reset()
     for t, tok in enumerate(d["m4_in"]):
         nt, mv = m.decode_step(int(tok), t)
@@ -99,8 +111,9 @@ def _compare_states(m, r, T):
 
 
 @pytest.mark.parametrize("mode", ["float", "eps"])
-def test_model4_vs_oracle_logits_and_state(model4, model4_eps, mode):
+def test_model4_vs_oracle_logits_and_state(model4, model4_eps, mode, engine):
     m = model4 if mode == "float" else model4_eps
+    m.set_engine(engine)
     m.reset()
     m.set_logits(True)
     g = m.geom
@@ -115,9 +128,10 @@ def test_model4_vs_oracle_logits_and_state(model4, model4_eps, mode):
     m.set_logits(False)
 
 
-def test_greedy_device_loop_matches_host_steps(model4):
+def test_greedy_device_loop_matches_host_steps(model4, engine):
     """f5_decode_launch (tokens fed back on the device) == host-fed steps."""
     m = model4
+    m.set_engine(engine)
     m.reset()
     toks, tok = [], 17
     for t in range(6):
@@ -145,12 +159,13 @@ def test_state_save_load_roundtrip(model4, tmp_path):
     assert m.decode_step(tok, 5) == ref_next
 
 
-def test_attention_long_context_vs_oracle(model4):
+def test_attention_long_context_vs_oracle(model4, engine):
     """Context 2048: the GPU fills the caches (bit-exact step by step), the
     oracle loads that state and both decode further steps."""
     m = model4
     T = 2048
     big = DecodeModel(Geometry(4, 4096), max_T=T + 8)
+    big.set_engine(engine)
     big.load_synthetic(SEED)
     big.reset()
     rng = np.random.default_rng(7)
@@ -182,21 +197,72 @@ def test_attention_long_context_vs_oracle(model4):
     del m
 
 
+@pytest.mark.parametrize("T0", [4990, 6100])
+def test_attention_random_cache_multi_fill_vs_oracle(T0):
+    """Random int8 K/V caches at context ~5k-6k: each persistent CTA's token
+    chunk spans several 64-row shared-memory fills; both engines and the
+    oracle decode from the same state."""
+    geom = Geometry(4, 4096)
+    rng = np.random.default_rng(T0)
+    big = DecodeModel(geom, max_T=6144)
+    big.load_synthetic(SEED)
+    r = O.OracleRunner(OracleModel(SEED, O.Geometry(4, 4096)), max_T=big.max_T)
+    for i, lt in enumerate(geom.layer_types):
+        if lt == "full_attention":
+            c = r.caches[i]
+            c.k8[...] = rng.integers(-127, 128, c.k8.shape)
+            c.v8[...] = rng.integers(-127, 128, c.v8.shape)
+            c.ke[...] = rng.integers(-8, 1, c.ke.shape)
+            c.ve[...] = rng.integers(-8, 1, c.ve.shape)
+            c.T = T0
+    outs = {}
+    for eng in ("persistent", "graph"):
+        big.set_engine(eng)
+        big.reset()
+        for i, lt in enumerate(geom.layer_types):
+            if lt == "full_attention":
+                c = r.caches[i]
+                for nm, buf in (("k8", L.BUF_K8), ("ke", L.BUF_KE), ("v8", L.BUF_V8), ("ve", L.BUF_VE)):
+                    big.write(buf, i, np.ascontiguousarray(getattr(c, nm), dtype=np.int8))
+        big.set_position(T0, T0)
+        big.set_logits(True)
+        res = []
+        tok = 321
+        for t in range(T0, T0 + 2):
+            nt, _ = big.decode_step(tok, t)
+            res.append((nt, big.logits().copy()))
+            tok = nt
+        outs[eng] = res
+    tok = 321
+    for k, t in enumerate(range(T0, T0 + 2)):
+        ref_tok, y = r.step(tok, t)
+        for eng in outs:
+            assert np.array_equal(outs[eng][k][1], y), f"{eng} step {t}"
+            assert outs[eng][k][0] == ref_tok
+        tok = ref_tok
+    big.close()
+
+
 @pytest.mark.slow
 def test_full_9b_vs_oracle():
     """The full 32-layer 9B model with the 248,320-row head: tokens, logits
-    and every layer's state after several steps."""
+    and every layer's state after several steps, in both engines."""
     m = DecodeModel(Geometry(), max_T=64)
     m.load_synthetic(SEED)
-    m.reset()
     m.set_logits(True)
     r = O.OracleRunner(OracleModel(SEED, O.GEOM_9B), max_T=64)
+    ref = []
     tok = 1234
     for t in range(3):
-        nt, mv = m.decode_step(tok, t)
         ref_tok, y = r.step(tok, t)
-        assert np.array_equal(m.logits(), y), f"step {t}"
-        assert nt == ref_tok and mv == int(y.max())
-        tok = nt
-    _compare_states(m, r, 3)
+        ref.append((tok, ref_tok, y))
+        tok = ref_tok
+    for eng in ("persistent", "graph"):
+        m.set_engine(eng)
+        m.reset()
+        for t, (tok, ref_tok, y) in enumerate(ref):
+            nt, mv = m.decode_step(tok, t)
+            assert np.array_equal(m.logits(), y), f"{eng} step {t}"
+            assert nt == ref_tok and mv == int(y.max())
+        _compare_states(m, r, 3)
     m.close()
