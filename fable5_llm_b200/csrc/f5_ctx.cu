@@ -118,6 +118,8 @@ struct f5_ctx {
   // activations
   int16_t *x16 = nullptr, *qkv16 = nullptr, *z16 = nullptr, *b16 = nullptr, *a16 = nullptr;
   int16_t *on16 = nullptr, *qg16 = nullptr, *k16 = nullptr, *v16 = nullptr, *prod16 = nullptr;
+  int16_t *qkvc16 = nullptr;   // post-conv q | k | v of a DeltaNet layer
+  int32_t *gates = nullptr;    // [2][LNH] beta | decay of a DeltaNet layer
   int64_t *prod64 = nullptr;
   int8_t *x8 = nullptr;
   int *xmeta = nullptr;
@@ -323,8 +325,9 @@ static cudaError_t gemv(f5_ctx *c, const GemvSeg *segs, int nseg, int K, const G
   return e;
 }
 
-// per attention layer: NQ score-max keys, NQ exp sums (u64), NQ*HD PV sums (i32)
-constexpr size_t ATT_ACC_BYTES = NQ * 8 + NQ * 8 + NQ * HD * 4;
+// per attention layer of the persistent program: marked exchange slots
+// [2 phases][NKV][cpg][4 heads][2 words] (u64) and the PV sums [NQ*HD] (i32)
+static size_t att_acc_bytes(int cpg) { return (size_t)2 * NKV * cpg * 4 * 2 * 8 + (size_t)NQ * HD * 4; }
 static size_t n_attn_layers(const f5_ctx *c) {
   size_t n = 0;
   for (const Layer &l : c->L) n += l.attn ? 1 : 0;
@@ -342,14 +345,22 @@ static cudaError_t enqueue_layer(f5_ctx *c, int li, bool pdl) {
   pro.in_f = RS_F;
   pro.one_plus = 1;
   if (!l.attn) {
-    // in-projection: qkv16 (Q.RS_F), z16 (Q.QKV_F), b, a (Q12), ref/layer_fixed.py:1503-1509
-    GemvSeg s[4] = {mkseg(l.m[0], c->qkv16, GM_TO16, RS_F), mkseg(l.m[1], c->z16, GM_TO16, QKV_F),
-                    mkseg(l.m[2], c->b16, GM_TO16, 12), mkseg(l.m[3], c->a16, GM_TO16, 12)};
+    // in-projection: qkv16 (Q.RS_F), z16 (Q.QKV_F), b, a (Q12), ref/layer_fixed.py:1503-1509,
+    // with conv4+SiLU per channel and the two gates per head in the epilogues
+    GemvSeg s[4] = {mkseg(l.m[0], c->qkv16, GM_CONV, RS_F), mkseg(l.m[1], c->z16, GM_TO16, QKV_F),
+                    mkseg(l.m[2], c->b16, GM_GATE_B, 12), mkseg(l.m[3], c->a16, GM_GATE_A, 12)};
+    s[0].aux_out = c->qkvc16;
+    s[0].aux0 = l.conv;
+    s[0].aux1 = l.conv_w;
+    s[0].T = &c->params->T;
+    s[2].aux_out = c->gates;
+    s[3].aux_out = c->gates + LNH;
+    s[3].aux0 = l.dt_bias;
+    s[3].aux1 = l.A;
     if ((e = gemv(c, s, 4, H, pro, nullptr, pdl))) return e;
     DnArgs d = {};
-    d.qkv16 = c->qkv16; d.z16 = c->z16; d.b16 = c->b16; d.a16 = c->a16;
-    d.conv = l.conv; d.conv_w = l.conv_w; d.dt_bias = l.dt_bias; d.A = l.A; d.norm_w = l.norm_w;
-    d.S = l.S; d.on16 = c->on16; d.T = &c->params->T; d.kh_out = l.kh; d.stats = c->stats; d.err = c->err;
+    d.qkvc = c->qkvc16; d.beta = c->gates; d.decay = c->gates + LNH; d.z16 = c->z16; d.norm_w = l.norm_w;
+    d.S = l.S; d.on16 = c->on16; d.kh_out = l.kh; d.stats = c->stats; d.err = c->err;
     d.lkd = LKD; d.vrep = LNH / LNKH; d.norm_mode = c->cfg.norm_mode;
     if (c->emit) {
       MegaOp op = {};
@@ -386,15 +397,13 @@ static cudaError_t enqueue_layer(f5_ctx *c, int li, bool pdl) {
       const int n_attn = (int)std::count_if(c->emit->begin(), c->emit->end(),
                                             [](const MegaOp &o) { return o.kind == MK_ATTN; });
       const int cpg = c->mega_grid / NKV;
-      uint8_t *acc = reinterpret_cast<uint8_t *>(c->d_attacc) + (size_t)n_attn * ATT_ACC_BYTES;
+      uint8_t *acc = reinterpret_cast<uint8_t *>(c->d_attacc) + (size_t)n_attn * att_acc_bytes(cpg);
       MegaOp op = {};
       op.kind = MK_ATTN;
       op.at.a = at;
       op.at.a.chunk_max = (((c->cfg.max_T + cpg - 1) / cpg) + 15) & ~15;
-      op.at.gmax = reinterpret_cast<unsigned long long *>(acc);
-      op.at.gsum = reinterpret_cast<unsigned long long *>(acc + NQ * 8);
-      op.at.gacc = reinterpret_cast<int32_t *>(acc + NQ * 16);
-      op.at.gbar = -1;   // assigned after the walk
+      op.at.slots = reinterpret_cast<unsigned long long *>(acc);
+      op.at.gacc = reinterpret_cast<int32_t *>(acc + (size_t)2 * NKV * cpg * 4 * 2 * 8);
       emit_op(c, op);
       p2.mode = PRO_ATTN_ACC;
       p2.src = op.at.gacc;
@@ -436,7 +445,7 @@ static cudaError_t enqueue_step(f5_ctx *c, bool pdl) {
     op.b.H = H;
     op.b.key = c->key;
     op.b.zero = c->d_attacc;
-    op.b.zero_n = (int)(n_attn_layers(c) * ATT_ACC_BYTES / 16);
+    op.b.zero_n = (int)(n_attn_layers(c) * att_acc_bytes(c->mega_grid / NKV) / 16);
     emit_op(c, op);
   } else {
     StepParams *p = c->params;
@@ -550,7 +559,7 @@ static int build_mega(f5_ctx *c, bool &unsupported) {
   const size_t n_attn = n_attn_layers(c);
   if (!c->d_attacc) {
     unsupported = false;
-    F5_ALLOC(c, c->d_attacc, (n_attn ? n_attn : 1) * ATT_ACC_BYTES);
+    F5_ALLOC(c, c->d_attacc, (n_attn ? n_attn : 1) * att_acc_bytes(cpg));
     unsupported = true;
   }
   std::vector<MegaOp> ops;
@@ -560,11 +569,7 @@ static int build_mega(f5_ctx *c, bool &unsupported) {
   c->emit = nullptr;
   if (e != cudaSuccess) return cuda_status(e, "emit persistent program");
   if (c->emit_err) return set_error(F5_ESTATE, "a GEMV of this model does not fit the persistent engine");
-  const int n_grid = (int)ops.size() - 1;
-  int ai = 0;
-  for (MegaOp &op : ops)
-    if (op.kind == MK_ATTN) op.at.gbar = n_grid + 2 * NKV * ai++;
-  const int nbars = n_grid + 2 * NKV * ai + 2;
+  const int nbars = (int)ops.size() - 1 + 2;   // grid barriers, abort flag, final arrivals
   unsupported = false;
   free_mega(c);
   F5_CU(cudaMalloc(&c->d_ops, ops.size() * sizeof(MegaOp)), "persistent program");
@@ -674,6 +679,7 @@ int f5_ctx_create(const f5_config *cfg, int device, f5_ctx **out) {
       (rc = alloc(c, (void **)&c->k16, NKV * HD * 2)) || (rc = alloc(c, (void **)&c->v16, NKV * HD * 2)) ||
       (rc = alloc(c, (void **)&c->prod16, FFN * 2)) || (rc = alloc(c, (void **)&c->prod64, NQ * HD * 8)) ||
       (rc = alloc(c, (void **)&c->x8, FFN)) || (rc = alloc(c, (void **)&c->xmeta, 16)) ||
+      (rc = alloc(c, (void **)&c->qkvc16, CONV_DIM * 2)) || (rc = alloc(c, (void **)&c->gates, 2 * LNH * 4)) ||
       (rc = alloc(c, (void **)&c->key, 8)) || (rc = alloc(c, (void **)&c->stats, 8)) ||
       (rc = alloc(c, (void **)&c->err, 4)) || (rc = alloc(c, (void **)&c->params, sizeof(StepParams))))
     return fail(rc);
@@ -900,7 +906,7 @@ int f5_ctx_trace_step(f5_ctx *c, uint64_t *out, size_t cap, int *grid, int *nops
   if (grid) *grid = c->mega_grid;
   if (nops) *nops = c->margs.nops;
   if (!out) return F5_OK;
-  const size_t n = (size_t)c->mega_grid * c->margs.nops * 2;
+  const size_t n = (size_t)c->mega_grid * c->margs.nops * MEGA_TRACE_SLOTS;
   if (cap < n) return set_error(F5_EINVAL, "f5_ctx_trace_step: %zu slots, need %zu", cap, n);
   unsigned long long *d = nullptr;
   F5_CU(cudaMalloc(&d, n * 8), "trace buffer");

@@ -3,12 +3,11 @@
 // GEMV (qkv16 / z16 / b / a) and the out-projection GEMV.
 //
 // One CTA per value head h (32 CTAs x 128 threads; thread t owns state
-// column dv = t).  Per CTA:
-//   conv4 + SiLU of the 384 channels the head reads (q, k of key head h/2,
-//   v of head h), with the conv window kept as a 4-slot ring in HBM (slot
-//   T%4 receives this step's input; the other three, oldest first, are the
-//   reference's conv state) -- no two CTAs read a slot another writes;
-//   gates beta / decay; l2norm of q and k; the recurrence on the int16
+// column dv = t).  The in-projection GEMV's epilogues already applied
+// conv4 + SiLU per channel (the conv window is a 4-slot ring in HBM: slot T%4
+// receives this step's input, the other three, oldest first, are the
+// reference's conv state) and the gates beta / decay.  Per CTA:
+//   l2norm of q and k; the recurrence on the int16
 //   128x128 state (decay, kv_mem, delta, rank-1 update, clip16, o), staged
 //   through shared memory; block-float shift k_h; the gated RMSNorm (float64
 //   host-scale law or the integer EPS-NORM law) x norm_w x silu(z); output
@@ -44,8 +43,8 @@ __global__ void __launch_bounds__(DN_THREADS) k_dn_step(const __grid_constant__ 
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const DnSmem sm = {s_sd, s_qn, s_kn, nullptr, red, s_gate, s_e};
   const BlockSync sy;
-  long long qkv[3];
-  dn_head_pre<BlockSync, 1>(sy, a, h, sm, qkv);
+  long long qkv[3], zn[2];
+  dn_head_pre<BlockSync, 1>(sy, a, h, sm, qkv, zn);
   const bool got = mbar_wait(&bar_s, 0, 2000000000ull);
   if (sy.any(!got)) {
     // the state never arrived: flag it, leave S untouched, emit zeros (the
@@ -55,7 +54,7 @@ __global__ void __launch_bounds__(DN_THREADS) k_dn_step(const __grid_constant__ 
     if (!got) mbar_wait(&bar_s, 0, 2000000000ull);
     return;
   }
-  dn_head_rec<BlockSync, 1>(sy, a, h, sm, qkv);
+  dn_head_rec<BlockSync, 1>(sy, a, h, sm, qkv, zn);
 }
 
 cudaError_t launch_dn_step(const DnArgs &a, int nheads, cudaStream_t st, bool pdl) {

@@ -5,19 +5,17 @@
 
 namespace f5 {
 
+// The in-projection GEMV's epilogues have already applied conv4+SiLU per
+// channel (GM_CONV: post-conv q|k|v, conv ring advanced) and the per-head
+// gates (GM_GATE_B / GM_GATE_A), so the step starts at the l2norms.
 struct DnArgs {
-  const int16_t *qkv16;   // [CONV_DIM] pre-conv in_qkv output (clip16, Q.RS_F)
+  const int16_t *qkvc;    // [CONV_DIM] post-conv q | k | v (Q.QKV_F)
+  const int32_t *beta;    // [LNH] sigmoid(b) (Q15)
+  const int32_t *decay;   // [LNH] exp(g) (Q15)
   const int16_t *z16;     // [LVD] (Q.QKV_F)
-  const int16_t *b16;     // [LNH] (Q12)
-  const int16_t *a16;     // [LNH] (Q12)
-  int16_t *conv;          // [CONV_DIM][4] ring of pre-conv inputs
-  const int32_t *conv_w;  // [CONV_DIM][4] (Q.CW_F)
-  const int32_t *dt_bias; // [LNH] (Q12)
-  const int32_t *A;       // [LNH] (Q15, port-saturated)
   const int32_t *norm_w;  // [LDV] (Q14)
   int16_t *S;             // [LNH][LDK][LDV] int16 state (Q.S_F)
   int16_t *on16;          // [LVD] out: clip16(on), Q.DN_NORM_F
-  const int *T;           // tokens already in the window (ring slot = T % 4)
   int *kh_out;            // optional [LNH] block-float shifts k_h
   unsigned long long *stats;  // optional: state saturation count
   uint32_t *err;          // device error word (DERR_TIMEOUT)

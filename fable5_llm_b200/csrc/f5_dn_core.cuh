@@ -1,6 +1,6 @@
 // Device core of the Gated-DeltaNet decode step for one value head
-// (ref/layer_fixed.py:1493-1580), shared by the per-op kernel k_dn_step and
-// the persistent decode kernel.  A group of NQ*128 threads runs one head:
+// (ref/layer_fixed.py:1522-1580, after the in-projection epilogues' conv and
+// gates), shared by the per-op kernel k_dn_step and the persistent kernel.  A group of NQ*128 threads runs one head:
 // thread t owns value column dv = t & 127 and, in the recurrence, the state
 // rows dk in quarter q = t >> 7 (NQ = 1: all 128 rows).  Integer sums are
 // order-free, so splitting the dk reductions across threads is exact.
@@ -23,40 +23,28 @@ struct DnSmem {
   int *e;           // [2]
 };
 
-// conv4 + SiLU, gates, l2norm of q and k, conv-window ring update
-// (ref/layer_fixed.py:1511-1543).  Needs the in-projection outputs; does not
-// touch the state.  qkv[] holds this column's q, k, v (valid for q == 0).
+// Inputs of the head and the l2norms of q and k (ref/layer_fixed.py:
+// 1522-1543).  Conv4+SiLU and the gates were applied by the in-projection's
+// epilogues, so every input is issued in one round of loads: post-conv q, k
+// (key head h / vrep) and v, z, norm_w, beta, decay.  qkv[] / zn[] hold this
+// column's q, k, v and z, norm_w (valid for q == 0).
 template <class SY, int NQ>
-F5_DEV void dn_head_pre(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, long long (&qkv)[3]) {
+F5_DEV void dn_head_pre(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, long long (&qkv)[3],
+                        long long (&zn)[2]) {
   const int t = sy.tid(), dv = t & 127, q = t >> 7;
   const int kh = h / a.vrep;
-  const int T = *a.T;
-  const int chans[3] = {kh * 128 + dv, a.lkd + kh * 128 + dv, 2 * a.lkd + h * 128 + dv};
   qkv[0] = qkv[1] = qkv[2] = 0;
+  zn[0] = zn[1] = 0;
   if (q == 0) {
-#pragma unroll
-    for (int i = 0; i < 3; ++i) {
-      const int c = chans[i];
-      const int16_t *ring = a.conv + (size_t)c * 4;
-      const int32_t *cw = a.conv_w + (size_t)c * 4;
-      const long long xnew = __ldcg(a.qkv16 + c);
-      long long acc = 0;
-#pragma unroll
-      for (int j = 0; j < 3; ++j) acc += (long long)__ldcg(ring + ((T + 1 + j) & 3)) * cw[j];
-      acc += xnew * cw[3];
-      const long long pre = clip(rshr(acc, RS_F + CW_F - 12), -(1 << 20), (1 << 20) - 1);
-      const long long co = clip16(silu_q(pre));
-      qkv[i] = rshr(co, 12 - QKV_F);
-    }
+    qkv[0] = __ldcg(a.qkvc + kh * 128 + dv);
+    qkv[1] = __ldcg(a.qkvc + a.lkd + kh * 128 + dv);
+    qkv[2] = __ldcg(a.qkvc + 2 * a.lkd + h * 128 + dv);
+    zn[0] = __ldcg(a.z16 + h * 128 + dv);
+    zn[1] = __ldcg(a.norm_w + dv);
   }
-  if (t == 0) {   // gates (ref/layer_fixed.py:1531-1538)
-    const long long beta = sigmoid_q(__ldcg(a.b16 + h));
-    const long long sp = softplus_q((long long)__ldcg(a.a16 + h) + a.dt_bias[h]);
-    const long long g = -rshr((long long)a.A[h] * sp, 15 + 12 - 16);
-    long long dec = rshr(exp_neg_q(g < 0 ? g : 0), 15);
-    if (dec > 32767) dec = 32767;
-    sm.gate[0] = beta;
-    sm.gate[1] = dec;
+  if (t == 0) {
+    sm.gate[0] = __ldcg(a.beta + h);
+    sm.gate[1] = __ldcg(a.decay + h);
   }
   const long long ssq = g_sum_ll(sy, qkv[0] * qkv[0], sm.red);
   const long long ssk = g_sum_ll(sy, qkv[1] * qkv[1], sm.red);
@@ -64,6 +52,8 @@ F5_DEV void dn_head_pre(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, 
     int64_t r; int e;
     rsqrt_q((uint64_t)(ssq == 0 ? 1 : ssq), 2 * QKV_F, r, e);
     sm.gate[2] = r; sm.e[0] = e;
+  } else if (t == 32) {
+    int64_t r; int e;
     rsqrt_q((uint64_t)(ssk == 0 ? 1 : ssk), 2 * QKV_F, r, e);
     sm.gate[3] = r; sm.e[1] = e;
   }
@@ -72,14 +62,6 @@ F5_DEV void dn_head_pre(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, 
     const long long qn = clip16(rshr(qkv[0] * sm.gate[2], QKV_F + 30 - sm.e[0] - NRM_F));
     sm.qn[dv] = (int32_t)rshr(qn * 2896, 15);    // round(2^15 / sqrt(128)) = 2896
     sm.kn[dv] = (int32_t)clip16(rshr(qkv[1] * sm.gate[3], QKV_F + 30 - sm.e[1] - NRM_F));
-    // conv ring: slot T%4 takes this step's pre-conv input; q/k channels are
-    // shared by the VREP value heads of a key head -> written by the first
-    const int slot_new = T & 3;
-    if ((h % a.vrep) == 0) {
-      a.conv[(size_t)chans[0] * 4 + slot_new] = __ldcg(a.qkv16 + chans[0]);
-      a.conv[(size_t)chans[1] * 4 + slot_new] = __ldcg(a.qkv16 + chans[1]);
-    }
-    a.conv[(size_t)chans[2] * 4 + slot_new] = __ldcg(a.qkv16 + chans[2]);
   }
   sy.sync();
 }
@@ -87,7 +69,8 @@ F5_DEV void dn_head_pre(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, 
 // recurrence, block-float shift, gated norm, x silu(z)  (ref/layer_fixed.py:
 // 1545-1580).  sm.sd must hold the head's state.
 template <class SY, int NQ>
-F5_DEV void dn_head_rec(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, const long long (&qkv)[3]) {
+F5_DEV void dn_head_rec(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, const long long (&qkv)[3],
+                        const long long (&zn)[2]) {
   const int t = sy.tid(), dv = t & 127, q = t >> 7;
   constexpr int RQ = 128 / NQ;
   int16_t *S = a.S + (size_t)h * 128 * 128;
@@ -156,8 +139,8 @@ F5_DEV void dn_head_rec(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, 
   }
   if (q == 0) {
     const long long tt = clip16(rshr(o16 * m, 15));
-    const long long nh = clip16(rshr(tt * a.norm_w[dv], 14));
-    const long long zg = clip16(silu_q((long long)__ldcg(a.z16 + h * 128 + dv) << (12 - QKV_F)));
+    const long long nh = clip16(rshr(tt * zn[1], 14));
+    const long long zg = clip16(silu_q(zn[0] << (12 - QKV_F)));
     a.on16[h * 128 + dv] = (int16_t)clip16(rshr(nh * zg, 12));
     if (dv == 0 && a.kh_out) a.kh_out[h] = kh_shift;
   }

@@ -197,8 +197,9 @@ F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red,
 #pragma unroll
         for (int j = 0; j < MAXB; ++j) {
           const int b = tid + j * BT;
-          wl[j][0] = b < nblk ? *reinterpret_cast<const int4 *>(P.w + 8 * b) : make_int4(0, 0, 0, 0);
-          wl[j][1] = b < nblk ? *reinterpret_cast<const int4 *>(P.w + 8 * b + 4) : make_int4(0, 0, 0, 0);
+          // gains streamed at L2 (__ldcg): L1 stays with the LUTs
+          wl[j][0] = b < nblk ? __ldcg(reinterpret_cast<const int4 *>(P.w + 8 * b)) : make_int4(0, 0, 0, 0);
+          wl[j][1] = b < nblk ? __ldcg(reinterpret_cast<const int4 *>(P.w + 8 * b + 4)) : make_int4(0, 0, 0, 0);
         }
         long long ss = 0;
 #pragma unroll
@@ -343,6 +344,35 @@ F5_DEV void epilogue_row(const GemvArgs &a, const GemvSeg &sg, int row, long lon
     case GM_RESID: {
       int16_t *o = static_cast<int16_t *>(sg.out) + orow;   // written by other CTAs: read at L2
       *o = (int16_t)clip16((int64_t)__ldcg(o) + clip16(shift_to(y, sh2)));
+    } break;
+    case GM_CONV: {   // ref/layer_fixed.py:1511-1520 for channel orow
+      const long long v = clip16(shift_to(y, sh2));
+      static_cast<int16_t *>(sg.out)[orow] = (int16_t)v;
+      int16_t *ring = static_cast<int16_t *>(sg.aux0) + (size_t)orow * 4;
+      const int4 cw = __ldcg(reinterpret_cast<const int4 *>(static_cast<const int32_t *>(sg.aux1) + (size_t)orow * 4));
+      const int T = *sg.T;
+      const uint2 rw = __ldcg(reinterpret_cast<const uint2 *>(ring));   // 4 int16 slots
+      const int16_t r4[4] = {(int16_t)(rw.x & 0xFFFFu), (int16_t)(rw.x >> 16), (int16_t)(rw.y & 0xFFFFu),
+                             (int16_t)(rw.y >> 16)};
+      long long acc = (long long)r4[(T + 1) & 3] * cw.x + (long long)r4[(T + 2) & 3] * cw.y +
+                      (long long)r4[(T + 3) & 3] * cw.z + v * cw.w;
+      const long long pre = clip(rshr(acc, RS_F + CW_F - 12), -(1 << 20), (1 << 20) - 1);
+      const long long co = clip16(silu_q(pre));
+      static_cast<int16_t *>(sg.aux_out)[orow] = (int16_t)rshr(co, 12 - QKV_F);
+      ring[T & 3] = (int16_t)v;
+    } break;
+    case GM_GATE_B: {   // ref/layer_fixed.py:1531
+      const long long v = clip16(shift_to(y, sh2));
+      static_cast<int16_t *>(sg.out)[orow] = (int16_t)v;
+      static_cast<int32_t *>(sg.aux_out)[orow] = (int32_t)sigmoid_q(v);
+    } break;
+    case GM_GATE_A: {   // ref/layer_fixed.py:1532-1538
+      const long long v = clip16(shift_to(y, sh2));
+      static_cast<int16_t *>(sg.out)[orow] = (int16_t)v;
+      const long long sp = softplus_q(v + static_cast<const int32_t *>(sg.aux0)[orow]);
+      const long long g = -rshr((long long)static_cast<const int32_t *>(sg.aux1)[orow] * sp, 15 + 12 - 16);
+      long long dec = rshr(exp_neg_q(g < 0 ? g : 0), 15);
+      static_cast<int32_t *>(sg.aux_out)[orow] = (int32_t)(dec > 32767 ? 32767 : dec);
     } break;
     default: break;
   }

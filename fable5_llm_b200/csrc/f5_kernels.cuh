@@ -41,6 +41,12 @@ enum GemvMode : int {
   GM_RESID = 3,     // out int16[row] = clip16(out[row] + clip16(shift))
   GM_SILU_MUL = 4,  // paired gate/up rows -> clip16(rshr(silu(g) * u, 12))
   GM_ARGMAX = 5,    // running (max y32, lowest row) key
+  // DeltaNet in-projection epilogues (ref/layer_fixed.py:1511-1538): the
+  // per-channel / per-head vector work that does not need the whole head
+  GM_CONV = 6,      // out int16 = v = clip16(shift) (pre-conv, Q.RS_F); aux_out int16 =
+                    // conv4+SiLU of the channel over its ring (Q.QKV_F); ring[T % 4] = v
+  GM_GATE_B = 7,    // out int16 = v (Q12); aux_out int32 = beta = sigmoid_q(v)
+  GM_GATE_A = 8,    // out int16 = v (Q12); aux_out int32 = decay of softplus(v + dt_bias) * A
 };
 
 constexpr int GEMV_MAX_SEG = 4;
@@ -81,6 +87,10 @@ struct GemvSeg {
   int out_f, out_f2;   // output fraction bits (TO16/TO64/RESID/SILU_MUL)
   int mode;
   int out_row0;
+  void *aux_out;      // GM_CONV / GM_GATE_*: second output (see GemvMode)
+  void *aux0;         // GM_CONV: int16 conv ring [rows][4]; GM_GATE_A: int32 dt_bias (Q12)
+  const void *aux1;   // GM_CONV: int32 conv weights [rows][4] (Q.CW_F); GM_GATE_A: int32 A (Q15)
+  const int *T;       // GM_CONV: tokens already in the window (ring slot T % 4)
 };
 
 struct GemvArgs {

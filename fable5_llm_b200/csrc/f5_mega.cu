@@ -101,16 +101,15 @@ F5_DEV bool mwait(uint64_t *b, uint32_t parity, const Abort &ab) {
   }
 }
 
-// Counter barrier over `target` CTAs (consumer groups).  The release
-// (fence + add) / acquire (load + fence) pair by one thread, bracketed by
-// the group's named barrier, orders every consumer thread's prior global
-// writes before any later read in the other CTAs.
+// Counter barrier over `target` CTAs (consumer groups).  One thread's
+// release add / acquire polls, bracketed by the group's named barrier, order
+// every consumer thread's prior global writes before any later read in the
+// other CTAs (release and acquire are cumulative over the bar.sync).
 F5_DEV bool counter_barrier(const CSync &sy, unsigned *cnt, unsigned target, const Abort &ab) {
   sy.sync();
   bool bad = false;
   if (sy.tid() == 0) {
-    __threadfence();
-    atomicAdd(cnt, 1u);
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
     unsigned long long t0 = 0, tpoll = 0;
     for (uint32_t it = 0;; ++it) {
       if (ld_acquire_u32(cnt) >= target) break;
@@ -126,9 +125,43 @@ F5_DEV bool counter_barrier(const CSync &sy, unsigned *cnt, unsigned target, con
         }
       }
     }
-    __threadfence();
   }
   return !sy.any(bad);
+}
+
+// Marked 64-bit values for the attention's group exchanges: the value goes
+// out as two naturally aligned 8-byte words {low or high half, marker 1} --
+// each word is single-copy atomic, so a reader that sees both markers has
+// the whole value, with no fence or counter.  The slots are zeroed by the
+// step's BEGIN op, grid barriers before any attention op.
+F5_DEV void slot_put(unsigned long long *slot, long long v) {
+  const unsigned long long lo = (unsigned long long)(uint32_t)v | (1ull << 32);
+  const unsigned long long hi = (unsigned long long)(uint32_t)((unsigned long long)v >> 32) | (1ull << 32);
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(slot), "l"(lo) : "memory");
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(slot + 1), "l"(hi) : "memory");
+}
+F5_DEV bool slot_get(const unsigned long long *slot, long long &v, const Abort &ab) {
+  unsigned long long t0 = 0, tpoll = 0;
+  for (uint32_t it = 0;; ++it) {
+    unsigned long long lo, hi;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(lo) : "l"(slot) : "memory");
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(hi) : "l"(slot + 1) : "memory");
+    if ((lo >> 32) == 1ull && (hi >> 32) == 1ull) {
+      v = (long long)((hi << 32) | (lo & 0xFFFFFFFFull));
+      return true;
+    }
+    if ((it & 7) == 7) {
+      const unsigned long long t = gtimer();
+      if (t0 == 0) {
+        t0 = t;
+        tpoll = t + MG_POLL_NS;
+      } else if (t >= tpoll) {
+        if (ab.raised()) return false;
+        if (t - t0 > MG_WAIT_NS) { ab.raise(); return false; }
+        tpoll = t + MG_POLL_NS;
+      }
+    }
+  }
 }
 
 F5_DEV void release_scratch(const CSync &sy, uint64_t *bfree) {
@@ -187,10 +220,18 @@ __shared__ __align__(8) uint64_t mg_bsd, mg_bsk, mg_bsv, mg_bfree, mg_bpd[2];
 __shared__ __align__(16) MegaOp mg_cop[2], mg_pop[2];   // op i's descriptor in [i & 1]
 __shared__ long long mg_red[64];
 __shared__ long long mg_r, mg_gate[4], mg_att[8];
+__shared__ long long mg_gat[64];   // group_gather's per-warp partials (apart from mg_red: no reuse race)
 __shared__ int mg_meta[4], mg_e[2];
 __shared__ int mg_cnt[6];   // issued fills: [0] ring, [1] sd, [2] sk, [3] sv (producer), [4] sk, [5] sv (consumers)
 __shared__ volatile int mg_abort;
 __shared__ int mg_last;
+__shared__ unsigned long long *mg_tr;   // this op's trace row (thread 0 only), null when not tracing
+
+// trace marker k (2..7) of the current op: consumer thread 0 only
+#define MG_MARK(k)                                                   \
+  do {                                                               \
+    if (threadIdx.x == 0 && mg_tr) mg_tr[(k)] = gtimer();            \
+  } while (0)
 
 struct MegaSmem {
   int ns;
@@ -304,6 +345,7 @@ F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const 
   const int G = gridDim.x, b = blockIdx.x, ns = S.ns;
   prologue<1>(sy, a, S.xs(), mg_red, (&mg_r), mg_meta);
   sy.sync();
+  MG_MARK(2);
   const int e_x = mg_meta[0], in_f = mg_meta[1];
   uint2 xr[4][4];
 #pragma unroll
@@ -366,6 +408,7 @@ F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const 
     }
   }
   if (sy.any(bad)) return false;
+  MG_MARK(3);
   if (argmax) {
     flush();
 #pragma unroll
@@ -399,6 +442,7 @@ F5_DEV bool c_gemv_split(const GemvArgs &a, const MegaSmem &S, RingPos &rp, cons
   const int G = gridDim.x, b = blockIdx.x, ns = S.ns;
   prologue<(NP * 4 * 128 + MG_CT - 1) / MG_CT>(sy, a, S.xs(), mg_red, (&mg_r), mg_meta);
   sy.sync();
+  MG_MARK(2);
   const int e_x = mg_meta[0], in_f = mg_meta[1];
   const int part = warp % NP, wrow = warp / NP;   // warps >= NP * (16 / NP) idle
   uint2 xr[4][4];
@@ -436,6 +480,7 @@ F5_DEV bool c_gemv_split(const GemvArgs &a, const MegaSmem &S, RingPos &rp, cons
     rp.next(ns);
   }
   if (sy.any(bad)) return false;
+  MG_MARK(3);
   unsigned long long best = 0ull;
   for (int i = tid; i < u1 - u0; i += MG_CT) {
     const int uu = u0 + i;
@@ -458,12 +503,15 @@ F5_DEV bool c_dn(const MegaArgs &ma, const DnArgs &d, const MegaSmem &S, int &w_
   const DnSmem sm = {reinterpret_cast<int16_t *>(S.scr() + DN_SD), reinterpret_cast<int32_t *>(S.scr() + DN_QN),
                      reinterpret_cast<int32_t *>(S.scr() + DN_KN), reinterpret_cast<long long *>(S.scr() + DN_PART),
                      mg_red, mg_gate, mg_e};
-  long long qkv[3];
-  dn_head_pre<CSync, 4>(sy, d, h, sm, qkv);
+  long long qkv[3], zn[2];
+  dn_head_pre<CSync, 4>(sy, d, h, sm, qkv, zn);
+  MG_MARK(2);
   const bool got = mwait((&mg_bsd), w_sd & 1, ab);
   ++w_sd;
   if (sy.any(!got)) return false;
-  dn_head_rec<CSync, 4>(sy, d, h, sm, qkv);
+  MG_MARK(3);
+  dn_head_rec<CSync, 4>(sy, d, h, sm, qkv, zn);
+  MG_MARK(6);
   release_scratch(sy, (&mg_bfree));
   return true;
 }
@@ -474,8 +522,8 @@ F5_DEV bool c_dn(const MegaArgs &ma, const DnArgs &d, const MegaSmem &S, int &w_
 // RMSNorm(1+w) over a 256-dim head (ref/layer_fixed.py:1242-1278) then
 // rope_fx on the first `rot` dims (ref/layer_fixed.py:1340-1348), for four
 // heads at once: thread t owns dims e and e+128 (e = t & 127) of head t>>7.
-F5_DEV void norm_rope4(const CSync &sy, long long x0, long long x1, const int32_t *w, const int16_t *cs, int rot,
-                       int16_t *xn, int16_t *out, int nslots, long long *red) {
+F5_DEV void norm_rope4(const CSync &sy, long long x0, long long x1, long long w0, long long w1, long long cosv,
+                       long long sinv, int rot, int16_t *xn, int16_t *out, int nslots, long long *red) {
   const int t = sy.tid(), hs = t >> 7, e = t & 127, warp = t >> 5, lane = t & 31;
   const long long ss = warp_sum_ll(x0 * x0 + x1 * x1);
   if (lane == 0) red[warp] = ss;
@@ -484,9 +532,8 @@ F5_DEV void norm_rope4(const CSync &sy, long long x0, long long x1, const int32_
   int64_t r;
   int ee;
   rsqrt_q((uint64_t)(tot == 0 ? 1 : tot), 2 * QKV_F + 8, r, ee);   // n = 256
-  const long long n0 = clip16(rshr(clip(rshr(x0 * r, 30 - ee), -(1ll << 32), (1ll << 32) - 1) * ((long long)w[e] + (1 << 14)), 14));
-  const long long n1 =
-      clip16(rshr(clip(rshr(x1 * r, 30 - ee), -(1ll << 32), (1ll << 32) - 1) * ((long long)w[e + 128] + (1 << 14)), 14));
+  const long long n0 = clip16(rshr(clip(rshr(x0 * r, 30 - ee), -(1ll << 32), (1ll << 32) - 1) * (w0 + (1 << 14)), 14));
+  const long long n1 = clip16(rshr(clip(rshr(x1 * r, 30 - ee), -(1ll << 32), (1ll << 32) - 1) * (w1 + (1 << 14)), 14));
   xn[hs * 256 + e] = (int16_t)n0;
   xn[hs * 256 + e + 128] = (int16_t)n1;
   sy.sync();
@@ -494,13 +541,42 @@ F5_DEV void norm_rope4(const CSync &sy, long long x0, long long x1, const int32_
   if (e < rot) {   // rot <= 128: dims e + 128 are never rotated
     const int hh = rot >> 1;
     const long long rr = e < hh ? -(long long)xn[hs * 256 + e + hh] : (long long)xn[hs * 256 + e - hh];
-    o0 = clip16(rshr(n0 * cs[e] + rr * cs[64 + e], ROPE_F));
+    o0 = clip16(rshr(n0 * cosv + rr * sinv, ROPE_F));
   }
   if (hs < nslots) {
     out[hs * 256 + e] = (int16_t)o0;
     out[hs * 256 + e + 128] = (int16_t)n1;
   }
   sy.sync();
+}
+
+// Gather the cpg CTAs' marked per-head values of one phase and combine them
+// per head (max or sum) into mg_att[0..3]: thread t < 4 cpg polls entry t
+// (CTA t / 4, head t % 4); lanes sharing t % 4 combine by shuffles, then
+// across warps.  Also a barrier of the consumer group.
+F5_DEV bool group_gather(const CSync &sy, const unsigned long long *slots, int cpg, bool is_max, const Abort &ab) {
+  const int tid = sy.tid(), lane = tid & 31, warp = tid >> 5;
+  const long long ident = is_max ? LLONG_MIN : 0;
+  long long v = ident;
+  bool ok = true;
+  if (tid < 4 * cpg) ok = slot_get(slots + (size_t)tid * 2, v, ab);
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1) {
+    const long long u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? (u > v ? u : v) : v + u;
+  }
+  if (lane < 4 && warp < 16) mg_gat[warp * 4 + lane] = v;
+  if (sy.any(!ok)) return false;
+  if (tid < 4) {
+    long long r = ident;
+    for (int w = 0; w < (4 * cpg + 31) / 32; ++w) {
+      const long long u = mg_gat[w * 4 + tid];
+      r = is_max ? (u > r ? u : r) : r + u;
+    }
+    mg_att[tid] = r;
+  }
+  sy.sync();
+  return true;
 }
 
 F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int T, int pos, int &w_sk, int &w_sv,
@@ -526,15 +602,20 @@ F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int
   if (!g.ok && blockIdx.x == 0 && tid == 0) atomicOr(a.err, (uint32_t)DERR_KV_FULL);
   const int16_t *cs = a.rope + (size_t)g.pos * 128;
   const size_t kvrow = (size_t)g.kv * a.max_T;
+  const bool k_act = hs == 0;
+
+  // ---- 0. every operand in one round of loads ----
+  const long long qx0 = __ldcg(a.qg16 + hq * 512 + e), qx1 = __ldcg(a.qg16 + hq * 512 + e + 128);
+  const long long kx0 = k_act ? __ldcg(a.k16 + g.kv * 256 + e) : 0, kx1 = k_act ? __ldcg(a.k16 + g.kv * 256 + e + 128) : 0;
+  const long long v0 = k_act ? __ldcg(a.v16 + g.kv * 256 + e) : 0, v1 = k_act ? __ldcg(a.v16 + g.kv * 256 + e + 128) : 0;
+  const long long qw0 = __ldcg(a.q_norm + e), qw1 = __ldcg(a.q_norm + e + 128);
+  const long long kw0 = __ldcg(a.k_norm + e), kw1 = __ldcg(a.k_norm + e + 128);
+  const long long cosv = e < a.rot ? __ldcg(cs + e) : 0, sinv = e < a.rot ? __ldcg(cs + 64 + e) : 0;
 
   // ---- 1. q / k norm + rope; kv_quant of the new k and v ----
-  norm_rope4(sy, __ldcg(a.qg16 + hq * 512 + e), __ldcg(a.qg16 + hq * 512 + e + 128), a.q_norm, cs, a.rot, xn, q16,
-             4, mg_red);
-  const bool k_act = hs == 0;
-  norm_rope4(sy, k_act ? __ldcg(a.k16 + g.kv * 256 + e) : 0, k_act ? __ldcg(a.k16 + g.kv * 256 + e + 128) : 0,
-             a.k_norm, cs, a.rot, xn, k16n, 1, mg_red);
+  norm_rope4(sy, qx0, qx1, qw0, qw1, cosv, sinv, a.rot, xn, q16, 4, mg_red);
+  norm_rope4(sy, kx0, kx1, kw0, kw1, cosv, sinv, a.rot, xn, k16n, 1, mg_red);
   const long long kn0 = k_act ? k16n[e] : 0, kn1 = k_act ? k16n[e + 128] : 0;
-  const long long v0 = k_act ? __ldcg(a.v16 + g.kv * 256 + e) : 0, v1 = k_act ? __ldcg(a.v16 + g.kv * 256 + e + 128) : 0;
   const unsigned long long mk0 = uabs(kn0) > uabs(kn1) ? uabs(kn0) : uabs(kn1);
   const unsigned long long mv0 = uabs(v0) > uabs(v1) ? uabs(v0) : uabs(v1);
   const int ek = dynq8_e(g_max_ull(sy, mk0, reinterpret_cast<unsigned long long *>(mg_red)));
@@ -556,6 +637,7 @@ F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int
   }
   const int ke_new = ek - QKV_F, ve_new = ev - QKV_F;
   sy.sync();
+  MG_MARK(2);
 
   // ---- 2. scores: warp per token, 4 heads at once; lane = 8 dims ----
   int32_t qr[4][8];
@@ -613,18 +695,21 @@ F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int
     }
   }
   if (sy.any(bad)) return false;
+  MG_MARK(3);
+  // group score max over the kv head's cpg CTAs (marked slots, phase 0)
+  unsigned long long *slots = m.slots + (size_t)g.kv * g.cpg * 8;
+  const size_t phase_stride = (size_t)a.nkv * g.cpg * 8;
   if (lane == 0)
 #pragma unroll
     for (int h = 0; h < 4; ++h) red4[warp * 4 + h] = lmax[h];
   sy.sync();
-  if (tid < 4 && len > 0) {
+  if (tid < 4) {
     long long mx = LLONG_MIN;
     for (int w = 0; w < MG_CONS; ++w) mx = red4[w * 4 + tid] > mx ? red4[w * 4 + tid] : mx;
-    atomicMax(&m.gmax[g.kv * 4 + tid], (unsigned long long)mx ^ (1ull << 63));
+    slot_put(slots + (size_t)(g.j * 4 + tid) * 2, mx);
   }
-  if (!counter_barrier(sy, &ma.bars[m.gbar + 2 * g.kv], (unsigned)g.cpg, ab)) return false;
-  if (tid < 4) mg_att[tid] = (long long)(__ldcg(&m.gmax[g.kv * 4 + tid]) ^ (1ull << 63));
-  sy.sync();
+  if (!group_gather(sy, slots, g.cpg, true, ab)) return false;
+  MG_MARK(4);
 
   // ---- 3. exp, group sum, reciprocal, probabilities (Q15) ----
   long long sum[4] = {0, 0, 0, 0};
@@ -643,14 +728,15 @@ F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int
 #pragma unroll
     for (int h = 0; h < 4; ++h) red4[warp * 4 + h] = sum[h];
   sy.sync();
-  if (tid < 4 && len > 0) {
+  if (tid < 4) {
     long long tot = 0;
     for (int w = 0; w < MG_CONS; ++w) tot += red4[w * 4 + tid];
-    atomicAdd(&m.gsum[g.kv * 4 + tid], (unsigned long long)tot);
+    slot_put(slots + phase_stride + (size_t)(g.j * 4 + tid) * 2, tot);
   }
-  if (!counter_barrier(sy, &ma.bars[m.gbar + 2 * g.kv + 1], (unsigned)g.cpg, ab)) return false;
+  if (!group_gather(sy, slots + phase_stride, g.cpg, false, ab)) return false;
+  MG_MARK(5);
   if (tid < 4) {
-    const long long den = (long long)__ldcg(&m.gsum[g.kv * 4 + tid]);
+    const long long den = mg_att[tid];
     int64_t rr;
     int re;
     recip_q((uint64_t)(den > 0 ? den : 1), 30, rr, re);
@@ -719,6 +805,7 @@ F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int
       if (s) atomicAdd(&m.gacc[(g.kv * 4 + h) * 256 + dd], s);
     }
   }
+  MG_MARK(6);
   release_scratch(sy, (&mg_bfree));
   return true;
 }
@@ -758,7 +845,7 @@ F5_DEV void consumers(const MegaArgs &ma, const MegaSmem &S, int tok, int T, int
   const CSync sy;
   RingPos rp;
   int w_sd = 0, w_sk = 0, w_sv = 0;
-  unsigned long long *tr = ma.trace ? ma.trace + (size_t)blockIdx.x * ma.nops * 2 : nullptr;
+  unsigned long long *tr = ma.trace ? ma.trace + (size_t)blockIdx.x * ma.nops * MEGA_TRACE_SLOTS : nullptr;
   stage_desc(ma, S, 0);
   stage_wait();
   sy.sync();
@@ -768,11 +855,13 @@ F5_DEV void consumers(const MegaArgs &ma, const MegaSmem &S, int tok, int T, int
     // descriptor and retires every reader of the buffer staged next.
     if (oi > 0) {
       stage_wait();
+      if (tr && threadIdx.x == 0) tr[(size_t)(oi - 1) * MEGA_TRACE_SLOTS + 7] = gtimer();   // arrival
       if (!counter_barrier(sy, &ma.bars[oi - 1], gridDim.x, ab)) return;
     }
+    if (threadIdx.x == 0) mg_tr = tr ? tr + (size_t)oi * MEGA_TRACE_SLOTS : nullptr;
     if (oi + 1 < ma.nops) stage_desc(ma, S, oi + 1);
     const MegaOp &op = mg_cop[oi & 1];
-    if (tr && threadIdx.x == 0) tr[2 * oi] = gtimer();
+    if (tr && threadIdx.x == 0) tr[(size_t)oi * MEGA_TRACE_SLOTS] = gtimer();
     bool ok = true;
     switch (op.kind) {
       case MK_BEGIN: c_begin(ma, op.b, tok); break;
@@ -781,7 +870,7 @@ F5_DEV void consumers(const MegaArgs &ma, const MegaSmem &S, int tok, int T, int
       case MK_ATTN: ok = c_attn(ma, op.at, S, T, pos, w_sk, w_sv, ab); break;
       default: break;
     }
-    if (tr && threadIdx.x == 0) tr[2 * oi + 1] = gtimer();
+    if (tr && threadIdx.x == 0) tr[(size_t)oi * MEGA_TRACE_SLOTS + 1] = gtimer();
     if (!ok) {
       stage_wait();
       return;
@@ -810,6 +899,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega(const __grid_constant_
     for (int i = 0; i < 6; ++i) mg_cnt[i] = 0;
     mg_abort = 0;
     mg_last = 0;
+    mg_tr = nullptr;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   // step parameters: written by the host or by the previous launch only

@@ -12,7 +12,7 @@
 namespace f5 {
 
 enum MegaKind : int {
-  MK_BEGIN = 0,   // x16 = emb[tok]; clear the argmax key and the attention sums
+  MK_BEGIN = 0,   // x16 = emb[tok]; clear the argmax key, the attention sums and slots
   MK_GEMV = 1,    // one fused GEMV (same descriptor as k_gemv)
   MK_DN = 2,      // Gated-DeltaNet core, one value head per CTA
   MK_ATTN = 3,    // attention core, kv head x token chunk per CTA
@@ -29,10 +29,8 @@ struct MegaBegin {
 
 struct MegaAttn {
   AttnArgs a;                 // same operands as the per-op attention kernel
-  unsigned long long *gmax;   // [nq] order-preserving keys of the score max
-  unsigned long long *gsum;   // [nq] sums of exp
+  unsigned long long *slots;  // [2 phases][nkv][G / nkv CTAs][4 heads][2 words] marked values
   int32_t *gacc;              // [nq * HD] PV sums
-  int gbar;                   // first of 2 * nkv group counters
 };
 
 // 16-byte aligned and sized: the kernel stages each descriptor in shared
@@ -60,13 +58,18 @@ struct MegaArgs {
   int advance;      // feed the argmax back as the next token (greedy loop)
   int dn_heads;     // CTAs [0, dn_heads) run one DeltaNet value head each
   int ns;           // ring stages (from mega_config)
-  unsigned long long *trace;   // optional [G][nops][2] globaltimer at each op's start / end
+  unsigned long long *trace;   // optional [G][nops][MEGA_TRACE_SLOTS] globaltimer marks
 };
 
 constexpr int MEGA_THREADS = 544;       // 16 consumer warps + 1 producer warp
 constexpr int MEGA_STAGE = 33792;       // ring stage: 16 rows of K=4096, 5 of K=12288
 constexpr int MEGA_RES = 256;           // deferred per-CTA row results
 constexpr int MEGA_SUB = 64;            // attention tokens per K/V shared-memory fill
+// trace marks per (CTA, op): 0 start (after the grid barrier), 1 end,
+// 2..6 op phases (GEMV: 2 prologue done, 3 rows done; DeltaNet: 2 l2norms,
+// 3 state ready, 6 head done; attention: 2 q/k ready, 3 scores, 4 max,
+// 5 sum, 6 PV sums), 7 arrival at the following grid barrier
+constexpr int MEGA_TRACE_SLOTS = 8;
 
 // Rows of one ring stage for a packed row stride.
 inline int mega_rows_per_stage(int stride) {

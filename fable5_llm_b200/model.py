@@ -174,15 +174,17 @@ class DecodeModel:
 
     def trace_step(self):
         """One persistent greedy step with per-op device timestamps ->
-        (ns int64[grid, nops, 2] start/end relative to the earliest start,
-        op kinds list).  Caches advance by one token."""
+        (ns int64[grid, nops, 8] marks relative to the earliest start, -1
+        where a CTA has no such mark (see f5_ctx_trace_step), op kinds list).
+        Caches advance by one token."""
         grid, nops = ctypes.c_int(), ctypes.c_int()
         L.check(self.lib.f5_ctx_trace_step(self.h, None, 0, ctypes.byref(grid), ctypes.byref(nops)), "trace")
-        out = np.zeros(grid.value * nops.value * 2, dtype=np.uint64)
+        out = np.zeros(grid.value * nops.value * 8, dtype=np.uint64)
         L.check(self.lib.f5_ctx_trace_step(self.h, _p(out), out.size, ctypes.byref(grid), ctypes.byref(nops)),
                 "trace")
-        t = out.astype(np.int64).reshape(grid.value, nops.value, 2)
-        t -= t[:, 0, 0].min()
+        t = out.astype(np.int64).reshape(grid.value, nops.value, 8)
+        t0 = t[:, 0, 0].min()
+        t = np.where(t > 0, t - t0, -1)
         kinds = ["begin"]
         for lt in self.geom.layer_types:
             core = "attn" if lt == "full_attention" else "dn"

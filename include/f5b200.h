@@ -231,9 +231,10 @@ int f5_ctx_get_engine(f5_ctx *ctx, int *engine);
 
 /* Timeline of one persistent step (no reference counterpart: profiling aid).
  * Runs one greedy step (caches advance) with every CTA recording the device
- * globaltimer (ns) at the start (after its grid barrier) and end of each op:
- * out[(cta * nops + op) * 2 + {0, 1}].  With out == NULL only *grid and *nops
- * are returned; otherwise cap must be >= grid * nops * 2. */
+ * globaltimer (ns) at 8 marks of each op: out[(cta * nops + op) * 8 + k],
+ * k = 0 start (after the grid barrier), 1 end, 2..6 op phases, 7 arrival at
+ * the next grid barrier (0 where a CTA has no such phase).  With out == NULL
+ * only *grid and *nops are returned; otherwise cap >= grid * nops * 8. */
 int f5_ctx_trace_step(f5_ctx *ctx, uint64_t *out, size_t cap, int *grid, int *nops);
 
 /* One full model step from a host token id: embedding row, every layer,
