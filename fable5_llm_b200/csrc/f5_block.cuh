@@ -85,6 +85,34 @@ struct NamedSync {
   }
 };
 
+// Sum over the group of per-thread values |v| < 2^40 with two 32-bit
+// redux.sync adds per warp (v = hi * 2^22 + lo, lo in [0, 2^22)): exact.
+template <class SY>
+F5_DEV long long g_sum_split(const SY &sy, long long v, long long *red) {
+  const unsigned slo = __reduce_add_sync(0xffffffffu, (unsigned)v & 0x3FFFFFu);
+  const int shi = __reduce_add_sync(0xffffffffu, (int)(v >> 22));
+  const long long w = ((long long)shi << 22) + (long long)slo;
+  const int wi = sy.tid() >> 5, nw = sy.n() >> 5;
+  sy.sync();
+  if ((sy.tid() & 31) == 0) red[wi] = w;
+  sy.sync();
+  long long t = 0;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  return t;
+}
+// Max over the group of 32-bit unsigned values (redux.sync.max per warp).
+template <class SY>
+F5_DEV unsigned g_max_u32(const SY &sy, unsigned v, long long *red) {
+  v = __reduce_max_sync(0xffffffffu, v);
+  const int wi = sy.tid() >> 5, nw = sy.n() >> 5;
+  sy.sync();
+  if ((sy.tid() & 31) == 0) red[wi] = v;
+  sy.sync();
+  unsigned t = 0;
+  for (int i = 0; i < nw; ++i) t = (unsigned)red[i] > t ? (unsigned)red[i] : t;
+  return t;
+}
+
 template <class SY>
 F5_DEV long long g_sum_ll(const SY &sy, long long v, long long *red) {
 #pragma unroll

@@ -13,6 +13,7 @@
 // Both are built by the same enqueue_step walk (the persistent program is
 // the walk in "emit" mode), so they run the same descriptors.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -333,6 +334,12 @@ static size_t n_attn_layers(const f5_ctx *c) {
   for (const Layer &l : c->L) n += l.attn ? 1 : 0;
   return n;
 }
+// per DeltaNet layer of the persistent program: marked o values [LNH][128][2] (u64)
+constexpr size_t DN_XSLOT_BYTES = (size_t)LNH * 128 * 2 * 8;
+// the per-step zeroed region: attention layers first, then DeltaNet layers
+static size_t step_acc_bytes(const f5_ctx *c, int cpg) {
+  return n_attn_layers(c) * att_acc_bytes(cpg) + (c->L.size() - n_attn_layers(c)) * DN_XSLOT_BYTES;
+}
 
 // the five launches of one layer (ref/layer_fixed.py:1669-1677)
 static cudaError_t enqueue_layer(f5_ctx *c, int li, bool pdl) {
@@ -363,6 +370,11 @@ static cudaError_t enqueue_layer(f5_ctx *c, int li, bool pdl) {
     d.S = l.S; d.on16 = c->on16; d.kh_out = l.kh; d.stats = c->stats; d.err = c->err;
     d.lkd = LKD; d.vrep = LNH / LNKH; d.norm_mode = c->cfg.norm_mode;
     if (c->emit) {
+      const int n_dn = (int)std::count_if(c->emit->begin(), c->emit->end(),
+                                          [](const MegaOp &o) { return o.kind == MK_DN; });
+      d.xslots = reinterpret_cast<unsigned long long *>(
+          reinterpret_cast<uint8_t *>(c->d_attacc) + n_attn_layers(c) * att_acc_bytes(c->mega_grid / NKV) +
+          (size_t)n_dn * DN_XSLOT_BYTES);
       MegaOp op = {};
       op.kind = MK_DN;
       op.d = d;
@@ -445,7 +457,7 @@ static cudaError_t enqueue_step(f5_ctx *c, bool pdl) {
     op.b.H = H;
     op.b.key = c->key;
     op.b.zero = c->d_attacc;
-    op.b.zero_n = (int)(n_attn_layers(c) * att_acc_bytes(c->mega_grid / NKV) / 16);
+    op.b.zero_n = (int)(step_acc_bytes(c, c->mega_grid / NKV) / 16);
     emit_op(c, op);
   } else {
     StepParams *p = c->params;
@@ -544,7 +556,7 @@ static int build_mega(f5_ctx *c, bool &unsupported) {
   unsupported = true;
   if (c->cfg.world_size > 1) return set_error(F5_ESTATE, "the persistent engine runs unsharded contexts");
   const int sms = sm_count();
-  if (sms < NKV) return set_error(F5_ESTATE, "too few SMs for the persistent engine");
+  if (sms < 4 * LNH) return set_error(F5_ESTATE, "the persistent engine needs >= %d SMs", 4 * LNH);
   const int cpg = sms / NKV;
   const int chunk_max = (((c->cfg.max_T + cpg - 1) / cpg) + 15) & ~15;
   int grid = 0, ns = 0;
@@ -559,7 +571,7 @@ static int build_mega(f5_ctx *c, bool &unsupported) {
   const size_t n_attn = n_attn_layers(c);
   if (!c->d_attacc) {
     unsupported = false;
-    F5_ALLOC(c, c->d_attacc, (n_attn ? n_attn : 1) * att_acc_bytes(cpg));
+    F5_ALLOC(c, c->d_attacc, step_acc_bytes(c, cpg) + 16);
     unsupported = true;
   }
   std::vector<MegaOp> ops;
@@ -589,6 +601,10 @@ static int build_mega(f5_ctx *c, bool &unsupported) {
   m.advance = 1;
   m.dn_heads = LNH;
   m.ns = ns;
+  // L2 prefetch lead per CTA (F5_MEGA_PREFETCH_KB overrides; 0 disables)
+  long long pf_kb = 256;
+  if (const char *ev = getenv("F5_MEGA_PREFETCH_KB")) pf_kb = atoll(ev);
+  m.pf_bytes = pf_kb * 1024;
   c->mega_dirty = false;
   return F5_OK;
 }

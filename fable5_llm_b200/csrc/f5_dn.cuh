@@ -14,7 +14,8 @@ struct DnArgs {
   const int32_t *decay;   // [LNH] exp(g) (Q15)
   const int16_t *z16;     // [LVD] (Q.QKV_F)
   const int32_t *norm_w;  // [LDV] (Q14)
-  int16_t *S;             // [LNH][LDK][LDV] int16 state (Q.S_F)
+  int16_t *S;             // [LNH][4][LDK][32] int16 state (Q.S_F): head, dv / 32, dk, dv % 32
+  unsigned long long *xslots;  // persistent kernel: [LNH][128][2] marked o values (zeroed per step)
   int16_t *on16;          // [LVD] out: clip16(on), Q.DN_NORM_F
   int *kh_out;            // optional [LNH] block-float shifts k_h
   unsigned long long *stats;  // optional: state saturation count

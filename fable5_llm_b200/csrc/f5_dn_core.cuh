@@ -14,8 +14,12 @@
 
 namespace f5 {
 
+// State layout of a head, in HBM and in shared memory: [dv / 32][dk][dv % 32]
+// (four 8 KB column quarters, each contiguous: one bulk copy per quarter).
+F5_DEV int sidx(int dk, int dv) { return ((dv >> 5) << 12) | (dk << 5) | (dv & 31); }
+
 struct DnSmem {
-  int16_t *sd;      // [128*128] head state [dk][dv] (decayed in place)
+  int16_t *sd;      // [128*128] head state, sidx layout (decayed in place)
   int32_t *qn, *kn; // [128]
   long long *part;  // [NQ*128] partial sums of the split recurrence
   long long *red;   // [32]
@@ -78,8 +82,8 @@ F5_DEV void dn_head_rec(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, 
   long long kvm = 0;
 #pragma unroll 8
   for (int dk = q * RQ; dk < (q + 1) * RQ; ++dk) {
-    const int sd = rshr32p((int32_t)sm.sd[dk * 128 + dv] * decay, GAT_F);   // |S*decay| < 2^30
-    sm.sd[dk * 128 + dv] = (int16_t)sd;
+    const int sd = rshr32p((int32_t)sm.sd[sidx(dk, dv)] * decay, GAT_F);   // |S*decay| < 2^30
+    sm.sd[sidx(dk, dv)] = (int16_t)sd;
     kvm += (long long)sd * sm.kn[dk];
   }
   if (NQ > 1) {
@@ -105,10 +109,10 @@ F5_DEV void dn_head_rec(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, 
   int sat = 0;
 #pragma unroll 8
   for (int dk = q * RQ; dk < (q + 1) * RQ; ++dk) {
-    long long sn = (long long)sm.sd[dk * 128 + dv] + rshr((long long)sm.kn[dk] * delta, NRM_F);
+    long long sn = (long long)sm.sd[sidx(dk, dv)] + rshr((long long)sm.kn[dk] * delta, NRM_F);
     if (sn > 32767 || sn < -32767) ++sat;   // |Sh| > 32767 (ref/layer_fixed.py:1557)
     sn = clip16(sn);
-    S[dk * 128 + dv] = (int16_t)sn;
+    S[sidx(dk, dv)] = (int16_t)sn;
     o += sn * sm.qn[dk];
   }
   if (a.stats && sat) atomicAdd(a.stats, (unsigned long long)sat);

@@ -7,6 +7,13 @@
 #include "f5_kernels.cuh"
 #include "f5_tma.cuh"
 
+// optional phase marks inside the prologue (the persistent kernel's trace)
+#ifndef F5_PRO_MARK
+#define F5_PRO_MARK(k) \
+  do {               \
+  } while (0)
+#endif
+
 namespace f5 {
 
 F5_DEV uint4 ld_stream16(const uint8_t *p) {
@@ -86,6 +93,16 @@ F5_DEV long long rms_elem(long long x, long long r, int e, long long gain) {
 F5_DEV long long get16(const uint4 &u, int j) {
   const uint32_t w = (j >> 1) == 0 ? u.x : ((j >> 1) == 1 ? u.y : ((j >> 1) == 2 ? u.z : u.w));
   return (long long)(int16_t)((j & 1) ? (w >> 16) : (w & 0xFFFFu));
+}
+F5_DEV int32_t get16i(const uint4 &u, int j) {
+  const uint32_t w = (j >> 1) == 0 ? u.x : ((j >> 1) == 1 ? u.y : ((j >> 1) == 2 ? u.z : u.w));
+  return (int32_t)(int16_t)((j & 1) ? (w >> 16) : (w & 0xFFFFu));
+}
+// the int8 values q[0..7] of block b into the lane-major even/odd layout
+F5_DEV void put8i(uint2 *xs, int b, const int32_t q[8]) {
+  const uint32_t ev = __byte_perm(__byte_perm(q[0], q[2], 0x0040), __byte_perm(q[4], q[6], 0x0040), 0x5410);
+  const uint32_t od = __byte_perm(__byte_perm(q[1], q[3], 0x0040), __byte_perm(q[5], q[7], 0x0040), 0x5410);
+  xs[(((b >> 7) << 2) + (b & 3)) * 32 + ((b >> 2) & 31)] = make_uint2(ev, od);
 }
 
 F5_DEV int seg_of(const GemvArgs &a, int u) {
@@ -201,12 +218,13 @@ F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red,
           wl[j][0] = b < nblk ? __ldcg(reinterpret_cast<const int4 *>(P.w + 8 * b)) : make_int4(0, 0, 0, 0);
           wl[j][1] = b < nblk ? __ldcg(reinterpret_cast<const int4 *>(P.w + 8 * b + 4)) : make_int4(0, 0, 0, 0);
         }
-        long long ss = 0;
+        long long ss = 0;   // < 16 * 2^30 per thread
 #pragma unroll
         for (int j = 0; j < MAXB; ++j)
 #pragma unroll
-          for (int k = 0; k < 8; ++k) { const long long v = get16(raw[j], k); ss += v * v; }
-        ss = g_sum_ll(sy, ss, red);
+          for (int k = 0; k < 8; ++k) { const int32_t v = get16i(raw[j], k); ss += (long long)(v * v); }
+        ss = g_sum_split(sy, ss, red);
+        F5_PRO_MARK(4);
         if (tid == 0) {
           int64_t r; int e;
           rsqrt_q((uint64_t)(ss == 0 ? 1 : ss), 2 * P.in_f + (31 - __clz(K)), r, e);
@@ -234,23 +252,29 @@ F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red,
     } else {
       if (P.mode == PRO_RMSNORM && tid == 0) atomicOr(a.err, DERR_RANGE);   // RMSNorm is bound to K <= 4096
     }
-    unsigned long long mx = 0;
+    unsigned mx = 0;   // int16 magnitudes: 32-bit max
 #pragma unroll
     for (int j = 0; j < MAXB; ++j)
 #pragma unroll
-      for (int k = 0; k < 8; ++k) { const unsigned long long m = uabs(get16(raw[j], k)); mx = m > mx ? m : mx; }
-    mx = g_max_ull(sy, mx, reinterpret_cast<unsigned long long *>(red));
+      for (int k = 0; k < 8; ++k) {
+        const int32_t v = get16i(raw[j], k);
+        const unsigned m = (unsigned)(v < 0 ? -v : v);
+        mx = m > mx ? m : mx;
+      }
+    mx = g_max_u32(sy, mx, red);
+    F5_PRO_MARK(5);
     const int ex = dynq8_e(mx);
 #pragma unroll
     for (int j = 0; j < MAXB; ++j) {
       const int b = tid + j * BT;
       if (b < nblk) {
+        int32_t qi[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          q[k] = dynq8_apply(get16(raw[j], k), ex);
-          if (store) P.xq_out.x8[8 * b + k] = (int8_t)q[k];
+          qi[k] = dynq8_apply32(get16i(raw[j], k), ex);
+          if (store) P.xq_out.x8[8 * b + k] = (int8_t)qi[k];
         }
-        put8(xs, b, q);
+        put8i(xs, b, qi);
       }
     }
     if (tid == 0) { s_meta[0] = ex; s_meta[1] = P.in_f; }

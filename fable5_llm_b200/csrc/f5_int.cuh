@@ -51,6 +51,27 @@ F5_DEV int dynq8_e(uint64_t m) {
   return e;
 }
 F5_DEV int32_t dynq8_apply(int64_t x, int e) { return (int32_t)clip(e ? rshr(x, e) : x, -127, 127); }
+// dynq8_apply for |x| < 2^30 in 32-bit arithmetic: sign(x) * min((|x| +
+// 2^(e-1)) >> e, 127) is round-half-away-from-zero then clip to +-127.
+F5_DEV int32_t dynq8_apply32(int32_t x, int e) {
+  const int32_t ax = x < 0 ? -x : x;
+  int32_t r = (ax + ((1 << e) >> 1)) >> e;
+  r = r < 127 ? r : 127;
+  return x < 0 ? -r : r;
+}
+
+// Pull the LUTs' cache lines into L1 (thread t in [0, 51) takes one line):
+// issued at the start of a phase that will look them up, so the lookups on
+// its dependency chain hit L1 even after an acquire invalidated it.
+F5_DEV void lut_prefetch_l1(int t) {
+  const char *p = nullptr;
+  if (t < 16) p = reinterpret_cast<const char *>(f5_lut_rsqrt) + t * 128;
+  else if (t < 24) p = reinterpret_cast<const char *>(f5_lut_recip) + (t - 16) * 128;
+  else if (t < 33) p = reinterpret_cast<const char *>(f5_lut_exp2) + (t - 24) * 128;
+  else if (t < 42) p = reinterpret_cast<const char *>(f5_lut_sigmoid) + (t - 33) * 128;
+  else if (t < 51) p = reinterpret_cast<const char *>(f5_lut_softplus) + (t - 42) * 128;
+  if (p) asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
 
 // ref/layer_fixed.py:442-467 bf_shift (guard 0)
 F5_DEV int bf_shift(uint64_t m) {

@@ -3,7 +3,7 @@
 // over every SM, replacing the 163-launch per-op chain and its ~6-8 us of
 // launch / drain / ramp cost per dependent kernel.
 //
-// Roles inside each CTA (one CTA per SM, 544 threads):
+// Roles inside each CTA (one CTA per SM, 576 threads):
 //  * producer (one lane of warp 16) walks the step's op list and streams
 //    EVERY weight row this CTA will ever consume, in consumption order,
 //    through a ring of MEGA_STAGE-byte shared-memory stages (cp.async.bulk,
@@ -13,6 +13,12 @@
 //    fills and HBM stays busy.  It also prefetches the CTA's DeltaNet head
 //    state and its attention K / V rows into a scratch region, gated by a
 //    scratch-free mbarrier the consumers arrive on after each use.
+//  * an L2-prefetch warp (warp 17) walks the same op list ahead of the
+//    producer and issues cp.async.bulk.prefetch.L2 over the rows the CTA will
+//    stream next, at most MegaArgs::pf_bytes ahead of the producer's issued
+//    bytes, so HBM keeps streaming into L2 while the smem ring is full and
+//    the consumers sit in a barrier, a prologue or a DeltaNet / attention
+//    core; the ring's TMA fills then read those rows from L2.
 //  * consumers (warps 0-15, named barrier 1) run the ops in order, separated
 //    by grid barriers (global counters, bounded spins): GEMV prologue /
 //    row dot products / epilogues (f5_gemv_core.cuh), the DeltaNet head core
@@ -26,6 +32,18 @@
 // to finish decodes the argmax, advances the step parameters and re-zeroes
 // the barrier counters for the next launch.
 #include <climits>
+
+#include <cuda_runtime.h>
+
+namespace f5 {
+// this op's trace row (consumer thread 0 only), null when not tracing;
+// declared ahead of the shared cores so their phase marks can reach it
+__shared__ unsigned long long *mg_tr;
+}  // namespace f5
+#define F5_PRO_MARK(k)                                     \
+  do {                                                     \
+    if (threadIdx.x == 0 && mg_tr) mg_tr[(k)] = gtimer();  \
+  } while (0)
 
 #include "f5_dn_core.cuh"
 #include "f5_gemv_core.cuh"
@@ -41,8 +59,9 @@ constexpr int MG_RESB = MEGA_RES * 8;
 constexpr unsigned long long MG_WAIT_NS = 1000000000ull;   // 1 s: a safety net only
 using CSync = NamedSync<1, MG_CT>;
 
-// scratch layout: DeltaNet head
-constexpr int DN_SD = 0, DN_QN = 32768, DN_KN = DN_QN + 512, DN_PART = DN_KN + 512, DN_END = DN_PART + 4096;
+// scratch layout: DeltaNet column quarter of a head
+constexpr int DN_SD = 0, DN_QN = 8192, DN_KN = DN_QN + 512, DN_PART = DN_KN + 512, DN_OG = DN_PART + 4096,
+              DN_VZN = DN_OG + 1024, DN_END = DN_VZN + 3 * 32 * 8;
 // scratch layout: attention (K / V fills are 16-byte aligned for cp.async.bulk)
 constexpr int AT_K = 0, AT_V = AT_K + MEGA_SUB * 256, AT_KE = AT_V + MEGA_SUB * 256, AT_VE = AT_KE + MEGA_SUB,
               AT_Q16 = AT_VE + MEGA_SUB, AT_K16 = AT_Q16 + 4 * 256 * 2, AT_K8N = AT_K16 + 4 * 256 * 2,
@@ -225,7 +244,8 @@ __shared__ int mg_meta[4], mg_e[2];
 __shared__ int mg_cnt[6];   // issued fills: [0] ring, [1] sd, [2] sk, [3] sv (producer), [4] sk, [5] sv (consumers)
 __shared__ volatile int mg_abort;
 __shared__ int mg_last;
-__shared__ unsigned long long *mg_tr;   // this op's trace row (thread 0 only), null when not tracing
+__shared__ __align__(16) MegaOp mg_fop;   // the L2 prefetcher's descriptor buffer
+__shared__ volatile long long mg_issued;  // weight bytes the producer has issued (its only writer)
 
 // trace marker k (2..7) of the current op: consumer thread 0 only
 #define MG_MARK(k)                                                   \
@@ -297,13 +317,14 @@ F5_DEV void producer(const MegaArgs &ma, const MegaSmem &S, int T, int pos, cons
         bulk_g2s(dst, sg.w + (size_t)ch.r0 * a.stride, nb, &mg_full[s]);
         if (pair) bulk_g2s(dst + nb, sg.w2 + (size_t)ch.r0 * a.stride, nb, &mg_full[s]);
         mg_cnt[0] = ++issued;
+        mg_issued = mg_issued + (pair ? 2 * nb : nb);
         rp.next(ns);
       }
     } else if (kind == MK_DN) {
-      if (b < ma.dn_heads) {
+      if (b < 4 * ma.dn_heads) {   // head b / 4, column quarter b % 4: one contiguous 8 KB block
         if (n_scr > 0 && !mwait((&mg_bfree), (n_scr - 1) & 1, ab)) { bad = true; break; }
-        mbar_expect_tx((&mg_bsd), 128 * 128 * 2);
-        bulk_g2s(S.scr() + DN_SD, op.d.S + (size_t)b * 128 * 128, 128 * 128 * 2, (&mg_bsd));
+        mbar_expect_tx((&mg_bsd), 8192);
+        bulk_g2s(S.scr() + DN_SD, op.d.S + (size_t)(b >> 2) * 16384 + (size_t)(b & 3) * 4096, 8192, (&mg_bsd));
         mg_cnt[1] += 1;
         ++n_scr;
       }
@@ -326,6 +347,62 @@ F5_DEV void producer(const MegaArgs &ma, const MegaSmem &S, int T, int pos, cons
     }
   }
   if (desc_pending >= 0) mbar_wait(&mg_bpd[desc_pending & 1], (desc_pending >> 1) & 1, MG_WAIT_NS);
+}
+
+// ---------------------------------------------------------------------------
+// L2 prefetcher (warp 17): advisory only -- nothing waits on a prefetch, so
+// it stops at the first sign of trouble and never delays the step's exit
+// ---------------------------------------------------------------------------
+constexpr uint32_t MG_PF_PIECE = 32768;
+
+F5_DEV bool pf_throttle(long long pf, long long lead, const Abort &ab) {
+  unsigned long long t0 = 0;
+  for (uint32_t it = 0; pf - mg_issued > lead; ++it) {
+    __nanosleep(128);
+    if ((it & 63) == 63) {
+      if (ab.raised()) return false;
+      const unsigned long long t = gtimer();
+      if (t0 == 0) t0 = t;
+      else if (t - t0 > MG_WAIT_NS) return false;
+    }
+  }
+  return true;
+}
+
+F5_DEV void prefetcher(const MegaArgs &ma, const Abort &ab) {
+  const int lane = threadIdx.x & 31, G = gridDim.x, b = blockIdx.x;
+  const long long lead = ma.pf_bytes;
+  if (lead <= 0) return;
+  long long pf = 0;
+  for (int oi = 0; oi < ma.nops; ++oi) {
+    __syncwarp();
+    if (lane < (int)(sizeof(MegaOp) / 16))
+      reinterpret_cast<uint4 *>(&mg_fop)[lane] = __ldcg(reinterpret_cast<const uint4 *>(ma.ops + oi) + lane);
+    __syncwarp();
+    if (mg_fop.kind != MK_GEMV) continue;
+    int stop = 0;
+    if (lane == 0) {
+      const GemvArgs &a = mg_fop.g;
+      const int u0 = part_lo(a.total_units, G, b), u1 = part_lo(a.total_units, G, b + 1);
+      for (int si = 0; si < a.nseg && !stop; ++si) {
+        const GemvSeg &sg = a.seg[si];
+        const int sb = sg.unit_begin, se = si + 1 < a.nseg ? a.seg[si + 1].unit_begin : a.total_units;
+        const int lo = max(u0, sb), hi = min(u1, se);
+        if (lo >= hi) continue;
+        const size_t off = (size_t)(lo - sb) * a.stride, len = (size_t)(hi - lo) * a.stride;
+        for (int k = 0; k < (sg.mode == GM_SILU_MUL ? 2 : 1) && !stop; ++k) {
+          const uint8_t *base = (k ? sg.w2 : sg.w) + off;
+          for (size_t p = 0; p < len; p += MG_PF_PIECE) {
+            const uint32_t n = (uint32_t)min((size_t)MG_PF_PIECE, len - p);
+            if (!pf_throttle(pf, lead, ab)) { stop = 1; break; }
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + p), "r"(n) : "memory");
+            pf += n;
+          }
+        }
+      }
+    }
+    if (__shfl_sync(0xffffffffu, stop, 0)) return;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -494,25 +571,137 @@ F5_DEV bool c_gemv_split(const GemvArgs &a, const MegaSmem &S, RingPos &rp, cons
 }
 
 // ---------------------------------------------------------------------------
-// consumers: DeltaNet head (ref/layer_fixed.py:1493-1580)
+// consumers: DeltaNet (ref/layer_fixed.py:1522-1580), one column quarter of a
+// head per CTA (CTAs [0, 4 * heads)).  The recurrence of a state column is
+// independent of the other columns (kv_mem, delta, the rank-1 update and o
+// are all per column), so the quarter runs locally on its 128 x 32 slice;
+// only the head-wide block-float shift and gated norm need all 128 o values,
+// which the four CTAs of a head exchange through marked slots.  Thread
+// (warp w, lane l) owns column 32 q + l, rows 8 w .. 8 w + 7.
 // ---------------------------------------------------------------------------
 F5_DEV bool c_dn(const MegaArgs &ma, const DnArgs &d, const MegaSmem &S, int &w_sd, const Abort &ab) {
-  const int h = blockIdx.x;
-  if (h >= ma.dn_heads) return true;
+  const int b = blockIdx.x;
+  if (b >= 4 * ma.dn_heads) return true;
   const CSync sy;
-  const DnSmem sm = {reinterpret_cast<int16_t *>(S.scr() + DN_SD), reinterpret_cast<int32_t *>(S.scr() + DN_QN),
-                     reinterpret_cast<int32_t *>(S.scr() + DN_KN), reinterpret_cast<long long *>(S.scr() + DN_PART),
-                     mg_red, mg_gate, mg_e};
-  long long qkv[3], zn[2];
-  dn_head_pre<CSync, 4>(sy, d, h, sm, qkv, zn);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int h = b >> 2, qd = b & 3, kh = h / d.vrep;
+  uint8_t *scr = S.scr();
+  int16_t *sd = reinterpret_cast<int16_t *>(scr + DN_SD);   // [128 dk][32]
+  int32_t *qn = reinterpret_cast<int32_t *>(scr + DN_QN), *kn = reinterpret_cast<int32_t *>(scr + DN_KN);
+  long long *part = reinterpret_cast<long long *>(scr + DN_PART);   // [16 warps][32]
+  long long *vzn = reinterpret_cast<long long *>(scr + DN_VZN);     // v, z, norm_w of the quarter
+
+  // ---- every input in one round of loads ----
+  long long qv = 0, kv = 0;
+  if (tid < 128) {
+    qv = __ldcg(d.qkvc + kh * 128 + tid);
+    kv = __ldcg(d.qkvc + d.lkd + kh * 128 + tid);
+  } else if (tid < 160) {
+    const int i = tid - 128, dv = qd * 32 + i;
+    vzn[i] = __ldcg(d.qkvc + 2 * d.lkd + h * 128 + dv);
+    vzn[32 + i] = __ldcg(d.z16 + h * 128 + dv);
+    vzn[64 + i] = __ldcg(d.norm_w + dv);
+  } else if (tid == 160) {
+    mg_gate[0] = __ldcg(d.beta + h);
+    mg_gate[1] = __ldcg(d.decay + h);
+  }
+  // ---- l2norm of q and k (ref/layer_fixed.py:1322-1330) ----
+  const long long ssq = g_sum_split(sy, qv * qv, mg_red);
+  const long long ssk = g_sum_split(sy, kv * kv, mg_red);
+  if (tid == 0) {
+    int64_t r; int e;
+    rsqrt_q((uint64_t)(ssq == 0 ? 1 : ssq), 2 * QKV_F, r, e);
+    mg_gate[2] = r; mg_e[0] = e;
+  } else if (tid == 32) {
+    int64_t r; int e;
+    rsqrt_q((uint64_t)(ssk == 0 ? 1 : ssk), 2 * QKV_F, r, e);
+    mg_gate[3] = r; mg_e[1] = e;
+  }
+  sy.sync();
+  if (tid < 128) {
+    const long long q16 = clip16(rshr(qv * mg_gate[2], QKV_F + 30 - mg_e[0] - NRM_F));
+    qn[tid] = (int32_t)rshr(q16 * 2896, 15);    // round(2^15 / sqrt(128)) = 2896
+    kn[tid] = (int32_t)clip16(rshr(kv * mg_gate[3], QKV_F + 30 - mg_e[1] - NRM_F));
+  }
   MG_MARK(2);
   const bool got = mwait((&mg_bsd), w_sd & 1, ab);
   ++w_sd;
-  if (sy.any(!got)) return false;
+  if (sy.any(!got)) return false;   // also publishes qn, kn, vzn, the gates
   MG_MARK(3);
-  dn_head_rec<CSync, 4>(sy, d, h, sm, qkv, zn);
-  MG_MARK(6);
+
+  // ---- recurrence (ref/layer_fixed.py:1545-1560) ----
+  const int decay = (int)mg_gate[1];
+  long long kvm = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int dk = warp * 8 + i;
+    const int s0 = rshr32p((int32_t)sd[dk * 32 + lane] * decay, GAT_F);   // |S*decay| < 2^30
+    sd[dk * 32 + lane] = (int16_t)s0;
+    kvm += (long long)(s0 * kn[dk]);                                      // |s0 * kn| < 2^30
+  }
+  part[warp * 32 + lane] = kvm;
+  sy.sync();
+  kvm = 0;
+#pragma unroll
+  for (int w = 0; w < MG_CONS; ++w) kvm += part[w * 32 + lane];
+  kvm = rshr(kvm, NRM_F);
+  const long long delta = rshr(((vzn[lane] << (S_F - QKV_F)) - kvm) * mg_gate[0], GAT_F);
+  sy.sync();   // part is reused below
+  long long o = 0;
+  int sat = 0;
+  int16_t *Sg = d.S + (size_t)h * 16384 + (size_t)qd * 4096;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int dk = warp * 8 + i;
+    long long sn = (long long)sd[dk * 32 + lane] + rshr((long long)kn[dk] * delta, NRM_F);
+    if (sn > 32767 || sn < -32767) ++sat;   // |Sh| > 32767 (ref/layer_fixed.py:1557)
+    sn = clip16(sn);
+    Sg[dk * 32 + lane] = (int16_t)sn;
+    o += sn * qn[dk];
+  }
+  if (d.stats && sat) atomicAdd(d.stats, (unsigned long long)sat);
+  part[warp * 32 + lane] = o;
+  sy.sync();
+  MG_MARK(4);
+
+  // ---- the head's 128 o values: publish this quarter, gather all four ----
+  unsigned long long *xsl = d.xslots + (size_t)h * 128 * 2;
+  if (warp == 0) {
+    long long ot = 0;
+#pragma unroll
+    for (int w = 0; w < MG_CONS; ++w) ot += part[w * 32 + lane];
+    slot_put(xsl + (size_t)(qd * 32 + lane) * 2, rshr(ot, NRM_F));
+  }
+  long long ov = 0;
+  bool ok = true;
+  if (tid < 128) ok = slot_get(xsl + (size_t)tid * 2, ov, ab);
+  if (sy.any(!ok)) return false;
+  MG_MARK(5);
+  // ---- block-float k_h (ref/layer_fixed.py:470-486) and the gated norm
+  // (ref/layer_fixed.py:509-546 or 694-781); identical in the four CTAs ----
+  const unsigned long long om = g_max_ull(sy, tid < 128 ? uabs(ov) : 0ull, reinterpret_cast<unsigned long long *>(mg_red));
+  const int kh_shift = bf_shift(om);
+  const long long o16 = clip16(kh_shift >= 0 ? rshr(ov, kh_shift) : (long long)((unsigned long long)ov << (-kh_shift)));
+  long long m;
+  if (d.norm_mode == 0) {
+    // numpy int64 sum of o*o (wrapping modulo 2^64, order-free)
+    const long long ss = (long long)g_sum_ull(sy, (unsigned long long)ov * (unsigned long long)ov,
+                                              reinterpret_cast<unsigned long long *>(mg_red));
+    m = dn_norm_scale(ss, kh_shift, 128);
+  } else {
+    const long long ss = g_sum_ll(sy, o16 * o16, mg_red);
+    m = eps_norm_scale(ss, kh_shift, 7);
+  }
+  if (tid >= qd * 32 && tid < qd * 32 + 32) {
+    const int i = tid - qd * 32;
+    const long long tt = clip16(rshr(o16 * m, 15));
+    const long long nh = clip16(rshr(tt * vzn[64 + i], 14));
+    const long long zg = clip16(silu_q(vzn[32 + i] << (12 - QKV_F)));
+    d.on16[h * 128 + tid] = (int16_t)clip16(rshr(nh * zg, 12));
+  }
+  if (qd == 0 && tid == 0 && d.kh_out) d.kh_out[h] = kh_shift;
   release_scratch(sy, (&mg_bfree));
+  MG_MARK(6);
   return true;
 }
 
@@ -860,6 +1049,7 @@ F5_DEV void consumers(const MegaArgs &ma, const MegaSmem &S, int tok, int T, int
     }
     if (threadIdx.x == 0) mg_tr = tr ? tr + (size_t)oi * MEGA_TRACE_SLOTS : nullptr;
     if (oi + 1 < ma.nops) stage_desc(ma, S, oi + 1);
+    if (threadIdx.x >= 64 && threadIdx.x < 64 + 51) lut_prefetch_l1(threadIdx.x - 64);
     const MegaOp &op = mg_cop[oi & 1];
     if (tr && threadIdx.x == 0) tr[(size_t)oi * MEGA_TRACE_SLOTS] = gtimer();
     bool ok = true;
@@ -900,6 +1090,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega(const __grid_constant_
     mg_abort = 0;
     mg_last = 0;
     mg_tr = nullptr;
+    mg_issued = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   // step parameters: written by the host or by the previous launch only
@@ -909,6 +1100,8 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega(const __grid_constant_
 
   if (warp == MG_CONS) {
     if (lane == 0) producer(ma, S, T, pos, ab);
+  } else if (warp == MG_CONS + 1) {
+    prefetcher(ma, ab);
   } else {
     consumers(ma, S, tok, T, pos, ab);
   }

@@ -59,9 +59,10 @@ struct MegaArgs {
   int dn_heads;     // CTAs [0, dn_heads) run one DeltaNet value head each
   int ns;           // ring stages (from mega_config)
   unsigned long long *trace;   // optional [G][nops][MEGA_TRACE_SLOTS] globaltimer marks
+  long long pf_bytes;          // L2 prefetch lead per CTA in weight bytes (0: off)
 };
 
-constexpr int MEGA_THREADS = 544;       // 16 consumer warps + 1 producer warp
+constexpr int MEGA_THREADS = 576;       // 16 consumer warps + producer warp + L2-prefetch warp
 constexpr int MEGA_STAGE = 33792;       // ring stage: 16 rows of K=4096, 5 of K=12288
 constexpr int MEGA_RES = 256;           // deferred per-CTA row results
 constexpr int MEGA_SUB = 64;            // attention tokens per K/V shared-memory fill

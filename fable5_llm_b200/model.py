@@ -259,8 +259,9 @@ class DecodeModel:
         g = self.geom
         ring = self.read(L.BUF_DN_CONV, layer).reshape(g.CONV_DIM, 4).astype(I64)
         conv = np.stack([ring[:, (T - 3 + j) & 3] for j in range(3)], axis=1)
-        S = self.read(L.BUF_DN_S, layer).reshape(g.LNH, g.LDK, g.LDV)
-        return {"conv": conv, "S": S}
+        # device layout [head][dv // 32][dk][dv % 32] -> reference [head][dk][dv]
+        S = self.read(L.BUF_DN_S, layer).reshape(g.LNH, g.LDV // 32, g.LDK, 32).transpose(0, 2, 1, 3)
+        return {"conv": conv, "S": np.ascontiguousarray(S).reshape(g.LNH, g.LDK, g.LDV)}
 
     def set_dn_state(self, layer, T, cache):
         g = self.geom
@@ -270,7 +271,8 @@ class DecodeModel:
         for j in range(3):
             ring[:, (T - 3 + j) & 3] = conv[:, j]
         self.write(L.BUF_DN_CONV, layer, ring)
-        self.write(L.BUF_DN_S, layer, np.asarray(cache["S"], dtype=np.int16))
+        S = np.asarray(cache["S"], dtype=np.int16).reshape(g.LNH, g.LDK, g.LDV // 32, 32).transpose(0, 2, 1, 3)
+        self.write(L.BUF_DN_S, layer, np.ascontiguousarray(S))
 
     def get_kv(self, layer, T):
         """-> {"k": [[(k8, ke)] * NKV] * T, "v": ...} (ref/layer_fixed.py:1400-1401)"""

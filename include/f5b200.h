@@ -183,7 +183,7 @@ enum f5_vec { F5_VEC_LN1 = 0, F5_VEC_LN2 = 1, F5_VEC_Q_NORM = 2, F5_VEC_K_NORM =
 enum f5_buf { F5_BUF_X16 = 0, F5_BUF_QKV16 = 1, F5_BUF_Z16 = 2, F5_BUF_B16 = 3, F5_BUF_A16 = 4,
               F5_BUF_ON16 = 5, F5_BUF_QG16 = 6, F5_BUF_K16 = 7, F5_BUF_V16 = 8,
               F5_BUF_PROD64 = 9, F5_BUF_PROD16 = 10, F5_BUF_STATS = 11,
-              F5_BUF_DN_S = 12 /* int16 [32][128][128] */, F5_BUF_DN_CONV = 13 /* int16 [8192][4] ring */,
+              F5_BUF_DN_S = 12 /* int16 [32 heads][4][128 dk][32]: dv = 32 * quarter + i */, F5_BUF_DN_CONV = 13 /* int16 [8192][4] ring */,
               F5_BUF_DN_KH = 14, F5_BUF_K8 = 15, F5_BUF_KE = 16, F5_BUF_V8 = 17, F5_BUF_VE = 18,
               F5_BUF_KA = 19, F5_BUF_LOGITS = 20 /* int32 [vocab], see f5_ctx_set_logits */ };
 
