@@ -166,6 +166,40 @@ def cpu_sample_step(seconds=20.0):
 
 
 # ---------------------------------------------------------------------------
+def trace_summary(t, kinds):
+    """Critical-path decomposition of one traced persistent step (us per step):
+    per op, median over CTAs of each phase, summed over the step's ops."""
+    def med(x):
+        x = x[x >= 0]
+        return float(np.median(x)) / 1e3 if x.size else 0.0
+    out = {"rows": 0.0, "prologue": 0.0, "epilogue": 0.0, "barrier": 0.0, "deltanet": 0.0, "attention": 0.0}
+    n = len(kinds)
+    for i, k in enumerate(kinds):
+        T = t[:, i, :]
+        if k in ("dn", "attn"):
+            sel = T[:128] if k == "dn" else T
+            out["deltanet" if k == "dn" else "attention"] += med(sel[:, 1] - sel[:, 0])
+        elif k != "begin":
+            out["prologue"] += med(T[:, 2] - T[:, 0])
+            out["rows"] += med(T[:, 3] - T[:, 2])
+            out["epilogue"] += med(T[:, 1] - T[:, 3])
+        if i + 1 < n:   # end of op i (median CTA) -> start of op i+1 (median CTA)
+            out["barrier"] += (float(np.median(t[:, i + 1, 0])) - float(np.median(T[:, 1]))) / 1e3
+    out["step"] = (float(t[:, -1, 1].max()) - float(t[:, 0, 0].min())) / 1e3
+    return {k: round(v, 1) for k, v in out.items()}
+
+
+def mega_traffic():
+    """DRAM bytes per persistent-kernel launch from the committed ncu summary
+    (profiles/k_mega_traffic.json), or None when no capture was made."""
+    p = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", "k_mega_traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return None
+
+
 def split_rows(nrows, nch):
     """Contiguous row split, first nrows % nch channels +1 row
     (ref/seq_format.py:1177-1189)."""
@@ -316,7 +350,14 @@ def run_step(args, ws, rank, local):
         tt = torch.tensor([e2e_ms], device="cuda")
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
         e2e_ms = float(tt.item())
-    # per-kernel device time (events around every launch of one eager step)
+    engine = m.engine()
+    # in-kernel phase decomposition of one persistent step (device globaltimer)
+    phases = None
+    if engine == "persistent":
+        t, kinds = m.trace_step()
+        phases = trace_summary(t, kinds)
+    # the graph engine for reference: its per-kernel device time (events
+    # around every launch of one eager step)
     kt = m.time_step(3)
     gemv_gbs = kt["gemv_bytes"] / (kt["gemv_ms"] * 1e-3) / 1e9
     cpu = None
@@ -324,6 +365,27 @@ def run_step(args, ws, rank, local):
         cpu = cpu_sample_step(seconds=20.0)
     if rank == 0:
         toks = 1000.0 / ms * ws
+        step_gbs = WEIGHT_BYTES_9B / (ms * 1e-3) / 1e9
+        tr = mega_traffic() if engine == "persistent" else None
+        if engine == "persistent":
+            roof = {"bound": "hbm", "achieved": round(step_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                    "frac": round(step_gbs / hbm_peak, 4),
+                    "traffic": tr["dram_bytes_per_launch"] if tr else None,
+                    "kernel": "k_mega (persistent decode step, 1 launch per token): 4,091,805,696 algorithmic "
+                              "W4 bytes per launch / CUDA-event time per launch",
+                    "peak_kind": peak_kind, "phases_us_per_step": phases,
+                    "rows_phase_gbs": round(WEIGHT_BYTES_9B / (phases["rows"] * 1e-6) / 1e9, 1)
+                    if phases and phases["rows"] > 0 else None,
+                    "traffic_source": tr.get("source") if tr else None}
+        else:
+            roof = {"bound": "hbm", "achieved": round(gemv_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                    "frac": round(gemv_gbs / hbm_peak, 4), "traffic": None,
+                    "kernel": "k_gemv: algorithmic W4 bytes per launch / CUDA-event launch time",
+                    "peak_kind": peak_kind}
+        roof["graph_engine"] = {"gemv_gbs": round(gemv_gbs, 1), "gemv_frac": round(gemv_gbs / hbm_peak, 4),
+                                "kernel_ms_per_step": {k: round(v, 4) for k, v in kt.items() if k.endswith("_ms")},
+                                "launches_per_step": int(kt["launches"])}
+        launches = 1 if engine == "persistent" else int(kt["launches"])
         line = {
             "metric": "9B W4A8 decode tok/s", "value": round(toks, 2), "unit": "tok/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
@@ -331,23 +393,20 @@ def run_step(args, ws, rank, local):
             "vs_baseline": round(toks / FPGA_TOKS, 2), "dtype": "int4xint8->int32/int64",
             "data": "synthetic (seeded int4 W4 images and integer vectors, Qwen3.5-9B shapes)",
             "config": {"workload": f"full 32-layer integer decode step + 248,320-row LM head argmax at "
-                                   f"context {ctx_len}, greedy device-fed, one CUDA graph per step",
+                                   f"context {ctx_len}, greedy device-fed, " +
+                                   ("one persistent-kernel launch per step" if engine == "persistent"
+                                    else "one CUDA graph per step"),
+                       "engine": engine,
                        "model": "Qwen3.5-9B (24 DeltaNet + 8 attention layers), synthetic int4",
                        "global_batch": ws, "seq_len": ctx_len, "weight_bytes_per_token": WEIGHT_BYTES_9B,
                        "l2": "inputs larger than L2 (4.09 GB of weights streamed per step)",
                        "parallelism": f"{ws} independent replicas" if ws > 1 else "single GPU",
-                       "launches_per_step": int(kt["launches"])},
-            "roofline": {"bound": "hbm", "achieved": round(gemv_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
-                         "frac": round(gemv_gbs / hbm_peak, 4), "traffic": None,
-                         "kernel": "k_gemv: algorithmic W4 bytes per launch / CUDA-event launch time",
-                         "peak_kind": peak_kind,
-                         "step_weight_gbs": round(WEIGHT_BYTES_9B / (ms * 1e-3) / 1e9, 1),
-                         "step_frac": round(WEIGHT_BYTES_9B / (ms * 1e-3) / 1e9 / hbm_peak, 4),
-                         "kernel_ms_per_step": {k: round(v, 4) for k, v in kt.items() if k.endswith("_ms")}},
+                       "launches_per_step": launches},
+            "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": {"value": round(1000.0 / e2e_ms * ws, 2), "unit": "tok/s", "h2d_bytes_per_step": 32,
                     "d2h_bytes_per_step": 32},
-            "gpu_launches": int(kt["launches"]) * args.steps,
+            "gpu_launches": launches * args.steps,
             "clocks": ck, "context_tokens_after": T,
         }
         print(json.dumps(line), flush=True)

@@ -601,8 +601,10 @@ static int build_mega(f5_ctx *c, bool &unsupported) {
   m.advance = 1;
   m.dn_heads = LNH;
   m.ns = ns;
-  // L2 prefetch lead per CTA (F5_MEGA_PREFETCH_KB overrides; 0 disables)
-  long long pf_kb = 256;
+  // L2 prefetch lead per CTA: off by default (a sweep of 128 KB - 1 MB
+  // leads measured no gain: the TMA ring refills from L2 barely faster than
+  // from HBM); F5_MEGA_PREFETCH_KB sets it for experiments
+  long long pf_kb = 0;
   if (const char *ev = getenv("F5_MEGA_PREFETCH_KB")) pf_kb = atoll(ev);
   m.pf_bytes = pf_kb * 1024;
   c->mega_dirty = false;

@@ -3,6 +3,7 @@
 // per-CTA prologues that quantize the input vector, and the epilogues.
 // The law and the memory layout are described in f5_gemv.cu.
 #pragma once
+#include <climits>
 #include "f5_block.cuh"
 #include "f5_kernels.cuh"
 #include "f5_tma.cuh"
@@ -82,11 +83,28 @@ F5_DEV void put8(uint2 *xs, int b, const long long x[8]) {
   xs[(((b >> 7) << 2) + (b & 3)) * 32 + ((b >> 2) & 31)] = make_uint2(ev, od);
 }
 
-// rmsnorm_fx element (ref/layer_fixed.py:1242-1278): clip33(rshr(x*r, 30-e)) * gain
+// rmsnorm_fx element (ref/layer_fixed.py:1242-1278): clip16(rshr(clip33(
+// rshr(x*r, 30-e)) * gain, 14)).  Fast form for the prologue: x is int16,
+// 0 < r < 2^31 (rsqrt_q), s = 30 - e >= 1 and |gain| < 2^31.  Clamping the
+// intermediate to int32 instead of 33 bits is exact: any |y| >= 2^31 with a
+// nonzero gain gives |y * gain| >= 2^31, which clip16 saturates either way
+// with the same sign (gain 0 gives 0 either way).
 F5_DEV long long rms_elem(long long x, long long r, int e, long long gain) {
   long long y = rshr(x * r, 30 - e);
   y = clip(y, -(1ll << 32), (1ll << 32) - 1);
   return clip16(rshr(y * gain, 14));
+}
+F5_DEV int32_t rms_elem32(int32_t x, int32_t r, int s, int32_t gain) {
+  const long long v = (long long)x * r;                        // |v| < 2^46
+  const unsigned long long av = (unsigned long long)(v < 0 ? -v : v);
+  const unsigned long long q = (av + (1ull << (s - 1))) >> s;  // rshr of |v|, half away from zero
+  const long long yq = q > 0x7FFFFFFFull ? 0x80000000ll : (long long)q;
+  const int32_t y = (int32_t)(v < 0 ? (yq > 0x7FFFFFFFll ? INT32_MIN : -(int32_t)yq) : (yq > 0x7FFFFFFFll ? INT32_MAX : (int32_t)yq));
+  const long long t = (long long)y * gain;                     // |t| < 2^62
+  const unsigned long long at = (unsigned long long)(t < 0 ? -t : t);
+  const unsigned long long u = (at + 8192) >> 14;
+  const long long c = u > 32768ull ? 32768 : (long long)u;
+  return (int32_t)(t < 0 ? -c : (c > 32767 ? 32767 : c));
 }
 
 // element j (0..7) of 8 int16 packed in a uint4
@@ -232,9 +250,13 @@ F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red,
           s_meta[2] = e;
         }
         sy.sync();
+        F5_PRO_MARK(6);
         const long long r = *s_r;
         const int e = s_meta[2];
-        const long long add1 = P.one_plus ? (1 << 14) : 0;
+        const int add1 = P.one_plus ? (1 << 14) : 0;
+        // fast path when rsqrt's r and shift are in rms_elem32's domain (always
+        // for int16 inputs of H = 4096); the general law otherwise
+        const bool fast = r > 0 && r < (1ll << 31) && 30 - e >= 1 && 30 - e <= 62;
 #pragma unroll
         for (int j = 0; j < MAXB; ++j) {
           const int wv[8] = {wl[j][0].x, wl[j][0].y, wl[j][0].z, wl[j][0].w,
@@ -242,8 +264,14 @@ F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red,
           uint32_t pk[4];
 #pragma unroll
           for (int k = 0; k < 8; k += 2) {
-            const long long x0 = rms_elem(get16(raw[j], k), r, e, wv[k] + add1);
-            const long long x1 = rms_elem(get16(raw[j], k + 1), r, e, wv[k + 1] + add1);
+            int32_t x0, x1;
+            if (fast) {
+              x0 = rms_elem32(get16i(raw[j], k), (int32_t)r, 30 - e, wv[k] + add1);
+              x1 = rms_elem32(get16i(raw[j], k + 1), (int32_t)r, 30 - e, wv[k + 1] + add1);
+            } else {
+              x0 = (int32_t)rms_elem(get16(raw[j], k), r, e, (long long)wv[k] + add1);
+              x1 = (int32_t)rms_elem(get16(raw[j], k + 1), r, e, (long long)wv[k + 1] + add1);
+            }
             pk[k >> 1] = ((uint32_t)x0 & 0xFFFFu) | ((uint32_t)x1 << 16);
           }
           raw[j] = make_uint4(pk[0], pk[1], pk[2], pk[3]);   // normalised, int16
