@@ -87,54 +87,62 @@ struct NamedSync {
 
 // Sum over the group of per-thread values |v| < 2^40 with two 32-bit
 // redux.sync adds per warp (v = hi * 2^22 + lo, lo in [0, 2^22)): exact.
+// The cross-warp stage of every group reduction below is parallel: after
+// the partials are published, each warp reads them one per lane (lanes
+// beyond the warp count read the identity) and reduces them itself, instead
+// of a serial loop over the partials on every thread's dependency chain.
+F5_DEV long long warp_sum_s64(long long v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
 template <class SY>
 F5_DEV long long g_sum_split(const SY &sy, long long v, long long *red) {
   const unsigned slo = __reduce_add_sync(0xffffffffu, (unsigned)v & 0x3FFFFFu);
   const int shi = __reduce_add_sync(0xffffffffu, (int)(v >> 22));
   const long long w = ((long long)shi << 22) + (long long)slo;
-  const int wi = sy.tid() >> 5, nw = sy.n() >> 5;
+  const int wi = sy.tid() >> 5, nw = sy.n() >> 5, lane = sy.tid() & 31;
   sy.sync();
-  if ((sy.tid() & 31) == 0) red[wi] = w;
+  if (lane == 0) red[wi] = w;
   sy.sync();
-  long long t = 0;
-  for (int i = 0; i < nw; ++i) t += red[i];
-  return t;
+  // warp partials are < 2^45 in magnitude (32 lanes of < 2^40): split again
+  const long long p = lane < nw ? red[lane] : 0;
+  const unsigned plo = __reduce_add_sync(0xffffffffu, (unsigned)p & 0x3FFFFFu);
+  const long long phi = warp_sum_s64(p >> 22);
+  return (phi << 22) + (long long)plo;
 }
 // Max over the group of 32-bit unsigned values (redux.sync.max per warp).
 template <class SY>
 F5_DEV unsigned g_max_u32(const SY &sy, unsigned v, long long *red) {
   v = __reduce_max_sync(0xffffffffu, v);
-  const int wi = sy.tid() >> 5, nw = sy.n() >> 5;
+  const int wi = sy.tid() >> 5, nw = sy.n() >> 5, lane = sy.tid() & 31;
   sy.sync();
-  if ((sy.tid() & 31) == 0) red[wi] = v;
+  if (lane == 0) red[wi] = v;
   sy.sync();
-  unsigned t = 0;
-  for (int i = 0; i < nw; ++i) t = (unsigned)red[i] > t ? (unsigned)red[i] : t;
-  return t;
+  return __reduce_max_sync(0xffffffffu, lane < nw ? (unsigned)red[lane] : 0u);
 }
 
 template <class SY>
 F5_DEV long long g_sum_ll(const SY &sy, long long v, long long *red) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int w = sy.tid() >> 5, nw = sy.n() >> 5;
+  v = warp_sum_s64(v);
+  const int w = sy.tid() >> 5, nw = sy.n() >> 5, lane = sy.tid() & 31;
   sy.sync();
-  if ((sy.tid() & 31) == 0) red[w] = v;
+  if (lane == 0) red[w] = v;
   sy.sync();
-  long long t = 0;
-  for (int i = 0; i < nw; ++i) t += red[i];
-  return t;
+  return warp_sum_s64(lane < nw ? red[lane] : 0);
 }
 template <class SY>
 F5_DEV unsigned long long g_sum_ull(const SY &sy, unsigned long long v, unsigned long long *red) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int w = sy.tid() >> 5, nw = sy.n() >> 5;
+  const int w = sy.tid() >> 5, nw = sy.n() >> 5, lane = sy.tid() & 31;
   sy.sync();
-  if ((sy.tid() & 31) == 0) red[w] = v;
+  if (lane == 0) red[w] = v;
   sy.sync();
-  unsigned long long t = 0;
-  for (int i = 0; i < nw; ++i) t += red[i];
+  unsigned long long t = lane < nw ? red[lane] : 0ull;   // wrapping sums: order-free modulo 2^64
+#pragma unroll
+  for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
   return t;
 }
 template <class SY>
@@ -144,12 +152,16 @@ F5_DEV unsigned long long g_max_ull(const SY &sy, unsigned long long v, unsigned
     const unsigned long long t = __shfl_xor_sync(0xffffffffu, v, o);
     v = t > v ? t : v;
   }
-  const int w = sy.tid() >> 5, nw = sy.n() >> 5;
+  const int w = sy.tid() >> 5, nw = sy.n() >> 5, lane = sy.tid() & 31;
   sy.sync();
-  if ((sy.tid() & 31) == 0) red[w] = v;
+  if (lane == 0) red[w] = v;
   sy.sync();
-  unsigned long long t = 0;
-  for (int i = 0; i < nw; ++i) t = red[i] > t ? red[i] : t;
+  unsigned long long t = lane < nw ? red[lane] : 0ull;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const unsigned long long u = __shfl_xor_sync(0xffffffffu, t, o);
+    t = u > t ? u : t;
+  }
   return t;
 }
 

@@ -150,6 +150,18 @@ struct f5_ctx {
   size_t mega_smem = 0;
   std::vector<f5::MegaOp> *emit = nullptr;   // enqueue_step in emit mode
   int emit_err = 0;
+  int emit_nbar = 0;
+  // dataflow-tagged twins (uint32 words) of the activation buffers the
+  // persistent program passes between ops, and each twin's last writer op
+  struct Twin {
+    void *plain;
+    size_t plain_bytes, elem;
+    uint32_t *tagged;
+    int last_op1;
+  };
+  std::vector<Twin> twins;
+  uint32_t *twin_mem = nullptr;
+  size_t twin_bytes = 0;
   std::vector<void *> allocs;
 };
 
@@ -270,11 +282,41 @@ static GemvSeg mkseg(const DevMat &m, void *out, int mode, int out_f, const DevM
   return s;
 }
 
-static void emit_op(f5_ctx *c, MegaOp &op) {
-  // every op waits for the previous one on grid barrier (index - 1); the
-  // persistent kernel relies on this numbering
-  op.bar = c->emit->empty() ? -1 : (int)c->emit->size() - 1;
+// Ops whose inputs are all dataflow-tagged run without a grid barrier; the
+// op after BEGIN (which also clears the step's slots and sums) and the
+// attention out-projection (its input sums are atomics) take one.
+static void emit_op(f5_ctx *c, MegaOp &op, bool need_bar) {
+  op.bar = need_bar ? c->emit_nbar++ : -1;
   c->emit->push_back(op);
+}
+
+// the tagged twin of a plain activation pointer (nullptr if none)
+static f5_ctx::Twin *twin_of(f5_ctx *c, const void *p, uint32_t **tp) {
+  for (f5_ctx::Twin &t : c->twins) {
+    const char *b = static_cast<const char *>(t.plain), *q = static_cast<const char *>(p);
+    if (q >= b && q < b + t.plain_bytes) {
+      if (tp) *tp = t.tagged + (q - b) / t.elem;
+      return &t;
+    }
+  }
+  return nullptr;
+}
+// writer side: route a segment's output to the twin, tagged by op index idx
+static void tag_output(f5_ctx *c, void *&out, int idx) {
+  uint32_t *tp;
+  f5_ctx::Twin *t = twin_of(c, out, &tp);
+  if (!t) return;
+  out = tp;
+  t->last_op1 = idx + 1;
+}
+// reader side: route an input to the twin; returns its writer's tag (op1)
+template <class P>
+static int tag_input(f5_ctx *c, P *&in) {
+  uint32_t *tp;
+  f5_ctx::Twin *t = twin_of(c, in, &tp);
+  if (!t) return 0;
+  in = reinterpret_cast<P *>(tp);
+  return t->last_op1;
 }
 
 static cudaError_t gemv(f5_ctx *c, const GemvSeg *segs, int nseg, int K, const GemvPrologue &pro,
@@ -314,10 +356,27 @@ static cudaError_t gemv(f5_ctx *c, const GemvSeg *segs, int nseg, int K, const G
         (K == 12288 && (paired || argmax)) || (!argmax && per_cta * res_per_unit > MEGA_RES) ||
         a.rows_per_stage < 2)
       c->emit_err = 1;
+    // dataflow tags: the prologue's input from its twin (tagged by its last
+    // writer), then this op's outputs to their twins
+    const int idx = (int)c->emit->size();
+    if (a.pro.mode == PRO_RMSNORM || a.pro.mode == PRO_DYNQ8) a.pro.tag_op1 = tag_input(c, a.pro.src);
+    else if (a.pro.mode == PRO_ATTN_ACC) a.pro.tag_op1 = tag_input(c, a.pro.src2);
+    for (int i = 0; i < nseg; ++i) {
+      GemvSeg &sg = a.seg[i];
+      switch (sg.mode) {
+        case GM_TO16: case GM_RESID: case GM_SILU_MUL:
+          if (twin_of(c, sg.out, nullptr)) { tag_output(c, sg.out, idx); sg.tag_op1 = idx + 1; }
+          break;
+        case GM_CONV: case GM_GATE_B: case GM_GATE_A:
+          if (twin_of(c, sg.aux_out, nullptr)) { tag_output(c, sg.aux_out, idx); sg.tag_op1 = idx + 1; sg.out = nullptr; }
+          break;
+        default: break;
+      }
+    }
     MegaOp op = {};
     op.kind = MK_GEMV;
     op.g = a;
-    emit_op(c, op);
+    emit_op(c, op, idx == 1 || a.pro.mode == PRO_ATTN_ACC);
     return cudaSuccess;
   }
   tl_begin(c);
@@ -375,10 +434,21 @@ static cudaError_t enqueue_layer(f5_ctx *c, int li, bool pdl) {
       d.xslots = reinterpret_cast<unsigned long long *>(
           reinterpret_cast<uint8_t *>(c->d_attacc) + n_attn_layers(c) * att_acc_bytes(c->mega_grid / NKV) +
           (size_t)n_dn * DN_XSLOT_BYTES);
+      const int idx = (int)c->emit->size();
+      d.in_tag_op1 = tag_input(c, d.qkvc);
+      tag_input(c, d.z16);
+      tag_input(c, d.beta);
+      tag_input(c, d.decay);
+      void *on = d.on16;
+      tag_output(c, on, idx);
+      if (on != (void *)d.on16) {
+        d.on16 = static_cast<int16_t *>(on);
+        d.out_tag_op1 = idx + 1;
+      }
       MegaOp op = {};
       op.kind = MK_DN;
       op.d = d;
-      emit_op(c, op);
+      emit_op(c, op, false);
     } else {
       tl_begin(c);
       e = launch_dn_step(d, LNH, c->st, pdl);
@@ -416,7 +486,10 @@ static cudaError_t enqueue_layer(f5_ctx *c, int li, bool pdl) {
       op.at.a.chunk_max = (((c->cfg.max_T + cpg - 1) / cpg) + 15) & ~15;
       op.at.slots = reinterpret_cast<unsigned long long *>(acc);
       op.at.gacc = reinterpret_cast<int32_t *>(acc + (size_t)2 * NKV * cpg * 4 * 2 * 8);
-      emit_op(c, op);
+      op.at.in_tag_op1 = tag_input(c, op.at.a.qg16);
+      tag_input(c, op.at.a.k16);
+      tag_input(c, op.at.a.v16);
+      emit_op(c, op, false);
       p2.mode = PRO_ATTN_ACC;
       p2.src = op.at.gacc;
       p2.src2 = c->qg16;
@@ -458,7 +531,10 @@ static cudaError_t enqueue_step(f5_ctx *c, bool pdl) {
     op.b.key = c->key;
     op.b.zero = c->d_attacc;
     op.b.zero_n = (int)(step_acc_bytes(c, c->mega_grid / NKV) / 16);
-    emit_op(c, op);
+    void *xt = c->x16;
+    tag_output(c, xt, 0);   // BEGIN writes the tagged residual as op 0
+    op.b.x16t = xt != (void *)c->x16 ? static_cast<uint32_t *>(xt) : nullptr;
+    emit_op(c, op, false);
   } else {
     StepParams *p = c->params;
     const int16_t *emb = c->emb;
@@ -574,18 +650,42 @@ static int build_mega(f5_ctx *c, bool &unsupported) {
     F5_ALLOC(c, c->d_attacc, step_acc_bytes(c, cpg) + 16);
     unsupported = true;
   }
+  if (!c->twin_mem) {
+    struct { void *p; size_t bytes, elem; } tw[] = {
+        {c->x16, H * 2, 2}, {c->qkvc16, CONV_DIM * 2, 2}, {c->z16, LVD * 2, 2}, {c->gates, 2 * LNH * 4, 4},
+        {c->on16, LVD * 2, 2}, {c->prod16, FFN * 2, 2}, {c->qg16, NQ * HD * 2 * 2, 2}, {c->k16, NKV * HD * 2, 2},
+        {c->v16, NKV * HD * 2, 2}};
+    size_t words = 0;
+    for (auto &t : tw) words += t.bytes / t.elem;
+    unsupported = false;
+    F5_ALLOC(c, c->twin_mem, words * 4);
+    c->twin_bytes = words * 4;
+    words = 0;
+    for (auto &t : tw) {
+      c->twins.push_back({t.p, t.bytes, t.elem, c->twin_mem + words, 0});
+      words += t.bytes / t.elem;
+    }
+    unsupported = true;
+  }
+  for (f5_ctx::Twin &t : c->twins) t.last_op1 = 0;
   std::vector<MegaOp> ops;
   c->emit = &ops;
   c->emit_err = 0;
+  c->emit_nbar = 0;
   e = enqueue_step(c, false);
   c->emit = nullptr;
   if (e != cudaSuccess) return cuda_status(e, "emit persistent program");
   if (c->emit_err) return set_error(F5_ESTATE, "a GEMV of this model does not fit the persistent engine");
-  const int nbars = (int)ops.size() - 1 + 2;   // grid barriers, abort flag, final arrivals
+  if (ops.size() > 256) return set_error(F5_ESTATE, "persistent program of %zu ops (dataflow tags index < 256)", ops.size());
+  const int nbars = c->emit_nbar + 2;   // grid barriers, abort flag, final arrivals
+  for (MegaOp &op : ops)
+    if (op.kind == MK_GEMV) op.g.abort_flag = nullptr;   // patched below once the barrier array exists
   unsupported = false;
   free_mega(c);
   F5_CU(cudaMalloc(&c->d_ops, ops.size() * sizeof(MegaOp)), "persistent program");
   F5_CU(cudaMalloc(&c->d_bars, (size_t)nbars * 4), "persistent barriers");
+  for (MegaOp &op : ops)
+    if (op.kind == MK_GEMV) op.g.abort_flag = c->d_bars + nbars - 2;
   F5_CU(cudaMemcpyAsync(c->d_ops, ops.data(), ops.size() * sizeof(MegaOp), cudaMemcpyHostToDevice, c->st),
         "persistent program");
   F5_CU(cudaMemsetAsync(c->d_bars, 0, (size_t)nbars * 4, c->st), "persistent barriers");
@@ -638,7 +738,11 @@ static int finish_host(f5_ctx *c, const char *what) {
   F5_CU(cudaMemcpyAsync(c->h_params, c->params, sizeof(StepParams), cudaMemcpyDeviceToHost, c->st), what);
   F5_CU(cudaStreamSynchronize(c->st), what);
   if (c->h_params->err & DERR_Y32_OVERFLOW) return set_error(F5_EOVERFLOW, "%s: y32 overflow (ref/w4a8_ref.py:288)", what);
-  if (c->h_params->err & DERR_TIMEOUT) return set_error(F5_ETIMEOUT, "%s: a bounded device wait gave up", what);
+  if (c->h_params->err & DERR_TIMEOUT) {
+    // an aborted persistent step may leave tagged words half written
+    if (c->twin_mem) cudaMemsetAsync(c->twin_mem, 0, c->twin_bytes, c->st);
+    return set_error(F5_ETIMEOUT, "%s: a bounded device wait gave up", what);
+  }
   if (c->h_params->err & DERR_KV_FULL) return set_error(F5_ESTATE, "%s: KV cache full or position outside the RoPE table", what);
   if (c->h_params->err & DERR_RANGE) return set_error(F5_EINVAL, "%s: token id outside the vocabulary", what);
   return F5_OK;
@@ -839,6 +943,7 @@ int f5_ctx_reset(f5_ctx *c) {
     }
   }
   F5_CU(cudaMemsetAsync(c->params, 0, sizeof(StepParams), c->st), "reset");
+  if (c->twin_mem) F5_CU(cudaMemsetAsync(c->twin_mem, 0, c->twin_bytes, c->st), "reset");
   F5_CU(cudaMemsetAsync(c->err, 0, 4, c->st), "reset");
   F5_CU(cudaMemsetAsync(c->stats, 0, 8, c->st), "reset");
   F5_CU(cudaStreamSynchronize(c->st), "reset");

@@ -16,6 +16,7 @@ struct DnArgs {
   const int32_t *norm_w;  // [LDV] (Q14)
   int16_t *S;             // [LNH][4][LDK][32] int16 state (Q.S_F): head, dv / 32, dk, dv % 32
   unsigned long long *xslots;  // persistent kernel: [LNH][128][2] marked o values (zeroed per step)
+  int in_tag_op1, out_tag_op1; // persistent kernel: dataflow tags of qkvc/z/beta/decay and of on16
   int16_t *on16;          // [LVD] out: clip16(on), Q.DN_NORM_F
   int *kh_out;            // optional [LNH] block-float shifts k_h
   unsigned long long *stats;  // optional: state saturation count

@@ -17,6 +17,52 @@
 
 namespace f5 {
 
+// ---- dataflow-tagged activation words (see StepParams / mega_epoch) ----
+F5_DEV uint32_t mk_tag(uint32_t epoch, int op1) { return (epoch << 8) | ((uint32_t)(op1 - 1) & 0xFFu); }
+F5_DEV uint32_t tag_word(uint32_t tag, int32_t v) { return (tag << 16) | ((uint32_t)v & 0xFFFFu); }
+F5_DEV int32_t tag_s16(uint32_t w) { return (int32_t)(int16_t)(w & 0xFFFFu); }
+
+// Bounded poll until the n words at p (n = 1, 2 or 8; 16-byte aligned for 8)
+// all carry `tag`; reads at L2.  Gives up after 1 s (or once the kernel's
+// abort flag is up, polled every ~20 us), then raises DERR_TIMEOUT and the
+// abort flag; the caller carries on with whatever it read.
+template <int N>
+F5_DEV bool ld_tagged(const uint32_t *p, uint32_t tag, uint32_t (&w)[N], unsigned *abortf, uint32_t *err) {
+  unsigned long long t0 = 0, tpoll = 0;
+  for (uint32_t it = 0;; ++it) {
+    if (N == 8) {
+      const uint4 a = __ldcg(reinterpret_cast<const uint4 *>(p)), b = __ldcg(reinterpret_cast<const uint4 *>(p) + 1);
+      w[0] = a.x; w[1 % N] = a.y; w[2 % N] = a.z; w[3 % N] = a.w;
+      w[4 % N] = b.x; w[5 % N] = b.y; w[6 % N] = b.z; w[7 % N] = b.w;
+    } else if (N == 2) {
+      const uint2 a = __ldcg(reinterpret_cast<const uint2 *>(p));
+      w[0] = a.x; w[1 % N] = a.y;
+    } else {
+      w[0] = __ldcg(p);
+    }
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < N; ++i) ok &= (w[i] >> 16) == tag;
+    if (ok) return true;
+    if ((it & 7) == 7) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t0 == 0) {
+        t0 = t;
+        tpoll = t + 20000;
+      } else if (t >= tpoll) {
+        if (abortf && *reinterpret_cast<volatile unsigned *>(abortf)) return false;
+        if (t - t0 > 1000000000ull) {
+          atomicOr(err, DERR_TIMEOUT);
+          if (abortf) atomicExch(abortf, 1u);
+          return false;
+        }
+        tpoll = t + 20000;
+      }
+    }
+  }
+}
+
 F5_DEV uint4 ld_stream16(const uint8_t *p) {
   uint4 v;
   asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -212,11 +258,15 @@ F5_DEV long long row_dot4096(const uint8_t *row, int lane, const uint2 (&xr)[4][
 // Redundant per-CTA computation of the GEMV's quantized input (see GemvPro).
 // Every value is read from global memory once and held in registers across
 // the reduction passes (MAXB 8-element blocks per thread).
+// `epoch` != 0 with P.tag_op1 != 0: the input vector is dataflow-tagged
+// (persistent kernel) and each thread polls its words until they are ready.
 template <int MAXB, class SY>
-F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red, long long *s_r, int *s_meta) {
+F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red, long long *s_r, int *s_meta,
+                     uint32_t epoch = 0) {
   const int tid = sy.tid(), BT = sy.n(), K = a.K, nblk = K >> 3;
   const GemvPrologue &P = a.pro;
   const bool store = (P.xq_out.x8 != nullptr) && blockIdx.x == 0;
+  const uint32_t in_tag = (epoch && P.tag_op1) ? mk_tag(epoch, P.tag_op1) : 0u;
   long long q[8];
   if (P.mode == PRO_RMSNORM || P.mode == PRO_DYNQ8) {
     const int16_t *src = static_cast<const int16_t *>(P.src);
@@ -224,7 +274,16 @@ F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red,
 #pragma unroll
     for (int j = 0; j < MAXB; ++j) {
       const int b = tid + j * BT;
-      raw[j] = b < nblk ? __ldcg(reinterpret_cast<const uint4 *>(src + 8 * b)) : make_uint4(0, 0, 0, 0);
+      if (b >= nblk) {
+        raw[j] = make_uint4(0, 0, 0, 0);
+      } else if (in_tag) {
+        uint32_t w[8];
+        ld_tagged<8>(static_cast<const uint32_t *>(P.src) + 8 * b, in_tag, w, a.abort_flag, a.err);
+        raw[j] = make_uint4((w[0] & 0xFFFFu) | (w[1] << 16), (w[2] & 0xFFFFu) | (w[3] << 16),
+                            (w[4] & 0xFFFFu) | (w[5] << 16), (w[6] & 0xFFFFu) | (w[7] << 16));
+      } else {
+        raw[j] = __ldcg(reinterpret_cast<const uint4 *>(src + 8 * b));
+      }
     }
     if constexpr (MAXB <= 2) {
       if (P.mode == PRO_RMSNORM) {     // ref/layer_fixed.py:1242-1278 (H = 4096)
@@ -321,8 +380,16 @@ F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red,
         const int4 a0 = __ldcg(reinterpret_cast<const int4 *>(static_cast<const int32_t *>(P.src) + 8 * b));
         const int4 a1 = __ldcg(reinterpret_cast<const int4 *>(static_cast<const int32_t *>(P.src) + 8 * b + 4));
         const int i0 = 8 * b, hq = i0 >> 8, d0 = i0 & 255;
-        const uint4 gr = __ldcg(reinterpret_cast<const uint4 *>(static_cast<const int16_t *>(P.src2) +
-                                                                 (size_t)hq * 512 + 256 + d0));
+        uint4 gr;
+        if (in_tag) {   // tagged q|gate words (ordered by the grid barrier before this op)
+          uint32_t w[8];
+          ld_tagged<8>(static_cast<const uint32_t *>(P.src2) + (size_t)hq * 512 + 256 + d0, in_tag, w, a.abort_flag,
+                       a.err);
+          gr = make_uint4((w[0] & 0xFFFFu) | (w[1] << 16), (w[2] & 0xFFFFu) | (w[3] << 16),
+                          (w[4] & 0xFFFFu) | (w[5] << 16), (w[6] & 0xFFFFu) | (w[7] << 16));
+        } else {
+          gr = __ldcg(reinterpret_cast<const uint4 *>(static_cast<const int16_t *>(P.src2) + (size_t)hq * 512 + 256 + d0));
+        }
         const int av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
         for (int k = 0; k < 8; ++k) v[j][k] = (long long)av[k] * sigmoid_q(get16(gr, k) << (12 - QKV_F));
@@ -376,8 +443,26 @@ F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red,
 // ---------------------------------------------------------------------------
 // Epilogues (ref/layer_fixed.py:1224-1236 matvec_to and its call sites)
 // ---------------------------------------------------------------------------
+// conv4 + SiLU of one channel (ref/layer_fixed.py:1511-1520): ring word rw
+// holds the 4 int16 slots, cw the 4 weights, v this step's pre-conv input
+F5_DEV int32_t conv_silu(long long v, uint2 rw, int4 cw, int T) {
+  const int16_t r4[4] = {(int16_t)(rw.x & 0xFFFFu), (int16_t)(rw.x >> 16), (int16_t)(rw.y & 0xFFFFu),
+                         (int16_t)(rw.y >> 16)};
+  const long long acc = (long long)r4[(T + 1) & 3] * cw.x + (long long)r4[(T + 2) & 3] * cw.y +
+                        (long long)r4[(T + 3) & 3] * cw.z + v * cw.w;
+  const long long pre = clip(rshr(acc, RS_F + CW_F - 12), -(1 << 20), (1 << 20) - 1);
+  const long long co = clip16(silu_q(pre));
+  return (int32_t)rshr(co, 12 - QKV_F);
+}
+// decay gate of one head (ref/layer_fixed.py:1532-1538)
+F5_DEV int32_t decay_gate(long long v, int32_t dt_bias, int32_t A) {
+  const long long sp = softplus_q(v + dt_bias);
+  const long long g = -rshr((long long)A * sp, 15 + 12 - 16);
+  const long long dec = rshr(exp_neg_q(g < 0 ? g : 0), 15);
+  return (int32_t)(dec > 32767 ? 32767 : dec);
+}
 F5_DEV void epilogue_row(const GemvArgs &a, const GemvSeg &sg, int row, long long acc16, int e_x,
-                         int in_f, unsigned long long &best) {
+                         int in_f, unsigned long long &best, uint32_t epoch = 0) {
   long long pex;
   const int32_t y = finish_y32(acc16, a.sh, a.err, &pex);
   const int orow = sg.out_row0 + row;
@@ -389,42 +474,52 @@ F5_DEV void epilogue_row(const GemvArgs &a, const GemvSeg &sg, int row, long lon
   }
   if (sg.p_out) sg.p_out[orow] = pex;
   const int sh2 = (15 - sg.e - a.sh) - e_x + in_f - sg.out_f;
+  const uint32_t tag = (epoch && sg.tag_op1) ? mk_tag(epoch, sg.tag_op1) : 0u;
   switch (sg.mode) {
     case GM_Y32: static_cast<int32_t *>(sg.out)[orow] = y; break;
-    case GM_TO16: static_cast<int16_t *>(sg.out)[orow] = (int16_t)clip16(shift_to(y, sh2)); break;
-    case GM_TO64: static_cast<int64_t *>(sg.out)[orow] = shift_to(y, sh2); break;
-    case GM_RESID: {
-      int16_t *o = static_cast<int16_t *>(sg.out) + orow;   // written by other CTAs: read at L2
-      *o = (int16_t)clip16((int64_t)__ldcg(o) + clip16(shift_to(y, sh2)));
+    case GM_TO16: {
+      const int32_t v = clip16(shift_to(y, sh2));
+      if (tag) static_cast<uint32_t *>(sg.out)[orow] = tag_word(tag, v);
+      else static_cast<int16_t *>(sg.out)[orow] = (int16_t)v;
     } break;
+    case GM_TO64: static_cast<int64_t *>(sg.out)[orow] = shift_to(y, sh2); break;
+    case GM_RESID:
+      if (tag) {   // the row's previous word was written by this CTA (same row partition)
+        uint32_t *o = static_cast<uint32_t *>(sg.out) + orow;
+        *o = tag_word(tag, clip16((int64_t)tag_s16(__ldcg(o)) + clip16(shift_to(y, sh2))));
+      } else {
+        int16_t *o = static_cast<int16_t *>(sg.out) + orow;   // written by other CTAs: read at L2
+        *o = (int16_t)clip16((int64_t)__ldcg(o) + clip16(shift_to(y, sh2)));
+      }
+      break;
     case GM_CONV: {   // ref/layer_fixed.py:1511-1520 for channel orow
       const long long v = clip16(shift_to(y, sh2));
-      static_cast<int16_t *>(sg.out)[orow] = (int16_t)v;
+      if (sg.out) static_cast<int16_t *>(sg.out)[orow] = (int16_t)v;
       int16_t *ring = static_cast<int16_t *>(sg.aux0) + (size_t)orow * 4;
-      const int4 cw = __ldcg(reinterpret_cast<const int4 *>(static_cast<const int32_t *>(sg.aux1) + (size_t)orow * 4));
+      // cached loads: the ring word is touched only by this row's epilogue
+      // (this step's write below, the next step's read in a later launch)
+      const int4 cw = *reinterpret_cast<const int4 *>(static_cast<const int32_t *>(sg.aux1) + (size_t)orow * 4);
       const int T = *sg.T;
-      const uint2 rw = __ldcg(reinterpret_cast<const uint2 *>(ring));   // 4 int16 slots
-      const int16_t r4[4] = {(int16_t)(rw.x & 0xFFFFu), (int16_t)(rw.x >> 16), (int16_t)(rw.y & 0xFFFFu),
-                             (int16_t)(rw.y >> 16)};
-      long long acc = (long long)r4[(T + 1) & 3] * cw.x + (long long)r4[(T + 2) & 3] * cw.y +
-                      (long long)r4[(T + 3) & 3] * cw.z + v * cw.w;
-      const long long pre = clip(rshr(acc, RS_F + CW_F - 12), -(1 << 20), (1 << 20) - 1);
-      const long long co = clip16(silu_q(pre));
-      static_cast<int16_t *>(sg.aux_out)[orow] = (int16_t)rshr(co, 12 - QKV_F);
+      const uint2 rw = *reinterpret_cast<const uint2 *>(ring);   // 4 int16 slots
+      const int32_t qc = conv_silu(v, rw, cw, T);
+      if (tag) static_cast<uint32_t *>(sg.aux_out)[orow] = tag_word(tag, qc);
+      else static_cast<int16_t *>(sg.aux_out)[orow] = (int16_t)qc;
       ring[T & 3] = (int16_t)v;
     } break;
-    case GM_GATE_B: {   // ref/layer_fixed.py:1531
+    case GM_GATE_B: {   // ref/layer_fixed.py:1531; beta in [0, 2^15]: a tagged word holds it unsigned
       const long long v = clip16(shift_to(y, sh2));
-      static_cast<int16_t *>(sg.out)[orow] = (int16_t)v;
-      static_cast<int32_t *>(sg.aux_out)[orow] = (int32_t)sigmoid_q(v);
+      if (sg.out) static_cast<int16_t *>(sg.out)[orow] = (int16_t)v;
+      const int32_t beta = (int32_t)sigmoid_q(v);
+      if (tag) static_cast<uint32_t *>(sg.aux_out)[orow] = tag_word(tag, beta);
+      else static_cast<int32_t *>(sg.aux_out)[orow] = beta;
     } break;
     case GM_GATE_A: {   // ref/layer_fixed.py:1532-1538
       const long long v = clip16(shift_to(y, sh2));
-      static_cast<int16_t *>(sg.out)[orow] = (int16_t)v;
-      const long long sp = softplus_q(v + static_cast<const int32_t *>(sg.aux0)[orow]);
-      const long long g = -rshr((long long)static_cast<const int32_t *>(sg.aux1)[orow] * sp, 15 + 12 - 16);
-      long long dec = rshr(exp_neg_q(g < 0 ? g : 0), 15);
-      static_cast<int32_t *>(sg.aux_out)[orow] = (int32_t)(dec > 32767 ? 32767 : dec);
+      if (sg.out) static_cast<int16_t *>(sg.out)[orow] = (int16_t)v;
+      const int32_t d = decay_gate(v, static_cast<const int32_t *>(sg.aux0)[orow],
+                                   static_cast<const int32_t *>(sg.aux1)[orow]);
+      if (tag) static_cast<uint32_t *>(sg.aux_out)[orow] = tag_word(tag, d);
+      else static_cast<int32_t *>(sg.aux_out)[orow] = d;
     } break;
     default: break;
   }
@@ -432,13 +527,15 @@ F5_DEV void epilogue_row(const GemvArgs &a, const GemvSeg &sg, int row, long lon
 
 // MLP gate/up pair (ref/layer_fixed.py:1597-1602)
 F5_DEV void epilogue_pair(const GemvArgs &a, const GemvSeg &sg, int row, long long accg, long long accu,
-                          int e_x, int in_f) {
+                          int e_x, int in_f, uint32_t epoch = 0) {
   const int32_t yg = finish_y32(accg, a.sh, a.err, nullptr);
   const int32_t yu = finish_y32(accu, a.sh, a.err, nullptr);
   const int64_t gq = shift_to(yg, (15 - sg.e - a.sh) - e_x + in_f - sg.out_f);
   const int64_t uq = shift_to(yu, (15 - sg.e2 - a.sh) - e_x + in_f - sg.out_f2);
   const int64_t sgv = clip16(silu_q(clip(gq, -(1 << 20), (1 << 20) - 1)));
-  static_cast<int16_t *>(sg.out)[sg.out_row0 + row] = (int16_t)clip16(rshr(sgv * uq, 12));
+  const int32_t v = clip16(rshr(sgv * uq, 12));
+  if (epoch && sg.tag_op1) static_cast<uint32_t *>(sg.out)[sg.out_row0 + row] = tag_word(mk_tag(epoch, sg.tag_op1), v);
+  else static_cast<int16_t *>(sg.out)[sg.out_row0 + row] = (int16_t)v;
 }
 
 }  // namespace f5

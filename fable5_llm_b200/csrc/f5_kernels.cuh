@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#define F5_DEV_HOST_INLINE __host__ __device__ __forceinline__
+
 namespace f5 {
 
 // ---- device error word bits (set by kernels, read by the host) ----
@@ -22,8 +24,16 @@ struct StepParams {
   int max_val;    // its y32 logit
   uint32_t err;   // device error bits (DERR_*)
   int steps;      // steps completed since reset
-  int pad;
+  int launch;     // persistent-kernel launches since reset (dataflow tag epoch)
 };
+
+// ---- dataflow tags of the persistent kernel ----
+// An activation word is (tag << 16) | uint16 value, tag = epoch << 8 | op:
+// epoch = 1 + launch % 255 (never 0, so zeroed buffers never match), op =
+// the writer's index in the step's op list (< 256).  A reader polls its
+// input words until every tag matches the expected writer: the word carries
+// its own readiness, so no grid barrier is needed between the two ops.
+F5_DEV_HOST_INLINE uint32_t mega_epoch(int launch) { return 1u + (uint32_t)(launch % 255); }
 
 // ---- quantized activation vector (DYNQ8 output, ref/fixedpoint.py:24-33) ----
 // x8 lives in its own buffer; meta[0] = e_x, meta[1] = in_f (fraction bits
@@ -66,6 +76,7 @@ enum GemvPro : int {
 };
 
 struct GemvPrologue {
+  int tag_op1;        // 0: plain input; else the input words are tagged by op tag_op1 - 1
   int mode;
   const void *src;
   const void *src2;   // PRO_ATTN_ACC: q|gate rows ([K/256][512] int16)
@@ -91,6 +102,8 @@ struct GemvSeg {
   void *aux0;         // GM_CONV: int16 conv ring [rows][4]; GM_GATE_A: int32 dt_bias (Q12)
   const void *aux1;   // GM_CONV: int32 conv weights [rows][4] (Q.CW_F); GM_GATE_A: int32 A (Q15)
   const int *T;       // GM_CONV: tokens already in the window (ring slot T % 4)
+  int tag_op1;        // 0: plain outputs; else tagged words from op tag_op1 - 1 (TO16, RESID,
+                      // SILU_MUL: out; CONV, GATE_*: aux_out, and out is skipped when null)
 };
 
 struct GemvArgs {
@@ -108,6 +121,7 @@ struct GemvArgs {
   GemvPrologue pro;    // mode PRO_X8 uses x8 / xmeta
   unsigned long long *argmax_key;
   uint32_t *err;
+  unsigned *abort_flag;   // persistent kernel: global abort flag polled by bounded tag waits
 };
 
 cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t st, bool pdl, int max_blocks);

@@ -246,6 +246,8 @@ __shared__ volatile int mg_abort;
 __shared__ int mg_last;
 __shared__ __align__(16) MegaOp mg_fop;   // the L2 prefetcher's descriptor buffer
 __shared__ volatile long long mg_issued;  // weight bytes the producer has issued (its only writer)
+constexpr int MG_XRES = 64;
+__shared__ int16_t mg_xres[MG_XRES];      // this CTA's rows of the residual (4096-row partition)
 
 // trace marker k (2..7) of the current op: consumer thread 0 only
 #define MG_MARK(k)                                                   \
@@ -408,6 +410,44 @@ F5_DEV void prefetcher(const MegaArgs &ma, const Abort &ab) {
 // ---------------------------------------------------------------------------
 // consumers: GEMV
 // ---------------------------------------------------------------------------
+// Epilogue operands that do not depend on this step (conv ring and weights,
+// the decay gate's constants) are pulled into L1 by the row's epilogue
+// thread right after the prologue, so the epilogue's cached loads of them
+// hit L1 (no acquire invalidates L1 inside an op).
+F5_DEV void epi_prefetch(const GemvArgs &a, int uu) {
+  const GemvSeg &sg = a.seg[seg_of(a, uu)];
+  const int orow = sg.out_row0 + (uu - sg.unit_begin);
+  const void *p0 = nullptr, *p1 = nullptr;
+  if (sg.mode == GM_CONV) {
+    p0 = static_cast<const int16_t *>(sg.aux0) + (size_t)orow * 4;
+    p1 = static_cast<const int32_t *>(sg.aux1) + (size_t)orow * 4;
+  } else if (sg.mode == GM_GATE_A) {
+    p0 = static_cast<const int32_t *>(sg.aux0) + orow;
+    p1 = static_cast<const int32_t *>(sg.aux1) + orow;
+  }
+  if (p0) {
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(p0));
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(p1));
+  }
+}
+// The persistent kernel's row epilogue: the residual rows come from and go
+// back to mg_xres (the CTA wrote them last: BEGIN and every residual op use
+// the same 4096-row partition); everything else is the shared epilogue_row.
+F5_DEV void mega_epilogue_row(const GemvArgs &a, const GemvSeg &sg, int i, int uu, long long acc, int e_x, int in_f,
+                              uint32_t epoch) {
+  const int row = uu - sg.unit_begin, orow = sg.out_row0 + row;
+  const uint32_t tag = (epoch && sg.tag_op1) ? mk_tag(epoch, sg.tag_op1) : 0u;
+  if (!(sg.mode == GM_RESID && tag && i < MG_XRES)) {
+    unsigned long long unused = 0ull;
+    epilogue_row(a, sg, row, acc, e_x, in_f, unused, epoch);
+    return;
+  }
+  const int32_t y = finish_y32(acc, a.sh, a.err, nullptr);
+  const long long v = clip16(shift_to(y, (15 - sg.e - a.sh) - e_x + in_f - sg.out_f));
+  const int32_t nv = clip16((int64_t)mg_xres[i] + v);
+  mg_xres[i] = (int16_t)nv;
+  static_cast<uint32_t *>(sg.out)[orow] = tag_word(tag, nv);
+}
 // K = 4096 (every GEMV of the step but the MLP down projection): one row per
 // consumer warp per 16-row stage.  The consumer loop is issue-bound, so it is
 // kept to the row's own arithmetic: chunks are walked segment by segment
@@ -416,11 +456,11 @@ F5_DEV void prefetcher(const MegaArgs &ma, const Abort &ab) {
 // sum uses two redux.sync adds, and the LM head's argmax epilogue is batched
 // -- lane k % 32 of a warp holds the warp's k-th row sum, and every 32 rows
 // all lanes turn their rows into (y32, row) keys at once.
-F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const Abort &ab) {
+F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const Abort &ab, uint32_t epoch) {
   const CSync sy;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, b = blockIdx.x, ns = S.ns;
-  prologue<1>(sy, a, S.xs(), mg_red, (&mg_r), mg_meta);
+  prologue<1>(sy, a, S.xs(), mg_red, (&mg_r), mg_meta, epoch);
   sy.sync();
   MG_MARK(2);
   const int e_x = mg_meta[0], in_f = mg_meta[1];
@@ -432,6 +472,7 @@ F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const 
   const int u0 = part_lo(a.total_units, G, b), u1 = part_lo(a.total_units, G, b + 1);
   const int stride = a.stride, sh = a.sh;
   const bool argmax = a.seg[0].mode == GM_ARGMAX;
+  if (!argmax && tid < u1 - u0) epi_prefetch(a, u0 + tid);
   long long *res = S.res();
   int32_t *logits = static_cast<int32_t *>(a.seg[0].out);   // argmax: optional y32 of every row
   unsigned long long best = 0ull;
@@ -496,13 +537,11 @@ F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const 
     if (lane == 0 && best) atomicMax(a.argmax_key, best);
     return true;
   }
-  unsigned long long unused = 0ull;
   for (int i = tid; i < u1 - u0; i += MG_CT) {
     const int uu = u0 + i;
     const GemvSeg &sg = a.seg[seg_of(a, uu)];
-    const int row = uu - sg.unit_begin;
-    if (sg.mode == GM_SILU_MUL) epilogue_pair(a, sg, row, res[2 * i], res[2 * i + 1], e_x, in_f);
-    else epilogue_row(a, sg, row, res[i], e_x, in_f, unused);
+    if (sg.mode == GM_SILU_MUL) epilogue_pair(a, sg, uu - sg.unit_begin, res[2 * i], res[2 * i + 1], e_x, in_f, epoch);
+    else mega_epilogue_row(a, sg, i, uu, res[i], e_x, in_f, epoch);
   }
   return true;
 }
@@ -513,11 +552,11 @@ F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const 
 // registers.  The partial sums are exact integers; the deferred epilogue adds
 // the NP partials of a row (order-free) before the group-scale law's shift.
 template <int NP>
-F5_DEV bool c_gemv_split(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const Abort &ab) {
+F5_DEV bool c_gemv_split(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const Abort &ab, uint32_t epoch) {
   const CSync sy;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, b = blockIdx.x, ns = S.ns;
-  prologue<(NP * 4 * 128 + MG_CT - 1) / MG_CT>(sy, a, S.xs(), mg_red, (&mg_r), mg_meta);
+  prologue<(NP * 4 * 128 + MG_CT - 1) / MG_CT>(sy, a, S.xs(), mg_red, (&mg_r), mg_meta, epoch);
   sy.sync();
   MG_MARK(2);
   const int e_x = mg_meta[0], in_f = mg_meta[1];
@@ -558,14 +597,15 @@ F5_DEV bool c_gemv_split(const GemvArgs &a, const MegaSmem &S, RingPos &rp, cons
   }
   if (sy.any(bad)) return false;
   MG_MARK(3);
-  unsigned long long best = 0ull;
   for (int i = tid; i < u1 - u0; i += MG_CT) {
     const int uu = u0 + i;
     const GemvSeg &sg = a.seg[seg_of(a, uu)];
     long long acc = 0;
 #pragma unroll
     for (int p = 0; p < NP; ++p) acc += S.res()[NP * i + p];
-    epilogue_row(a, sg, uu - sg.unit_begin, acc, e_x, in_f, best);
+    if (i == 0) MG_MARK(4);
+    mega_epilogue_row(a, sg, i, uu, acc, e_x, in_f, epoch);
+    if (i == 0) MG_MARK(5);
   }
   return true;
 }
@@ -579,7 +619,22 @@ F5_DEV bool c_gemv_split(const GemvArgs &a, const MegaSmem &S, RingPos &rp, cons
 // which the four CTAs of a head exchange through marked slots.  Thread
 // (warp w, lane l) owns column 32 q + l, rows 8 w .. 8 w + 7.
 // ---------------------------------------------------------------------------
-F5_DEV bool c_dn(const MegaArgs &ma, const DnArgs &d, const MegaSmem &S, int &w_sd, const Abort &ab) {
+// plain or dataflow-tagged scalar input (tagged: polled until ready)
+F5_DEV long long ld_in16(const int16_t *p, int i, uint32_t tag, const Abort &ab) {
+  if (!tag) return __ldcg(p + i);
+  uint32_t w[1];
+  ld_tagged<1>(reinterpret_cast<const uint32_t *>(p) + i, tag, w, ab.flag, ab.err);
+  return tag_s16(w[0]);
+}
+F5_DEV long long ld_inu(const int32_t *p, int i, uint32_t tag, const Abort &ab) {   // unsigned 16-bit gates
+  if (!tag) return __ldcg(p + i);
+  uint32_t w[1];
+  ld_tagged<1>(reinterpret_cast<const uint32_t *>(p) + i, tag, w, ab.flag, ab.err);
+  return (long long)(w[0] & 0xFFFFu);
+}
+
+F5_DEV bool c_dn(const MegaArgs &ma, const DnArgs &d, const MegaSmem &S, int &w_sd, const Abort &ab,
+                 uint32_t epoch) {
   const int b = blockIdx.x;
   if (b >= 4 * ma.dn_heads) return true;
   const CSync sy;
@@ -591,19 +646,20 @@ F5_DEV bool c_dn(const MegaArgs &ma, const DnArgs &d, const MegaSmem &S, int &w_
   long long *part = reinterpret_cast<long long *>(scr + DN_PART);   // [16 warps][32]
   long long *vzn = reinterpret_cast<long long *>(scr + DN_VZN);     // v, z, norm_w of the quarter
 
-  // ---- every input in one round of loads ----
+  // ---- every input in one round of loads (tagged: each polled until ready) ----
+  const uint32_t itag = (epoch && d.in_tag_op1) ? mk_tag(epoch, d.in_tag_op1) : 0u;
   long long qv = 0, kv = 0;
   if (tid < 128) {
-    qv = __ldcg(d.qkvc + kh * 128 + tid);
-    kv = __ldcg(d.qkvc + d.lkd + kh * 128 + tid);
+    qv = ld_in16(d.qkvc, kh * 128 + tid, itag, ab);
+    kv = ld_in16(d.qkvc, d.lkd + kh * 128 + tid, itag, ab);
   } else if (tid < 160) {
     const int i = tid - 128, dv = qd * 32 + i;
-    vzn[i] = __ldcg(d.qkvc + 2 * d.lkd + h * 128 + dv);
-    vzn[32 + i] = __ldcg(d.z16 + h * 128 + dv);
+    vzn[i] = ld_in16(d.qkvc, 2 * d.lkd + h * 128 + dv, itag, ab);
+    vzn[32 + i] = ld_in16(d.z16, h * 128 + dv, itag, ab);
     vzn[64 + i] = __ldcg(d.norm_w + dv);
   } else if (tid == 160) {
-    mg_gate[0] = __ldcg(d.beta + h);
-    mg_gate[1] = __ldcg(d.decay + h);
+    mg_gate[0] = ld_inu(d.beta, h, itag, ab);
+    mg_gate[1] = ld_inu(d.decay, h, itag, ab);
   }
   // ---- l2norm of q and k (ref/layer_fixed.py:1322-1330) ----
   const long long ssq = g_sum_split(sy, qv * qv, mg_red);
@@ -697,7 +753,11 @@ F5_DEV bool c_dn(const MegaArgs &ma, const DnArgs &d, const MegaSmem &S, int &w_
     const long long tt = clip16(rshr(o16 * m, 15));
     const long long nh = clip16(rshr(tt * vzn[64 + i], 14));
     const long long zg = clip16(silu_q(vzn[32 + i] << (12 - QKV_F)));
-    d.on16[h * 128 + tid] = (int16_t)clip16(rshr(nh * zg, 12));
+    const int32_t ov16 = clip16(rshr(nh * zg, 12));
+    if (epoch && d.out_tag_op1)
+      reinterpret_cast<uint32_t *>(d.on16)[h * 128 + tid] = tag_word(mk_tag(epoch, d.out_tag_op1), ov16);
+    else
+      d.on16[h * 128 + tid] = (int16_t)ov16;
   }
   if (qd == 0 && tid == 0 && d.kh_out) d.kh_out[h] = kh_shift;
   release_scratch(sy, (&mg_bfree));
@@ -769,7 +829,7 @@ F5_DEV bool group_gather(const CSync &sy, const unsigned long long *slots, int c
 }
 
 F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int T, int pos, int &w_sk, int &w_sv,
-                   const Abort &ab) {
+                   const Abort &ab, uint32_t epoch) {
   const AttnArgs &a = m.a;
   const AttGeo g = att_geo(a, T, pos, gridDim.x, blockIdx.x);
   if (g.kv >= a.nkv) return true;
@@ -794,9 +854,12 @@ F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int
   const bool k_act = hs == 0;
 
   // ---- 0. every operand in one round of loads ----
-  const long long qx0 = __ldcg(a.qg16 + hq * 512 + e), qx1 = __ldcg(a.qg16 + hq * 512 + e + 128);
-  const long long kx0 = k_act ? __ldcg(a.k16 + g.kv * 256 + e) : 0, kx1 = k_act ? __ldcg(a.k16 + g.kv * 256 + e + 128) : 0;
-  const long long v0 = k_act ? __ldcg(a.v16 + g.kv * 256 + e) : 0, v1 = k_act ? __ldcg(a.v16 + g.kv * 256 + e + 128) : 0;
+  const uint32_t itag = (epoch && m.in_tag_op1) ? mk_tag(epoch, m.in_tag_op1) : 0u;
+  const long long qx0 = ld_in16(a.qg16, hq * 512 + e, itag, ab), qx1 = ld_in16(a.qg16, hq * 512 + e + 128, itag, ab);
+  const long long kx0 = k_act ? ld_in16(a.k16, g.kv * 256 + e, itag, ab) : 0;
+  const long long kx1 = k_act ? ld_in16(a.k16, g.kv * 256 + e + 128, itag, ab) : 0;
+  const long long v0 = k_act ? ld_in16(a.v16, g.kv * 256 + e, itag, ab) : 0;
+  const long long v1 = k_act ? ld_in16(a.v16, g.kv * 256 + e + 128, itag, ab) : 0;
   const long long qw0 = __ldcg(a.q_norm + e), qw1 = __ldcg(a.q_norm + e + 128);
   const long long kw0 = __ldcg(a.k_norm + e), kw1 = __ldcg(a.k_norm + e + 128);
   const long long cosv = e < a.rot ? __ldcg(cs + e) : 0, sinv = e < a.rot ? __ldcg(cs + 64 + e) : 0;
@@ -1000,15 +1063,28 @@ F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int
 }
 
 // ---------------------------------------------------------------------------
-F5_DEV void c_begin(const MegaArgs &ma, const MegaBegin &B, int tok) {
+F5_DEV void c_begin(const MegaArgs &ma, const MegaBegin &B, int tok, uint32_t epoch) {
   const int tid = threadIdx.x, G = gridDim.x, b = blockIdx.x;
   if (tok < 0 || tok >= B.vocab) {
     if (b == 0 && tid == 0) atomicOr(ma.err, DERR_RANGE);
     tok = 0;
   }
-  const uint4 *src = reinterpret_cast<const uint4 *>(B.emb + (size_t)tok * B.H);
-  uint4 *dst = reinterpret_cast<uint4 *>(B.x16);
-  for (int i = b * MG_CT + tid; i < B.H / 8; i += G * MG_CT) dst[i] = src[i];
+  if (B.x16t) {
+    // tagged residual: each CTA writes the rows its residual epilogues own
+    // (the 4096-row partition), tagged as op 0
+    const int16_t *src = B.emb + (size_t)tok * B.H;
+    const uint32_t tag = mk_tag(epoch, 1);
+    const int r0 = part_lo(B.H, G, b);
+    for (int i = r0 + tid; i < part_lo(B.H, G, b + 1); i += MG_CT) {
+      const int16_t v = src[i];
+      B.x16t[i] = tag_word(tag, v);
+      if (i - r0 < MG_XRES) mg_xres[i - r0] = v;
+    }
+  } else {
+    const uint4 *src = reinterpret_cast<const uint4 *>(B.emb + (size_t)tok * B.H);
+    uint4 *dst = reinterpret_cast<uint4 *>(B.x16);
+    for (int i = b * MG_CT + tid; i < B.H / 8; i += G * MG_CT) dst[i] = src[i];
+  }
   for (int i = b * MG_CT + tid; i < B.zero_n; i += G * MG_CT) B.zero[i] = make_uint4(0, 0, 0, 0);
   if (b == 0 && tid == 0) *B.key = 0ull;
 }
@@ -1030,23 +1106,22 @@ F5_DEV void stage_wait() {
   if (threadIdx.x < MG_DESC_V4) asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
-F5_DEV void consumers(const MegaArgs &ma, const MegaSmem &S, int tok, int T, int pos, const Abort &ab) {
+F5_DEV void consumers(const MegaArgs &ma, const MegaSmem &S, int tok, int T, int pos, const Abort &ab,
+                      uint32_t epoch) {
   const CSync sy;
   RingPos rp;
   int w_sd = 0, w_sk = 0, w_sv = 0;
   unsigned long long *tr = ma.trace ? ma.trace + (size_t)blockIdx.x * ma.nops * MEGA_TRACE_SLOTS : nullptr;
   stage_desc(ma, S, 0);
-  stage_wait();
-  sy.sync();
   for (int oi = 0; oi < ma.nops; ++oi) {
-    // Op oi waits for op oi-1 on every CTA (grid barrier oi-1: the emitter
-    // numbers them so).  The barrier's entry sync also publishes the staged
-    // descriptor and retires every reader of the buffer staged next.
-    if (oi > 0) {
-      stage_wait();
-      if (tr && threadIdx.x == 0) tr[(size_t)(oi - 1) * MEGA_TRACE_SLOTS + 7] = gtimer();   // arrival
-      if (!counter_barrier(sy, &ma.bars[oi - 1], gridDim.x, ab)) return;
-    }
+    // The sync publishes op oi's staged descriptor and retires every reader
+    // of the buffer staged next.  Ops whose inputs are dataflow-tagged need
+    // no grid barrier: their loads wait for the words themselves.
+    stage_wait();
+    if (oi > 0 && tr && threadIdx.x == 0) tr[(size_t)(oi - 1) * MEGA_TRACE_SLOTS + 7] = gtimer();   // arrival
+    sy.sync();
+    const int bar = mg_cop[oi & 1].bar;
+    if (bar >= 0 && !counter_barrier(sy, &ma.bars[bar], gridDim.x, ab)) return;
     if (threadIdx.x == 0) mg_tr = tr ? tr + (size_t)oi * MEGA_TRACE_SLOTS : nullptr;
     if (oi + 1 < ma.nops) stage_desc(ma, S, oi + 1);
     if (threadIdx.x >= 64 && threadIdx.x < 64 + 51) lut_prefetch_l1(threadIdx.x - 64);
@@ -1054,10 +1129,12 @@ F5_DEV void consumers(const MegaArgs &ma, const MegaSmem &S, int tok, int T, int
     if (tr && threadIdx.x == 0) tr[(size_t)oi * MEGA_TRACE_SLOTS] = gtimer();
     bool ok = true;
     switch (op.kind) {
-      case MK_BEGIN: c_begin(ma, op.b, tok); break;
-      case MK_GEMV: ok = op.g.K > 4096 ? c_gemv_split<3>(op.g, S, rp, ab) : c_gemv4096(op.g, S, rp, ab); break;
-      case MK_DN: ok = c_dn(ma, op.d, S, w_sd, ab); break;
-      case MK_ATTN: ok = c_attn(ma, op.at, S, T, pos, w_sk, w_sv, ab); break;
+      case MK_BEGIN: c_begin(ma, op.b, tok, epoch); break;
+      case MK_GEMV:
+        ok = op.g.K > 4096 ? c_gemv_split<3>(op.g, S, rp, ab, epoch) : c_gemv4096(op.g, S, rp, ab, epoch);
+        break;
+      case MK_DN: ok = c_dn(ma, op.d, S, w_sd, ab, epoch); break;
+      case MK_ATTN: ok = c_attn(ma, op.at, S, T, pos, w_sk, w_sv, ab, epoch); break;
       default: break;
     }
     if (tr && threadIdx.x == 0) tr[(size_t)oi * MEGA_TRACE_SLOTS + 1] = gtimer();
@@ -1096,6 +1173,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega(const __grid_constant_
   // step parameters: written by the host or by the previous launch only
   const volatile StepParams *vp = ma.params;
   const int tok = vp->tok, T = vp->T, pos = vp->pos;
+  const uint32_t epoch = mega_epoch(vp->launch);
   __syncthreads();
 
   if (warp == MG_CONS) {
@@ -1103,7 +1181,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega(const __grid_constant_
   } else if (warp == MG_CONS + 1) {
     prefetcher(ma, ab);
   } else {
-    consumers(ma, S, tok, T, pos, ab);
+    consumers(ma, S, tok, T, pos, ab, epoch);
   }
   __syncwarp();   // reconverge each warp (the producer lane joins its warp) before the CTA barrier
   __syncthreads();
@@ -1141,6 +1219,12 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega(const __grid_constant_
       p->T += 1;
       p->steps += 1;
     }
+    p->launch += 1;
+  }
+  {   // the plain residual for readers outside the step (tagged words -> int16)
+    const MegaBegin &B = ma.ops[0].b;
+    if (B.x16t)
+      for (int i = tid; i < B.H; i += MEGA_THREADS) B.x16[i] = (int16_t)tag_s16(__ldcg(B.x16t + i));
   }
   __syncthreads();
   for (int i = tid; i < ma.nbars; i += MEGA_THREADS) ma.bars[i] = 0u;

@@ -20,7 +20,8 @@ enum MegaKind : int {
 
 struct MegaBegin {
   const int16_t *emb;         // [vocab][H]
-  int16_t *x16;               // [H]
+  int16_t *x16;               // [H] plain residual (written back at the step's end)
+  uint32_t *x16t;             // [H] tagged residual the step works on
   int vocab, H;
   unsigned long long *key;    // LM-head argmax key
   uint4 *zero;                // attention accumulators, cleared every step
@@ -31,13 +32,14 @@ struct MegaAttn {
   AttnArgs a;                 // same operands as the per-op attention kernel
   unsigned long long *slots;  // [2 phases][nkv][G / nkv CTAs][4 heads][2 words] marked values
   int32_t *gacc;              // [nq * HD] PV sums
+  int in_tag_op1;             // dataflow tag of q|gate, k, v (tagged words)
 };
 
 // 16-byte aligned and sized: the kernel stages each descriptor in shared
 // memory (bulk copy for the producer, vector loads for the consumers)
 struct alignas(16) MegaOp {
   int kind;
-  int bar;         // grid-barrier counter taken before the op (-1: none)
+  int bar;         // grid-barrier counter taken before the op (-1: the op's inputs are tagged)
   int pad[2];
   union {
     GemvArgs g;
