@@ -134,35 +134,34 @@ def cpu_sample_projections(seconds=12.0, threads=0):
 
 
 def cpu_sample_step(seconds=20.0):
-    """Time the oracle's full decode step (numpy law + C matvec) on a bounded
-    number of layers of the 9B model; scaled to one token."""
+    """Time the oracle's full decode step (numpy law + C matvec) on the first
+    4 layers of the 9B model for about `seconds` of greedy steps, plus one
+    LM-head matvec; scaled to one 32-layer token."""
     import oracle as O
     from oracle.model import OracleModel
     t_build = time.time()
-    nl = 4
+    nl, max_T = 4, 2048
     geom = O.Geometry(n_layers=nl, vocab=8192)
     m = OracleModel(2026, geom)
-    r = O.OracleRunner(m, max_T=16)
+    r = O.OracleRunner(m, max_T=max_T)
     build_s = time.time() - t_build
-    steps, spent = 0, 0.0
-    while spent < seconds and steps < 8:
+    steps, spent, tok = 0, 0.0, 17
+    while spent < seconds and steps < max_T - 1:
         t0 = time.perf_counter()
-        r.step(17 + steps, steps)
+        tok, _ = r.step(tok, steps)
         spent += time.perf_counter() - t0
         steps += 1
     per_layer_step = spent / steps / nl
-    # full step = 32 layers + a 248,320-row head (time the head matvec share)
-    head_bytes = 248320 * 2112
-    s_head = (m.head.N * 2112) / (spent / steps)   # crude; refined below
+    # the 248,320-row head: one matvec of the sample's head, scaled by rows
     t0 = time.perf_counter()
     O.matvec_img(m.head.img, m.head.N, 4096, m.head.sh, np.zeros(4096, np.int8))
     head_s = (time.perf_counter() - t0) * (248320 / m.head.N)
     full = per_layer_step * 32 + head_s
-    del s_head, head_bytes
     return {"value": round(1.0 / full, 5), "unit": "tok/s", "cores": O.oracle_threads(), "kind": "port",
-            "sample": f"{steps} decode steps of the first {nl} layers (3 DeltaNet + 1 attention) of the "
-                      f"synthetic 9B model through the oracle ({spent:.1f} s; model build {build_s:.0f} s "
-                      f"untimed), scaled to 32 layers + the 248,320-row head"}
+            "sample": f"{steps} greedy decode steps (context 0..{steps - 1}) of the first {nl} layers "
+                      f"(3 DeltaNet + 1 attention) of the synthetic 9B model through the oracle "
+                      f"({spent:.1f} s; model build {build_s:.0f} s untimed), scaled to 32 layers, plus "
+                      f"one LM-head matvec scaled to 248,320 rows"}
 
 
 # ---------------------------------------------------------------------------
@@ -191,12 +190,19 @@ def trace_summary(t, kinds):
 
 def mega_traffic():
     """DRAM bytes per persistent-kernel launch from the committed ncu summary
-    (profiles/k_mega_traffic.json), or None when no capture was made."""
-    p = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", "k_mega_traffic.json")
+    (profiles/k_mega_traffic.txt), or None when no capture was made."""
+    p = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", "k_mega_traffic.txt")
     try:
+        vals = {}
         with open(p) as f:
-            return json.load(f)
-    except (OSError, ValueError):
+            for ln in f:
+                if ln.strip() and not ln.startswith("#"):
+                    k, v = ln.split()
+                    vals[k] = int(v)
+        return {"dram_bytes_per_launch": vals["dram_read_bytes"] + vals["dram_write_bytes"],
+                "source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one k_mega launch, full 9B step "
+                          "(profiles/k_mega_decode_step_traffic.md)"}
+    except (OSError, ValueError, KeyError):
         return None
 
 
@@ -304,7 +310,7 @@ def run_step(args, ws, rank, local):
         pass
     hbm_peak, peak_kind = peaks()
     ctx_len = args.context
-    m = DecodeModel(Geometry(), max_T=ctx_len + args.warmup + 2 * args.steps + 8, device=local,
+    m = DecodeModel(Geometry(args.layers, args.vocab), max_T=ctx_len + args.warmup + 2 * args.steps + 8, device=local,
                     max_pos=ctx_len + args.warmup + 2 * args.steps + 8)
     m.load_synthetic(args.seed)
     m.reset()
@@ -574,6 +580,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="step", choices=["step", "projections", "gemv"])
     ap.add_argument("--context", type=int, default=2048)
+    ap.add_argument("--layers", type=int, default=32,
+                    help="step workload on the first N layers (small ncu cases only; the bench line is 32)")
+    ap.add_argument("--vocab", type=int, default=248320,
+                    help="LM-head rows (small ncu cases only; the bench line is 248,320)")
     ap.add_argument("--seed", type=int, default=2026)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
