@@ -38,7 +38,7 @@ constexpr int GT_RES_MAX = 2048;                // deferred row results per CTA
 constexpr unsigned long long GT_WAIT_NS = 2000000000ull;   // 2 s: a safety net only
 
 // Persistent TMA-pipelined GEMV: a producer warp streams contiguous blocks
-// of packed rows (cp.async.bulk, 16-byte aligned, no multicast) into
+// of packed rows (cp.async.bulk, 16-byte aligned, single destination) into
 // shared-memory stages guarded by full/empty mbarriers; sixteen consumer
 // warps reduce one row per warp out of shared memory, park the row's p16 in
 // shared memory and release the stage at once.  The per-row epilogues run

@@ -7,7 +7,7 @@
 //  * producer (one lane of warp 16) walks the step's op list and streams
 //    EVERY weight row this CTA will ever consume, in consumption order,
 //    through a ring of MEGA_STAGE-byte shared-memory stages (cp.async.bulk,
-//    no multicast, full / empty mbarriers).  Weights do not depend on
+//    single-destination copies, full / empty mbarriers).  Weights do not depend on
 //    activations, so the stream never waits for a grid barrier: while the
 //    consumers sit at a barrier or in a DeltaNet / attention core, the ring
 //    fills and HBM stays busy.  It also prefetches the CTA's DeltaNet head

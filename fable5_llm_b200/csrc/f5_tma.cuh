@@ -1,12 +1,12 @@
 // mbarrier + bulk-copy (TMA, non-tensor) helpers for sm_100a kernels.
-// No load anywhere uses .multicast::cluster.
+// Every bulk copy here is a plain CTA-local copy (one destination CTA).
 #pragma once
 #include "f5_int.cuh"
 
 namespace f5 {
 
 // ---------------------------------------------------------------------------
-// mbarrier / bulk-copy helpers (PTX ISA 8.x, sm_90+; no multicast anywhere)
+// mbarrier / bulk-copy helpers (PTX ISA 8.x, sm_90+; single-destination copies only)
 // ---------------------------------------------------------------------------
 F5_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 F5_DEV void mbar_init(uint64_t *b, int cnt) {
