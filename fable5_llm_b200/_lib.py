@@ -66,6 +66,8 @@ SIGNATURES = [
     ("f5_ctx_prepare", c_int, [c_vp]),
     ("f5_ctx_set_engine", c_int, [c_vp, c_int]),
     ("f5_ctx_get_engine", c_int, [c_vp, c_vp]),
+    ("f5_ctx_ipc_handle", c_int, [c_vp, c_vp, c_size]),
+    ("f5_ctx_attach_peers", c_int, [c_vp, c_vp, c_int]),
     ("f5_ctx_trace_step", c_int, [c_vp, c_vp, c_size, c_vp, c_vp]),
     ("f5_decode_step", c_int, [c_vp, c_int, c_int, c_vp, c_vp]),
     ("f5_decode_launch", c_int, [c_vp, c_int, c_vp]),

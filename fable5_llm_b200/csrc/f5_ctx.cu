@@ -161,7 +161,12 @@ struct f5_ctx {
   };
   std::vector<Twin> twins;
   uint32_t *twin_mem = nullptr;
-  size_t twin_bytes = 0;
+  size_t twin_bytes = 0;        // twins + the cross-rank argmax key slots at the end
+  unsigned long long *xkey = nullptr;
+  // row sharding: peers' twin allocations mapped through CUDA IPC
+  void *peer_base[f5::F5_MAX_RANKS] = {};
+  long long peer_delta[f5::F5_MAX_RANKS] = {};
+  bool peers_attached = false;
   std::vector<void *> allocs;
 };
 
@@ -614,6 +619,30 @@ static int build_graph(f5_ctx *c) {
   return F5_OK;
 }
 
+// The dataflow-tagged twins of the activations the persistent program passes
+// between ops, plus the cross-rank argmax key slots, in ONE allocation (one
+// CUDA IPC handle per rank; the layout is identical on every rank).
+static int ensure_twins(f5_ctx *c) {
+  if (c->twin_mem) return F5_OK;
+  struct { void *p; size_t bytes, elem; } tw[] = {
+      {c->x16, H * 2, 2}, {c->qkvc16, CONV_DIM * 2, 2}, {c->z16, LVD * 2, 2}, {c->gates, 2 * LNH * 4, 4},
+      {c->on16, LVD * 2, 2}, {c->prod16, FFN * 2, 2}, {c->qg16, NQ * HD * 2 * 2, 2}, {c->k16, NKV * HD * 2, 2},
+      {c->v16, NKV * HD * 2, 2}};
+  size_t words = 0;
+  for (auto &t : tw) words += t.bytes / t.elem;
+  words = (words + 3) & ~(size_t)3;   // 16-byte aligned key slots
+  const size_t key_bytes = (size_t)F5_MAX_RANKS * 2 * 8;
+  F5_ALLOC(c, c->twin_mem, words * 4 + key_bytes);
+  c->twin_bytes = words * 4 + key_bytes;
+  c->xkey = reinterpret_cast<unsigned long long *>(c->twin_mem + words);
+  words = 0;
+  for (auto &t : tw) {
+    c->twins.push_back({t.p, t.bytes, t.elem, c->twin_mem + words, 0});
+    words += t.bytes / t.elem;
+  }
+  return F5_OK;
+}
+
 static void free_mega(f5_ctx *c) {
   if (c->d_ops) cudaFree(c->d_ops);
   if (c->d_bars) cudaFree(c->d_bars);
@@ -630,7 +659,9 @@ static int build_mega(f5_ctx *c, bool &unsupported) {
   int rc = ready(c);
   if (rc) return rc;
   unsupported = true;
-  if (c->cfg.world_size > 1) return set_error(F5_ESTATE, "the persistent engine runs unsharded contexts");
+  if (c->cfg.world_size > 1 && !c->peers_attached)
+    return set_error(F5_ESTATE, "row-sharded context: exchange IPC handles (f5_ctx_ipc_handle / f5_ctx_attach_peers) first");
+  if (c->cfg.world_size > F5_MAX_RANKS) return set_error(F5_EINVAL, "at most %d ranks", F5_MAX_RANKS);
   const int sms = sm_count();
   if (sms < 4 * LNH) return set_error(F5_ESTATE, "the persistent engine needs >= %d SMs", 4 * LNH);
   const int cpg = sms / NKV;
@@ -650,23 +681,9 @@ static int build_mega(f5_ctx *c, bool &unsupported) {
     F5_ALLOC(c, c->d_attacc, step_acc_bytes(c, cpg) + 16);
     unsupported = true;
   }
-  if (!c->twin_mem) {
-    struct { void *p; size_t bytes, elem; } tw[] = {
-        {c->x16, H * 2, 2}, {c->qkvc16, CONV_DIM * 2, 2}, {c->z16, LVD * 2, 2}, {c->gates, 2 * LNH * 4, 4},
-        {c->on16, LVD * 2, 2}, {c->prod16, FFN * 2, 2}, {c->qg16, NQ * HD * 2 * 2, 2}, {c->k16, NKV * HD * 2, 2},
-        {c->v16, NKV * HD * 2, 2}};
-    size_t words = 0;
-    for (auto &t : tw) words += t.bytes / t.elem;
-    unsupported = false;
-    F5_ALLOC(c, c->twin_mem, words * 4);
-    c->twin_bytes = words * 4;
-    words = 0;
-    for (auto &t : tw) {
-      c->twins.push_back({t.p, t.bytes, t.elem, c->twin_mem + words, 0});
-      words += t.bytes / t.elem;
-    }
-    unsupported = true;
-  }
+  unsupported = false;
+  if ((rc = ensure_twins(c))) return rc;
+  unsupported = true;
   for (f5_ctx::Twin &t : c->twins) t.last_op1 = 0;
   std::vector<MegaOp> ops;
   c->emit = &ops;
@@ -684,8 +701,19 @@ static int build_mega(f5_ctx *c, bool &unsupported) {
   free_mega(c);
   F5_CU(cudaMalloc(&c->d_ops, ops.size() * sizeof(MegaOp)), "persistent program");
   F5_CU(cudaMalloc(&c->d_bars, (size_t)nbars * 4), "persistent barriers");
-  for (MegaOp &op : ops)
-    if (op.kind == MK_GEMV) op.g.abort_flag = c->d_bars + nbars - 2;
+  for (MegaOp &op : ops) {
+    if (op.kind == MK_GEMV) {
+      op.g.abort_flag = c->d_bars + nbars - 2;
+      op.g.nrank = c->cfg.world_size;
+      for (int r = 0; r < F5_MAX_RANKS; ++r) op.g.peer_delta[r] = c->peer_delta[r];
+    } else if (op.kind == MK_BEGIN) {
+      // this rank's rows of the 4096-row residual GEMVs (every layer's out /
+      // o_proj / down matrix splits N = 4096 the same way)
+      const DevMat &dm = c->L[0].m[c->L[0].attn ? 3 : 4];
+      op.b.res_row0 = dm.row0;
+      op.b.res_rows = dm.rows;
+    }
+  }
   F5_CU(cudaMemcpyAsync(c->d_ops, ops.data(), ops.size() * sizeof(MegaOp), cudaMemcpyHostToDevice, c->st),
         "persistent program");
   F5_CU(cudaMemsetAsync(c->d_bars, 0, (size_t)nbars * 4, c->st), "persistent barriers");
@@ -701,6 +729,10 @@ static int build_mega(f5_ctx *c, bool &unsupported) {
   m.advance = 1;
   m.dn_heads = LNH;
   m.ns = ns;
+  m.nrank = c->cfg.world_size;
+  m.rank = c->cfg.rank;
+  for (int r = 0; r < F5_MAX_RANKS; ++r) m.peer_delta[r] = c->peer_delta[r];
+  m.xkey = c->xkey;
   // L2 prefetch lead per CTA: off by default (a sweep of 128 KB - 1 MB
   // leads measured no gain: the TMA ring refills from L2 barely faster than
   // from HBM); F5_MEGA_PREFETCH_KB sets it for experiments
@@ -818,6 +850,8 @@ int f5_ctx_destroy(f5_ctx *c) {
   if (c->st) cudaStreamSynchronize(c->st);
   if (c->step_exec) cudaGraphExecDestroy(c->step_exec);
   free_mega(c);
+  for (int r = 0; r < F5_MAX_RANKS; ++r)
+    if (c->peer_base[r]) cudaIpcCloseMemHandle(c->peer_base[r]);
   for (void *p : c->allocs) cudaFree(p);
   if (c->h_params) cudaFreeHost(c->h_params);
   if (c->st) cudaStreamDestroy(c->st);
@@ -1018,6 +1052,42 @@ int f5_ctx_get_engine(f5_ctx *c, int *engine) {
   if (!engine) return set_error(F5_EINVAL, "f5_ctx_get_engine: null out");
   DevGuard dg(c->device);
   return resolve_engine(c, *engine);
+}
+
+int f5_ctx_ipc_handle(f5_ctx *c, void *handle, size_t cap) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  if (!handle || cap < sizeof(cudaIpcMemHandle_t)) return set_error(F5_EINVAL, "f5_ctx_ipc_handle: %zu-byte buffer", sizeof(cudaIpcMemHandle_t));
+  DevGuard dg(c->device);
+  if ((rc = ensure_twins(c))) return rc;
+  cudaIpcMemHandle_t h;
+  F5_CU(cudaIpcGetMemHandle(&h, c->twin_mem), "cudaIpcGetMemHandle");
+  memcpy(handle, &h, sizeof(h));
+  return F5_OK;
+}
+
+int f5_ctx_attach_peers(f5_ctx *c, const void *handles, int n) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  if (!handles || n != c->cfg.world_size || n > F5_MAX_RANKS)
+    return set_error(F5_EINVAL, "f5_ctx_attach_peers: %d handles for world size %d", n, c->cfg.world_size);
+  if (c->peers_attached) return set_error(F5_ESTATE, "peers already attached");
+  DevGuard dg(c->device);
+  if ((rc = ensure_twins(c))) return rc;
+  const cudaIpcMemHandle_t *hs = static_cast<const cudaIpcMemHandle_t *>(handles);
+  for (int r = 0; r < n; ++r) {
+    if (r == c->cfg.rank) {
+      c->peer_delta[r] = 0;
+      continue;
+    }
+    void *p = nullptr;
+    F5_CU(cudaIpcOpenMemHandle(&p, hs[r], cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+    c->peer_base[r] = p;
+    c->peer_delta[r] = static_cast<char *>(p) - reinterpret_cast<char *>(c->twin_mem);
+  }
+  c->peers_attached = true;
+  c->graph_dirty = c->mega_dirty = true;
+  return F5_OK;
 }
 
 int f5_ctx_trace_step(f5_ctx *c, uint64_t *out, size_t cap, int *grid, int *nops) {

@@ -21,6 +21,15 @@ namespace f5 {
 F5_DEV uint32_t mk_tag(uint32_t epoch, int op1) { return (epoch << 8) | ((uint32_t)(op1 - 1) & 0xFFu); }
 F5_DEV uint32_t tag_word(uint32_t tag, int32_t v) { return (tag << 16) | ((uint32_t)v & 0xFFFFu); }
 F5_DEV int32_t tag_s16(uint32_t w) { return (int32_t)(int16_t)(w & 0xFFFFu); }
+// a tagged output word: into this GPU's twin and, row-sharded, every peer's
+// (the fused all-gather of the GEMV's output rows: plain 4-byte stores)
+F5_DEV void st_tagged(const GemvArgs &a, uint32_t *p, uint32_t w) {
+  if (a.nrank <= 1) {
+    *p = w;
+    return;
+  }
+  for (int r = 0; r < a.nrank; ++r) *reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(p) + a.peer_delta[r]) = w;
+}
 
 // Bounded poll until the n words at p (n = 1, 2 or 8; 16-byte aligned for 8)
 // all carry `tag`; reads at L2.  Gives up after 1 s (or once the kernel's
@@ -479,14 +488,14 @@ F5_DEV void epilogue_row(const GemvArgs &a, const GemvSeg &sg, int row, long lon
     case GM_Y32: static_cast<int32_t *>(sg.out)[orow] = y; break;
     case GM_TO16: {
       const int32_t v = clip16(shift_to(y, sh2));
-      if (tag) static_cast<uint32_t *>(sg.out)[orow] = tag_word(tag, v);
+      if (tag) st_tagged(a, static_cast<uint32_t *>(sg.out) + orow, tag_word(tag, v));
       else static_cast<int16_t *>(sg.out)[orow] = (int16_t)v;
     } break;
     case GM_TO64: static_cast<int64_t *>(sg.out)[orow] = shift_to(y, sh2); break;
     case GM_RESID:
       if (tag) {   // the row's previous word was written by this CTA (same row partition)
         uint32_t *o = static_cast<uint32_t *>(sg.out) + orow;
-        *o = tag_word(tag, clip16((int64_t)tag_s16(__ldcg(o)) + clip16(shift_to(y, sh2))));
+        st_tagged(a, o, tag_word(tag, clip16((int64_t)tag_s16(__ldcg(o)) + clip16(shift_to(y, sh2)))));
       } else {
         int16_t *o = static_cast<int16_t *>(sg.out) + orow;   // written by other CTAs: read at L2
         *o = (int16_t)clip16((int64_t)__ldcg(o) + clip16(shift_to(y, sh2)));
@@ -502,7 +511,7 @@ F5_DEV void epilogue_row(const GemvArgs &a, const GemvSeg &sg, int row, long lon
       const int T = *sg.T;
       const uint2 rw = *reinterpret_cast<const uint2 *>(ring);   // 4 int16 slots
       const int32_t qc = conv_silu(v, rw, cw, T);
-      if (tag) static_cast<uint32_t *>(sg.aux_out)[orow] = tag_word(tag, qc);
+      if (tag) st_tagged(a, static_cast<uint32_t *>(sg.aux_out) + orow, tag_word(tag, qc));
       else static_cast<int16_t *>(sg.aux_out)[orow] = (int16_t)qc;
       ring[T & 3] = (int16_t)v;
     } break;
@@ -510,7 +519,7 @@ F5_DEV void epilogue_row(const GemvArgs &a, const GemvSeg &sg, int row, long lon
       const long long v = clip16(shift_to(y, sh2));
       if (sg.out) static_cast<int16_t *>(sg.out)[orow] = (int16_t)v;
       const int32_t beta = (int32_t)sigmoid_q(v);
-      if (tag) static_cast<uint32_t *>(sg.aux_out)[orow] = tag_word(tag, beta);
+      if (tag) st_tagged(a, static_cast<uint32_t *>(sg.aux_out) + orow, tag_word(tag, beta));
       else static_cast<int32_t *>(sg.aux_out)[orow] = beta;
     } break;
     case GM_GATE_A: {   // ref/layer_fixed.py:1532-1538
@@ -518,7 +527,7 @@ F5_DEV void epilogue_row(const GemvArgs &a, const GemvSeg &sg, int row, long lon
       if (sg.out) static_cast<int16_t *>(sg.out)[orow] = (int16_t)v;
       const int32_t d = decay_gate(v, static_cast<const int32_t *>(sg.aux0)[orow],
                                    static_cast<const int32_t *>(sg.aux1)[orow]);
-      if (tag) static_cast<uint32_t *>(sg.aux_out)[orow] = tag_word(tag, d);
+      if (tag) st_tagged(a, static_cast<uint32_t *>(sg.aux_out) + orow, tag_word(tag, d));
       else static_cast<int32_t *>(sg.aux_out)[orow] = d;
     } break;
     default: break;
@@ -534,7 +543,7 @@ F5_DEV void epilogue_pair(const GemvArgs &a, const GemvSeg &sg, int row, long lo
   const int64_t uq = shift_to(yu, (15 - sg.e2 - a.sh) - e_x + in_f - sg.out_f2);
   const int64_t sgv = clip16(silu_q(clip(gq, -(1 << 20), (1 << 20) - 1)));
   const int32_t v = clip16(rshr(sgv * uq, 12));
-  if (epoch && sg.tag_op1) static_cast<uint32_t *>(sg.out)[sg.out_row0 + row] = tag_word(mk_tag(epoch, sg.tag_op1), v);
+  if (epoch && sg.tag_op1) st_tagged(a, static_cast<uint32_t *>(sg.out) + sg.out_row0 + row, tag_word(mk_tag(epoch, sg.tag_op1), v));
   else static_cast<int16_t *>(sg.out)[sg.out_row0 + row] = (int16_t)v;
 }
 

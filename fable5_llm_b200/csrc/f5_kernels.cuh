@@ -60,6 +60,7 @@ enum GemvMode : int {
 };
 
 constexpr int GEMV_MAX_SEG = 4;
+constexpr int F5_MAX_RANKS = 8;
 
 // How a GEMV CTA obtains its quantized input x8 (+ e_x, in_f).  Every CTA
 // computes the prologue redundantly from the producer's vector (<= 32 KB,
@@ -122,6 +123,11 @@ struct GemvArgs {
   unsigned long long *argmax_key;
   uint32_t *err;
   unsigned *abort_flag;   // persistent kernel: global abort flag polled by bounded tag waits
+  // persistent kernel, row-sharded across nrank GPUs: every tagged output
+  // word is also stored into each rank's twin buffer, at the local address
+  // + peer_delta[r] (CUDA IPC mappings over NVLink; own rank: delta 0)
+  int nrank;
+  long long peer_delta[F5_MAX_RANKS];
 };
 
 cudaError_t launch_gemv(const GemvArgs &a, cudaStream_t st, bool pdl, int max_blocks);

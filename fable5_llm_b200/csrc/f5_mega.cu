@@ -446,7 +446,7 @@ F5_DEV void mega_epilogue_row(const GemvArgs &a, const GemvSeg &sg, int i, int u
   const long long v = clip16(shift_to(y, (15 - sg.e - a.sh) - e_x + in_f - sg.out_f));
   const int32_t nv = clip16((int64_t)mg_xres[i] + v);
   mg_xres[i] = (int16_t)nv;
-  static_cast<uint32_t *>(sg.out)[orow] = tag_word(tag, nv);
+  st_tagged(a, static_cast<uint32_t *>(sg.out) + orow, tag_word(tag, nv));
 }
 // K = 4096 (every GEMV of the step but the MLP down projection): one row per
 // consumer warp per 16-row stage.  The consumer loop is issue-bound, so it is
@@ -1070,16 +1070,14 @@ F5_DEV void c_begin(const MegaArgs &ma, const MegaBegin &B, int tok, uint32_t ep
     tok = 0;
   }
   if (B.x16t) {
-    // tagged residual: each CTA writes the rows its residual epilogues own
-    // (the 4096-row partition), tagged as op 0
+    // tagged residual, the whole vector on every GPU (tagged as op 0); the
+    // CTA's own residual rows -- the rows its residual epilogues own: this
+    // rank's share, partitioned over the CTAs -- are also kept in mg_xres
     const int16_t *src = B.emb + (size_t)tok * B.H;
     const uint32_t tag = mk_tag(epoch, 1);
-    const int r0 = part_lo(B.H, G, b);
-    for (int i = r0 + tid; i < part_lo(B.H, G, b + 1); i += MG_CT) {
-      const int16_t v = src[i];
-      B.x16t[i] = tag_word(tag, v);
-      if (i - r0 < MG_XRES) mg_xres[i - r0] = v;
-    }
+    for (int i = part_lo(B.H, G, b) + tid; i < part_lo(B.H, G, b + 1); i += MG_CT) B.x16t[i] = tag_word(tag, src[i]);
+    const int r0 = B.res_row0 + part_lo(B.res_rows, G, b), r1 = B.res_row0 + part_lo(B.res_rows, G, b + 1);
+    for (int i = r0 + tid; i < r1 && i - r0 < MG_XRES; i += MG_CT) mg_xres[i - r0] = src[i];
   } else {
     const uint4 *src = reinterpret_cast<const uint4 *>(B.emb + (size_t)tok * B.H);
     uint4 *dst = reinterpret_cast<uint4 *>(B.x16);
@@ -1207,8 +1205,41 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega(const __grid_constant_
   if (tid == 0) {
     // step end (ref/gen_model_script.py:641 argmax, first max wins)
     StepParams *p = ma.params;
-    const unsigned long long k = __ldcg(ma.ops[ma.nops - 1].g.argmax_key);
-    const bool aborted = __ldcg(ma.bars + ma.nbars - 2) != 0;
+    unsigned long long k = __ldcg(ma.ops[ma.nops - 1].g.argmax_key);
+    bool aborted = __ldcg(ma.bars + ma.nbars - 2) != 0;
+    if (ma.nrank > 1) {
+      // vocab-sharded head: publish this rank's key to every rank (two words
+      // {half, marker = launch + 1}), then combine all ranks' keys; the
+      // global row index is in the key, so max over ranks = the first max
+      const unsigned long long mk = (unsigned long long)(uint32_t)(vp->launch + 1) << 32;
+      for (int r = 0; r < ma.nrank; ++r) {
+        unsigned long long *d = reinterpret_cast<unsigned long long *>(
+            reinterpret_cast<char *>(ma.xkey + 2 * ma.rank) + ma.peer_delta[r]);
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(d), "l"(mk | (k & 0xFFFFFFFFull)) : "memory");
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(d + 1), "l"(mk | (k >> 32)) : "memory");
+      }
+      unsigned long long best = 0ull, t0 = 0;
+      for (int r = 0; r < ma.nrank && !aborted; ++r) {
+        for (uint32_t it = 0;; ++it) {
+          unsigned long long lo, hi;
+          asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(lo) : "l"(ma.xkey + 2 * r) : "memory");
+          asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(hi) : "l"(ma.xkey + 2 * r + 1) : "memory");
+          if ((lo & ~0xFFFFFFFFull) == mk && (hi & ~0xFFFFFFFFull) == mk) {
+            const unsigned long long kr = (hi << 32) | (lo & 0xFFFFFFFFull);
+            best = kr > best ? kr : best;
+            break;
+          }
+          const unsigned long long t = gtimer();
+          if (t0 == 0) t0 = t;
+          else if (t - t0 > MG_WAIT_NS) {
+            atomicOr(ma.err, DERR_TIMEOUT);
+            aborted = true;
+            break;
+          }
+        }
+      }
+      k = best;
+    }
     const int row = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
     p->next_tok = row;
     p->max_val = (int)((uint32_t)(k >> 32) ^ 0x80000000u);

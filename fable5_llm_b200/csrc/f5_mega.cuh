@@ -22,6 +22,7 @@ struct MegaBegin {
   const int16_t *emb;         // [vocab][H]
   int16_t *x16;               // [H] plain residual (written back at the step's end)
   uint32_t *x16t;             // [H] tagged residual the step works on
+  int res_row0, res_rows;     // this rank's rows of the 4096-row residual GEMVs
   int vocab, H;
   unsigned long long *key;    // LM-head argmax key
   uint4 *zero;                // attention accumulators, cleared every step
@@ -62,6 +63,12 @@ struct MegaArgs {
   int ns;           // ring stages (from mega_config)
   unsigned long long *trace;   // optional [G][nops][MEGA_TRACE_SLOTS] globaltimer marks
   long long pf_bytes;          // L2 prefetch lead per CTA in weight bytes (0: off)
+  // row-sharded across nrank GPUs: the LM head's argmax keys are exchanged
+  // through xkey ([F5_MAX_RANKS][2] marked words, in the twin allocation,
+  // peers at + peer_delta[r])
+  int nrank, rank;
+  long long peer_delta[F5_MAX_RANKS];
+  unsigned long long *xkey;
 };
 
 constexpr int MEGA_THREADS = 576;       // 16 consumer warps + producer warp + L2-prefetch warp

@@ -172,6 +172,20 @@ class DecodeModel:
         code = {"graph": L.ENGINE_GRAPH, "persistent": L.ENGINE_PERSISTENT}[engine]
         L.check(self.lib.f5_ctx_set_engine(self.h, code), "set_engine")
 
+    # ---- row sharding (one process / context per GPU) ----
+    def ipc_handle(self):
+        """This rank's 64-byte CUDA IPC handle of its dataflow buffers."""
+        buf = ctypes.create_string_buffer(64)
+        L.check(self.lib.f5_ctx_ipc_handle(self.h, buf, 64), "f5_ctx_ipc_handle")
+        return buf.raw
+
+    def attach_peers(self, handles):
+        """All ranks' handles in rank order (this rank's own included)."""
+        blob = b"".join(handles)
+        assert len(blob) == 64 * len(handles)
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        L.check(self.lib.f5_ctx_attach_peers(self.h, buf, len(handles)), "f5_ctx_attach_peers")
+
     def trace_step(self):
         """One persistent greedy step with per-op device timestamps ->
         (ns int64[grid, nops, 8] marks relative to the earliest start, -1

@@ -229,6 +229,17 @@ int f5_ctx_set_engine(f5_ctx *ctx, int engine);
 /* the engine the next step uses (builds its program if needed) */
 int f5_ctx_get_engine(f5_ctx *ctx, int *engine);
 
+/* Row-sharded decode across world_size GPUs (one process and context per
+ * GPU; replaces the reference's 4-DIMM channel split, ref/seq_format.py:
+ * 1177-1189 split_rows).  Each rank streams only its rows of every matrix
+ * and its GEMV epilogues store their output words into every rank's buffers
+ * (peer stores over NVLink, fused into the epilogue); the vector work is
+ * replicated.  Before the first step, each rank exports its handle
+ * (cudaIpcMemHandle_t, 64 bytes), the caller all-gathers them, and every
+ * rank attaches all of them in rank order.  Persistent engine only. */
+int f5_ctx_ipc_handle(f5_ctx *ctx, void *handle, size_t cap);
+int f5_ctx_attach_peers(f5_ctx *ctx, const void *handles, int n);
+
 /* Timeline of one persistent step (no reference counterpart: profiling aid).
  * Runs one greedy step (caches advance) with every CTA recording the device
  * globaltimer (ns) at 8 marks of each op: out[(cta * nops + op) * 8 + k],
