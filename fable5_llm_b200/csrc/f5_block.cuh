@@ -112,6 +112,82 @@ F5_DEV long long g_sum_split(const SY &sy, long long v, long long *red) {
   const long long phi = warp_sum_s64(p >> 22);
   return (phi << 22) + (long long)plo;
 }
+// Two sums (|a|, |b| < 2^40 per thread) in one barrier round.
+template <class SY>
+F5_DEV void g_sum2_split(const SY &sy, long long a, long long b, long long *red, long long &sa, long long &sb) {
+  const long long wa = ((long long)__reduce_add_sync(0xffffffffu, (int)(a >> 22)) << 22) +
+                       (long long)__reduce_add_sync(0xffffffffu, (unsigned)a & 0x3FFFFFu);
+  const long long wb = ((long long)__reduce_add_sync(0xffffffffu, (int)(b >> 22)) << 22) +
+                       (long long)__reduce_add_sync(0xffffffffu, (unsigned)b & 0x3FFFFFu);
+  const int wi = sy.tid() >> 5, nw = sy.n() >> 5, lane = sy.tid() & 31;
+  sy.sync();
+  if (lane == 0) {
+    red[wi] = wa;
+    red[32 + wi] = wb;
+  }
+  sy.sync();
+  const long long pa = lane < nw ? red[lane] : 0, pb = lane < nw ? red[32 + lane] : 0;
+  sa = ((warp_sum_s64(pa >> 22)) << 22) + (long long)__reduce_add_sync(0xffffffffu, (unsigned)pa & 0x3FFFFFu);
+  sb = ((warp_sum_s64(pb >> 22)) << 22) + (long long)__reduce_add_sync(0xffffffffu, (unsigned)pb & 0x3FFFFFu);
+}
+// Max of u64 a and wrapping u64 sum of b in one barrier round.
+template <class SY>
+F5_DEV void g_max_sum_ull(const SY &sy, unsigned long long a, unsigned long long b, unsigned long long *red,
+                          unsigned long long &ma, unsigned long long &sb) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(0xffffffffu, a, o);
+    a = t > a ? t : a;
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  const int wi = sy.tid() >> 5, nw = sy.n() >> 5, lane = sy.tid() & 31;
+  sy.sync();
+  if (lane == 0) {
+    red[wi] = a;
+    red[32 + wi] = b;
+  }
+  sy.sync();
+  a = lane < nw ? red[lane] : 0ull;
+  b = lane < nw ? red[32 + lane] : 0ull;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(0xffffffffu, a, o);
+    a = t > a ? t : a;
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  ma = a;
+  sb = b;
+}
+
+// Two u64 maxima in one barrier round.
+template <class SY>
+F5_DEV void g_max2_ull(const SY &sy, unsigned long long a, unsigned long long b, unsigned long long *red,
+                       unsigned long long &ma, unsigned long long &mb) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(0xffffffffu, a, o), u = __shfl_xor_sync(0xffffffffu, b, o);
+    a = t > a ? t : a;
+    b = u > b ? u : b;
+  }
+  const int wi = sy.tid() >> 5, nw = sy.n() >> 5, lane = sy.tid() & 31;
+  sy.sync();
+  if (lane == 0) {
+    red[wi] = a;
+    red[32 + wi] = b;
+  }
+  sy.sync();
+  a = lane < nw ? red[lane] : 0ull;
+  b = lane < nw ? red[32 + lane] : 0ull;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(0xffffffffu, a, o), u = __shfl_xor_sync(0xffffffffu, b, o);
+    a = t > a ? t : a;
+    b = u > b ? u : b;
+  }
+  ma = a;
+  mb = b;
+}
+
 // Max over the group of 32-bit unsigned values (redux.sync.max per warp).
 template <class SY>
 F5_DEV unsigned g_max_u32(const SY &sy, unsigned v, long long *red) {

@@ -309,18 +309,14 @@ F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red,
         for (int j = 0; j < MAXB; ++j)
 #pragma unroll
           for (int k = 0; k < 8; ++k) { const int32_t v = get16i(raw[j], k); ss += (long long)(v * v); }
-        ss = g_sum_split(sy, ss, red);
+        ss = g_sum_split(sy, ss, red);   // the same value in every thread
         F5_PRO_MARK(4);
-        if (tid == 0) {
-          int64_t r; int e;
-          rsqrt_q((uint64_t)(ss == 0 ? 1 : ss), 2 * P.in_f + (31 - __clz(K)), r, e);
-          *s_r = r;
-          s_meta[2] = e;
-        }
-        sy.sync();
+        // every thread evaluates rsqrt_q itself (uniform input: the LUT read
+        // is a broadcast) instead of one thread and a barrier to publish it
+        int64_t r;
+        int e;
+        rsqrt_q((uint64_t)(ss == 0 ? 1 : ss), 2 * P.in_f + (31 - __clz(K)), r, e);
         F5_PRO_MARK(6);
-        const long long r = *s_r;
-        const int e = s_meta[2];
         const int add1 = P.one_plus ? (1 << 14) : 0;
         // fast path when rsqrt's r and shift are in rms_elem32's domain (always
         // for int16 inputs of H = 4096); the general law otherwise

@@ -661,23 +661,18 @@ F5_DEV bool c_dn(const MegaArgs &ma, const DnArgs &d, const MegaSmem &S, int &w_
     mg_gate[0] = ld_inu(d.beta, h, itag, ab);
     mg_gate[1] = ld_inu(d.decay, h, itag, ab);
   }
-  // ---- l2norm of q and k (ref/layer_fixed.py:1322-1330) ----
-  const long long ssq = g_sum_split(sy, qv * qv, mg_red);
-  const long long ssk = g_sum_split(sy, kv * kv, mg_red);
-  if (tid == 0) {
-    int64_t r; int e;
-    rsqrt_q((uint64_t)(ssq == 0 ? 1 : ssq), 2 * QKV_F, r, e);
-    mg_gate[2] = r; mg_e[0] = e;
-  } else if (tid == 32) {
-    int64_t r; int e;
-    rsqrt_q((uint64_t)(ssk == 0 ? 1 : ssk), 2 * QKV_F, r, e);
-    mg_gate[3] = r; mg_e[1] = e;
-  }
-  sy.sync();
+  // ---- l2norm of q and k (ref/layer_fixed.py:1322-1330): both sums in one
+  // round; the q / k rsqrt by the threads that use them (uniform inputs) ----
+  long long ssq, ssk;
+  g_sum2_split(sy, qv * qv, kv * kv, mg_red, ssq, ssk);
   if (tid < 128) {
-    const long long q16 = clip16(rshr(qv * mg_gate[2], QKV_F + 30 - mg_e[0] - NRM_F));
+    int64_t rq, rk;
+    int eq, ek;
+    rsqrt_q((uint64_t)(ssq == 0 ? 1 : ssq), 2 * QKV_F, rq, eq);
+    rsqrt_q((uint64_t)(ssk == 0 ? 1 : ssk), 2 * QKV_F, rk, ek);
+    const long long q16 = clip16(rshr(qv * rq, QKV_F + 30 - eq - NRM_F));
     qn[tid] = (int32_t)rshr(q16 * 2896, 15);    // round(2^15 / sqrt(128)) = 2896
-    kn[tid] = (int32_t)clip16(rshr(kv * mg_gate[3], QKV_F + 30 - mg_e[1] - NRM_F));
+    kn[tid] = (int32_t)clip16(rshr(kv * rk, QKV_F + 30 - ek - NRM_F));
   }
   MG_MARK(2);
   const bool got = mwait((&mg_bsd), w_sd & 1, ab);
@@ -735,15 +730,19 @@ F5_DEV bool c_dn(const MegaArgs &ma, const DnArgs &d, const MegaSmem &S, int &w_
   MG_MARK(5);
   // ---- block-float k_h (ref/layer_fixed.py:470-486) and the gated norm
   // (ref/layer_fixed.py:509-546 or 694-781); identical in the four CTAs ----
-  const unsigned long long om = g_max_ull(sy, tid < 128 ? uabs(ov) : 0ull, reinterpret_cast<unsigned long long *>(mg_red));
+  // float mode: max |o| and the numpy int64 (wrapping, order-free) sum of
+  // o*o in one round; eps mode needs k_h before its sum
+  unsigned long long om, ssu = 0ull;
+  if (d.norm_mode == 0)
+    g_max_sum_ull(sy, tid < 128 ? uabs(ov) : 0ull, (unsigned long long)ov * (unsigned long long)ov,
+                  reinterpret_cast<unsigned long long *>(mg_red), om, ssu);
+  else
+    om = g_max_ull(sy, tid < 128 ? uabs(ov) : 0ull, reinterpret_cast<unsigned long long *>(mg_red));
   const int kh_shift = bf_shift(om);
   const long long o16 = clip16(kh_shift >= 0 ? rshr(ov, kh_shift) : (long long)((unsigned long long)ov << (-kh_shift)));
   long long m;
   if (d.norm_mode == 0) {
-    // numpy int64 sum of o*o (wrapping modulo 2^64, order-free)
-    const long long ss = (long long)g_sum_ull(sy, (unsigned long long)ov * (unsigned long long)ov,
-                                              reinterpret_cast<unsigned long long *>(mg_red));
-    m = dn_norm_scale(ss, kh_shift, 128);
+    m = dn_norm_scale((long long)ssu, kh_shift, 128);
   } else {
     const long long ss = g_sum_ll(sy, o16 * o16, mg_red);
     m = eps_norm_scale(ss, kh_shift, 7);
@@ -769,34 +768,54 @@ F5_DEV bool c_dn(const MegaArgs &ma, const DnArgs &d, const MegaSmem &S, int &w_
 // consumers: attention (ref/layer_fixed.py:1383-1449)
 // ---------------------------------------------------------------------------
 // RMSNorm(1+w) over a 256-dim head (ref/layer_fixed.py:1242-1278) then
-// rope_fx on the first `rot` dims (ref/layer_fixed.py:1340-1348), for four
-// heads at once: thread t owns dims e and e+128 (e = t & 127) of head t>>7.
-F5_DEV void norm_rope4(const CSync &sy, long long x0, long long x1, long long w0, long long w1, long long cosv,
-                       long long sinv, int rot, int16_t *xn, int16_t *out, int nslots, long long *red) {
+// rope_fx on the first `rot` dims (ref/layer_fixed.py:1340-1348), for the four
+// q heads and the one k head at once: thread t owns dims e and e+128
+// (e = t & 127) of q head t>>7, and threads t < 128 the same dims of k.  The
+// five sums share one barrier round.  q goes to q16 (shared), k stays in the
+// registers k0 / k1 of threads t < 128.
+F5_DEV void norm_rope_qk(const CSync &sy, long long qx0, long long qx1, long long qw0, long long qw1, long long kx0,
+                         long long kx1, long long kw0, long long kw1, long long cosv, long long sinv, int rot,
+                         int16_t *qn, int16_t *kn, int16_t *q16, long long &k0, long long &k1, long long *red) {
   const int t = sy.tid(), hs = t >> 7, e = t & 127, warp = t >> 5, lane = t & 31;
-  const long long ss = warp_sum_ll(x0 * x0 + x1 * x1);
-  if (lane == 0) red[warp] = ss;
+  const bool kt = t < 128;
+  const long long ssq = warp_sum_ll(qx0 * qx0 + qx1 * qx1);
+  const long long ssk = warp_sum_ll(kx0 * kx0 + kx1 * kx1);
+  if (lane == 0) {
+    red[warp] = ssq;
+    red[16 + warp] = ssk;
+  }
   sy.sync();
-  const long long tot = red[4 * hs] + red[4 * hs + 1] + red[4 * hs + 2] + red[4 * hs + 3];
-  int64_t r;
-  int ee;
-  rsqrt_q((uint64_t)(tot == 0 ? 1 : tot), 2 * QKV_F + 8, r, ee);   // n = 256
-  const long long n0 = clip16(rshr(clip(rshr(x0 * r, 30 - ee), -(1ll << 32), (1ll << 32) - 1) * (w0 + (1 << 14)), 14));
-  const long long n1 = clip16(rshr(clip(rshr(x1 * r, 30 - ee), -(1ll << 32), (1ll << 32) - 1) * (w1 + (1 << 14)), 14));
-  xn[hs * 256 + e] = (int16_t)n0;
-  xn[hs * 256 + e + 128] = (int16_t)n1;
+  auto nrm = [&](long long tot, long long x0, long long x1, long long w0, long long w1, long long &n0, long long &n1) {
+    int64_t r;
+    int ee;
+    rsqrt_q((uint64_t)(tot == 0 ? 1 : tot), 2 * QKV_F + 8, r, ee);   // n = 256
+    n0 = clip16(rshr(clip(rshr(x0 * r, 30 - ee), -(1ll << 32), (1ll << 32) - 1) * (w0 + (1 << 14)), 14));
+    n1 = clip16(rshr(clip(rshr(x1 * r, 30 - ee), -(1ll << 32), (1ll << 32) - 1) * (w1 + (1 << 14)), 14));
+  };
+  long long n0, n1, m0 = 0, m1 = 0;
+  nrm(red[4 * hs] + red[4 * hs + 1] + red[4 * hs + 2] + red[4 * hs + 3], qx0, qx1, qw0, qw1, n0, n1);
+  qn[hs * 256 + e] = (int16_t)n0;
+  qn[hs * 256 + e + 128] = (int16_t)n1;
+  if (kt) {
+    nrm(red[16] + red[17] + red[18] + red[19], kx0, kx1, kw0, kw1, m0, m1);
+    kn[e] = (int16_t)m0;
+    kn[e + 128] = (int16_t)m1;
+  }
   sy.sync();
+  const int hh = rot >> 1;
   long long o0 = n0;
   if (e < rot) {   // rot <= 128: dims e + 128 are never rotated
-    const int hh = rot >> 1;
-    const long long rr = e < hh ? -(long long)xn[hs * 256 + e + hh] : (long long)xn[hs * 256 + e - hh];
+    const long long rr = e < hh ? -(long long)qn[hs * 256 + e + hh] : (long long)qn[hs * 256 + e - hh];
     o0 = clip16(rshr(n0 * cosv + rr * sinv, ROPE_F));
   }
-  if (hs < nslots) {
-    out[hs * 256 + e] = (int16_t)o0;
-    out[hs * 256 + e + 128] = (int16_t)n1;
+  q16[hs * 256 + e] = (int16_t)o0;
+  q16[hs * 256 + e + 128] = (int16_t)n1;
+  k0 = m0;
+  k1 = m1;
+  if (kt && e < rot) {
+    const long long rr = e < hh ? -(long long)kn[e + hh] : (long long)kn[e - hh];
+    k0 = clip16(rshr(m0 * cosv + rr * sinv, ROPE_F));
   }
-  sy.sync();
 }
 
 // Gather the cpg CTAs' marked per-head values of one phase and combine them
@@ -865,13 +884,14 @@ F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int
   const long long cosv = e < a.rot ? __ldcg(cs + e) : 0, sinv = e < a.rot ? __ldcg(cs + 64 + e) : 0;
 
   // ---- 1. q / k norm + rope; kv_quant of the new k and v ----
-  norm_rope4(sy, qx0, qx1, qw0, qw1, cosv, sinv, a.rot, xn, q16, 4, mg_red);
-  norm_rope4(sy, kx0, kx1, kw0, kw1, cosv, sinv, a.rot, xn, k16n, 1, mg_red);
-  const long long kn0 = k_act ? k16n[e] : 0, kn1 = k_act ? k16n[e + 128] : 0;
+  long long kn0, kn1;
+  norm_rope_qk(sy, qx0, qx1, qw0, qw1, kx0, kx1, kw0, kw1, cosv, sinv, a.rot, xn, k16n, q16, kn0, kn1, mg_red);
   const unsigned long long mk0 = uabs(kn0) > uabs(kn1) ? uabs(kn0) : uabs(kn1);
   const unsigned long long mv0 = uabs(v0) > uabs(v1) ? uabs(v0) : uabs(v1);
-  const int ek = dynq8_e(g_max_ull(sy, mk0, reinterpret_cast<unsigned long long *>(mg_red)));
-  const int ev = dynq8_e(g_max_ull(sy, mv0, reinterpret_cast<unsigned long long *>(mg_red)));
+  unsigned long long mk, mv;
+  g_max2_ull(sy, mk0, mv0, reinterpret_cast<unsigned long long *>(mg_red), mk, mv);
+  const int ek = dynq8_e(mk);
+  const int ev = dynq8_e(mv);
   if (k_act) {
     const int8_t k0 = (int8_t)dynq8_apply(kn0, ek), k1 = (int8_t)dynq8_apply(kn1, ek);
     const int8_t w0 = (int8_t)dynq8_apply(v0, ev), w1 = (int8_t)dynq8_apply(v1, ev);
