@@ -228,3 +228,112 @@ done:
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// batched matvec_y32 on the tensor cores
+// ---------------------------------------------------------------------------
+#include "f5_batch.cuh"
+
+namespace {
+struct BmLayout {
+  int NG, Bp, S, tiles;
+  size_t xt, xmeta, p, total;
+};
+size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
+bool bm_layout(int N, int K, int B, BmLayout &L) {
+  if (N <= 0 || K <= 0 || K % 1024 || K > 12288 || B < 1 || B > 64) return false;
+  L.NG = K / 128;
+  L.Bp = B <= 16 ? 16 : (B <= 32 ? 32 : 64);
+  L.tiles = (N + f5::BG_TILE - 1) / f5::BG_TILE;
+  L.S = f5::bgemm_splits(L.tiles, L.NG, f5::sm_count(), false);
+  size_t o = 0;
+  L.xt = o; o += al256((size_t)L.NG * L.Bp * 128);
+  L.xmeta = o; o += al256((size_t)L.Bp * 2 * 4);
+  L.p = o; o += al256((size_t)L.S * L.Bp * N * 8);
+  L.total = o;
+  return true;
+}
+}  // namespace
+
+extern "C" {
+
+int f5_batch_trace(int enable, uint64_t *out, size_t cap) {
+  unsigned long long *&tb = bgemm_trace_buffer();
+  if (enable) {
+    if (!tb) {
+      cudaError_t e = cudaMalloc(&tb, BG_TRACE_WORDS * sizeof(unsigned long long));
+      if (e != cudaSuccess) { tb = nullptr; return cuda_status(e, "f5_batch_trace"); }
+    }
+    return cuda_status(cudaMemset(tb, 0, BG_TRACE_WORDS * sizeof(unsigned long long)), "f5_batch_trace");
+  }
+  if (!tb) return set_error(F5_ESTATE, "f5_batch_trace: tracing is not enabled");
+  int rc = F5_OK;
+  if (out) {
+    const size_t n = cap < (size_t)BG_TRACE_WORDS ? cap : (size_t)BG_TRACE_WORDS;
+    rc = cuda_status(cudaMemcpy(out, tb, n * sizeof(uint64_t), cudaMemcpyDeviceToHost), "f5_batch_trace");
+  }
+  cudaFree(tb);
+  tb = nullptr;
+  return rc;
+}
+
+size_t f5_batch_matvec_ws_bytes(int N, int K, int B) {
+  BmLayout L;
+  return bm_layout(N, K, B, L) ? L.total : 0;
+}
+
+int f5_batch_matvec_y32_dev(const uint8_t *d_w, int N, int K, int g, int sh, const int8_t *d_x8, int B,
+                            int32_t *d_y32, int64_t *d_p, void *d_ws, size_t ws_bytes, uint32_t *d_err,
+                            void *stream) {
+  int st = check_matrix_shape(N, K, g);
+  if (st) return st;
+  BmLayout L;
+  if (g != 128 || !bm_layout(N, K, B, L))
+    return set_error(F5_EINVAL, "f5_batch_matvec_y32_dev: needs g=128, K a multiple of 1024, 1 <= B <= 64");
+  if (!d_w || !d_x8 || !d_y32 || !d_ws || !d_err) return set_error(F5_EINVAL, "f5_batch_matvec_y32_dev: null pointer");
+  if (ws_bytes < L.total) return set_error(F5_EINVAL, "f5_batch_matvec_y32_dev: workspace %zu < %zu bytes", ws_bytes, L.total);
+  if ((reinterpret_cast<uintptr_t>(d_w) | reinterpret_cast<uintptr_t>(d_ws)) & 255)
+    return set_error(F5_EINVAL, "f5_batch_matvec_y32_dev: image and workspace must be 256-byte aligned");
+  uint8_t *ws = static_cast<uint8_t *>(d_ws);
+  cudaStream_t cs = (cudaStream_t)stream;
+  // padded sequences read zero x tiles
+  cudaError_t e = cudaMemsetAsync(ws + L.xt, 0, L.xmeta - L.xt, cs);   // padded sequences: zero x
+  if (e != cudaSuccess) return cuda_status(e, "f5_batch_matvec_y32_dev");
+  BprepArgs pa = {};
+  pa.pro.mode = PRO_X8;
+  pa.K = K; pa.NG = L.NG; pa.B = B; pa.Bp = L.Bp;
+  pa.x8_in = d_x8;
+  pa.xmeta = reinterpret_cast<int *>(ws + L.xmeta);
+  pa.xt = reinterpret_cast<int8_t *>(ws + L.xt);
+  pa.err = d_err;
+  if ((e = launch_bprep(pa, cs, false)) != cudaSuccess) return cuda_status(e, "f5_batch_matvec_y32_dev/prep");
+  BgemmArgs ga = {};
+  ga.nseg = 1;
+  ga.seg[0].w = d_w;
+  ga.seg[0].rows = N;
+  ga.ntiles = L.tiles;
+  ga.K = K; ga.NG = L.NG; ga.stride = row_stride(K, g); ga.sh = sh;
+  ga.S = L.S; ga.B = B; ga.Bp = L.Bp;
+  ga.xt = pa.xt;
+  ga.p = reinterpret_cast<int64_t *>(ws + L.p);
+  ga.ptot = N;
+  ga.err = d_err;
+  if ((e = launch_bgemm(ga, cs, false, sm_count())) != cudaSuccess) return cuda_status(e, "f5_batch_matvec_y32_dev/gemm");
+  BepiArgs ea = {};
+  ea.g.nseg = 1;
+  ea.g.K = K; ea.g.sh = sh; ea.g.err = d_err;
+  ea.g.total_units = N;
+  ea.g.seg[0].out = d_y32;
+  ea.g.seg[0].p_out = d_p;
+  ea.g.seg[0].rows = N;
+  ea.g.seg[0].mode = GM_Y32;
+  ea.bs[0].out_bs = (long long)N * 4;
+  ea.bs[0].pout_bs = (long long)N * 8;
+  ea.S = L.S; ea.B = B; ea.Bp = L.Bp; ea.ptot = N;
+  ea.p = ga.p;
+  ea.xmeta = pa.xmeta;
+  if ((e = launch_bepi(ea, cs, false)) != cudaSuccess) return cuda_status(e, "f5_batch_matvec_y32_dev/epi");
+  return F5_OK;
+}
+
+}  // extern "C"

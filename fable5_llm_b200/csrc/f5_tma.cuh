@@ -48,4 +48,18 @@ F5_DEV void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) 
                : "memory");
 }
 
+// bring [src, src + bytes) into L2 (16-byte aligned address and size)
+F5_DEV void prefetch_l2(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// 2D tiled tensor copy (box of the tensor map at element coordinates x, y;
+// x * element size must be a multiple of 16 bytes), single destination
+F5_DEV void tma_load_2d(void *dst, const void *tmap, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 }  // namespace f5

@@ -99,3 +99,22 @@ def matvec_y32_host(img, N, K, g, sh, x8, want_p=False):
         raise AssertionError("y32 overflow -- sh miscomputed")
     L.check(rc, "f5_matvec_y32_host")
     return (y, p) if want_p else y
+
+
+def batch_matvec_y32(d_img, N, K, sh, d_x8, want_p=False):
+    """Batched matvec_y32 on the tensor cores: d_x8 [B][K] int8 (device),
+    d_img the packed image (device, 256-byte aligned) -> (y32 [B][N], err
+    word[, p [B][N]]) as device tensors, launched on the current stream."""
+    B = int(d_x8.shape[0])
+    ws_bytes = L.lib().f5_batch_matvec_ws_bytes(N, K, B)
+    if not ws_bytes:
+        raise ValueError(f"batched matvec: unsupported shape N={N} K={K} B={B}")
+    ws = torch.empty(ws_bytes + 256, dtype=torch.uint8, device="cuda")
+    off = (-ws.data_ptr()) % 256
+    y = torch.empty((B, N), dtype=torch.int32, device="cuda")
+    p = torch.empty((B, N), dtype=torch.int64, device="cuda") if want_p else None
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    L.check(L.lib().f5_batch_matvec_y32_dev(ptr(d_img), N, K, 128, sh, ptr(d_x8), B, ptr(y), ptr(p),
+                                            ctypes.c_void_p(ws.data_ptr() + off), ws_bytes, ptr(err),
+                                            stream_ptr()), "f5_batch_matvec_y32_dev")
+    return (y, err, p) if want_p else (y, err)

@@ -123,6 +123,27 @@ int f5_synth_w4_dev(uint8_t *d_img, long long nrows, int K, int g, long long row
 int f5_synth_emb_dev(int16_t *d_emb, long long nrows, int H, long long row0,
                      uint64_t key_e, void *stream);
 
+/* Batched ref/w4a8_ref.py:254-289 matvec_y32 on the tensor cores (tcgen05
+ * int8 MMA, int32 TMEM accumulators): y32[b][row] for B quantized inputs
+ * d_x8 [B][K] against one packed image (d_w, 256-byte aligned), the way B
+ * independent decode sequences share a weight matrix.  g = 128, K a multiple
+ * of 1024 (<= 12288), 1 <= B <= 64.  d_ws: 256-byte aligned device workspace
+ * of f5_batch_matvec_ws_bytes(N, K, B) bytes (0: unsupported shape).  d_p
+ * (nullable): int64 p[b][row]; d_err: uint32 error word (bit 0 |y32| >= 2^31,
+ * bit 1 a bounded device wait expired).  No counterpart in the reference,
+ * which runs one sequence at a time: the batched form of matvec_y32. */
+size_t f5_batch_matvec_ws_bytes(int N, int K, int B);
+/* Pipeline trace of the batched GEMM (profiling aid): enable = 1 attaches a
+ * zeroed device buffer of 10240 globaltimer words to every following batched
+ * GEMM launch of the process (CTA 0 records, per stage, when it was issued
+ * and unpacked, and per group when it was unpacked, multiplied, read back
+ * and folded); enable = 0 copies up to cap words into out (nullable) and
+ * detaches.  Synchronous. */
+int f5_batch_trace(int enable, uint64_t *out, size_t cap);
+int f5_batch_matvec_y32_dev(const uint8_t *d_w, int N, int K, int g, int sh, const int8_t *d_x8, int B,
+                            int32_t *d_y32, int64_t *d_p, void *d_ws, size_t ws_bytes, uint32_t *d_err,
+                            void *stream);
+
 /* ---------------------------------------------------------------------------
  * Host-buffer entry points (allocate device scratch per call)
  * ------------------------------------------------------------------------- */
