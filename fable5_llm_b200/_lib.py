@@ -51,6 +51,17 @@ SIGNATURES = [
     ("f5_batch_trace", c_int, [c_int, c_vp, c_size]),
     ("f5_batch_matvec_y32_dev", c_int, [c_vp, c_int, c_int, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp,
                                         c_size, c_vp, c_vp]),
+    ("f5_bctx_create", c_int, [c_vp, c_int, c_int, c_vp]),
+    ("f5_bctx_destroy", c_int, [c_vp]),
+    ("f5_bctx_reset", c_int, [c_vp]),
+    ("f5_bctx_set_position", c_int, [c_vp, c_int, c_int, c_int]),
+    ("f5_bctx_get_position", c_int, [c_vp, c_int, c_vp, c_vp]),
+    ("f5_bctx_step", c_int, [c_vp, c_vp, c_vp, c_vp]),
+    ("f5_bctx_launch", c_int, [c_vp, c_int]),
+    ("f5_bctx_sync", c_int, [c_vp, c_vp, c_vp]),
+    ("f5_bctx_stream", c_int, [c_vp, c_vp]),
+    ("f5_bctx_read", c_int, [c_vp, c_int, c_int, c_int, c_vp, c_size]),
+    ("f5_bctx_write", c_int, [c_vp, c_int, c_int, c_int, c_vp, c_size]),
     ("f5_matvec_y32_host", c_int, [c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp]),
     ("f5_matvec_y32_host_noalloc", c_int, [c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp]),
     ("f5_ctx_create", c_int, [c_vp, c_int, c_vp]),
@@ -95,7 +106,7 @@ S_GATE, S_UP, S_DOWN, S_HEAD = 8, 9, 10, 0
 VEC_LN1, VEC_LN2, VEC_Q_NORM, VEC_K_NORM, VEC_CONV_W, VEC_DT_BIAS, VEC_A, VEC_NORM_W, VEC_LN_F = range(9)
 (BUF_X16, BUF_QKV16, BUF_Z16, BUF_B16, BUF_A16, BUF_ON16, BUF_QG16, BUF_K16, BUF_V16, BUF_PROD64,
  BUF_PROD16, BUF_STATS, BUF_DN_S, BUF_DN_CONV, BUF_DN_KH, BUF_K8, BUF_KE, BUF_V8, BUF_VE, BUF_KA,
- BUF_LOGITS) = range(21)
+ BUF_LOGITS, BUF_QKVC16, BUF_GATES) = range(23)
 
 _LIB = None
 

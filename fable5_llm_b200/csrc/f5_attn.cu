@@ -59,7 +59,10 @@ F5_DEV long long head_norm_rope(long long x, const int32_t *w, const int16_t *cs
   return out;
 }
 
-__global__ void __launch_bounds__(ATT_THREADS) k_attn(const __grid_constant__ AttnArgs a) {
+// The per-sequence buffers of a batched launch are explicit local pointers
+// (a is only read): with nvcc 12.9 for sm_100a, advancing the first member of
+// a local copy of the argument struct did not reach later reads of it.
+__global__ void __launch_bounds__(ATT_THREADS) k_attn(const __grid_constant__ AttnArgs a, const AttnBatch bs) {
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ long long red[32];
   __shared__ long long s_buf[8 + 256];
@@ -72,6 +75,18 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(const __grid_constant__ At
   __shared__ int32_t s_cacc[256];
   __shared__ __align__(8) uint64_t bar_k, bar_v;
 
+  // sequence blockIdx.z of a batched launch
+  const long long sb = blockIdx.z;
+  const int16_t *const qg16 = a.qg16 + sb * bs.qg;
+  const int16_t *const k16 = a.k16 + sb * bs.kv16;
+  const int16_t *const v16 = a.v16 + sb * bs.kv16;
+  int8_t *const k8 = a.k8 + sb * bs.cache;
+  int8_t *const v8 = a.v8 + sb * bs.cache;
+  int8_t *const ke = a.ke + sb * bs.cache_e;
+  int8_t *const ve = a.ve + sb * bs.cache_e;
+  int64_t *const prod = a.prod + sb * bs.prod;
+  const int *const Tp = a.T + sb * bs.params;
+  const int *const posp = a.pos + sb * bs.params;
   cg::cluster_group cl = cg::this_cluster();
   const int c = (int)cl.block_rank();
   const int nsplit = (int)cl.num_blocks();
@@ -81,8 +96,8 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(const __grid_constant__ At
   const int kv = h / group;
   // T and pos are only written by the host or by the previous step's last
   // kernel, so they can be read before the dependency wait.
-  const int T = *a.T;
-  int pos = *a.pos;
+  const int T = *Tp;
+  int pos = *posp;
   bool ok = T >= 0 && T < a.max_T;
   if (pos < 0 || pos >= a.max_pos) { ok = false; pos = 0; }
   const int Tn = ok ? T + 1 : max(0, min(T, a.max_T));   // tokens attended (incl. the new one)
@@ -105,8 +120,8 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(const __grid_constant__ At
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     if (n_old > 0) {
       mbar_expect_tx(&bar_k, row_bytes + e_bytes);
-      bulk_g2s(buf, a.k8 + kv_row0 * 256, row_bytes, &bar_k);
-      bulk_g2s(s_e8, a.ke + kv_row0, e_bytes, &bar_k);
+      bulk_g2s(buf, k8 + kv_row0 * 256, row_bytes, &bar_k);
+      bulk_g2s(s_e8, ke + kv_row0, e_bytes, &bar_k);
     }
   }
   asm volatile("griddepcontrol.launch_dependents;");
@@ -115,11 +130,11 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(const __grid_constant__ At
   const int16_t *cs = a.rope + (size_t)pos * 128;
 
   // ---- 1. q, k norm + rope; kv_quant(k), kv_quant(v) ----
-  const long long qv = head_norm_rope(a.qg16[h * 512 + d], a.q_norm, cs, a.rot, red, s_buf, s_int);
+  const long long qv = head_norm_rope(qg16[h * 512 + d], a.q_norm, cs, a.rot, red, s_buf, s_int);
   s_q[d] = (int32_t)qv;
-  const long long kn = head_norm_rope(a.k16[kv * 256 + d], a.k_norm, cs, a.rot, red, s_buf, s_int);
+  const long long kn = head_norm_rope(k16[kv * 256 + d], a.k_norm, cs, a.rot, red, s_buf, s_int);
   const int ek = dynq8_e(block_max_ull(uabs(kn), reinterpret_cast<unsigned long long *>(red)));
-  const long long vv = a.v16[kv * 256 + d];
+  const long long vv = v16[kv * 256 + d];
   const int ev = dynq8_e(block_max_ull(uabs(vv), reinterpret_cast<unsigned long long *>(red)));
   const int8_t k8n = (int8_t)dynq8_apply(kn, ek), v8n = (int8_t)dynq8_apply(vv, ev);
   s_k8[d] = k8n;
@@ -127,11 +142,11 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(const __grid_constant__ At
   const int ke_new = ek - QKV_F, ve_new = ev - QKV_F;
   if (ok && c == 0 && (h % group) == 0) {
     const size_t row = ((size_t)kv * a.max_T + T) * 256;
-    a.k8[row + d] = k8n;
-    a.v8[row + d] = v8n;
+    k8[row + d] = k8n;
+    v8[row + d] = v8n;
     if (d == 0) {
-      a.ke[(size_t)kv * a.max_T + T] = (int8_t)ke_new;
-      a.ve[(size_t)kv * a.max_T + T] = (int8_t)ve_new;
+      ke[(size_t)kv * a.max_T + T] = (int8_t)ke_new;
+      ve[(size_t)kv * a.max_T + T] = (int8_t)ve_new;
     }
   }
   bool got = n_old == 0 || mbar_wait(&bar_k, 0, 2000000000ull);
@@ -171,8 +186,8 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(const __grid_constant__ At
   if (d == 0 && n_old > 0 && got) {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic reads before async writes
     mbar_expect_tx(&bar_v, row_bytes + e_bytes);
-    bulk_g2s(buf, a.v8 + kv_row0 * 256, row_bytes, &bar_v);
-    bulk_g2s(s_e8, a.ve + kv_row0, e_bytes, &bar_v);
+    bulk_g2s(buf, v8 + kv_row0 * 256, row_bytes, &bar_v);
+    bulk_g2s(s_e8, ve + kv_row0, e_bytes, &bar_v);
   }
   if (d == 0) s_part[0] = lmax;
   cl.sync();
@@ -242,8 +257,8 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(const __grid_constant__ At
     long long tot = 0;
     for (int r = 0; r < nsplit; ++r) tot += *cl.map_shared_rank(&s_cacc[d], r);
     // og = sigmoid_q(rshr(gate, QKV_F - 12)) = sigmoid_q(gate << 4)  (ref/layer_fixed.py:1436-1437)
-    const long long og = sigmoid_q((long long)a.qg16[h * 512 + 256 + d] << (12 - QKV_F));
-    a.prod[h * 256 + d] = tot * og;
+    const long long og = sigmoid_q((long long)qg16[h * 512 + 256 + d] << (12 - QKV_F));
+    prod[h * 256 + d] = tot * og;
   }
   // drain: no copy may still target this CTA's shared memory at exit
   if (d == 0 && n_old > 0 && !got) mbar_wait(&bar_v, 0, 2000000000ull);
@@ -251,12 +266,16 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(const __grid_constant__ At
 }
 
 cudaError_t launch_attn(const AttnArgs &a_in, cudaStream_t st, bool pdl) {
+  return launch_attn_b(a_in, AttnBatch{}, 1, st, pdl);
+}
+
+cudaError_t launch_attn_b(const AttnArgs &a_in, const AttnBatch &bs, int B, cudaStream_t st, bool pdl) {
   const int nsplit = ATT_SPLIT;
   AttnArgs a = a_in;
   if (a.max_T % 16) return cudaErrorInvalidValue;
   a.chunk_max = (((a.max_T + nsplit - 1) / nsplit) + 15) & ~15;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(nsplit, a.nq);
+  cfg.gridDim = dim3(nsplit, a.nq, B);
   cfg.blockDim = dim3(ATT_THREADS);
   cfg.dynamicSmemBytes = (size_t)a.chunk_max * (256 + 2 + 8);
   cfg.stream = st;
@@ -269,12 +288,16 @@ cudaError_t launch_attn(const AttnArgs &a_in, cudaStream_t st, bool pdl) {
   at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 2 : 1;
-  if (cfg.dynamicSmemBytes > 48 * 1024) {
+  // static shared memory (~13 KB) + the K/V chunk: raise the per-kernel limit
+  // whenever the sum may pass the 48 KB default, not only when the chunk does
+  static int attr_bytes = 0;
+  if ((int)cfg.dynamicSmemBytes > attr_bytes) {
     cudaError_t e = cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)cfg.dynamicSmemBytes);
     if (e != cudaSuccess) return e;
+    attr_bytes = (int)cfg.dynamicSmemBytes;
   }
-  return cudaLaunchKernelEx(&cfg, k_attn, a);
+  return cudaLaunchKernelEx(&cfg, k_attn, a, bs);
 }
 
 }  // namespace f5

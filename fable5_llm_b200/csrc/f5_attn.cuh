@@ -25,6 +25,14 @@ struct AttnArgs {
   int nq, nkv, rot;
 };
 
+// Batched launch (B independent sequences, blockIdx.z = sequence): element
+// strides between consecutive sequences' buffers (params: ints between the
+// sequences' T / pos words)
+struct AttnBatch {
+  long long qg, kv16, cache, cache_e, prod, params;
+};
+
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st, bool pdl);
+cudaError_t launch_attn_b(const AttnArgs &a, const AttnBatch &bs, int B, cudaStream_t st, bool pdl);
 
 }  // namespace f5

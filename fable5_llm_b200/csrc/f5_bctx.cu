@@ -1,0 +1,661 @@
+// Batched decode context: B independent sequences over one loaded model.
+//
+// The reference decodes one sequence at a time (ref/fidelity_check.py:
+// 404-448 FxRunner.step); B sequences are B independent runs of that step.
+// Here they share the model context's weights (borrowed, not copied) and
+// every projection of the step becomes a W4A8 GEMM on the tensor cores
+// (f5_bgemm.cu): the B quantized inputs against one weight image.  Each
+// sequence owns its decode state (DeltaNet recurrent states, conv windows,
+// KV caches, positions) laid out sequence-major, so the vector stages run
+// as the single-sequence kernels with one more grid dimension.
+//
+// Step program (CUDA graph, programmatic dependent launch between kernels):
+//   begin: x16[b] = emb[tok[b]], argmax keys cleared
+//   per layer, per projection group: k_bprep (the GEMV prologue of each
+//   sequence: RMSNorm / DYNQ8 / attention gate -> x8 tiles), k_bgemm,
+//   k_bepi (the GEMV epilogue of each (sequence, row): conv4 + SiLU, gates,
+//   residual adds, silu(g) * u); the DeltaNet and attention cores in
+//   between, one grid slice per sequence
+//   LM head: the GEMM reduces each sequence's argmax; end: next token,
+//   advance T / pos per sequence.
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+#include "../../include/f5b200.h"
+#include "f5_attn.cuh"
+#include "f5_batch.cuh"
+#include "f5_capi_util.h"
+#include "f5_ctx_priv.h"
+#include "f5_dn.cuh"
+#include "f5_int.cuh"
+
+namespace f5 {
+
+__global__ void k_bstep_begin(StepParams *p, const int16_t *emb, int vocab, int Hd, int16_t *x16,
+                              unsigned long long *key) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int b = blockIdx.x;
+  int tok = p[b].tok;
+  if (tok < 0 || tok >= vocab) {
+    if (threadIdx.x == 0) atomicOr(&p[b].err, DERR_RANGE);
+    tok = 0;
+  }
+  for (int i = threadIdx.x; i < Hd; i += blockDim.x) x16[(size_t)b * Hd + i] = emb[(size_t)tok * Hd + i];
+  if (threadIdx.x == 0) key[b] = 0ull;
+}
+
+__global__ void k_bstep_end(StepParams *p, const unsigned long long *key, const uint32_t *err, int B, int advance) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int b = threadIdx.x;
+  if (b >= B) return;
+  const unsigned long long k = key[b];
+  const int row = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+  const int val = (int)((uint32_t)(k >> 32) ^ 0x80000000u);
+  p[b].next_tok = row;
+  p[b].max_val = val;
+  p[b].err |= *err;
+  if (advance) {
+    p[b].tok = row;
+    p[b].pos += 1;
+    p[b].T += 1;
+    p[b].steps += 1;
+  }
+}
+
+namespace {
+
+struct BLayer {
+  int16_t *conv = nullptr, *S = nullptr;
+  int8_t *k8 = nullptr, *ke = nullptr, *v8 = nullptr, *ve = nullptr;
+  int *kh = nullptr, *ka = nullptr;
+};
+
+// one segment of a batched projection group
+struct BSeg {
+  const DevMat *m = nullptr, *m2 = nullptr;   // m2: the up image of a gate/up pair
+  int mode = GM_TO16, out_f = 0, out_f2 = 0;
+  void *out = nullptr;
+  long long out_bs = 0;                        // bytes between sequences
+  void *aux_out = nullptr;
+  long long aux_bs = 0;
+  void *aux0 = nullptr;
+  long long ring_bs = 0;
+  const void *aux1 = nullptr;
+};
+
+constexpr size_t PARAM_INTS = sizeof(StepParams) / sizeof(int);
+
+struct BDevGuard {
+  int prev = 0;
+  explicit BDevGuard(int d) { cudaGetDevice(&prev); cudaSetDevice(d); }
+  ~BDevGuard() { cudaSetDevice(prev); }
+};
+
+}  // namespace
+}  // namespace f5
+
+using namespace f5;
+
+struct f5_bctx {
+  f5_ctx *m = nullptr;
+  int B = 0, Bp = 0, max_T = 0, device = 0;
+  cudaStream_t st = nullptr;
+  std::vector<BLayer> L;
+  int16_t *x16 = nullptr, *qkv16 = nullptr, *qkvc16 = nullptr, *z16 = nullptr, *b16 = nullptr, *a16 = nullptr;
+  int16_t *on16 = nullptr, *qg16 = nullptr, *k16 = nullptr, *v16 = nullptr, *prod16 = nullptr;
+  int32_t *gates = nullptr;
+  int64_t *prod64 = nullptr;
+  int8_t *xt = nullptr;
+  int *xmeta = nullptr;
+  int64_t *p = nullptr;
+  size_t p_words = 0;
+  unsigned long long *key = nullptr, *stats = nullptr;
+  uint32_t *err = nullptr;
+  StepParams *params = nullptr, *h_params = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  bool dirty = true;
+  bool pdl = true;             // programmatic dependent launch between the step's kernels
+  bool sizing = false;         // enqueue walk that only sizes the p scratch
+  size_t need_p = 0;
+  std::vector<void *> allocs;
+};
+
+#define F5_CU(x, what)                        \
+  do {                                        \
+    int _rc = cuda_status((x), (what));       \
+    if (_rc) return _rc;                      \
+  } while (0)
+
+namespace f5 {
+namespace {
+
+int balloc(f5_bctx *c, void **p, size_t bytes) {
+  cudaError_t e = cudaMalloc(p, bytes);
+  if (e != cudaSuccess) return cuda_status(e, "cudaMalloc");
+  c->allocs.push_back(*p);
+  return cuda_status(cudaMemsetAsync(*p, 0, bytes, c->st), "cudaMemset");
+}
+#define F5_BALLOC(c, p, bytes)                                            \
+  do {                                                                    \
+    int _rc = balloc((c), reinterpret_cast<void **>(&(p)), (bytes));      \
+    if (_rc) return _rc;                                                  \
+  } while (0)
+
+// One batched projection group: prologue -> GEMM -> per-sequence epilogue.
+cudaError_t bop(f5_bctx *c, const BSeg *sg, int nseg, int K, const GemvPrologue &pro, long long src_bs,
+                long long src2_bs, bool head) {
+  const int NG = K / 128;
+  BgemmArgs ga = {};
+  BepiArgs ea = {};
+  int tiles = 0, prow = 0, units = 0, gs = 0;
+  for (int i = 0; i < nseg; ++i) {
+    const BSeg &s = sg[i];
+    const DevMat *ms[2] = {s.m, s.m2};
+    const int nm = s.mode == GM_SILU_MUL ? 2 : 1;
+    const int p0 = prow;
+    for (int k = 0; k < nm; ++k) {
+      if (gs >= BG_MAX_SEG) return cudaErrorInvalidValue;
+      BgemmSeg &g = ga.seg[gs++];
+      g.w = ms[k]->w;
+      g.rows = ms[k]->N;
+      g.tile_begin = tiles;
+      g.p_row0 = prow;
+      g.argmax = head ? 1 : 0;
+      tiles += (ms[k]->N + BG_TILE - 1) / BG_TILE;
+      if (!head) prow += ms[k]->N;
+    }
+    GemvSeg &e = ea.g.seg[i];
+    e.out = s.out;
+    e.rows = s.m->N;
+    e.unit_begin = units;
+    e.e = s.m->e;
+    e.e2 = s.m2 ? s.m2->e : 0;
+    e.out_f = s.out_f;
+    e.out_f2 = s.out_f2;
+    e.mode = s.mode;
+    e.aux_out = s.aux_out;
+    e.aux0 = s.aux0;
+    e.aux1 = s.aux1;
+    BepiSeg &b = ea.bs[i];
+    b.p_row0 = p0;
+    b.p_row0_up = p0 + s.m->N;
+    b.out_bs = s.out_bs;
+    b.aux_bs = s.aux_bs;
+    b.ring_bs = s.ring_bs;
+    units += s.m->N;
+  }
+  ga.nseg = gs;
+  ga.ntiles = tiles;
+  ga.K = K;
+  ga.NG = NG;
+  ga.stride = sg[0].m->stride;
+  ga.sh = sg[0].m->sh;
+  ga.S = bgemm_splits(tiles, NG, sm_count(), head);
+  ga.B = c->B;
+  ga.Bp = c->Bp;
+  ga.xt = c->xt;
+  ga.p = c->p;
+  ga.ptot = prow;
+  ga.key = head ? c->key : nullptr;
+  ga.err = c->err;
+  if (c->sizing) {
+    c->need_p = std::max(c->need_p, (size_t)ga.S * c->Bp * (size_t)prow);
+    return cudaSuccess;
+  }
+  BprepArgs pa = {};
+  pa.pro = pro;
+  pa.src_bs = src_bs;
+  pa.src2_bs = src2_bs;
+  pa.K = K;
+  pa.NG = NG;
+  pa.B = c->B;
+  pa.Bp = c->Bp;
+  pa.xmeta = c->xmeta;
+  pa.xt = c->xt;
+  pa.err = c->err;
+  cudaError_t e;
+  if ((e = launch_bprep(pa, c->st, c->pdl))) return e;
+  if ((e = launch_bgemm(ga, c->st, c->pdl, sm_count()))) return e;
+  if (head) return cudaSuccess;
+  ea.g.nseg = nseg;
+  ea.g.total_units = units;
+  ea.g.K = K;
+  ea.g.sh = ga.sh;
+  ea.g.err = c->err;
+  ea.S = ga.S;
+  ea.B = c->B;
+  ea.Bp = c->Bp;
+  ea.ptot = prow;
+  ea.p = c->p;
+  ea.xmeta = c->xmeta;
+  ea.params = c->params;
+  return launch_bepi(ea, c->st, c->pdl);
+}
+
+cudaError_t enqueue_blayer(f5_bctx *c, int li) {
+  const Layer &l = c->m->L[li];
+  BLayer &s = c->L[li];
+  cudaError_t e;
+  GemvPrologue pro = {};
+  pro.mode = PRO_RMSNORM;
+  pro.src = c->x16;
+  pro.w = l.ln1;
+  pro.in_f = RS_F;
+  pro.one_plus = 1;
+  const long long xbs = (long long)H * 2;
+  if (!l.attn) {
+    // in-projection with conv4 + SiLU and the two gates (ref/layer_fixed.py:1503-1538)
+    BSeg sg[4];
+    sg[0].m = &l.m[0]; sg[0].mode = GM_CONV; sg[0].out_f = RS_F;
+    sg[0].out = c->qkv16; sg[0].out_bs = (long long)CONV_DIM * 2;
+    sg[0].aux_out = c->qkvc16; sg[0].aux_bs = (long long)CONV_DIM * 2;
+    sg[0].aux0 = s.conv; sg[0].ring_bs = (long long)CONV_DIM * 4 * 2; sg[0].aux1 = l.conv_w;
+    sg[1].m = &l.m[1]; sg[1].mode = GM_TO16; sg[1].out_f = QKV_F; sg[1].out = c->z16; sg[1].out_bs = (long long)LVD * 2;
+    sg[2].m = &l.m[2]; sg[2].mode = GM_GATE_B; sg[2].out_f = 12; sg[2].out = c->b16; sg[2].out_bs = (long long)LNH * 2;
+    sg[2].aux_out = c->gates; sg[2].aux_bs = (long long)2 * LNH * 4;
+    sg[3].m = &l.m[3]; sg[3].mode = GM_GATE_A; sg[3].out_f = 12; sg[3].out = c->a16; sg[3].out_bs = (long long)LNH * 2;
+    sg[3].aux_out = c->gates + LNH; sg[3].aux_bs = (long long)2 * LNH * 4;
+    sg[3].aux0 = l.dt_bias; sg[3].aux1 = l.A;
+    if ((e = bop(c, sg, 4, H, pro, xbs, 0, false))) return e;
+    if (!c->sizing) {
+      DnArgs d = {};
+      d.qkvc = c->qkvc16; d.beta = c->gates; d.decay = c->gates + LNH; d.z16 = c->z16; d.norm_w = l.norm_w;
+      d.S = s.S; d.on16 = c->on16; d.kh_out = s.kh; d.stats = c->stats; d.err = c->err;
+      d.lkd = LKD; d.vrep = LNH / LNKH; d.norm_mode = c->m->cfg.norm_mode;
+      DnBatch bs;
+      bs.qkvc = CONV_DIM; bs.gates = 2 * LNH; bs.z = LVD; bs.S = (long long)LNH * LDK * LDV; bs.on = LVD; bs.kh = LNH;
+      if ((e = launch_dn_step_b(d, bs, LNH, c->B, c->st, c->pdl))) return e;
+    }
+    GemvPrologue p2 = {};
+    p2.mode = PRO_DYNQ8;
+    p2.src = c->on16;
+    p2.in_f = DN_NORM_F;
+    BSeg so;
+    so.m = &l.m[4]; so.mode = GM_RESID; so.out_f = RS_F; so.out = c->x16; so.out_bs = xbs;
+    if ((e = bop(c, &so, 1, LVD, p2, (long long)LVD * 2, 0, false))) return e;
+  } else {
+    BSeg sg[3];
+    sg[0].m = &l.m[0]; sg[0].out = c->qg16; sg[0].out_bs = (long long)NQ * HD * 2 * 2;
+    sg[1].m = &l.m[1]; sg[1].out = c->k16; sg[1].out_bs = (long long)NKV * HD * 2;
+    sg[2].m = &l.m[2]; sg[2].out = c->v16; sg[2].out_bs = (long long)NKV * HD * 2;
+    for (BSeg &x : sg) { x.mode = GM_TO16; x.out_f = QKV_F; }
+    if ((e = bop(c, sg, 3, H, pro, xbs, 0, false))) return e;
+    if (!c->sizing) {
+      AttnArgs at = {};
+      at.qg16 = c->qg16; at.k16 = c->k16; at.v16 = c->v16; at.q_norm = l.q_norm; at.k_norm = l.k_norm;
+      at.rope = c->m->rope; at.k8 = s.k8; at.ke = s.ke; at.v8 = s.v8; at.ve = s.ve; at.prod = c->prod64;
+      at.T = &c->params->T; at.pos = &c->params->pos; at.err = c->err;
+      at.max_T = c->max_T; at.max_pos = c->m->rope_npos; at.nq = NQ; at.nkv = NKV; at.rot = ROT;
+      AttnBatch bs;
+      bs.qg = (long long)NQ * HD * 2; bs.kv16 = (long long)NKV * HD;
+      bs.cache = (long long)NKV * c->max_T * HD; bs.cache_e = (long long)NKV * c->max_T;
+      bs.prod = (long long)NQ * HD; bs.params = (long long)PARAM_INTS;
+      if ((e = launch_attn_b(at, bs, c->B, c->st, c->pdl))) return e;
+    }
+    GemvPrologue p2 = {};
+    p2.mode = PRO_ATTN_GATE;
+    p2.src = c->prod64;
+    p2.dbg = s.ka;
+    BSeg so;
+    so.m = &l.m[3]; so.mode = GM_RESID; so.out_f = RS_F; so.out = c->x16; so.out_bs = xbs;
+    if ((e = bop(c, &so, 1, NQ * HD, p2, (long long)NQ * HD * 8, 0, false))) return e;
+  }
+  // MLP (ref/layer_fixed.py:1597-1604)
+  GemvPrologue p3 = {};
+  p3.mode = PRO_RMSNORM;
+  p3.src = c->x16;
+  p3.w = l.ln2;
+  p3.in_f = RS_F;
+  p3.one_plus = 1;
+  BSeg gu;
+  gu.m = &l.m[8]; gu.m2 = &l.m[9]; gu.mode = GM_SILU_MUL; gu.out_f = 12; gu.out_f2 = RS_F;
+  gu.out = c->prod16; gu.out_bs = (long long)FFN * 2;
+  if ((e = bop(c, &gu, 1, H, p3, xbs, 0, false))) return e;
+  GemvPrologue p4 = {};
+  p4.mode = PRO_DYNQ8;
+  p4.src = c->prod16;
+  p4.in_f = RS_F;
+  BSeg sd;
+  sd.m = &l.m[10]; sd.mode = GM_RESID; sd.out_f = RS_F; sd.out = c->x16; sd.out_bs = xbs;
+  return bop(c, &sd, 1, FFN, p4, (long long)FFN * 2, 0, false);
+}
+
+cudaError_t launch_pdl_b(const void *fn, void **args, dim3 grid, dim3 block, cudaStream_t st, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+cudaError_t enqueue_bstep(f5_bctx *c) {
+  cudaError_t e;
+  if (!c->sizing) {
+    StepParams *p = c->params;
+    const int16_t *emb = c->m->emb;
+    int vocab = c->m->cfg.vocab, hd = H;
+    int16_t *x = c->x16;
+    unsigned long long *k = c->key;
+    void *args[] = {&p, &emb, &vocab, &hd, &x, &k};
+    if ((e = launch_pdl_b((const void *)k_bstep_begin, args, dim3(c->B), dim3(256), c->st, c->pdl))) return e;
+  }
+  for (int li = 0; li < (int)c->L.size(); ++li)
+    if ((e = enqueue_blayer(c, li))) return e;
+  GemvPrologue pf = {};
+  pf.mode = PRO_RMSNORM;
+  pf.src = c->x16;
+  pf.w = c->m->ln_f;
+  pf.in_f = RS_F;
+  pf.one_plus = 0;   // ln_f pre-folded (1+w) at Q3.12
+  BSeg sh;
+  sh.m = &c->m->head;
+  sh.mode = GM_ARGMAX;
+  if ((e = bop(c, &sh, 1, H, pf, (long long)H * 2, 0, true))) return e;
+  if (!c->sizing) {
+    StepParams *p = c->params;
+    const unsigned long long *k = c->key;
+    const uint32_t *er = c->err;
+    int B = c->B, adv = 1;
+    void *args[] = {&p, &k, &er, &B, &adv};
+    if ((e = launch_pdl_b((const void *)k_bstep_end, args, dim3(1), dim3(64), c->st, c->pdl))) return e;
+  }
+  return cudaSuccess;
+}
+
+int build_bgraph(f5_bctx *c) {
+  if (!c->dirty && c->exec) return F5_OK;
+  if (c->exec) {
+    cudaGraphExecDestroy(c->exec);
+    c->exec = nullptr;
+  }
+  cudaGraph_t g = nullptr;
+  F5_CU(cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal), "capture");
+  cudaError_t e = enqueue_bstep(c);
+  cudaError_t e2 = cudaStreamEndCapture(c->st, &g);
+  if (e != cudaSuccess || e2 != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    return cuda_status(e != cudaSuccess ? e : e2, "batched step capture");
+  }
+  e = cudaGraphInstantiate(&c->exec, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return cuda_status(e, "batched graph instantiate");
+  c->dirty = false;
+  return F5_OK;
+}
+
+int bfinish(f5_bctx *c, const char *what) {
+  cudaError_t e = cudaStreamSynchronize(c->st);
+  if (e != cudaSuccess) return cuda_status(e, what);
+  F5_CU(cudaMemcpy(c->h_params, c->params, sizeof(StepParams) * c->B, cudaMemcpyDeviceToHost), what);
+  uint32_t any = 0;
+  for (int b = 0; b < c->B; ++b) any |= c->h_params[b].err;
+  if (any & DERR_TIMEOUT) return set_error(F5_ETIMEOUT, "%s: a bounded device wait expired", what);
+  if (any & DERR_Y32_OVERFLOW) return set_error(F5_EOVERFLOW, "%s: |y32| >= 2^31", what);
+  if (any & DERR_KV_FULL) return set_error(F5_ESTATE, "%s: KV cache full (max_T)", what);
+  if (any & DERR_RANGE) return set_error(F5_EINVAL, "%s: input out of range", what);
+  return F5_OK;
+}
+
+// device buffer of (what, layer) for sequence seq, with its per-sequence bytes
+int bbuf(f5_bctx *c, int what, int layer, int seq, uint8_t **ptr, size_t *bytes) {
+  if (seq < 0 || seq >= c->B) return set_error(F5_EINVAL, "sequence %d outside [0, %d)", seq, c->B);
+  const bool per_layer = what == F5_BUF_DN_S || what == F5_BUF_DN_CONV || what == F5_BUF_DN_KH ||
+                         what == F5_BUF_K8 || what == F5_BUF_KE || what == F5_BUF_V8 || what == F5_BUF_VE ||
+                         what == F5_BUF_KA;
+  if (per_layer && (layer < 0 || layer >= (int)c->L.size())) return set_error(F5_EINVAL, "layer %d", layer);
+  const bool attn = per_layer && c->m->L[layer].attn;
+  const size_t T = (size_t)c->max_T;
+  uint8_t *base = nullptr;
+  size_t n = 0;
+  switch (what) {
+    case F5_BUF_X16: base = (uint8_t *)c->x16; n = (size_t)H * 2; break;
+    case F5_BUF_QKV16: base = (uint8_t *)c->qkv16; n = (size_t)CONV_DIM * 2; break;
+    case F5_BUF_Z16: base = (uint8_t *)c->z16; n = (size_t)LVD * 2; break;
+    case F5_BUF_B16: base = (uint8_t *)c->b16; n = (size_t)LNH * 2; break;
+    case F5_BUF_A16: base = (uint8_t *)c->a16; n = (size_t)LNH * 2; break;
+    case F5_BUF_K16: base = (uint8_t *)c->k16; n = (size_t)NKV * HD * 2; break;
+    case F5_BUF_V16: base = (uint8_t *)c->v16; n = (size_t)NKV * HD * 2; break;
+    case F5_BUF_PROD64: base = (uint8_t *)c->prod64; n = (size_t)NQ * HD * 8; break;
+    case F5_BUF_QKVC16: base = (uint8_t *)c->qkvc16; n = (size_t)CONV_DIM * 2; break;
+    case F5_BUF_GATES: base = (uint8_t *)c->gates; n = (size_t)2 * LNH * 4; break;
+    case F5_BUF_ON16: base = (uint8_t *)c->on16; n = (size_t)LVD * 2; break;
+    case F5_BUF_QG16: base = (uint8_t *)c->qg16; n = (size_t)NQ * HD * 4; break;
+    case F5_BUF_PROD16: base = (uint8_t *)c->prod16; n = (size_t)FFN * 2; break;
+    case F5_BUF_DN_S: if (attn) break; base = (uint8_t *)c->L[layer].S; n = (size_t)LNH * LDK * LDV * 2; break;
+    case F5_BUF_DN_CONV: if (attn) break; base = (uint8_t *)c->L[layer].conv; n = (size_t)CONV_DIM * 4 * 2; break;
+    case F5_BUF_DN_KH: if (attn) break; base = (uint8_t *)c->L[layer].kh; n = (size_t)LNH * 4; break;
+    case F5_BUF_K8: if (!attn) break; base = (uint8_t *)c->L[layer].k8; n = NKV * T * HD; break;
+    case F5_BUF_V8: if (!attn) break; base = (uint8_t *)c->L[layer].v8; n = NKV * T * HD; break;
+    case F5_BUF_KE: if (!attn) break; base = (uint8_t *)c->L[layer].ke; n = NKV * T; break;
+    case F5_BUF_VE: if (!attn) break; base = (uint8_t *)c->L[layer].ve; n = NKV * T; break;
+    case F5_BUF_KA: if (!attn) break; base = (uint8_t *)c->L[layer].ka; n = 4; break;
+    default: break;
+  }
+  if (!base) return set_error(F5_EINVAL, "buffer %d is not held by layer %d of a batched context", what, layer);
+  *ptr = base + (size_t)seq * n;
+  *bytes = n;
+  return F5_OK;
+}
+
+}  // namespace
+}  // namespace f5
+
+extern "C" {
+
+int f5_bctx_create(f5_ctx *m, int batch, int max_T, f5_bctx **out) {
+  if (!m || !out) return set_error(F5_EINVAL, "f5_bctx_create: null argument");
+  *out = nullptr;
+  if (batch < 1 || batch > 64) return set_error(F5_EINVAL, "f5_bctx_create: batch %d outside [1, 64]", batch);
+  if (max_T < 16 || max_T % 16) return set_error(F5_EINVAL, "f5_bctx_create: max_T must be a positive multiple of 16");
+  if (m->cfg.world_size != 1) return set_error(F5_EINVAL, "f5_bctx_create: the model context must hold every row (world_size 1)");
+  for (size_t i = 0; i < m->L.size(); ++i)
+    for (int s = 0; s < NSLOT; ++s) {
+      const bool used = (s >= 8 && s <= 10) || (m->L[i].attn ? s <= 3 : s <= 4);
+      if (used && !m->L[i].m[s].w) return set_error(F5_ESTATE, "f5_bctx_create: layer %zu slot %d not uploaded", i, s);
+      if (used && m->L[i].m[s].g != 128) return set_error(F5_EINVAL, "f5_bctx_create: g=128 images only");
+    }
+  if (!m->head.w || !m->emb || !m->rope || !m->ln_f) return set_error(F5_ESTATE, "f5_bctx_create: model not fully loaded");
+  f5_bctx *c = new f5_bctx();
+  c->m = m;
+  c->B = batch;
+  c->Bp = batch <= 16 ? 16 : (batch <= 32 ? 32 : 64);
+  c->max_T = max_T;
+  c->device = m->device;
+  if (const char *v = getenv("F5_BATCH_PDL")) c->pdl = atoi(v) != 0;
+  BDevGuard dg(c->device);
+  int rc = F5_OK;
+  auto fail = [&](int r) { f5_bctx_destroy(c); return r; };
+  if (cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking) != cudaSuccess)
+    return fail(set_error(F5_ECUDA, "stream"));
+  const size_t B = batch;
+#define BA(p, n) do { if ((rc = balloc(c, reinterpret_cast<void **>(&(p)), (n)))) return fail(rc); } while (0)
+  c->L.resize(m->L.size());
+  for (size_t i = 0; i < m->L.size(); ++i) {
+    BLayer &s = c->L[i];
+    if (!m->L[i].attn) {
+      BA(s.conv, B * CONV_DIM * 4 * 2);
+      BA(s.S, B * LNH * LDK * LDV * 2);
+      BA(s.kh, B * LNH * 4);
+    } else {
+      BA(s.k8, B * NKV * max_T * HD);
+      BA(s.v8, B * NKV * max_T * HD);
+      BA(s.ke, B * NKV * max_T);
+      BA(s.ve, B * NKV * max_T);
+      BA(s.ka, B * 4);
+    }
+  }
+  BA(c->x16, B * H * 2);
+  BA(c->qkv16, B * CONV_DIM * 2);
+  BA(c->qkvc16, B * CONV_DIM * 2);
+  BA(c->z16, B * LVD * 2);
+  BA(c->b16, B * LNH * 2);
+  BA(c->a16, B * LNH * 2);
+  BA(c->gates, B * 2 * LNH * 4);
+  BA(c->on16, B * LVD * 2);
+  BA(c->qg16, B * NQ * HD * 2 * 2);
+  BA(c->k16, B * NKV * HD * 2);
+  BA(c->v16, B * NKV * HD * 2);
+  BA(c->prod16, B * FFN * 2);
+  BA(c->prod64, B * NQ * HD * 8);
+  BA(c->xt, (size_t)(FFN / 128) * c->Bp * 128);   // rows >= B stay zero
+  BA(c->xmeta, (size_t)c->Bp * 2 * 4);
+  BA(c->key, (size_t)c->Bp * 8);
+  BA(c->stats, 8);
+  BA(c->err, 4);
+  BA(c->params, B * sizeof(StepParams));
+  if (cudaMallocHost(&c->h_params, B * sizeof(StepParams)) != cudaSuccess)
+    return fail(set_error(F5_ENOMEM, "pinned params"));
+  memset(c->h_params, 0, B * sizeof(StepParams));
+  // size the partial-p scratch with a dry walk of the step
+  c->sizing = true;
+  enqueue_bstep(c);
+  c->sizing = false;
+  BA(c->p, std::max<size_t>(c->need_p, 1) * 8);
+#undef BA
+  if ((rc = cuda_status(cudaStreamSynchronize(c->st), "f5_bctx_create"))) return fail(rc);
+  *out = c;
+  return F5_OK;
+}
+
+int f5_bctx_destroy(f5_bctx *c) {
+  if (!c) return F5_OK;
+  BDevGuard dg(c->device);
+  if (c->st) cudaStreamSynchronize(c->st);
+  if (c->exec) cudaGraphExecDestroy(c->exec);
+  for (void *p : c->allocs) cudaFree(p);
+  if (c->h_params) cudaFreeHost(c->h_params);
+  if (c->st) cudaStreamDestroy(c->st);
+  delete c;
+  return F5_OK;
+}
+
+int f5_bctx_reset(f5_bctx *c) {
+  if (!c) return set_error(F5_EINVAL, "null batched context");
+  BDevGuard dg(c->device);
+  for (BLayer &s : c->L) {
+    const size_t B = c->B;
+    if (s.S) {
+      F5_CU(cudaMemsetAsync(s.S, 0, B * LNH * LDK * LDV * 2, c->st), "reset");
+      F5_CU(cudaMemsetAsync(s.conv, 0, B * CONV_DIM * 4 * 2, c->st), "reset");
+      F5_CU(cudaMemsetAsync(s.kh, 0, B * LNH * 4, c->st), "reset");
+    } else {
+      F5_CU(cudaMemsetAsync(s.k8, 0, B * NKV * c->max_T * HD, c->st), "reset");
+      F5_CU(cudaMemsetAsync(s.v8, 0, B * NKV * c->max_T * HD, c->st), "reset");
+      F5_CU(cudaMemsetAsync(s.ke, 0, B * NKV * c->max_T, c->st), "reset");
+      F5_CU(cudaMemsetAsync(s.ve, 0, B * NKV * c->max_T, c->st), "reset");
+    }
+  }
+  F5_CU(cudaMemsetAsync(c->stats, 0, 8, c->st), "reset");
+  F5_CU(cudaMemsetAsync(c->err, 0, 4, c->st), "reset");
+  F5_CU(cudaMemsetAsync(c->params, 0, sizeof(StepParams) * c->B, c->st), "reset");
+  return cuda_status(cudaStreamSynchronize(c->st), "f5_bctx_reset");
+}
+
+int f5_bctx_set_position(f5_bctx *c, int seq, int T, int pos) {
+  if (!c) return set_error(F5_EINVAL, "null batched context");
+  if (T < 0 || T > c->max_T || pos < 0) return set_error(F5_EINVAL, "set_position: T=%d pos=%d", T, pos);
+  BDevGuard dg(c->device);
+  F5_CU(cudaStreamSynchronize(c->st), "set_position");
+  F5_CU(cudaMemcpy(c->h_params, c->params, sizeof(StepParams) * c->B, cudaMemcpyDeviceToHost), "set_position");
+  for (int b = 0; b < c->B; ++b)
+    if (seq < 0 || seq == b) {
+      c->h_params[b].T = T;
+      c->h_params[b].pos = pos;
+    }
+  return cuda_status(cudaMemcpy(c->params, c->h_params, sizeof(StepParams) * c->B, cudaMemcpyHostToDevice),
+                     "set_position");
+}
+
+int f5_bctx_get_position(f5_bctx *c, int seq, int *T, int *pos) {
+  if (!c || seq < 0 || seq >= c->B) return set_error(F5_EINVAL, "get_position: bad sequence");
+  BDevGuard dg(c->device);
+  F5_CU(cudaStreamSynchronize(c->st), "get_position");
+  StepParams p;
+  F5_CU(cudaMemcpy(&p, c->params + seq, sizeof(p), cudaMemcpyDeviceToHost), "get_position");
+  if (T) *T = p.T;
+  if (pos) *pos = p.pos;
+  return F5_OK;
+}
+
+int f5_bctx_step(f5_bctx *c, const int32_t *tok, int32_t *next_tok, int32_t *max_logit) {
+  if (!c || !tok) return set_error(F5_EINVAL, "f5_bctx_step: null argument");
+  BDevGuard dg(c->device);
+  int rc = build_bgraph(c);
+  if (rc) return rc;
+  F5_CU(cudaStreamSynchronize(c->st), "f5_bctx_step");
+  F5_CU(cudaMemcpy(c->h_params, c->params, sizeof(StepParams) * c->B, cudaMemcpyDeviceToHost), "f5_bctx_step");
+  for (int b = 0; b < c->B; ++b) {
+    c->h_params[b].tok = tok[b];
+    c->h_params[b].err = 0;
+  }
+  F5_CU(cudaMemcpyAsync(c->params, c->h_params, sizeof(StepParams) * c->B, cudaMemcpyHostToDevice, c->st), "f5_bctx_step");
+  F5_CU(cudaMemsetAsync(c->err, 0, 4, c->st), "f5_bctx_step");
+  F5_CU(cudaGraphLaunch(c->exec, c->st), "f5_bctx_step");
+  rc = bfinish(c, "f5_bctx_step");
+  for (int b = 0; b < c->B; ++b) {
+    if (next_tok) next_tok[b] = c->h_params[b].next_tok;
+    if (max_logit) max_logit[b] = c->h_params[b].max_val;
+  }
+  return rc;
+}
+
+int f5_bctx_launch(f5_bctx *c, int n_steps) {
+  if (!c || n_steps < 0) return set_error(F5_EINVAL, "f5_bctx_launch: bad argument");
+  BDevGuard dg(c->device);
+  int rc = build_bgraph(c);
+  if (rc) return rc;
+  for (int i = 0; i < n_steps; ++i) F5_CU(cudaGraphLaunch(c->exec, c->st), "f5_bctx_launch");
+  return F5_OK;
+}
+
+int f5_bctx_sync(f5_bctx *c, int32_t *last_tok, int32_t *max_logit) {
+  if (!c) return set_error(F5_EINVAL, "null batched context");
+  BDevGuard dg(c->device);
+  int rc = bfinish(c, "f5_bctx_sync");
+  for (int b = 0; b < c->B; ++b) {
+    if (last_tok) last_tok[b] = c->h_params[b].next_tok;
+    if (max_logit) max_logit[b] = c->h_params[b].max_val;
+  }
+  return rc;
+}
+
+int f5_bctx_stream(f5_bctx *c, void **stream) {
+  if (!c || !stream) return set_error(F5_EINVAL, "null argument");
+  *stream = c->st;
+  return F5_OK;
+}
+
+int f5_bctx_read(f5_bctx *c, int seq, int what, int layer, void *dst, size_t bytes) {
+  if (!c || !dst) return set_error(F5_EINVAL, "null argument");
+  BDevGuard dg(c->device);
+  uint8_t *p;
+  size_t n;
+  int rc = bbuf(c, what, layer, seq, &p, &n);
+  if (rc) return rc;
+  if (bytes != n) return set_error(F5_EINVAL, "f5_bctx_read: %zu bytes, buffer holds %zu", bytes, n);
+  F5_CU(cudaStreamSynchronize(c->st), "f5_bctx_read");
+  return cuda_status(cudaMemcpy(dst, p, n, cudaMemcpyDeviceToHost), "f5_bctx_read");
+}
+
+int f5_bctx_write(f5_bctx *c, int seq, int what, int layer, const void *src, size_t bytes) {
+  if (!c || !src) return set_error(F5_EINVAL, "null argument");
+  BDevGuard dg(c->device);
+  uint8_t *p;
+  size_t n;
+  int rc = bbuf(c, what, layer, seq, &p, &n);
+  if (rc) return rc;
+  if (bytes != n) return set_error(F5_EINVAL, "f5_bctx_write: %zu bytes, buffer holds %zu", bytes, n);
+  F5_CU(cudaStreamSynchronize(c->st), "f5_bctx_write");
+  return cuda_status(cudaMemcpy(p, src, n, cudaMemcpyHostToDevice), "f5_bctx_write");
+}
+
+}  // extern "C"

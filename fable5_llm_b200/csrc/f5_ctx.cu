@@ -1155,6 +1155,8 @@ int f5_ctx_read(f5_ctx *c, int what, int layer, void *dst, size_t bytes) {
     case F5_BUF_VE: if (l && l->attn) { src = l->ve; n = (size_t)NKV * c->cfg.max_T; } break;
     case F5_BUF_KA: if (l && l->attn) { src = l->ka; n = 4; } break;
     case F5_BUF_LOGITS: if (c->logits) { src = c->logits; n = (size_t)c->cfg.vocab * 4; } break;
+    case F5_BUF_QKVC16: src = c->qkvc16; n = CONV_DIM * 2; break;
+    case F5_BUF_GATES: src = c->gates; n = 2 * LNH * 4; break;
     default: break;
   }
   if (!src) return set_error(F5_EINVAL, "f5_ctx_read: no buffer %d for layer %d", what, layer);

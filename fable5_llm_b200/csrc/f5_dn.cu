@@ -22,7 +22,11 @@ namespace f5 {
 
 constexpr int DN_THREADS = 128;
 
-__global__ void __launch_bounds__(DN_THREADS) k_dn_step(const __grid_constant__ DnArgs a) {
+// The per-sequence arguments of a batched launch are built member by member
+// (no copy of a0 is modified): with nvcc 12.9 for sm_100a, advancing the
+// first member of a local copy of the argument struct did not reach later
+// reads of it.
+__global__ void __launch_bounds__(DN_THREADS) k_dn_step(const __grid_constant__ DnArgs a0, const DnBatch bs) {
   __shared__ __align__(128) int16_t s_sd[128 * 128];   // head state [dk][dv] -> decayed in place
   __shared__ int32_t s_qn[128], s_kn[128];
   __shared__ long long red[32];
@@ -31,6 +35,24 @@ __global__ void __launch_bounds__(DN_THREADS) k_dn_step(const __grid_constant__ 
   __shared__ __align__(8) uint64_t bar_s;
 
   const int h = blockIdx.x, t = threadIdx.x;
+  const long long b = blockIdx.y;   // sequence of a batched launch
+  DnArgs a;
+  a.qkvc = a0.qkvc + b * bs.qkvc;
+  a.beta = a0.beta + b * bs.gates;
+  a.decay = a0.decay + b * bs.gates;
+  a.z16 = a0.z16 + b * bs.z;
+  a.norm_w = a0.norm_w;
+  a.S = a0.S + b * bs.S;
+  a.xslots = a0.xslots;
+  a.in_tag_op1 = a0.in_tag_op1;
+  a.out_tag_op1 = a0.out_tag_op1;
+  a.on16 = a0.on16 + b * bs.on;
+  a.kh_out = a0.kh_out ? a0.kh_out + b * bs.kh : nullptr;
+  a.stats = a0.stats;
+  a.err = a0.err;
+  a.lkd = a0.lkd;
+  a.vrep = a0.vrep;
+  a.norm_mode = a0.norm_mode;
   // The head's 32 KB state does not depend on the previous kernel: start its
   // bulk copy into shared memory before the dependency wait.
   if (t == 0) {
@@ -58,8 +80,12 @@ __global__ void __launch_bounds__(DN_THREADS) k_dn_step(const __grid_constant__ 
 }
 
 cudaError_t launch_dn_step(const DnArgs &a, int nheads, cudaStream_t st, bool pdl) {
+  return launch_dn_step_b(a, DnBatch{}, nheads, 1, st, pdl);
+}
+
+cudaError_t launch_dn_step_b(const DnArgs &a, const DnBatch &bs, int nheads, int B, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(nheads);
+  cfg.gridDim = dim3(nheads, B);
   cfg.blockDim = dim3(DN_THREADS);
   cfg.stream = st;
   cudaLaunchAttribute at[1];
@@ -67,7 +93,7 @@ cudaError_t launch_dn_step(const DnArgs &a, int nheads, cudaStream_t st, bool pd
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, k_dn_step, a);
+  return cudaLaunchKernelEx(&cfg, k_dn_step, a, bs);
 }
 
 }  // namespace f5

@@ -26,6 +26,13 @@ struct DnArgs {
   int norm_mode;          // 0 float64 host-scale law, 1 integer EPS-NORM
 };
 
+// Batched launch (B independent sequences, blockIdx.y = sequence): element
+// strides between consecutive sequences' buffers
+struct DnBatch {
+  long long qkvc, gates, z, S, on, kh;
+};
+
 cudaError_t launch_dn_step(const DnArgs &a, int nheads, cudaStream_t st, bool pdl);
+cudaError_t launch_dn_step_b(const DnArgs &a, const DnBatch &bs, int nheads, int B, cudaStream_t st, bool pdl);
 
 }  // namespace f5

@@ -254,7 +254,8 @@ class DecodeModel:
                  L.BUF_DN_KH: (g.LNH, np.int32), L.BUF_K8: (g.NKV * self.max_T * g.HD, np.int8),
                  L.BUF_KE: (g.NKV * self.max_T, np.int8), L.BUF_V8: (g.NKV * self.max_T * g.HD, np.int8),
                  L.BUF_VE: (g.NKV * self.max_T, np.int8), L.BUF_KA: (1, np.int32),
-                 L.BUF_LOGITS: (g.vocab, np.int32)}
+                 L.BUF_LOGITS: (g.vocab, np.int32), L.BUF_QKVC16: (g.CONV_DIM, np.int16),
+                 L.BUF_GATES: (2 * g.LNH, np.int32)}
         n, dt = sizes[what]
         out = np.empty(n, dtype=dt)
         L.check(self.lib.f5_ctx_read(self.h, what, layer, _p(out), out.nbytes), f"read({what})")

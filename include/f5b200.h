@@ -206,7 +206,9 @@ enum f5_buf { F5_BUF_X16 = 0, F5_BUF_QKV16 = 1, F5_BUF_Z16 = 2, F5_BUF_B16 = 3, 
               F5_BUF_PROD64 = 9, F5_BUF_PROD16 = 10, F5_BUF_STATS = 11,
               F5_BUF_DN_S = 12 /* int16 [32 heads][4][128 dk][32]: dv = 32 * quarter + i */, F5_BUF_DN_CONV = 13 /* int16 [8192][4] ring */,
               F5_BUF_DN_KH = 14, F5_BUF_K8 = 15, F5_BUF_KE = 16, F5_BUF_V8 = 17, F5_BUF_VE = 18,
-              F5_BUF_KA = 19, F5_BUF_LOGITS = 20 /* int32 [vocab], see f5_ctx_set_logits */ };
+              F5_BUF_KA = 19, F5_BUF_LOGITS = 20 /* int32 [vocab], see f5_ctx_set_logits */,
+              F5_BUF_QKVC16 = 21 /* post-conv q|k|v of the last DeltaNet layer (graph engine) */,
+              F5_BUF_GATES = 22 /* int32 [2][32] beta | decay of the last DeltaNet layer (graph engine) */ };
 
 /* create / destroy (state zeroed, T = 0) */
 int f5_ctx_create(const f5_config *cfg, int device, f5_ctx **out);
@@ -293,6 +295,37 @@ int f5_layer_step(f5_ctx *ctx, int layer, int16_t *x16_inout, int T, int pos);
 /* raw device buffer copies (enum f5_buf); bytes must equal the buffer size */
 int f5_ctx_read(f5_ctx *ctx, int what, int layer, void *dst, size_t bytes);
 int f5_ctx_write(f5_ctx *ctx, int what, int layer, const void *src, size_t bytes);
+
+/* ---------------------------------------------------------------------------
+ * Batched decode: B independent greedy sequences over one loaded model
+ * ------------------------------------------------------------------------- */
+
+/* The reference decodes one sequence at a time (ref/fidelity_check.py:
+ * 404-448); a batched context runs B such independent decode steps at once.
+ * It borrows the weights of a fully loaded model context `model` (which must
+ * outlive it, world_size 1, g = 128 images) and owns B sequences' decode
+ * state (DeltaNet states and conv windows, KV caches of max_T tokens, T and
+ * pos), all zero at creation.  Every projection runs as a W4A8 GEMM of the B
+ * quantized inputs on the tensor cores; per sequence, every result equals
+ * the single-sequence step's bit for bit.  1 <= batch <= 64. */
+typedef struct f5_bctx f5_bctx;
+int f5_bctx_create(f5_ctx *model, int batch, int max_T, f5_bctx **out);
+int f5_bctx_destroy(f5_bctx *bctx);
+int f5_bctx_reset(f5_bctx *bctx);                                /* all states zero, T = pos = 0 */
+int f5_bctx_set_position(f5_bctx *bctx, int seq, int T, int pos); /* seq = -1: every sequence */
+int f5_bctx_get_position(f5_bctx *bctx, int seq, int *T, int *pos);
+/* one step of every sequence: tok[B] in, next_tok[B] / max_logit[B] out
+ * (nullable); advances each sequence's T and pos by one */
+int f5_bctx_step(f5_bctx *bctx, const int32_t *tok, int32_t *next_tok, int32_t *max_logit);
+/* enqueue n greedy steps (each sequence fed its own argmax), no host sync */
+int f5_bctx_launch(f5_bctx *bctx, int n_steps);
+int f5_bctx_sync(f5_bctx *bctx, int32_t *last_tok, int32_t *max_logit);
+int f5_bctx_stream(f5_bctx *bctx, void **stream);
+/* sequence seq's copy of an f5_buf buffer (same sizes as f5_ctx_read): the
+ * state buffers of a layer, and the activations of the last layer that wrote
+ * them (X16, QKV16, Z16, B16, A16, ON16, QG16, K16, V16, PROD64, PROD16) */
+int f5_bctx_read(f5_bctx *bctx, int seq, int what, int layer, void *dst, size_t bytes);
+int f5_bctx_write(f5_bctx *bctx, int seq, int what, int layer, const void *src, size_t bytes);
 
 #ifdef __cplusplus
 }

@@ -62,3 +62,91 @@ def test_batch_matvec_extremes():
         x8[0::2], x8[1::2] = 127, -127
         x8[3] = np.where(np.arange(K) % 2 == 0, 127, -127)
         check_batch(img, N, K, x8)
+
+
+# ---------------------------------------------------------------------------
+# batched decode engine vs B independent single-sequence runs
+# ---------------------------------------------------------------------------
+from fable5_llm_b200 import _lib as L                      # noqa: E402
+from fable5_llm_b200.batch import BatchModel              # noqa: E402
+from fable5_llm_b200.config import Geometry               # noqa: E402
+from fable5_llm_b200.model import DecodeModel             # noqa: E402
+
+SEED = 2026
+
+
+@pytest.fixture(scope="module")
+def model4b():
+    m = DecodeModel(Geometry(4, 4096), max_T=64)
+    m.load_synthetic(SEED)
+    return m
+
+
+def single_run(m, toks, T0=0):
+    """The single-sequence engine from a zero state: per step (next, y32)."""
+    m.reset()
+    m.set_position(T0, T0)
+    out = []
+    for t, tok in enumerate(toks):
+        out.append(m.decode_step(int(tok), T0 + t))
+    return out
+
+
+def state_of(read, geom, layers=None):
+    st = {}
+    for i, lt in enumerate(geom.layer_types):
+        if layers is not None and i not in layers:
+            continue
+        bufs = (L.BUF_K8, L.BUF_KE, L.BUF_V8, L.BUF_VE) if lt == "full_attention" else (L.BUF_DN_S, L.BUF_DN_CONV, L.BUF_DN_KH)
+        for b in bufs:
+            st[(i, b)] = read(b, i)
+    return st
+
+
+@pytest.mark.parametrize("B", [3, 17, 40])
+def test_batch_engine_matches_single(model4b, B):
+    """Every sequence of a batched step equals the single-sequence engine
+    (which is pinned to the reference) in every token, logit and state word."""
+    m = model4b
+    rng = np.random.default_rng(B)
+    nsteps = 3
+    toks = rng.integers(0, m.geom.vocab, (B, nsteps))
+    bm = BatchModel(m, B)
+    bm.reset()
+    got = [bm.step(toks[:, t]) for t in range(nsteps)]
+    check = sorted({0, B // 2, B - 1})
+    for b in check:
+        ref = single_run(m, toks[b])
+        for t in range(nsteps):
+            assert (int(got[t][0][b]), int(got[t][1][b])) == ref[t], f"sequence {b} step {t}"
+        s_ref = state_of(lambda w, i: m.read(w, i), m.geom)
+        s_got = state_of(lambda w, i: bm.read(b, w, i), m.geom)
+        for k in s_ref:
+            assert np.array_equal(s_ref[k], s_got[k]), f"sequence {b} state {k}"
+        assert bm.position(b) == (nsteps, nsteps)
+    bm.close()
+
+
+def test_batch_engine_greedy_loop_and_offsets(model4b):
+    """Sequences at different RoPE positions, then device-fed greedy steps."""
+    m = model4b
+    B = 5
+    bm = BatchModel(m, B)
+    bm.reset()
+    rng = np.random.default_rng(7)
+    off = [0, 3, 11, 20, 33]
+    for b in range(B):
+        bm.set_position(0, off[b], b)
+    pre = rng.integers(0, m.geom.vocab, (B, 5))
+    for t in range(5):
+        bm.step(pre[:, t])
+    bm.launch(3)
+    last, mv = bm.sync()
+    for b in (0, 2, B - 1):
+        m.reset()
+        for t in range(5):
+            m.decode_step(int(pre[b, t]), off[b] + t)
+        m.decode_launch(3)
+        assert (int(last[b]), int(mv[b])) == m.sync(), f"sequence {b}"
+        assert bm.position(b) == (8, off[b] + 8)
+    bm.close()
