@@ -37,6 +37,7 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 WEIGHT_BYTES_9B = 4091805696
+WEIGHT_ELEMS_9B = WEIGHT_BYTES_9B * 64 // 33   # 4.125 bits per weight: 7,935,623,168 int4 weights
 FPGA_TOKS = 8.182   # published best 9B decode (evidence/qwen9b/sr/SR17_ROUND_CLOSE.md:36)
 
 
@@ -373,6 +374,17 @@ def run_step(args, ws, rank, local):
         gemv_gbs = kt["gemv_bytes"] / (kt["gemv_ms"] * 1e-3) / 1e9
     else:
         kt, gemv_gbs = {"launches": 0.0}, 0.0
+    # config 5 at a glance (single GPU): B sequences at context 1024 over
+    # zero-filled caches, 10 timed steps each (bench.py --batch B measures it
+    # properly, prefilled)
+    batched = None
+    if ws == 1 and args.layers == 32 and not args.no_batched:
+        batched = {}
+        for B in (8, 32, 64):
+            bms, _, _ = time_batched(m, B, 1024, 10, 3, args.seed)
+            batched[f"B{B}"] = {"tok_s": round(B * 1000.0 / bms, 1), "ms_per_step": round(bms, 3),
+                                "gbs": round((WEIGHT_BYTES_9B + B * batched_state_bytes(m.geom, 1024)) /
+                                             (bms * 1e-3) / 1e9, 1)}
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         cpu = cpu_sample_step(seconds=20.0)
@@ -429,6 +441,131 @@ def run_step(args, ws, rank, local):
             "gpu_launches": launches * args.steps,
             "clocks": ck, "context_tokens_after": T,
         }
+        if batched:
+            line["batched_config5"] = {"per_B": batched, "context": 1024,
+                                       "note": "B independent sequences, tcgen05 W4A8 GEMMs; caches zero-filled "
+                                               "at T=1024 (bench.py --batch B prefills from seeded ids)"}
+        print(json.dumps(line), flush=True)
+    m.close()
+    return 0
+
+
+def batched_state_bytes(geom, T):
+    """Algorithmic per-sequence state bytes of one batched decode step at
+    context T: DeltaNet states read + written, the conv windows (4-slot ring
+    read, one slot written), the int8 KV rows and exponents read, plus the
+    appended row."""
+    n_attn = sum(1 for t in geom.layer_types if t == "full_attention")
+    n_dn = geom.n_layers - n_attn
+    dn = n_dn * geom.LNH * geom.LDK * geom.LDV * 2 * 2
+    conv = n_dn * geom.CONV_DIM * (8 + 2)
+    kv = n_attn * geom.NKV * (T + 1) * (geom.HD + 1) * 2
+    return dn + conv + kv
+
+
+def batched_launches(geom):
+    """Kernels per batched step: begin, per layer 4 projection groups x
+    (prologue, GEMM, epilogue) + the DeltaNet / attention core, the LM head
+    (prologue, GEMM with the argmax), end."""
+    return 2 + geom.n_layers * 13 + 2
+
+
+def time_batched(m, B, ctx_len, steps, warmup, seed, prefill=False):
+    """-> (ms per step, e2e ms per step, last tokens) of B sequences at
+    context ctx_len: prefilled with seeded random ids through the batched
+    step (prefill=True) or positioned at ctx_len over zero-filled caches
+    (the work of a step does not depend on the cached values)."""
+    import torch
+    from fable5_llm_b200.batch import BatchModel
+    bm = BatchModel(m, B, max_T=ctx_len + warmup + 2 * steps + 16)
+    bm.reset()
+    rng = np.random.default_rng(seed + B)
+    if prefill:
+        ids = rng.integers(0, m.geom.vocab, (ctx_len, B))
+        for t in range(ctx_len):
+            bm.step(ids[t])
+    else:
+        bm.set_position(ctx_len, ctx_len)
+        bm.step(rng.integers(0, m.geom.vocab, B))
+    bm.launch(warmup)
+    bm.sync()
+    st = torch.cuda.ExternalStream(bm.stream_handle())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    bm.launch(steps)
+    e1.record(st)
+    last, _ = bm.sync()
+    ms = e0.elapsed_time(e1) / steps
+    # e2e: the public C-ABI batched step, host tokens in, host tokens out
+    tok = last
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(st)
+    for _ in range(steps):
+        tok, _ = bm.step(tok)
+    f1.record(st)
+    torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1) / steps
+    bm.close()
+    return ms, e2e_ms, last
+
+
+def run_batched(args, ws, rank, local):
+    """Config 5: B independent greedy sequences per GPU at context 1024,
+    prefilled from seeded random ids; N GPUs run N independent replicas
+    (each holds the weights and serves its own B sequences)."""
+    import torch
+    from fable5_llm_b200.config import Geometry
+    from fable5_llm_b200.model import DecodeModel
+    hbm_peak, peak_kind = peaks()
+    B, ctx_len = args.batch, args.context
+    geom = Geometry(args.layers, args.vocab)
+    m = DecodeModel(geom, max_T=16, device=local, max_pos=ctx_len + args.warmup + 2 * args.steps + 16)
+    m.load_synthetic(args.seed)
+    clocks = ClockSampler(local)
+    if ws > 1:
+        torch.distributed.barrier()
+    clocks.start()
+    ms, e2e_ms, _ = time_batched(m, B, ctx_len, args.steps, args.warmup, args.seed + rank, prefill=True)
+    ck = clocks.stop()
+    if ws > 1:
+        tt = torch.tensor([ms, e2e_ms], device="cuda")
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        ms, e2e_ms = float(tt[0].item()), float(tt[1].item())
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu = cpu_sample_step(seconds=20.0)
+        cpu["sample"] += f"; B sequences take B times as long, so the tok/s is the single-sequence one"
+    if rank == 0:
+        toks = ws * B * 1000.0 / ms
+        bytes_step = WEIGHT_BYTES_9B + B * batched_state_bytes(geom, ctx_len)
+        gbs = bytes_step / (ms * 1e-3) / 1e9
+        tops = 2.0 * WEIGHT_ELEMS_9B * B / (ms * 1e-3) / 1e12
+        launches = batched_launches(geom)
+        line = {
+            "metric": "9B W4A8 batched greedy decode tok/s", "value": round(toks, 1), "unit": "tok/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int4xint8->int32/int64 (tcgen05 kind::i8)",
+            "data": "synthetic (seeded int4 W4 images and integer vectors, Qwen3.5-9B shapes); "
+                    f"each sequence prefilled with {ctx_len} seeded random token ids",
+            "config": {"workload": f"config 5: {B} independent greedy sequences per GPU at context {ctx_len}, "
+                                   "projections as W4A8 GEMMs on the tensor cores, one CUDA graph per step",
+                       "model": "Qwen3.5-9B (24 DeltaNet + 8 attention layers), synthetic int4",
+                       "global_batch": B * ws, "seq_len": ctx_len,
+                       "l2": "inputs larger than L2 (4.09 GB of weights + per-sequence state per step)",
+                       "parallelism": f"{ws} independent replicas (B={B} each)" if ws > 1 else "single GPU"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": round(hbm_peak * ws, 1), "unit": "GB/s",
+                         "frac": round(gbs / (hbm_peak * ws), 4), "traffic": None,
+                         "kernel": f"whole batched step: 4,091,805,696 W4 bytes + {B} x "
+                                   f"{batched_state_bytes(geom, ctx_len):,} state bytes per step / step time",
+                         "peak_kind": peak_kind if ws == 1 else f"{peak_kind}, x {ws} GPUs",
+                         "int8_tensor_tops": round(tops, 1)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(ws * B * 1000.0 / e2e_ms, 1), "unit": "tok/s",
+                    "h2d_bytes_per_step": B * 4 + B * 32, "d2h_bytes_per_step": B * 32},
+            "gpu_launches": launches * args.steps,
+            "clocks": ck,
+        }
         print(json.dumps(line), flush=True)
     m.close()
     return 0
@@ -438,6 +575,16 @@ def run_ours(args):
     import torch
     ws, rank, local = dist_env()
     torch.cuda.set_device(local)
+    if args.batch:
+        if ws > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local))
+        rc = run_batched(args, ws, rank, local)
+        if ws > 1:
+            torch.distributed.destroy_process_group()
+        return rc
     if args.workload == "step":
         if ws > 1:
             import datetime
@@ -600,8 +747,13 @@ def main():
                     help="LM-head rows (small ncu cases only; the bench line is 248,320)")
     ap.add_argument("--seed", type=int, default=2026)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batched", action="store_true", help="skip the config-5 summary of the default line")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="config 5: B independent greedy sequences per GPU (context --context, default 1024)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.batch and "--context" not in sys.argv:
+        args.context = 1024
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
