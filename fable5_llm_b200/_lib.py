@@ -60,6 +60,7 @@ SIGNATURES = [
     ("f5_bctx_launch", c_int, [c_vp, c_int]),
     ("f5_bctx_sync", c_int, [c_vp, c_vp, c_vp]),
     ("f5_bctx_stream", c_int, [c_vp, c_vp]),
+    ("f5_bctx_time_step", c_int, [c_vp, c_int, c_vp, c_int]),
     ("f5_bctx_read", c_int, [c_vp, c_int, c_int, c_int, c_vp, c_size]),
     ("f5_bctx_write", c_int, [c_vp, c_int, c_int, c_int, c_vp, c_size]),
     ("f5_matvec_y32_host", c_int, [c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp]),

@@ -75,6 +75,18 @@ class BatchModel:
         L.check(self.lib.f5_bctx_sync(self.h, _p(nt), _p(mv)), "f5_bctx_sync")
         return nt, mv
 
+    def time_step(self, reps=2):
+        """Per-kernel-class device time of one eager batched step (CUDA
+        events around every launch); advances every sequence reps steps."""
+        out = np.zeros(14, dtype=np.float64)
+        L.check(self.lib.f5_bctx_time_step(self.h, int(reps), _p(out), 14), "f5_bctx_time_step")
+        kinds = ("prep", "gemm", "epi", "dn", "attn", "other")
+        r = {f"{k}_ms": float(out[i]) for i, k in enumerate(kinds)}
+        r["gemm_bytes"] = float(out[7])
+        r["launches"] = int(out[12])
+        r["sum_ms"] = float(out[13])
+        return r
+
     def stream_handle(self):
         sp = ctypes.c_void_p()
         L.check(self.lib.f5_bctx_stream(self.h, ctypes.byref(sp)), "f5_bctx_stream")

@@ -119,6 +119,13 @@ struct f5_bctx {
   cudaGraphExec_t exec = nullptr;
   bool dirty = true;
   bool pdl = true;             // programmatic dependent launch between the step's kernels
+  struct Timed {
+    cudaEvent_t a, b;
+    int kind;
+    double bytes;
+  };
+  bool timing = false;         // bracket every launch with events (f5_bctx_time_step)
+  std::vector<Timed> timed;
   bool sizing = false;         // enqueue walk that only sizes the p scratch
   size_t need_p = 0;
   std::vector<void *> allocs;
@@ -144,6 +151,23 @@ int balloc(f5_bctx *c, void **p, size_t bytes) {
     int _rc = balloc((c), reinterpret_cast<void **>(&(p)), (bytes));      \
     if (_rc) return _rc;                                                  \
   } while (0)
+
+enum { BK_PREP = 0, BK_GEMM = 1, BK_EPI = 2, BK_DN = 3, BK_ATTN = 4, BK_OTHER = 5, BK_N = 6 };
+void tb(f5_bctx *c) {
+  if (!c->timing) return;
+  f5_bctx::Timed t = {};
+  cudaEventCreate(&t.a);
+  cudaEventCreate(&t.b);
+  cudaEventRecord(t.a, c->st);
+  c->timed.push_back(t);
+}
+void te(f5_bctx *c, int kind, double bytes) {
+  if (!c->timing) return;
+  f5_bctx::Timed &t = c->timed.back();
+  t.kind = kind;
+  t.bytes = bytes;
+  cudaEventRecord(t.b, c->st);
+}
 
 // One batched projection group: prologue -> GEMM -> per-sequence epilogue.
 cudaError_t bop(f5_bctx *c, const BSeg *sg, int nseg, int K, const GemvPrologue &pro, long long src_bs,
@@ -218,8 +242,16 @@ cudaError_t bop(f5_bctx *c, const BSeg *sg, int nseg, int K, const GemvPrologue 
   pa.xt = c->xt;
   pa.err = c->err;
   cudaError_t e;
-  if ((e = launch_bprep(pa, c->st, c->pdl))) return e;
-  if ((e = launch_bgemm(ga, c->st, c->pdl, sm_count()))) return e;
+  double wbytes = 0;
+  for (int i = 0; i < gs; ++i) wbytes += (double)ga.seg[i].rows * ga.stride;
+  tb(c);
+  e = launch_bprep(pa, c->st, c->pdl);
+  te(c, BK_PREP, 0);
+  if (e) return e;
+  tb(c);
+  e = launch_bgemm(ga, c->st, c->pdl, sm_count());
+  te(c, BK_GEMM, wbytes);
+  if (e) return e;
   if (head) return cudaSuccess;
   ea.g.nseg = nseg;
   ea.g.total_units = units;
@@ -233,7 +265,10 @@ cudaError_t bop(f5_bctx *c, const BSeg *sg, int nseg, int K, const GemvPrologue 
   ea.p = c->p;
   ea.xmeta = c->xmeta;
   ea.params = c->params;
-  return launch_bepi(ea, c->st, c->pdl);
+  tb(c);
+  e = launch_bepi(ea, c->st, c->pdl);
+  te(c, BK_EPI, 0);
+  return e;
 }
 
 cudaError_t enqueue_blayer(f5_bctx *c, int li) {
@@ -268,7 +303,10 @@ cudaError_t enqueue_blayer(f5_bctx *c, int li) {
       d.lkd = LKD; d.vrep = LNH / LNKH; d.norm_mode = c->m->cfg.norm_mode;
       DnBatch bs;
       bs.qkvc = CONV_DIM; bs.gates = 2 * LNH; bs.z = LVD; bs.S = (long long)LNH * LDK * LDV; bs.on = LVD; bs.kh = LNH;
-      if ((e = launch_dn_step_b(d, bs, LNH, c->B, c->st, c->pdl))) return e;
+      tb(c);
+      e = launch_dn_step_b(d, bs, LNH, c->B, c->st, c->pdl);
+      te(c, BK_DN, 0);
+      if (e) return e;
     }
     GemvPrologue p2 = {};
     p2.mode = PRO_DYNQ8;
@@ -294,7 +332,10 @@ cudaError_t enqueue_blayer(f5_bctx *c, int li) {
       bs.qg = (long long)NQ * HD * 2; bs.kv16 = (long long)NKV * HD;
       bs.cache = (long long)NKV * c->max_T * HD; bs.cache_e = (long long)NKV * c->max_T;
       bs.prod = (long long)NQ * HD; bs.params = (long long)PARAM_INTS;
-      if ((e = launch_attn_b(at, bs, c->B, c->st, c->pdl))) return e;
+      tb(c);
+      e = launch_attn_b(at, bs, c->B, c->st, c->pdl);
+      te(c, BK_ATTN, 0);
+      if (e) return e;
     }
     GemvPrologue p2 = {};
     p2.mode = PRO_ATTN_GATE;
@@ -626,6 +667,39 @@ int f5_bctx_sync(f5_bctx *c, int32_t *last_tok, int32_t *max_logit) {
     if (max_logit) max_logit[b] = c->h_params[b].max_val;
   }
   return rc;
+}
+
+int f5_bctx_time_step(f5_bctx *c, int reps, double *out, int nout) {
+  if (!c || !out || nout < 2 * BK_N + 2 || reps < 1) return set_error(F5_EINVAL, "f5_bctx_time_step: bad argument");
+  BDevGuard dg(c->device);
+  double ms[BK_N] = {}, bytes[BK_N] = {};
+  double launches = 0;
+  for (int r = 0; r < reps; ++r) {
+    c->timing = true;
+    c->timed.clear();
+    cudaError_t e = enqueue_bstep(c);
+    c->timing = false;
+    if (e != cudaSuccess) return cuda_status(e, "f5_bctx_time_step");
+    F5_CU(cudaStreamSynchronize(c->st), "f5_bctx_time_step");
+    for (f5_bctx::Timed &t : c->timed) {
+      float x = 0;
+      cudaEventElapsedTime(&x, t.a, t.b);
+      ms[t.kind] += x / reps;
+      bytes[t.kind] += t.bytes / reps;
+      cudaEventDestroy(t.a);
+      cudaEventDestroy(t.b);
+    }
+    launches = (double)c->timed.size() + 2;
+    c->timed.clear();
+  }
+  for (int k = 0; k < BK_N; ++k) {
+    out[k] = ms[k];
+    out[BK_N + k] = bytes[k];
+  }
+  out[2 * BK_N] = launches;
+  out[2 * BK_N + 1] = 0;
+  for (int k = 0; k < BK_N; ++k) out[2 * BK_N + 1] += ms[k];
+  return bfinish(c, "f5_bctx_time_step");
 }
 
 int f5_bctx_stream(f5_bctx *c, void **stream) {

@@ -15,23 +15,27 @@
 //
 // The weights stay in the reference's packed row format in HBM.  A stage
 // brings 4 groups (256 bytes) of each of the tile's 128 rows into shared
-// memory with one 2D tensor-map copy.  The nibbles become 16 * w4 as signed
-// bytes with one shift and two masks per 8 weights ((word << 4) & 0xF0F0F0F0
-// for even k, word & 0xF0F0F0F0 for odd k), written in the MMA's
-// 128-byte-swizzled K-major layout; the accumulator then holds 16 * acc_g
-// (|.| <= 2^21) and p = (sum_g m_g * 16 acc_g) >> 4 exactly.  Within each
-// 8-weight block the unpacked bytes are the even k then the odd k; the
-// prologue writes x8 in the same order.
+// memory as two 2D tensor-map boxes (128 rows x 128 bytes, 128-byte
+// swizzle).  Four unpack warps, one per tensor-memory lane quarter, turn a
+// row's nibbles into 16 * w4 as signed bytes ((word << 4) & 0xF0F0F0F0 for
+// even k, word & 0xF0F0F0F0 for odd k) and store them straight into tensor
+// memory with tcgen05.st: the MMA reads its A operand (128 rows x 32 bytes
+// of K per instruction) from tensor memory, so the unpacked weights never
+// touch shared memory.  The accumulator holds 16 * acc_g (|.| <= 2^21) and
+// p = (sum_g m_g * 16 acc_g) >> 4 exactly.  Within each 8-weight block the
+// unpacked bytes are the even k then the odd k; the prologue writes x8 (the
+// B operand, 128-byte-swizzled K-major rows in shared memory) in the same
+// order.
 //
-// Warp roles (512 threads, one CTA per SM): warp 0 streams the stages (the
-// weight box and the prepared x8 tiles), warp 1 allocates TMEM and issues
-// the MMAs (one thread), warps 2-7 unpack pairs of groups, warps 8-15 read
-// the accumulators back (TMEM lane quarter = warp % 4, column half =
-// (warp-8)/4) and fold m_g * acc_g into int64 registers.  Each role only
-// waits on the one before it, through rings deep enough (4 A tiles, 8 TMEM
-// accumulators) that no role stalls on a later one in steady state.  Every hand-off is
-// an mbarrier; every wait is bounded and an expired wait sets DERR_TIMEOUT
-// and unwinds the CTA (no copy or MMA left in flight).
+// Warp roles (one CTA per SM): warp 0 streams the stages,
+// warp 1 allocates tensor memory and issues the MMAs (one thread: 4
+// tcgen05.mma kind::i8 M=128 N=Bp K=32 per group into one of up to 8
+// accumulators, tcgen05.commit to mbarriers), warps 2-5 unpack, Bp / 4
+// fold warps from warp 6 read each group's accumulator back (lane quarter =
+// warp % 4, 16-column block = (warp - 6) / 4) and fold m_g * acc_g into
+// int64 registers.
+// Every hand-off is an mbarrier; every wait is bounded and an expired wait
+// sets DERR_TIMEOUT and unwinds the CTA (no copy or MMA left in flight).
 //
 // Work: units = (128-row tile, K split); split s covers groups
 // [s*NG/S, (s+1)*NG/S) and writes its partial p to p[s][b][row]; k_bepi
@@ -49,11 +53,12 @@
 
 namespace f5 {
 
-constexpr int BG_WORKERS = 6;      // unpack warps 2-7; warps 8-15 fold the accumulators
-constexpr int BG_THREADS = 32 * (2 + BG_WORKERS + 8);
-constexpr int BG_NA = 4;           // unpacked A-tile slots (16 KB each), two per group pair
-constexpr int BG_NT = 8;           // TMEM accumulator buffers
-constexpr int BG_WBYTES = BG_TILE * 64 * BG_GPS;   // packed weights per stage (32 KB)
+constexpr int BG_UNPACK = 4;       // unpack warps 2-5 (one per TMEM lane quarter)
+constexpr int BG_FOLDQ = 16;       // accumulator columns per fold thread: Bp / 16 fold warps per lane quarter
+constexpr int bg_fold_warps(int Bp) { return 4 * (Bp / BG_FOLDQ); }
+constexpr int bg_threads(int Bp) { return 32 * (2 + BG_UNPACK + bg_fold_warps(Bp)); }
+constexpr int BG_MAX_NS = 6;       // pipeline stages at most
+constexpr int BG_WBYTES = BG_TILE * 64 * BG_GPS;   // packed weights per stage (32 KB: two 16 KB boxes)
 constexpr int BG_SMEM_MAX = 232448 - 4096;
 constexpr unsigned long long BG_WAIT_NS = 2000000000ull;
 
@@ -65,14 +70,18 @@ F5_DEV int bg_seg_of_tile(const BgemmArgs &a, int tile) {
   return s;
 }
 
-template <int BPH>
-__global__ void __launch_bounds__(BG_THREADS, 1) k_bgemm(const __grid_constant__ BgemmArgs a) {
-  constexpr int BP = 2 * BPH;
+template <int BP>
+__global__ void __launch_bounds__(bg_threads(BP), 1) k_bgemm(const __grid_constant__ BgemmArgs a) {
+  constexpr int BPQ = BG_FOLDQ;                             // accumulator columns per fold thread
+  constexpr int BG_FOLD = bg_fold_warps(BP);
   constexpr int XBYTES = BP * 128 * BG_GPS;
   constexpr int STAGE = BG_WBYTES + XBYTES;
-  constexpr uint32_t TCOLS = BG_NT * BP < 32 ? 32 : BG_NT * BP;
+  // tensor memory: NP pair slots of [A of 2 groups: 64 columns | 2 accumulators: 2 x BP]
+  constexpr int SLOT = 64 + 2 * BP;
+  constexpr int NP = 512 / SLOT > 4 ? 4 : 512 / SLOT;
+  static_assert(NP >= 2, "two pair slots at least");
   extern __shared__ uint8_t bg_dyn[];
-  __shared__ __align__(8) uint64_t full[4], empty[4], afull[BG_NA], aempty[BG_NA], tfull[BG_NT], tempty[BG_NT];
+  __shared__ __align__(8) uint64_t full[BG_MAX_NS], empty[BG_MAX_NS], afull[4], done[4], tfree[4];
   __shared__ __align__(8) uint64_t drain;
   __shared__ uint32_t s_tmem;
   __shared__ volatile int s_abort;
@@ -80,9 +89,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1) k_bgemm(const __grid_constant__
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int NS = a.ns;
-  uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(bg_dyn) + 1023) & ~(uintptr_t)1023);
-  uint8_t *aslot = base;                                   // BG_NA x 16 KB
-  uint8_t *stg = base + BG_NA * 16384;                     // NS x STAGE
+  uint8_t *stg = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(bg_dyn) + 1023) & ~(uintptr_t)1023);
   const int gpu = a.NG / a.S;                              // groups per unit
   const int spu = gpu / BG_GPS;                            // stages per unit
   const int ppu = gpu / 2;                                 // group pairs per unit
@@ -92,22 +99,19 @@ __global__ void __launch_bounds__(BG_THREADS, 1) k_bgemm(const __grid_constant__
   if (tid == 0) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], BG_WORKERS + 1);   // every worker warp + the MMA commit
+      mbar_init(&empty[i], BG_UNPACK + 1);   // every unpack warp + the MMA commit
     }
-    for (int i = 0; i < BG_NA; ++i) {
-      mbar_init(&afull[i], BG_WORKERS);
-      mbar_init(&aempty[i], 1);
-    }
-    for (int i = 0; i < BG_NT; ++i) {
-      mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 8);
+    for (int i = 0; i < NP; ++i) {
+      mbar_init(&afull[i], BG_UNPACK);   // both groups' A written
+      mbar_init(&done[i], 1);            // both groups' MMAs complete (commit)
+      mbar_init(&tfree[i], BG_FOLD);     // both accumulators read back
     }
     mbar_init(&drain, 1);
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (tid < BP) s_key[tid] = 0ull;
-  if (warp == 1) tc_alloc(&s_tmem, TCOLS);
+  if (warp == 1) tc_alloc(&s_tmem, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -117,27 +121,12 @@ __global__ void __launch_bounds__(BG_THREADS, 1) k_bgemm(const __grid_constant__
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (warp == 0) {
-    // ---------------- producer ----------------
-    // A stage reads 256 bytes from each of 128 rows 2112 (6336) bytes apart,
-    // a poor DRAM access pattern; so each unit's rows are first streamed into
-    // L2 contiguously (one bulk prefetch per row, one unit ahead) and the
-    // stage boxes then hit L2.
-    auto prefetch_unit = [&](int u) {
-      if (u >= units) return;
-      const int tile = u / a.S, sp = u % a.S;
-      const BgemmSeg &sg = a.seg[bg_seg_of_tile(a, tile)];
-      const int r0 = (tile - sg.tile_begin) * BG_TILE;
-      const int nr = min(BG_TILE, sg.rows - r0);
-      const uint8_t *b0 = sg.w + (size_t)r0 * a.stride + (size_t)sp * gpu * 64;
-      for (int r = lane; r < nr; r += 32) prefetch_l2(b0 + (size_t)r * a.stride, (uint32_t)gpu * 64);
-    };
-    prefetch_unit(blockIdx.x);
+    // ---------------- producer: two 128-byte-swizzled weight boxes + the x tiles per stage ----------------
     int sc = 0;
     for (int u = blockIdx.x; u < units && !s_abort; u += gridDim.x) {
       const int tile = u / a.S, sp = u % a.S;
       const int si = bg_seg_of_tile(a, tile);
       const int r0 = (tile - a.seg[si].tile_begin) * BG_TILE;
-      prefetch_unit(u + gridDim.x);
       for (int st = 0; st < spu; ++st, ++sc) {
         const int s = sc % NS;
         bool ok = true;
@@ -151,184 +140,189 @@ __global__ void __launch_bounds__(BG_THREADS, 1) k_bgemm(const __grid_constant__
         uint8_t *dst = stg + (size_t)s * STAGE;
         if (tr && lane == 0 && sc < 1024) a.trace[sc] = gtimer();
         if (lane == 0) {
-          // one box of 128 rows x 256 bytes (rows past the image read as zeros)
+          // rows past the image read as zeros
           mbar_expect_tx(&full[s], (uint32_t)STAGE);
           tma_load_2d(dst, &a.tmap[si], g * 64, r0, &full[s]);
+          tma_load_2d(dst + BG_WBYTES / 2, &a.tmap[si], g * 64 + 128, r0, &full[s]);
           bulk_g2s(dst + BG_WBYTES, a.xt + (size_t)g * BP * 128, XBYTES, &full[s]);
         }
         __syncwarp();
       }
     }
-    // drain: wait until every issued stage has landed (bounded)
     if (lane == 0 && s_abort)
       for (int i = max(0, sc - NS); i < sc; ++i) mbar_wait(&full[i % NS], (i / NS) & 1, BG_WAIT_NS);
   } else if (warp == 1) {
-    // ---------------- MMA issuer (one thread) ----------------
+    // ---------------- MMA issuer (one thread): one wait, 8 MMAs, one commit per group pair ----------------
     if (lane == 0) {
       const uint32_t idesc = idesc_s8s8(BG_TILE, BP);
-      int sc = 0, ac = 0, tc = 0;
+      int sc = 0, pc = 0;
       bool issued = false;
       for (int u = blockIdx.x; u < units && !s_abort; u += gridDim.x) {
         for (int st = 0; st < spu && !s_abort; ++st, ++sc) {
           const int s = sc % NS;
           if (!mbar_wait(&full[s], (sc / NS) & 1, BG_WAIT_NS)) { s_abort = 1; atomicOr(a.err, DERR_TIMEOUT); break; }
-          const uint32_t xbase = smem_u32(stg + (size_t)s * STAGE + BG_WBYTES);
-          for (int gi = 0; gi < BG_GPS; ++gi, ++ac, ++tc) {
-            const int as = ac % BG_NA, ts = tc % BG_NT;
-            if (!mbar_wait(&afull[as], (ac / BG_NA) & 1, BG_WAIT_NS) ||
-                (tc >= BG_NT && !mbar_wait(&tempty[ts], ((tc / BG_NT) - 1) & 1, BG_WAIT_NS))) {
+          const uint64_t bd0 = sw128_desc(smem_u32(stg + (size_t)s * STAGE + BG_WBYTES));
+          for (int pi = 0; pi < BG_GPS / 2; ++pi, ++pc) {
+            const int j = pc % NP;
+            // afull implies the unpack saw this slot's accumulators freed by the fold
+            if (!mbar_wait(&afull[j], (pc / NP) & 1, BG_WAIT_NS)) {
               s_abort = 1;
               atomicOr(a.err, DERR_TIMEOUT);
               break;
             }
             tc_fence_after();
-            const uint64_t ad = sw128_desc(smem_u32(aslot + (size_t)as * 16384));
-            const uint64_t bd = sw128_desc(xbase + (uint32_t)(gi * BP * 128));
+            const uint32_t base = tmem + (uint32_t)(j * SLOT);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) tc_mma_i8(tmem + (uint32_t)(ts * BP), ad + 2 * k, bd + 2 * k, idesc, k > 0);
+            for (int e = 0; e < 2; ++e) {
+              const uint64_t bd = bd0 + (uint64_t)(((2 * pi + e) * BP * 128) >> 4);
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                tc_mma_i8_ts(base + 64 + (uint32_t)(e * BP), base + (uint32_t)(32 * e + 8 * k), bd + 2 * k, idesc,
+                             k > 0);
+            }
             issued = true;
-            if (tr && tc < 2048) a.trace[4096 + tc] = gtimer();
-            tc_commit(&aempty[as]);
-            tc_commit(&tfull[ts]);
+            if (tr && pc < 2048) a.trace[4096 + pc] = gtimer();
+            tc_commit(&done[j]);
           }
           tc_commit(&empty[s]);
         }
       }
-      // every MMA complete before TMEM is released
       if (issued) {
         tc_commit(&drain);
         mbar_wait(&drain, 0, BG_WAIT_NS);
       }
     }
     __syncwarp();
-  } else if (warp < 2 + BG_WORKERS) {
-    // ---------------- unpack (warps 2-7) ----------------
-    // 8 lanes take one row's 128 contiguous packed bytes (conflict-free
-    // reads) of a pair of groups; lane chunk j = 4 h + c is packed chunk c
-    // of group gs + h.  Lanes of the second group store their two output
-    // chunks in the opposite order, so each store phase covers 8 distinct
-    // 16-byte bank groups.  Nibbles become 16 w as int8: (w << 4) & 0xF0 for
-    // even k, w & 0xF0 for odd k.  Row quads (4 rows per warp instruction)
-    // are dealt round-robin: warp u takes quads u, u + 6, ...
-    const int wu = warp - 2;
-    const int j = lane & 7, h = j >> 2, c = j & 3;
+  } else if (warp < 2 + BG_UNPACK) {
+    // ---------------- unpack (warps 2-5, one per TMEM lane quarter): thread = row ----------------
+    // Row r's packed group gi is 64 bytes = 16-byte chunks 4 (gi & 1) + c of
+    // the 128-byte swizzled row r of box gi / 2 (chunk j at j ^ (r & 7)):
+    // eight consecutive rows read eight different bank groups.  Nibbles
+    // become 16 w as signed bytes ((w << 4) & 0xF0F0F0F0 even k, w &
+    // 0xF0F0F0F0 odd k), written to the row's lane of the pair slot's A
+    // columns: column 2i = the even k of packed word i, 2i + 1 the odd k.
+    const int q = warp & 3;
+    const int r = 32 * q + lane;
+    const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);
     bool ok = true;
     int sc = 0, pc = 0;
     for (int u = blockIdx.x; u < units && ok && !s_abort; u += gridDim.x) {
-      for (int pi = 0; pi < ppu; ++pi, ++pc) {
-        const int s = sc % NS, gs = (2 * pi) % BG_GPS;   // stage, first group within it
-        if (gs == 0) {
-          if (lane == 0) ok = mbar_wait(&full[s], (sc / NS) & 1, BG_WAIT_NS);
-          ok = __shfl_sync(0xffffffffu, ok, 0);
-          if (tr && tid == 64 && sc < 1024) a.trace[1024 + sc] = gtimer();
-        }
-        const int ac = 2 * pc, as0 = ac % BG_NA, as1 = (ac + 1) % BG_NA;
-        if (ok && ac >= BG_NA) {
-          if (lane == 0)
-            ok = mbar_wait(&aempty[as0], ((ac / BG_NA) - 1) & 1, BG_WAIT_NS) &&
-                 mbar_wait(&aempty[as1], (((ac + 1) / BG_NA) - 1) & 1, BG_WAIT_NS);
-          ok = __shfl_sync(0xffffffffu, ok, 0);
-        }
+      for (int st = 0; st < spu; ++st, ++sc) {
+        const int s = sc % NS;
+        if (lane == 0) ok = mbar_wait(&full[s], (sc / NS) & 1, BG_WAIT_NS);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (tr && tid == 64 && sc < 1024) a.trace[1024 + sc] = gtimer();
         if (!ok || s_abort) {
           if (lane == 0 && !ok) { s_abort = 1; atomicOr(a.err, DERR_TIMEOUT); }
           ok = false;
           break;
         }
-        const uint8_t *src = stg + (size_t)s * STAGE + gs * 64 + j * 16;
-        uint8_t *dst = aslot + (size_t)(h ? as1 : as0) * 16384;
-#pragma unroll 2
-        for (int qd = wu; qd < BG_TILE / 4; qd += BG_WORKERS) {
-          const int r = qd * 4 + (lane >> 3);
-          const uint4 w = *reinterpret_cast<const uint4 *>(src + r * 256);
-          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-          uint32_t o[8];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            o[2 * k] = (wv[k] << 4) & 0xF0F0F0F0u;
-            o[2 * k + 1] = wv[k] & 0xF0F0F0F0u;
+        const uint8_t *src = stg + (size_t)s * STAGE + r * 128;
+        for (int pi = 0; pi < BG_GPS / 2; ++pi, ++pc) {
+          const int j = pc % NP;
+          if (pc >= NP) {   // the slot's previous pair fully read back by the fold
+            if (lane == 0) ok = mbar_wait(&tfree[j], ((pc / NP) - 1) & 1, BG_WAIT_NS);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+              if (lane == 0) { s_abort = 1; atomicOr(a.err, DERR_TIMEOUT); }
+              break;
+            }
+            tc_fence_after();
           }
-          const uint32_t o0 = sw128_off(r, c * 32), o1 = sw128_off(r, c * 32 + 16);
-          const uint4 v0 = make_uint4(o[0], o[1], o[2], o[3]), v1 = make_uint4(o[4], o[5], o[6], o[7]);
-          *reinterpret_cast<uint4 *>(dst + (h ? o1 : o0)) = h ? v1 : v0;
-          *reinterpret_cast<uint4 *>(dst + (h ? o0 : o1)) = h ? v0 : v1;
+          const uint8_t *bx = src + pi * (BG_WBYTES / 2);   // box of groups 2 pi, 2 pi + 1
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            uint32_t o[32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const int jc = 4 * e + c;
+              const uint4 w = *reinterpret_cast<const uint4 *>(bx + ((jc ^ (r & 7)) << 4));
+              const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                o[8 * c + 2 * k] = (wv[k] << 4) & 0xF0F0F0F0u;
+                o[8 * c + 2 * k + 1] = wv[k] & 0xF0F0F0F0u;
+              }
+            }
+            tc_st32(tq + (uint32_t)(j * SLOT + 32 * e), o);
+          }
+          tc_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&afull[j]);
+          if (tr && tid == 64 && pc < 2048) a.trace[2048 + pc] = gtimer();
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic writes -> MMA reads
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&afull[as0]);
-          mbar_arrive(&afull[as1]);
-          if (gs + 2 == BG_GPS) mbar_arrive(&empty[s]);   // the stage's packed bytes are consumed
-        }
-        if (tr && tid == 64 && ac < 2048) a.trace[2048 + ac] = gtimer();
-        if (gs + 2 == BG_GPS) ++sc;
+        if (lane == 0) mbar_arrive(&empty[s]);   // the stage's packed bytes are consumed
+        if (!ok) break;
       }
     }
   } else {
-    // ---------------- accumulator fold (warps 8-15) ----------------
-    const int q = warp & 3, hf = (warp - 2 - BG_WORKERS) >> 2;
+    // ---------------- accumulator fold (warps 6-21) ----------------
+    // warp w reads TMEM lane quarter w % 4 (rows 32 (w % 4) + lane) and the
+    // 16-column block cq = (w - 6) / 4 of both accumulators of a pair slot
+    const int q = warp & 3, cq = (warp - 2 - BG_UNPACK) >> 2;
     const int rt = 32 * q + lane;                              // row within the tile
-    const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(hf * BPH);
-    constexpr int LDW = BPH < 16 ? BPH : 16;                   // columns per TMEM load
-    int tc = 0;
+    const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16) + 64 + (uint32_t)(cq * BPQ);
+    int pc = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok && !s_abort; u += gridDim.x) {
       const int tile = u / a.S, sp = u % a.S;
       const BgemmSeg &sg = a.seg[bg_seg_of_tile(a, tile)];
       const int r0 = (tile - sg.tile_begin) * BG_TILE;
       const bool valid = rt < sg.rows - r0;
-      long long acc[BPH];
+      long long acc[BPQ];
 #pragma unroll
-      for (int jj = 0; jj < BPH; ++jj) acc[jj] = 0;
+      for (int jj = 0; jj < BPQ; ++jj) acc[jj] = 0;
       // group scales 8 at a time, the next 8 prefetched one block ahead
       const uint4 *ms = reinterpret_cast<const uint4 *>(sg.w + (size_t)(valid ? r0 + rt : r0) * a.stride +
                                                         (size_t)a.NG * 64 + 2 * sp * gpu);
       uint4 mv = __ldg(ms), mvn = gpu > 8 ? __ldg(ms + 1) : make_uint4(0, 0, 0, 0);
-      for (int gi = 0; gi < gpu; ++gi, ++tc) {
+      for (int pi = 0; pi < ppu; ++pi, ++pc) {
+        const int gi = 2 * pi;
         if ((gi & 7) == 0 && gi) {
           mv = mvn;
           if (gi + 8 < gpu) mvn = __ldg(ms + (gi >> 3) + 1);
         }
         const uint32_t mw = (gi & 6) == 0 ? mv.x : ((gi & 6) == 2 ? mv.y : ((gi & 6) == 4 ? mv.z : mv.w));
-        const int32_t m = (int32_t)((gi & 1) ? (mw >> 16) : (mw & 0xFFFFu));
-        const int ts = tc % BG_NT;
-        if (lane == 0) ok = mbar_wait(&tfull[ts], (tc / BG_NT) & 1, BG_WAIT_NS);
+        const int32_t m0 = (int32_t)(mw & 0xFFFFu), m1 = (int32_t)(mw >> 16);
+        const int j = pc % NP;
+        if (lane == 0) ok = mbar_wait(&done[j], (pc / NP) & 1, BG_WAIT_NS);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok || s_abort) {
           if (lane == 0 && !ok) { s_abort = 1; atomicOr(a.err, DERR_TIMEOUT); }
           ok = false;
           break;
         }
-        if (tr && tid == 2 * 32 + BG_WORKERS * 32 && tc < 2048) a.trace[6144 + tc] = gtimer();
+        if (tr && warp == 2 + BG_UNPACK && lane == 0 && pc < 2048) a.trace[6144 + pc] = gtimer();
         tc_fence_after();
-#pragma unroll
-        for (int hh = 0; hh < BPH / LDW; ++hh) {
-          int32_t d[LDW];
-          tc_ld<LDW>(tl + (uint32_t)(ts * BP + hh * LDW), d);
-          tc_wait_ld();
-#pragma unroll
-          for (int jj = 0; jj < LDW; ++jj) acc[hh * LDW + jj] += (long long)m * d[jj];   // 16 p
-        }
+        int32_t d0[BPQ], d1[BPQ];
+        tc_ld<BPQ>(tl + (uint32_t)(j * SLOT), d0);
+        tc_ld<BPQ>(tl + (uint32_t)(j * SLOT + BP), d1);
+        tc_wait_ld();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[ts]);
-        if (tr && tid == 2 * 32 + BG_WORKERS * 32 && tc < 2048) a.trace[8192 + tc] = gtimer();
+        if (lane == 0) mbar_arrive(&tfree[j]);
+#pragma unroll
+        for (int jj = 0; jj < BPQ; ++jj) acc[jj] += (long long)m0 * d0[jj] + (long long)m1 * d1[jj];   // 16 p
+        if (tr && warp == 2 + BG_UNPACK && lane == 0 && pc < 2048) a.trace[8192 + pc] = gtimer();
       }
       if (!ok) break;
       if (sg.argmax) {
         const int row = r0 + rt;
 #pragma unroll
-        for (int jj = 0; jj < BPH; ++jj) {
-          const int b = hf * BPH + jj;
+        for (int jj = 0; jj < BPQ; ++jj) {
+          const int b = cq * BPQ + jj;
           if (valid && b < a.B) {
             const int32_t y = finish_y32(acc[jj], a.sh, a.err, nullptr);
             atomicMax(&s_key[b], argmax_key(y, row));
           }
         }
       } else if (valid) {
-        int64_t *po = a.p + ((size_t)sp * BP + hf * BPH) * a.ptot + sg.p_row0 + r0 + rt;
+        int64_t *po = a.p + ((size_t)sp * BP + cq * BPQ) * a.ptot + sg.p_row0 + r0 + rt;
 #pragma unroll
-        for (int jj = 0; jj < BPH; ++jj)
-          if (hf * BPH + jj < a.B) po[(size_t)jj * a.ptot] = acc[jj] >> 4;
+        for (int jj = 0; jj < BPQ; ++jj)
+          if (cq * BPQ + jj < a.B) po[(size_t)jj * a.ptot] = acc[jj] >> 4;
       }
     }
   }
@@ -336,7 +330,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1) k_bgemm(const __grid_constant__
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tc_dealloc(tmem, TCOLS);
+  if (warp == 1) tc_dealloc(tmem, 512);
   if (a.key && tid < a.B && s_key[tid]) atomicMax(&a.key[tid], s_key[tid]);
 }
 
@@ -448,11 +442,11 @@ bool bgemm_tmap(TmapBytes *out, const uint8_t *w, int rows, int stride) {
   static_assert(sizeof(CUtensorMap) == sizeof(TmapBytes), "CUtensorMap is 128 bytes");
   const cuuint64_t dims[2] = {(cuuint64_t)stride, (cuuint64_t)rows};
   const cuuint64_t gstride[1] = {(cuuint64_t)stride};
-  const cuuint32_t box[2] = {256, (cuuint32_t)BG_TILE};
+  const cuuint32_t box[2] = {128, (cuuint32_t)BG_TILE};   // 2 groups x 128 rows, 128-byte swizzle
   const cuuint32_t estride[2] = {1, 1};
   const CUresult r = encode(reinterpret_cast<CUtensorMap *>(out), CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
                             const_cast<uint8_t *>(w), dims, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -484,9 +478,9 @@ cudaError_t launch_bprep(const BprepArgs &a, cudaStream_t st, bool pdl) {
 
 size_t bgemm_smem(int Bp, int *ns) {
   const size_t stage = (size_t)BG_WBYTES + (size_t)Bp * 128 * BG_GPS;
-  const size_t fixed = 1024 + (size_t)BG_NA * 16384;
+  const size_t fixed = 1024;
   int n = (int)((BG_SMEM_MAX - fixed) / stage);
-  if (n > 4) n = 4;
+  if (n > BG_MAX_NS) n = BG_MAX_NS;
   if (ns) *ns = n;
   return fixed + (size_t)n * stage;
 }
@@ -504,14 +498,14 @@ int bgemm_splits(int tiles, int NG, int ctas, bool argmax) {
   return best;
 }
 
-template <int BPH>
+template <int BP>
 static cudaError_t launch_bg(const BgemmArgs &a, cudaStream_t st, bool pdl, int max_ctas) {
   int ns = 0;
-  const size_t smem = bgemm_smem(2 * BPH, &ns);
+  const size_t smem = bgemm_smem(BP, &ns);
   if (ns < 2) return cudaErrorInvalidValue;
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(k_bgemm<BPH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(k_bgemm<BP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     attr = true;
   }
@@ -520,7 +514,7 @@ static cudaError_t launch_bg(const BgemmArgs &a, cudaStream_t st, bool pdl, int 
   const int units = a.ntiles * a.S;
   const int grid = units < max_ctas ? units : max_ctas;
   void *args[] = {&b};
-  return launch_ex((const void *)k_bgemm<BPH>, args, dim3(grid), dim3(BG_THREADS), smem, st, pdl);
+  return launch_ex((const void *)k_bgemm<BP>, args, dim3(grid), dim3(bg_threads(BP)), smem, st, pdl);
 }
 
 static unsigned long long *g_bg_trace = nullptr;   // process-wide trace buffer (f5_batch_trace)
@@ -535,9 +529,9 @@ cudaError_t launch_bgemm(BgemmArgs a, cudaStream_t st, bool pdl, int max_ctas) {
       a.B < 1 || a.B > a.Bp || a.stride % 16)
     return cudaErrorInvalidValue;
   switch (a.Bp) {
-    case 16: return launch_bg<8>(a, st, pdl, max_ctas);
-    case 32: return launch_bg<16>(a, st, pdl, max_ctas);
-    case 64: return launch_bg<32>(a, st, pdl, max_ctas);
+    case 16: return launch_bg<16>(a, st, pdl, max_ctas);
+    case 32: return launch_bg<32>(a, st, pdl, max_ctas);
+    case 64: return launch_bg<64>(a, st, pdl, max_ctas);
     default: return cudaErrorInvalidValue;
   }
 }

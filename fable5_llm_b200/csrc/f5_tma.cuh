@@ -24,6 +24,9 @@ F5_DEV unsigned long long gtimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+#ifndef F5_MBAR_SLEEP_NS
+#define F5_MBAR_SLEEP_NS 0
+#endif
 // Bounded wait on an mbarrier phase: gives up after ~`limit_ns` (the
 // caller then records DERR_TIMEOUT and unwinds; nothing ever spins forever).
 F5_DEV bool mbar_wait(uint64_t *b, uint32_t parity, unsigned long long limit_ns) {
@@ -31,10 +34,19 @@ F5_DEV bool mbar_wait(uint64_t *b, uint32_t parity, unsigned long long limit_ns)
   unsigned long long t0 = 0;
   for (uint32_t it = 0;; ++it) {
     uint32_t ok;
+#if F5_MBAR_SLEEP_NS
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok) : "r"(addr), "r"(parity), "r"((uint32_t)F5_MBAR_SLEEP_NS) : "memory");
+#else
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
         : "=r"(ok) : "r"(addr), "r"(parity) : "memory");
+#endif
     if (ok) return true;
+#ifdef F5_MBAR_BACKOFF_NS
+    if (it >= 4) __nanosleep(F5_MBAR_BACKOFF_NS);
+#endif
     if ((it & 63) == 0) {
       const unsigned long long t = gtimer();
       if (t0 == 0) t0 = t;

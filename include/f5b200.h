@@ -321,6 +321,12 @@ int f5_bctx_step(f5_bctx *bctx, const int32_t *tok, int32_t *next_tok, int32_t *
 int f5_bctx_launch(f5_bctx *bctx, int n_steps);
 int f5_bctx_sync(f5_bctx *bctx, int32_t *last_tok, int32_t *max_logit);
 int f5_bctx_stream(f5_bctx *bctx, void **stream);
+/* device time of one eager batched step per kernel class, averaged over reps
+ * steps (CUDA events around every launch; each step advances every
+ * sequence): out[0..5] ms of prologue / GEMM / epilogue / DeltaNet /
+ * attention / other kernels, out[6..11] their algorithmic weight bytes,
+ * out[12] launches per step, out[13] the sum of the kernel times (nout >= 14) */
+int f5_bctx_time_step(f5_bctx *bctx, int reps, double *out, int nout);
 /* sequence seq's copy of an f5_buf buffer (same sizes as f5_ctx_read): the
  * state buffers of a layer, and the activations of the last layer that wrote
  * them (X16, QKV16, Z16, B16, A16, ON16, QG16, K16, V16, PROD64, PROD16) */
