@@ -48,6 +48,7 @@
 
 #include "f5_batch.cuh"
 #include "f5_block.cuh"
+#include "f5_bprep.cuh"
 #include "f5_gemv_core.cuh"
 #include "f5_tc.cuh"
 
@@ -345,48 +346,9 @@ __global__ void __launch_bounds__(BP_THREADS) k_bprep(const __grid_constant__ Bp
   __shared__ long long red[32];
   __shared__ long long s_r;
   __shared__ int s_meta[4];
-  uint2 *xs = reinterpret_cast<uint2 *>(bp_dyn);
-  const int b = blockIdx.y, tid = threadIdx.x;
-  const int nblk = pa.K >> 3;
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  if (pa.pro.mode == PRO_X8) {
-    const int8_t *x8 = pa.x8_in + (size_t)b * pa.K;
-    for (int bb = tid; bb < nblk; bb += BP_THREADS) {
-      const uint2 v = *reinterpret_cast<const uint2 *>(x8 + 8 * bb);
-      xs[(((bb >> 7) << 2) + (bb & 3)) * 32 + ((bb >> 2) & 31)] =
-          make_uint2(__byte_perm(v.x, v.y, 0x6420), __byte_perm(v.x, v.y, 0x7531));
-    }
-    if (tid == 0) {
-      s_meta[0] = pa.xmeta_in ? pa.xmeta_in[2 * b] : 0;
-      s_meta[1] = pa.xmeta_in ? pa.xmeta_in[2 * b + 1] : 0;
-    }
-  } else {
-    GemvArgs ga;
-    ga.K = pa.K;
-    ga.err = pa.err;
-    ga.abort_flag = nullptr;
-    ga.pro = pa.pro;
-    ga.pro.tag_op1 = 0;
-    ga.pro.src = static_cast<const uint8_t *>(pa.pro.src) + b * pa.src_bs;
-    if (pa.pro.src2) ga.pro.src2 = static_cast<const uint8_t *>(pa.pro.src2) + b * pa.src2_bs;
-    if (pa.pro.dbg) ga.pro.dbg = pa.pro.dbg + b;
-    ga.pro.xq_out.x8 = pa.x8 ? pa.x8 + (size_t)b * pa.K : nullptr;   // stored by blockIdx.x == 0
-    ga.pro.xq_out.meta = pa.x8 ? pa.xmeta + 2 * b : nullptr;
-    prologue<MAXB>(BlockSync(), ga, xs, red, &s_r, s_meta);
-  }
-  __syncthreads();
-  if (tid == 0) {
-    pa.xmeta[2 * b] = s_meta[0];
-    pa.xmeta[2 * b + 1] = s_meta[1];
-  }
-  // 8-element block bb = bytes [8bb, 8bb+8) of the permuted row: group bb/16,
-  // 16-byte chunk (bb%16)/2 of the group's 128-byte swizzled row b
-  for (int bb = tid; bb < nblk; bb += BP_THREADS) {
-    const uint2 v = xs[(((bb >> 7) << 2) + (bb & 3)) * 32 + ((bb >> 2) & 31)];
-    const int g = bb >> 4;
-    *reinterpret_cast<uint2 *>(pa.xt + (size_t)g * pa.Bp * 128 + sw128_off(b, (bb & 15) * 8)) = v;
-  }
+  bprep_seq<MAXB>(BlockSync(), pa, blockIdx.y, reinterpret_cast<uint2 *>(bp_dyn), red, &s_r, s_meta);
 }
 
 // ---------------------------------------------------------------------------
@@ -400,30 +362,31 @@ __global__ void __launch_bounds__(BE_THREADS) k_bepi(const __grid_constant__ Bep
   const int b = blockIdx.y;
   const int u = blockIdx.x * BE_THREADS + threadIdx.x;
   const GemvArgs &a = ea.g;
-  if (u >= a.total_units) return;
-  const int si = seg_of(a, u);
-  const BepiSeg &bs = ea.bs[si];
-  GemvSeg sg = a.seg[si];
-  const int row = u - sg.unit_begin;
-  const size_t pstride = (size_t)ea.Bp * ea.ptot;
-  const int64_t *pb = ea.p + (size_t)b * ea.ptot;
-  long long p = 0, pu = 0;
-  for (int s = 0; s < ea.S; ++s) p += pb[s * pstride + bs.p_row0 + row];
-  const int e_x = ea.xmeta[2 * b], in_f = ea.xmeta[2 * b + 1];
-  if (sg.out) sg.out = static_cast<uint8_t *>(sg.out) + b * bs.out_bs;
-  if (sg.aux_out) sg.aux_out = static_cast<uint8_t *>(sg.aux_out) + b * bs.aux_bs;
-  if (sg.p_out) sg.p_out = reinterpret_cast<int64_t *>(reinterpret_cast<uint8_t *>(sg.p_out) + b * bs.pout_bs);
-  if (sg.mode == GM_SILU_MUL) {
-    for (int s = 0; s < ea.S; ++s) pu += pb[s * pstride + bs.p_row0_up + row];
-    epilogue_pair(a, sg, row, p << 4, pu << 4, e_x, in_f);
-    return;
+  if (u < a.total_units) {
+    const int si = seg_of(a, u);
+    const BepiSeg &bs = ea.bs[si];
+    GemvSeg sg = a.seg[si];
+    const int row = u - sg.unit_begin;
+    const size_t pstride = (size_t)ea.Bp * ea.ptot;
+    const int64_t *pb = ea.p + (size_t)b * ea.ptot;
+    long long p = 0, pu = 0;
+    for (int s = 0; s < ea.S; ++s) p += pb[s * pstride + bs.p_row0 + row];
+    const int e_x = ea.xmeta[2 * b], in_f = ea.xmeta[2 * b + 1];
+    if (sg.out) sg.out = static_cast<uint8_t *>(sg.out) + b * bs.out_bs;
+    if (sg.aux_out) sg.aux_out = static_cast<uint8_t *>(sg.aux_out) + b * bs.aux_bs;
+    if (sg.p_out) sg.p_out = reinterpret_cast<int64_t *>(reinterpret_cast<uint8_t *>(sg.p_out) + b * bs.pout_bs);
+    if (sg.mode == GM_SILU_MUL) {
+      for (int s = 0; s < ea.S; ++s) pu += pb[s * pstride + bs.p_row0_up + row];
+      epilogue_pair(a, sg, row, p << 4, pu << 4, e_x, in_f);
+    } else {
+      if (sg.mode == GM_CONV) {
+        sg.aux0 = static_cast<uint8_t *>(sg.aux0) + b * bs.ring_bs;
+        sg.T = &ea.params[b].T;
+      }
+      unsigned long long best = 0;
+      epilogue_row(a, sg, row, p << 4, e_x, in_f, best);
+    }
   }
-  if (sg.mode == GM_CONV) {
-    sg.aux0 = static_cast<uint8_t *>(sg.aux0) + b * bs.ring_bs;
-    sg.T = &ea.params[b].T;
-  }
-  unsigned long long best = 0;
-  epilogue_row(a, sg, row, p << 4, e_x, in_f, best);
 }
 
 // ---------------------------------------------------------------------------
