@@ -45,10 +45,13 @@ F5_DEV int bitlen(uint64_t v) { return v ? 64 - __clzll((long long)v) : 0; }
 F5_DEV uint64_t uabs(int64_t v) { return v < 0 ? (uint64_t)(-v) : (uint64_t)v; }
 
 // ref/fixedpoint.py:24-33 dyn_quant_i8: smallest e with (m + (1<<e>>1)) >> e <= 127
+// the smallest e with (m + (1 << e >> 1)) >> e <= 127: for m > 127 it is
+// e0 = bitlen(m) - 7 (m >> e0 in [64, 127]) or e0 + 1 when the rounding
+// carries past 127; e0 - 1 never suffices (m >> (e0 - 1) >= 128)
 F5_DEV int dynq8_e(uint64_t m) {
-  int e = 0;
-  while (((m + ((1ull << e) >> 1)) >> e) > 127ull) ++e;
-  return e;
+  if (m <= 127ull) return 0;
+  const int e0 = 64 - __clzll((long long)m) - 7;
+  return e0 + (((m + (1ull << (e0 - 1))) >> e0) > 127ull ? 1 : 0);
 }
 F5_DEV int32_t dynq8_apply(int64_t x, int e) { return (int32_t)clip(e ? rshr(x, e) : x, -127, 127); }
 // dynq8_apply for |x| < 2^30 in 32-bit arithmetic: sign(x) * min((|x| +
