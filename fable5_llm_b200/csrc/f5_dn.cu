@@ -2,8 +2,8 @@
 // ref/layer_fixed.py:1493-1580 deltanet_decode_fx between the in-projection
 // GEMV (qkv16 / z16 / b / a) and the out-projection GEMV.
 //
-// One CTA per value head h (32 CTAs x 128 threads; thread t owns state
-// column dv = t).  The in-projection GEMV's epilogues already applied
+// One CTA per value head h (32 CTAs per sequence; 128 * NQ threads, thread
+// t owns state column dv = t & 127).  The in-projection GEMV's epilogues already applied
 // conv4 + SiLU per channel (the conv window is a 4-slot ring in HBM: slot T%4
 // receives this step's input, the other three, oldest first, are the
 // reference's conv state) and the gates beta / decay.  Per CTA:
@@ -20,15 +20,20 @@
 
 namespace f5 {
 
-constexpr int DN_THREADS = 128;
-
+// One CTA of 128 * NQ threads per (value head, sequence): thread t owns
+// state column t & 127 and the key rows of quarter t >> 7 (NQ = 1: all 128).
+// Launched with NQ = 2: at 8 and 64 sequences, NQ = 1 and 2 measured the
+// same and NQ = 4 was slower at 64.
+//
 // The per-sequence arguments of a batched launch are built member by member
 // (no copy of a0 is modified): with nvcc 12.9 for sm_100a, advancing the
 // first member of a local copy of the argument struct did not reach later
 // reads of it.
-__global__ void __launch_bounds__(DN_THREADS) k_dn_step(const __grid_constant__ DnArgs a0, const DnBatch bs) {
+template <int NQ>
+__global__ void __launch_bounds__(128 * NQ) k_dn_step(const __grid_constant__ DnArgs a0, const DnBatch bs) {
   __shared__ __align__(128) int16_t s_sd[128 * 128];   // head state [dk][dv] -> decayed in place
-  __shared__ int32_t s_qn[128], s_kn[128];
+  __shared__ int4 s_kq[128];
+  __shared__ long long s_part[NQ > 1 ? NQ * 128 : 1];
   __shared__ long long red[32];
   __shared__ long long s_gate[4];             // beta, decay, rq, rk
   __shared__ int s_e[2];
@@ -63,20 +68,20 @@ __global__ void __launch_bounds__(DN_THREADS) k_dn_step(const __grid_constant__ 
   }
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const DnSmem sm = {s_sd, s_qn, s_kn, nullptr, red, s_gate, s_e};
+  const DnSmem sm = {s_sd, s_kq, NQ > 1 ? s_part : nullptr, red, s_gate, s_e};
   const BlockSync sy;
   long long qkv[3], zn[2];
-  dn_head_pre<BlockSync, 1>(sy, a, h, sm, qkv, zn);
+  dn_head_pre<BlockSync, NQ>(sy, a, h, sm, qkv, zn);
   const bool got = mbar_wait(&bar_s, 0, 2000000000ull);
   if (sy.any(!got)) {
     // the state never arrived: flag it, leave S untouched, emit zeros (the
     // decision is block-uniform, so no thread is left at a barrier)
     if (t == 0) atomicOr(a.err, DERR_TIMEOUT);
-    a.on16[h * 128 + t] = 0;
+    if (t < 128) a.on16[h * 128 + t] = 0;
     if (!got) mbar_wait(&bar_s, 0, 2000000000ull);
     return;
   }
-  dn_head_rec<BlockSync, 1>(sy, a, h, sm, qkv, zn);
+  dn_head_rec<BlockSync, NQ>(sy, a, h, sm, qkv, zn);
 }
 
 cudaError_t launch_dn_step(const DnArgs &a, int nheads, cudaStream_t st, bool pdl) {
@@ -84,16 +89,19 @@ cudaError_t launch_dn_step(const DnArgs &a, int nheads, cudaStream_t st, bool pd
 }
 
 cudaError_t launch_dn_step_b(const DnArgs &a, const DnBatch &bs, int nheads, int B, cudaStream_t st, bool pdl) {
+  const int nq = 2;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nheads, B);
-  cfg.blockDim = dim3(DN_THREADS);
+  cfg.blockDim = dim3(128 * nq);
   cfg.stream = st;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, k_dn_step, a, bs);
+  if (nq == 4) return cudaLaunchKernelEx(&cfg, k_dn_step<4>, a, bs);
+  if (nq == 2) return cudaLaunchKernelEx(&cfg, k_dn_step<2>, a, bs);
+  return cudaLaunchKernelEx(&cfg, k_dn_step<1>, a, bs);
 }
 
 }  // namespace f5

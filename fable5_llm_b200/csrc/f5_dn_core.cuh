@@ -20,7 +20,7 @@ F5_DEV int sidx(int dk, int dv) { return ((dv >> 5) << 12) | (dk << 5) | (dv & 3
 
 struct DnSmem {
   int16_t *sd;      // [128*128] head state, sidx layout (decayed in place)
-  int32_t *qn, *kn; // [128]
+  int4 *kq;         // [128] per key row dk: kn, |kn|, sign(kn) (0 / -1), qn
   long long *part;  // [NQ*128] partial sums of the split recurrence
   long long *red;   // [32]
   long long *gate;  // [4] beta, decay, rq, rk
@@ -64,8 +64,9 @@ F5_DEV void dn_head_pre(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, 
   sy.sync();
   if (q == 0) {
     const long long qn = clip16(rshr(qkv[0] * sm.gate[2], QKV_F + 30 - sm.e[0] - NRM_F));
-    sm.qn[dv] = (int32_t)rshr(qn * 2896, 15);    // round(2^15 / sqrt(128)) = 2896
-    sm.kn[dv] = (int32_t)clip16(rshr(qkv[1] * sm.gate[3], QKV_F + 30 - sm.e[1] - NRM_F));
+    const int32_t kn = clip16(rshr(qkv[1] * sm.gate[3], QKV_F + 30 - sm.e[1] - NRM_F));
+    sm.kq[dv] = make_int4(kn, kn < 0 ? -kn : kn, kn >> 31,
+                          (int32_t)rshr(qn * 2896, 15));    // round(2^15 / sqrt(128)) = 2896
   }
   sy.sync();
 }
@@ -84,7 +85,7 @@ F5_DEV void dn_head_rec(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, 
   for (int dk = q * RQ; dk < (q + 1) * RQ; ++dk) {
     const int sd = rshr32p((int32_t)sm.sd[sidx(dk, dv)] * decay, GAT_F);   // |S*decay| < 2^30
     sm.sd[sidx(dk, dv)] = (int16_t)sd;
-    kvm += (long long)sd * sm.kn[dk];
+    kvm += (long long)sd * sm.kq[dk].x;
   }
   if (NQ > 1) {
     sm.part[q * 128 + dv] = kvm;
@@ -107,13 +108,40 @@ F5_DEV void dn_head_rec(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, 
   }
   long long o = 0;
   int sat = 0;
+  const unsigned long long dabs = uabs(delta);
+  if (dabs < (1ull << 24)) {
+    // |delta| < 2^24 (always, for beta <= 2^15): the rank-1 term in 32-bit
+    // integers.  rshr(kn * delta, NRM_F) = sign(kn * delta) *
+    // floor((|kn| |delta| + 2^(NRM_F-1)) / 2^NRM_F), and with |delta| =
+    // dh 2^NRM_F + dl that floor is |kn| dh + ((|kn| dl + 2^(NRM_F-1)) >> NRM_F).
+    const int32_t dh = (int32_t)(dabs >> NRM_F), dl = (int32_t)(dabs & ((1u << NRM_F) - 1));
+    const int32_t sdl = delta < 0 ? -1 : 0;
+#pragma unroll
+    for (int c0 = q * RQ; c0 < (q + 1) * RQ; c0 += 16) {
+      int32_t oc = 0;   // 16 terms of |sn * qn| <= 2^15 * 2896 stay below 2^31
+#pragma unroll
+      for (int dk = c0; dk < c0 + 16; ++dk) {
+        const int4 kq = sm.kq[dk];
+        const int32_t sg = kq.z ^ sdl;
+        const int32_t r = kq.y * dh + ((kq.y * dl + (1 << (NRM_F - 1))) >> NRM_F);
+        int32_t sn = (int32_t)sm.sd[sidx(dk, dv)] + ((r ^ sg) - sg);
+        sat += (uint32_t)(sn + 32767) > 65534u;   // |Sh| > 32767 (ref/layer_fixed.py:1557)
+        sn = min(max(sn, -32768), 32767);
+        S[sidx(dk, dv)] = (int16_t)sn;
+        oc += sn * kq.w;
+      }
+      o += oc;
+    }
+  } else {
 #pragma unroll 8
-  for (int dk = q * RQ; dk < (q + 1) * RQ; ++dk) {
-    long long sn = (long long)sm.sd[sidx(dk, dv)] + rshr((long long)sm.kn[dk] * delta, NRM_F);
-    if (sn > 32767 || sn < -32767) ++sat;   // |Sh| > 32767 (ref/layer_fixed.py:1557)
-    sn = clip16(sn);
-    S[sidx(dk, dv)] = (int16_t)sn;
-    o += sn * sm.qn[dk];
+    for (int dk = q * RQ; dk < (q + 1) * RQ; ++dk) {
+      const int4 kq = sm.kq[dk];
+      long long sn = (long long)sm.sd[sidx(dk, dv)] + rshr((long long)kq.x * delta, NRM_F);
+      if (sn > 32767 || sn < -32767) ++sat;   // |Sh| > 32767 (ref/layer_fixed.py:1557)
+      sn = clip16(sn);
+      S[sidx(dk, dv)] = (int16_t)sn;
+      o += sn * kq.w;
+    }
   }
   if (a.stats && sat) atomicAdd(a.stats, (unsigned long long)sat);
   if (NQ > 1) {
