@@ -29,8 +29,9 @@
 //
 // Warp roles (one CTA per SM): warp 0 streams the stages,
 // warp 1 allocates tensor memory and issues the MMAs (one thread: 4
-// tcgen05.mma kind::i8 M=128 N=Bp K=32 per group into one of up to 8
-// accumulators, tcgen05.commit to mbarriers), warps 2-5 unpack, Bp / 4
+// tcgen05.mma kind::i8 M=128 N=Bp K=32 per group, A from one of 2-4 A
+// buffers into one of up to 4 accumulator buffers, tcgen05.commit to
+// mbarriers), warps 2-5 unpack, Bp / 4
 // fold warps from warp 6 read each group's accumulator back (lane quarter =
 // warp % 4, 16-column block = (warp - 6) / 4) and fold m_g * acc_g into
 // int64 registers.
@@ -54,10 +55,12 @@
 
 namespace f5 {
 
+constexpr int BG_MMAW = 1;         // MMA warp 1 (one issuing thread)
 constexpr int BG_UNPACK = 4;       // unpack warps 2-5 (one per TMEM lane quarter)
+constexpr int BG_U0 = 1 + BG_MMAW, BG_F0 = BG_U0 + BG_UNPACK;   // first unpack / fold warp
 constexpr int BG_FOLDQ = 16;       // accumulator columns per fold thread: Bp / 16 fold warps per lane quarter
 constexpr int bg_fold_warps(int Bp) { return 4 * (Bp / BG_FOLDQ); }
-constexpr int bg_threads(int Bp) { return 32 * (2 + BG_UNPACK + bg_fold_warps(Bp)); }
+constexpr int bg_threads(int Bp) { return 32 * (BG_F0 + bg_fold_warps(Bp)); }
 constexpr int BG_MAX_NS = 6;       // pipeline stages at most
 constexpr int BG_WBYTES = BG_TILE * 64 * BG_GPS;   // packed weights per stage (32 KB: two 16 KB boxes)
 constexpr int BG_SMEM_MAX = 232448 - 4096;
@@ -77,12 +80,22 @@ __global__ void __launch_bounds__(bg_threads(BP), 1) k_bgemm(const __grid_consta
   constexpr int BG_FOLD = bg_fold_warps(BP);
   constexpr int XBYTES = BP * 128 * BG_GPS;
   constexpr int STAGE = BG_WBYTES + XBYTES;
-  // tensor memory: NP pair slots of [A of 2 groups: 64 columns | 2 accumulators: 2 x BP]
-  constexpr int SLOT = 64 + 2 * BP;
-  constexpr int NP = 512 / SLOT > 4 ? 4 : 512 / SLOT;
-  static_assert(NP >= 2, "two pair slots at least");
+  // tensor memory: NA A buffers of a group pair (64 columns each) at column
+  // 0, then ND accumulator buffers of a pair (2 x BP columns each).  A and
+  // accumulator buffers recycle independently: the unpack reuses an A buffer
+  // once the MMAs that read it completed, the MMA reuses an accumulator
+  // buffer once the fold read it back.
+  constexpr int NA = BP <= 16 ? 4 : (BP <= 32 ? 3 : 2);
+  constexpr int DCOL = 2 * BP;
+  constexpr int ND = (512 - 64 * NA) / DCOL > 4 ? 4 : (512 - 64 * NA) / DCOL;
+  // NA == ND (Bp = 16): the unpack waits until the fold read back pair
+  // pc - NA, which frees both its A and its accumulators, and the MMA thread
+  // (the bottleneck at small N) waits only for A.  NA < ND: the unpack waits
+  // for the MMAs of pc - NA, the MMA thread for the fold of pc - ND.
+  constexpr bool COUPLED = NA == ND;
+  static_assert(ND >= 2 && NA <= ND, "two accumulator buffers at least, no more A buffers than accumulators");
   extern __shared__ uint8_t bg_dyn[];
-  __shared__ __align__(8) uint64_t full[BG_MAX_NS], empty[BG_MAX_NS], afull[4], done[4], tfree[4];
+  __shared__ __align__(8) uint64_t full[BG_MAX_NS], empty[BG_MAX_NS], afull[NA], done[4], tfree[4];
   __shared__ __align__(8) uint64_t drain;
   __shared__ uint32_t s_tmem;
   __shared__ volatile int s_abort;
@@ -100,14 +113,14 @@ __global__ void __launch_bounds__(bg_threads(BP), 1) k_bgemm(const __grid_consta
   if (tid == 0) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], BG_UNPACK + 1);   // every unpack warp + the MMA commit
+      mbar_init(&empty[i], BG_UNPACK + BG_MMAW);   // every unpack warp + every MMA warp's commit
     }
-    for (int i = 0; i < NP; ++i) {
-      mbar_init(&afull[i], BG_UNPACK);   // both groups' A written
+    for (int i = 0; i < NA; ++i) mbar_init(&afull[i], BG_UNPACK);   // both groups' A written
+    for (int i = 0; i < ND; ++i) {
       mbar_init(&done[i], 1);            // both groups' MMAs complete (commit)
       mbar_init(&tfree[i], BG_FOLD);     // both accumulators read back
     }
-    mbar_init(&drain, 1);
+    mbar_init(&drain, BG_MMAW);
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -157,45 +170,44 @@ __global__ void __launch_bounds__(bg_threads(BP), 1) k_bgemm(const __grid_consta
     if (lane == 0) {
       const uint32_t idesc = idesc_s8s8(BG_TILE, BP);
       int sc = 0, pc = 0;
-      bool issued = false;
       for (int u = blockIdx.x; u < units && !s_abort; u += gridDim.x) {
         for (int st = 0; st < spu && !s_abort; ++st, ++sc) {
           const int s = sc % NS;
           if (!mbar_wait(&full[s], (sc / NS) & 1, BG_WAIT_NS)) { s_abort = 1; atomicOr(a.err, DERR_TIMEOUT); break; }
           const uint64_t bd0 = sw128_desc(smem_u32(stg + (size_t)s * STAGE + BG_WBYTES));
           for (int pi = 0; pi < BG_GPS / 2; ++pi, ++pc) {
-            const int j = pc % NP;
-            // afull implies the unpack saw this slot's accumulators freed by the fold
-            if (!mbar_wait(&afull[j], (pc / NP) & 1, BG_WAIT_NS)) {
+            const int ja = pc % NA, jd = pc % ND;
+            // afull implies the unpack saw this A buffer's previous MMAs complete
+            if (!mbar_wait(&afull[ja], (pc / NA) & 1, BG_WAIT_NS) ||
+                (!COUPLED && pc >= ND && !mbar_wait(&tfree[jd], ((pc / ND) - 1) & 1, BG_WAIT_NS))) {
               s_abort = 1;
               atomicOr(a.err, DERR_TIMEOUT);
               break;
             }
             tc_fence_after();
-            const uint32_t base = tmem + (uint32_t)(j * SLOT);
+            const uint32_t abase = tmem + (uint32_t)(64 * ja), dbase = tmem + (uint32_t)(64 * NA + jd * DCOL);
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
               const uint64_t bd = bd0 + (uint64_t)(((2 * pi + e) * BP * 128) >> 4);
 #pragma unroll
               for (int k = 0; k < 4; ++k)
-                tc_mma_i8_ts(base + 64 + (uint32_t)(e * BP), base + (uint32_t)(32 * e + 8 * k), bd + 2 * k, idesc,
+                tc_mma_i8_ts(dbase + (uint32_t)(e * BP), abase + (uint32_t)(32 * e + 8 * k), bd + 2 * k, idesc,
                              k > 0);
             }
-            issued = true;
             if (tr && pc < 2048) a.trace[4096 + pc] = gtimer();
-            tc_commit(&done[j]);
+            tc_commit(&done[jd]);
           }
           tc_commit(&empty[s]);
         }
       }
-      if (issued) {
-        tc_commit(&drain);
-        mbar_wait(&drain, 0, BG_WAIT_NS);
-      }
+      // a commit with no MMA before it arrives at once: the drain completes
+      // when every issued MMA has
+      tc_commit(&drain);
+      mbar_wait(&drain, 0, BG_WAIT_NS);
     }
     __syncwarp();
-  } else if (warp < 2 + BG_UNPACK) {
-    // ---------------- unpack (warps 2-5, one per TMEM lane quarter): thread = row ----------------
+  } else if (warp < BG_F0) {
+    // ---------------- unpack (warps 5-8, one per TMEM lane quarter): thread = row ----------------
     // Row r's packed group gi is 64 bytes = 16-byte chunks 4 (gi & 1) + c of
     // the 128-byte swizzled row r of box gi / 2 (chunk j at j ^ (r & 7)):
     // eight consecutive rows read eight different bank groups.  Nibbles
@@ -212,7 +224,7 @@ __global__ void __launch_bounds__(bg_threads(BP), 1) k_bgemm(const __grid_consta
         const int s = sc % NS;
         if (lane == 0) ok = mbar_wait(&full[s], (sc / NS) & 1, BG_WAIT_NS);
         ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (tr && tid == 64 && sc < 1024) a.trace[1024 + sc] = gtimer();
+        if (tr && tid == 32 * BG_U0 && sc < 1024) a.trace[1024 + sc] = gtimer();
         if (!ok || s_abort) {
           if (lane == 0 && !ok) { s_abort = 1; atomicOr(a.err, DERR_TIMEOUT); }
           ok = false;
@@ -220,9 +232,12 @@ __global__ void __launch_bounds__(bg_threads(BP), 1) k_bgemm(const __grid_consta
         }
         const uint8_t *src = stg + (size_t)s * STAGE + r * 128;
         for (int pi = 0; pi < BG_GPS / 2; ++pi, ++pc) {
-          const int j = pc % NP;
-          if (pc >= NP) {   // the slot's previous pair fully read back by the fold
-            if (lane == 0) ok = mbar_wait(&tfree[j], ((pc / NP) - 1) & 1, BG_WAIT_NS);
+          const int j = pc % NA;
+          if (pc >= NA) {   // this A buffer's previous pair (pc - NA): its MMAs completed (or, coupled,
+            // its accumulators read back); NA <= ND, so the barrier cannot be a phase further on
+            if (lane == 0)
+              ok = mbar_wait(COUPLED ? &tfree[(pc - NA) % ND] : &done[(pc - NA) % ND], ((pc - NA) / ND) & 1,
+                             BG_WAIT_NS);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) {
               if (lane == 0) { s_abort = 1; atomicOr(a.err, DERR_TIMEOUT); }
@@ -245,13 +260,13 @@ __global__ void __launch_bounds__(bg_threads(BP), 1) k_bgemm(const __grid_consta
                 o[8 * c + 2 * k + 1] = wv[k] & 0xF0F0F0F0u;
               }
             }
-            tc_st32(tq + (uint32_t)(j * SLOT + 32 * e), o);
+            tc_st32(tq + (uint32_t)(64 * j + 32 * e), o);
           }
           tc_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&afull[j]);
-          if (tr && tid == 64 && pc < 2048) a.trace[2048 + pc] = gtimer();
+          if (tr && tid == 32 * BG_U0 && pc < 2048) a.trace[2048 + pc] = gtimer();
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);   // the stage's packed bytes are consumed
@@ -262,9 +277,9 @@ __global__ void __launch_bounds__(bg_threads(BP), 1) k_bgemm(const __grid_consta
     // ---------------- accumulator fold (warps 6-21) ----------------
     // warp w reads TMEM lane quarter w % 4 (rows 32 (w % 4) + lane) and the
     // 16-column block cq = (w - 6) / 4 of both accumulators of a pair slot
-    const int q = warp & 3, cq = (warp - 2 - BG_UNPACK) >> 2;
+    const int q = warp & 3, cq = (warp - BG_F0) >> 2;
     const int rt = 32 * q + lane;                              // row within the tile
-    const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16) + 64 + (uint32_t)(cq * BPQ);
+    const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16) + 64 * NA + (uint32_t)(cq * BPQ);
     int pc = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok && !s_abort; u += gridDim.x) {
@@ -287,26 +302,26 @@ __global__ void __launch_bounds__(bg_threads(BP), 1) k_bgemm(const __grid_consta
         }
         const uint32_t mw = (gi & 6) == 0 ? mv.x : ((gi & 6) == 2 ? mv.y : ((gi & 6) == 4 ? mv.z : mv.w));
         const int32_t m0 = (int32_t)(mw & 0xFFFFu), m1 = (int32_t)(mw >> 16);
-        const int j = pc % NP;
-        if (lane == 0) ok = mbar_wait(&done[j], (pc / NP) & 1, BG_WAIT_NS);
+        const int j = pc % ND;
+        if (lane == 0) ok = mbar_wait(&done[j], (pc / ND) & 1, BG_WAIT_NS);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok || s_abort) {
           if (lane == 0 && !ok) { s_abort = 1; atomicOr(a.err, DERR_TIMEOUT); }
           ok = false;
           break;
         }
-        if (tr && warp == 2 + BG_UNPACK && lane == 0 && pc < 2048) a.trace[6144 + pc] = gtimer();
+        if (tr && warp == BG_F0 && lane == 0 && pc < 2048) a.trace[6144 + pc] = gtimer();
         tc_fence_after();
         int32_t d0[BPQ], d1[BPQ];
-        tc_ld<BPQ>(tl + (uint32_t)(j * SLOT), d0);
-        tc_ld<BPQ>(tl + (uint32_t)(j * SLOT + BP), d1);
+        tc_ld<BPQ>(tl + (uint32_t)(j * DCOL), d0);
+        tc_ld<BPQ>(tl + (uint32_t)(j * DCOL + BP), d1);
         tc_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tfree[j]);
 #pragma unroll
         for (int jj = 0; jj < BPQ; ++jj) acc[jj] += (long long)m0 * d0[jj] + (long long)m1 * d1[jj];   // 16 p
-        if (tr && warp == 2 + BG_UNPACK && lane == 0 && pc < 2048) a.trace[8192 + pc] = gtimer();
+        if (tr && warp == BG_F0 && lane == 0 && pc < 2048) a.trace[8192 + pc] = gtimer();
       }
       if (!ok) break;
       if (sg.argmax) {
