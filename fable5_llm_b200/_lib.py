@@ -29,6 +29,13 @@ class F5Error(RuntimeError):
         self.status = status
 
 
+class TopK32(ctypes.Structure):
+    """f5_topk32 (include/f5b200.h)."""
+    _fields_ = [("val", ctypes.c_int32 * 32), ("idx", ctypes.c_int32 * 32), ("count", ctypes.c_int32),
+                ("ovf_lit", ctypes.c_int32), ("ovf_disp", ctypes.c_int32), ("amax_idx", ctypes.c_int32),
+                ("amax_val", ctypes.c_int32), ("e_x", ctypes.c_int32), ("n", ctypes.c_int32)]
+
+
 class GemvSeg(ctypes.Structure):
     _fields_ = [("w", c_vp), ("w2", c_vp), ("out", c_vp), ("p_out", c_vp),
                 ("rows", c_int), ("e", c_int), ("e2", c_int), ("out_f", c_int),
@@ -78,6 +85,10 @@ SIGNATURES = [
     ("f5_ctx_set_position", c_int, [c_vp, c_int, c_int]),
     ("f5_ctx_get_position", c_int, [c_vp, c_vp, c_vp]),
     ("f5_ctx_set_logits", c_int, [c_vp, c_int]),
+    ("f5_topk32_ws_bytes", c_size, [c_ll]),
+    ("f5_topk32_dev", c_int, [c_vp, c_ll, c_vp, c_vp, c_vp]),
+    ("f5_topk32_host", c_int, [c_vp, c_ll, c_vp]),
+    ("f5_ctx_topk", c_int, [c_vp, c_vp]),
     ("f5_ctx_stream", c_int, [c_vp, c_vp]),
     ("f5_ctx_prepare", c_int, [c_vp]),
     ("f5_ctx_set_engine", c_int, [c_vp, c_int]),

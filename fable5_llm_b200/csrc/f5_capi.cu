@@ -6,6 +6,7 @@
 #include "../../include/f5b200.h"
 #include "f5_capi_util.h"
 #include "f5_kernels.cuh"
+#include "f5_topk.cuh"
 
 namespace f5 {
 cudaError_t launch_synth_w4(uint8_t *, long long, int, int, long long, uint64_t, uint64_t, int,
@@ -227,6 +228,43 @@ done:
   return rc;
 }
 
+
+// ---------------------------------------------------------------------------
+// TOPK-32 capture
+// ---------------------------------------------------------------------------
+size_t f5_topk32_ws_bytes(long long n) { return f5::topk32_ws_bytes(n); }
+
+int f5_topk32_dev(const int32_t *vals, long long n, void *ws, f5_topk32 *out, void *stream) {
+  if (n < 0 || n > 0x7FFFFFFFll) return set_error(F5_EINVAL, "f5_topk32_dev: n=%lld outside [0, 2^31)", n);
+  if ((n > 0 && !vals) || !ws || !out) return set_error(F5_EINVAL, "f5_topk32_dev: null pointer");
+  return cuda_status(f5::launch_topk32(vals, n, ws, out, nullptr, (cudaStream_t)stream), "f5_topk32_dev");
+}
+
+int f5_topk32_host(const int32_t *vals, long long n, f5_topk32 *out) {
+  if (n < 0 || n > 0x7FFFFFFFll) return set_error(F5_EINVAL, "f5_topk32_host: n=%lld outside [0, 2^31)", n);
+  if ((n > 0 && !vals) || !out) return set_error(F5_EINVAL, "f5_topk32_host: null pointer");
+  int32_t *d_v = nullptr;
+  void *d_ws = nullptr;
+  f5_topk32 *d_out = nullptr;
+  cudaError_t e = cudaSuccess;
+#define F5_TRY(x)                          \
+  do {                                     \
+    e = (x);                               \
+    if (e != cudaSuccess) goto done;       \
+  } while (0)
+  F5_TRY(cudaMalloc(&d_v, sizeof(int32_t) * (size_t)(n > 0 ? n : 1)));
+  F5_TRY(cudaMalloc(&d_ws, f5::topk32_ws_bytes(n)));
+  F5_TRY(cudaMalloc(&d_out, sizeof(f5_topk32)));
+  if (n > 0) F5_TRY(cudaMemcpy(d_v, vals, sizeof(int32_t) * (size_t)n, cudaMemcpyHostToDevice));
+  F5_TRY(f5::launch_topk32(d_v, n, d_ws, d_out, nullptr, 0));
+  F5_TRY(cudaMemcpy(out, d_out, sizeof(f5_topk32), cudaMemcpyDeviceToHost));
+done:
+#undef F5_TRY
+  cudaFree(d_v);
+  cudaFree(d_ws);
+  cudaFree(d_out);
+  return e == cudaSuccess ? F5_OK : cuda_status(e, "f5_topk32_host");
+}
 }  // extern "C"
 
 // ---------------------------------------------------------------------------

@@ -25,6 +25,8 @@
 #include "f5_int.cuh"
 #include "f5_kernels.cuh"
 #include "f5_mega.cuh"
+#include "f5_batch.cuh"
+#include "f5_topk.cuh"
 
 namespace f5 {
 cudaError_t launch_synth_w4(uint8_t *, long long, int, int, long long, uint64_t, uint64_t, int, cudaStream_t);
@@ -930,6 +932,44 @@ int f5_ctx_set_logits(f5_ctx *c, int on) {
     c->want_logits = on != 0;
     c->graph_dirty = c->mega_dirty = true;
   }
+  return F5_OK;
+}
+
+int f5_ctx_topk(f5_ctx *c, f5_topk32 *out) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  if (!out) return set_error(F5_EINVAL, "f5_ctx_topk: null out");
+  if (!c->logits || !c->want_logits)
+    return set_error(F5_ESTATE, "f5_ctx_topk: logits not stored (f5_ctx_set_logits(ctx, 1) before the step)");
+  if (c->cfg.world_size > 1) return set_error(F5_ESTATE, "f5_ctx_topk: single-GPU contexts only");
+  if (!c->ln_f) return set_error(F5_ESTATE, "f5_ctx_topk: final norm not uploaded");
+  DevGuard dg(c->device);
+  const int vocab = c->cfg.vocab;
+  if (!c->tk_ws) {
+    F5_ALLOC(c, c->tk_ws, f5::topk32_ws_bytes(vocab));
+    F5_ALLOC(c, c->tk_out, sizeof(f5_topk32));
+    F5_ALLOC(c, c->tk_xt, (size_t)(H / 128) * 16 * 128);
+    F5_ALLOC(c, c->tk_xmeta, 16 * 2 * sizeof(int));
+  }
+  // e_x: the head's prologue (rmsnorm_fx(x, ln_f, RS_F, one_plus=0) then
+  // DYNQ8, ref/fidelity_check.py:442-446) over the final residual
+  f5::BprepArgs pa = {};
+  pa.pro.mode = PRO_RMSNORM;
+  pa.pro.src = c->x16;
+  pa.pro.w = c->ln_f;
+  pa.pro.in_f = RS_F;
+  pa.pro.one_plus = 0;
+  pa.K = H;
+  pa.NG = H / 128;
+  pa.B = 1;
+  pa.Bp = 16;
+  pa.xmeta = c->tk_xmeta;
+  pa.xt = c->tk_xt;
+  pa.err = c->err;
+  F5_CU(f5::launch_bprep(pa, c->st, false), "f5_ctx_topk prologue");
+  F5_CU(f5::launch_topk32(c->logits, vocab, c->tk_ws, c->tk_out, c->tk_xmeta, c->st), "f5_ctx_topk");
+  F5_CU(cudaMemcpyAsync(out, c->tk_out, sizeof(f5_topk32), cudaMemcpyDeviceToHost, c->st), "f5_ctx_topk");
+  F5_CU(cudaStreamSynchronize(c->st), "f5_ctx_topk");
   return F5_OK;
 }
 

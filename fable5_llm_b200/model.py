@@ -42,6 +42,7 @@ class DecodeModel:
         self.max_T = (int(max_T) + 15) & ~15      # the context rounds KV capacity to 16 rows
         self.norm_mode = norm_mode
         self.device = device
+        self.head_e_sh = None   # (e, sh) of the uploaded LM head
         self.lib = L.lib()
         types = "".join("A" if t == "full_attention" else "D" for t in self.geom.layer_types)
         self._types = types.encode()
@@ -70,6 +71,8 @@ class DecodeModel:
         img = np.ascontiguousarray(img, dtype=np.uint8)
         L.check(self.lib.f5_ctx_upload_matrix(self.h, layer, slot, _p(img), N, K, g, e, sh),
                 f"upload_matrix({layer},{slot})")
+        if layer == -1 and slot == L.S_HEAD:
+            self.head_e_sh = (int(e), int(sh))
 
     def upload_qmat(self, layer, slot, qm):
         """qm: the reference dict {"w4","m","e","sh","g"} or an object with
@@ -126,6 +129,8 @@ class DecodeModel:
                 self.h, s.layer, slot, s.N, s.K, s.g, s.e, s.sh,
                 synth.stream_key(seed, s.mid, synth.STREAM_W), synth.stream_key(seed, s.mid, synth.STREAM_M),
                 int(s.symmetric)), f"synth {s.name}@{s.layer}")
+            if s.name == "head":
+                self.head_e_sh = (int(s.e), int(s.sh))
         vec, ln_f = synth.vector_params(seed, g)
         for i, lt in enumerate(g.layer_types):
             p = vec[i]
@@ -267,6 +272,31 @@ class DecodeModel:
 
     def logits(self):
         return self.read(L.BUF_LOGITS)
+
+    # ---- TOPK-32 capture and sampling (sw/chat_seq.py:1776-1928) ----
+    def head_logit_exp0(self):
+        """Dequant exponent of the head at e_x = 0: e + sh - 15 - RS_F
+        (sw/chat_seq.py:355-357 head_logit_exp0 with this model's head)."""
+        if self.head_e_sh is None:
+            raise RuntimeError("head_logit_exp0: no LM head uploaded")
+        e, sh = self.head_e_sh
+        return e + sh - 15 - RS_F
+
+    def topk(self):
+        """The last step's TOPK-32 capture over the LM head's logits (needs
+        set_logits(True) before the step) -> sampling.TopK32Result."""
+        from .sampling import TopK32Result
+        r = L.TopK32()
+        L.check(self.lib.f5_ctx_topk(self.h, ctypes.byref(r)), "f5_ctx_topk")
+        return TopK32Result.from_struct(r)
+
+    def sample_step(self, tok, pos, sampler):
+        """One decode step whose next token is drawn by `sampler`
+        (sampling.Sampler, the reference's temperature / top-k / top-p
+        draw over the capture list) -> (token, info)."""
+        self.decode_step(tok, pos)
+        r = self.topk()
+        return sampler.pick(r.values, r.indices, r.e_x)
 
     # ---- reference-layout state I/O (ref/layer_fixed.py:1654-1666) ----
     def get_dn_state(self, layer, T):

@@ -241,6 +241,34 @@ int f5_ctx_stream(f5_ctx *ctx, void **stream);
 /* record the decode-step CUDA graph now (otherwise at the first step) */
 int f5_ctx_prepare(f5_ctx *ctx);
 
+/* TOPK-32 capture: the LM head's top-k unit (tb/scripts/gen_topk_cases.py:
+ * 20-45, numpy model `Ref.push` :75-102) whose list the sampler of
+ * sw/chat_seq.py:1776-1928 (`Sampler.pick(values, indices, e_x)`) consumes.
+ * Elements arrive in array order with index = position.  No reference C
+ * interface: the unit is RTL, read back through CSRs. */
+typedef struct f5_topk32 {
+  int32_t val[32];    /* value descending, ties by ascending index */
+  int32_t idx[32];    /* index of each entry; -1 past count */
+  int32_t count;      /* min(n, 32) */
+  int32_t ovf_lit;    /* sticky: a rejected element tied entry[31] */
+  int32_t ovf_disp;   /* sticky: ovf_lit, or a displaced element tied the new entry[31] */
+  int32_t amax_idx;   /* the AMAX32 winner (first max) = entry 0; 0 when n = 0 */
+  int32_t amax_val;
+  int32_t e_x;        /* f5_ctx_topk: DYNQ8 exponent of the head's input, else 0 */
+  int32_t n;          /* elements scanned */
+} f5_topk32;
+/* device scratch for f5_topk32_dev over n elements */
+size_t f5_topk32_ws_bytes(long long n);
+/* device pointers; out is device memory; runs on `stream` (cudaStream_t, NULL = default) */
+int f5_topk32_dev(const int32_t *vals, long long n, void *ws, f5_topk32 *out, void *stream);
+/* host pointers (allocates, copies, synchronises) */
+int f5_topk32_host(const int32_t *vals, long long n, f5_topk32 *out);
+/* the last step's TOPK-32 over the LM head's logits (needs
+ * f5_ctx_set_logits(ctx, 1) before the step) and the head input's DYNQ8
+ * exponent e_x (the sampler's dequant, sw/chat_seq.py:1842-1845), computed
+ * from the final residual; single-GPU contexts */
+int f5_ctx_topk(f5_ctx *ctx, f5_topk32 *out);
+
 /* Decode engines (no reference counterpart: the reference has one sequencer).
  * F5_ENGINE_PERSISTENT runs each step as ONE cooperative launch of the
  * persistent decode kernel (one CTA per SM, weights streamed continuously

@@ -1,0 +1,74 @@
+#!/usr/bin/env python3
+"""Generate ``topk_cases.npz`` from the UNMODIFIED reference's top-k case
+generator (``tb/scripts/gen_topk_cases.py``, the numpy reference of the
+RUNG-4 TOPK-32 block).
+
+Run in a container that has the reference checkout (default
+``/root/reference``; override with F5_REFERENCE); the GPU box never runs it.
+The reference script is run as a subprocess with a fixed seed and writes its
+own text format (``topk_cases.txt``: per case a header line ``name nwords
+ncmds count count ovf_lit ovf_disp am_idx am_val(hex) nelem``, the scratch
+words (16-bit hex, int32 elements as little-endian word pairs), the commands
+``srca len fresh`` (srca in words) and the expected list ``val(hex) idx``);
+this script converts that file to arrays.
+
+    python tests/golden/gen_topk_golden.py
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+import tempfile
+
+import numpy as np
+
+REF = os.environ.get("F5_REFERENCE", "/root/reference")
+HERE = os.path.dirname(os.path.abspath(__file__))
+SEED = 20261202
+
+
+def s32(h: str) -> int:
+    v = int(h, 16)
+    return v - (1 << 32) if v >= (1 << 31) else v
+
+
+def main():
+    script = os.path.join(REF, "tb", "scripts", "gen_topk_cases.py")
+    with tempfile.TemporaryDirectory() as td:
+        subprocess.run([sys.executable, script, td, str(SEED)], check=True,
+                       env=dict(os.environ, PYTHONDONTWRITEBYTECODE="1"))
+        lines = open(os.path.join(td, "topk_cases.txt")).read().split("\n")
+    pos = 0
+    ncase = int(lines[pos]); pos += 1
+    out = {"names": []}
+    for ci in range(ncase):
+        h = lines[pos].split(); pos += 1
+        name, nwords, ncmds, count = h[0], int(h[1]), int(h[2]), int(h[3])
+        ovf_lit, ovf_disp, am_idx, am_val, nelem = int(h[5]), int(h[6]), int(h[7]), s32(h[8]), int(h[9])
+        words = np.array([int(lines[pos + i], 16) for i in range(nwords)], dtype=np.int64); pos += nwords
+        elems = (words[0::2] | (words[1::2] << 16)).astype(np.uint32).astype(np.int32)
+        cmds = []
+        for _ in range(ncmds):
+            sa, ln, fr = (int(x) for x in lines[pos].split()); pos += 1
+            assert sa % 2 == 0
+            cmds.append((sa // 2, ln, fr))
+        val, idx = [], []
+        for _ in range(count):
+            v, i = lines[pos].split(); pos += 1
+            val.append(s32(v)); idx.append(int(i))
+        out["names"].append(name)
+        out[f"{ci}_elems"] = elems
+        out[f"{ci}_cmds"] = np.array(cmds, dtype=np.int64).reshape(-1, 3)
+        out[f"{ci}_val"] = np.array(val, dtype=np.int64)
+        out[f"{ci}_idx"] = np.array(idx, dtype=np.int64)
+        out[f"{ci}_meta"] = np.array([count, ovf_lit, ovf_disp, am_idx, am_val, nelem], dtype=np.int64)
+    out["names"] = np.array(out["names"])
+    out["seed"] = np.array([SEED])
+    path = os.path.join(HERE, "topk_cases.npz")
+    np.savez_compressed(path, **out)
+    print(f"wrote {path}: {ncase} cases")
+
+
+if __name__ == "__main__":
+    main()
