@@ -19,15 +19,17 @@
 //     own top-32 keys, sorted descending.  Every warp extracts the top 32 of
 //     its 256 elements (32 rounds of a warp max over 64-bit keys), then each
 //     of the 256 survivors is ranked against the others.
-//   k_topk_merge (one CTA): walks the chunks in order with the running list
-//     L in warp 0 (lane j holds entry j).  With theta = entry[31]'s value
-//     (L full), only elements with value >= theta can change L or a flag.
-//     If fewer than 32 of the chunk's top-32 reach theta, they are all of the
-//     chunk's such elements and are taken from the list (sorted back into
-//     arrival order); otherwise (and while L is not full) the chunk is read
-//     from memory, filtered against theta and compacted in arrival order.
-//     A chunk whose maximum is below theta is skipped.  The candidates are
-//     then inserted one by one exactly as the sequential unit does.
+//   k_topk_merge (one CTA): warp 0 holds the running list L (lane j =
+//     entry j), starting from the first 32 elements in key order (no flag
+//     can fire before the list is full), and walks the chunk lists alone.
+//     With theta = entry[31]'s value only elements with value >= theta can
+//     change L or a flag.  If fewer than 32 of a chunk's top-32 reach theta,
+//     those entries are all of the chunk's such elements: they are sorted
+//     back into arrival order and inserted one by one exactly as the
+//     sequential unit does (a chunk with none is skipped).  Otherwise the
+//     other seven warps, parked on a named barrier, join to scan the chunk in
+//     256-element sub-blocks, each filtered against the rising theta and
+//     compacted in arrival order.
 #include <climits>
 
 #include "f5_int.cuh"
@@ -94,16 +96,17 @@ __global__ void __launch_bounds__(TK_THREADS) k_topk_chunks(const int32_t *__res
 struct TkList {
   unsigned long long e;   // this lane's entry
   int count;              // entries held (warp-uniform)
+  int32_t last;           // entry[31]'s value once count == 32 (warp-uniform)
   bool lit, disp;         // sticky flags (warp-uniform)
 };
 
 F5_DEV void tk_insert(TkList &L, unsigned long long kn) {
   const int lane = threadIdx.x & 31;
   const int32_t v = tk_val(kn);
-  const int32_t last = tk_val(__shfl_sync(0xffffffffu, L.e, TK_K - 1));
-  if (L.count == TK_K) {
-    if (v < last) return;
-    if (v == last) {   // rejected while tying entry[31]
+  const bool full = L.count == TK_K;
+  if (full) {
+    if (v < L.last) return;
+    if (v == L.last) {   // rejected while tying entry[31]
       L.lit = L.disp = true;
       return;
     }
@@ -112,128 +115,166 @@ F5_DEV void tk_insert(TkList &L, unsigned long long kn) {
   const unsigned ge = __ballot_sync(0xffffffffu, lane < L.count && tk_val(L.e) >= v);
   const int p = __popc(ge);
   const unsigned long long up = __shfl_up_sync(0xffffffffu, L.e, 1);
-  const unsigned long long dropped = __shfl_sync(0xffffffffu, L.e, TK_K - 1);
   if (lane == p) L.e = kn;
   else if (lane > p) L.e = up;
+  if (!full) ++L.count;
   if (L.count == TK_K) {
-    // the displaced old entry[31] ties the new entry[31]
     const int32_t nl = tk_val(__shfl_sync(0xffffffffu, L.e, TK_K - 1));
-    if (tk_val(dropped) == nl) L.disp = true;
-  } else {
-    ++L.count;
+    // the displaced old entry[31] ties the new entry[31]
+    if (full && L.last == nl) L.disp = true;
+    L.last = nl;
   }
 }
 
+F5_DEV void bar_named(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
 constexpr int TK_TILE = 64;   // chunk lists staged in shared memory at a time
+
+struct TkShared {
+  unsigned long long lists[TK_TILE * TK_K];
+  unsigned long long cand[TK_THREADS];
+  int wcnt[TK_THREADS / 32];
+  int full, skip;
+  int32_t theta;
+  long long cmd;   // chunk to scan, -1: done
+};
+
+// One chunk scanned by the whole block in 256-element sub-blocks: elements
+// reaching the running theta (all while the list is not full), compacted in
+// arrival order, inserted by warp 0.  The chunk's elements before S.skip
+// are already in the list.
+F5_DEV void tk_scan_chunk(TkShared &S, TkList &L, const int32_t *__restrict__ vals, long long n, long long c) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int skip = S.skip;   // set by warp 0 before the named barrier that started the scan
+  for (int sb = 0; sb < TK_CHUNK / TK_THREADS; ++sb) {
+    if (sb * TK_THREADS + TK_THREADS <= skip) continue;   // uniform
+    if (tid == 0) {
+      S.full = L.count == TK_K ? 1 : 0;
+      S.theta = L.last;
+    }
+    __syncthreads();
+    const int off_in = sb * TK_THREADS + tid;
+    const long long e = c * TK_CHUNK + off_in;
+    bool keep = false;
+    unsigned long long kk = 0;
+    if (e < n && off_in >= skip) {
+      const int32_t v = vals[e];
+      keep = !S.full || v >= S.theta;
+      kk = tk_key(v, (uint32_t)e);
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, keep);
+    if (lane == 0) S.wcnt[warp] = __popc(bal);
+    __syncthreads();
+    int off = __popc(bal & ((1u << lane) - 1));
+    int tot = 0;
+    for (int w = 0; w < TK_THREADS / 32; ++w) {
+      off += w < warp ? S.wcnt[w] : 0;
+      tot += S.wcnt[w];
+    }
+    if (keep) S.cand[off] = kk;
+    __syncthreads();
+    if (warp == 0)
+      for (int i = 0; i < tot; ++i) tk_insert(L, S.cand[i]);
+    __syncthreads();   // S.cand and S.wcnt are rewritten by the next sub-block
+  }
+}
 
 __global__ void __launch_bounds__(TK_THREADS) k_topk_merge(const int32_t *__restrict__ vals, long long n,
                                                            const unsigned long long *__restrict__ ws,
                                                            f5_topk32 *__restrict__ out, const int *e_x) {
-  __shared__ unsigned long long s_lists[TK_TILE * TK_K];
-  __shared__ unsigned long long s_cand[TK_THREADS];
-  __shared__ int s_wcnt[TK_THREADS / 32];
-  __shared__ int s_ncand, s_mode[2], s_full;
-  __shared__ int32_t s_theta;
+  __shared__ TkShared S;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const long long nchunks = (n + TK_CHUNK - 1) / TK_CHUNK;
   TkList L;
   L.e = 0;
   L.count = 0;
+  L.last = INT_MIN;
   L.lit = L.disp = false;
-  if (tid == 0) {
-    s_full = 0;
-    s_theta = INT_MIN;
+  if (warp != 0) {
+    // helpers: wait on named barrier 1 for a chunk to scan, or the end
+    for (;;) {
+      bar_named(1, TK_THREADS);
+      const long long c = S.cmd;
+      if (c < 0) return;
+      tk_scan_chunk(S, L, vals, n, c);
+    }
   }
-  for (long long t0 = 0; t0 < nchunks; t0 += TK_TILE) {
+  // warp 0: the first min(32, n) elements enter the list in key order (no
+  // flag can fire before the list is full)
+  {
+    const unsigned long long k0 = lane < n ? tk_key(vals[lane], (uint32_t)lane) : 0ull;
+    int r = 0;
+    for (int j = 0; j < TK_K; ++j) r += __shfl_sync(0xffffffffu, k0, j) > k0;
+    unsigned long long mine = 0;
+    for (int j = 0; j < TK_K; ++j) {
+      const unsigned long long kj = __shfl_sync(0xffffffffu, k0, j);
+      const int rj = __shfl_sync(0xffffffffu, r, j);
+      if (kj != 0 && rj == lane) mine = kj;
+    }
+    L.e = mine;
+    L.count = n < TK_K ? (int)n : TK_K;
+    if (L.count == TK_K) L.last = tk_val(__shfl_sync(0xffffffffu, L.e, TK_K - 1));
+  }
+  // with n <= 32 every element is in the list already
+  for (long long t0 = 0; n > TK_K && t0 < nchunks; t0 += TK_TILE) {
     const int nt = (int)(nchunks - t0 < TK_TILE ? nchunks - t0 : TK_TILE);
-    __syncthreads();   // the previous tile is no longer read
-    for (int i = tid; i < nt * TK_K; i += TK_THREADS) s_lists[i] = ws[(size_t)t0 * TK_K + i];
-    __syncthreads();
+#pragma unroll 8
+    for (int i = lane; i < nt * TK_K; i += 32) S.lists[i] = __ldcg(ws + (size_t)t0 * TK_K + i);
+    __syncwarp();
     for (int ci = 0; ci < nt; ++ci) {
       const long long c = t0 + ci;
-      if (warp == 0) {
-        // 0 skip, 1 the candidates are the chunk-list entries reaching theta, 2 scan the chunk
-        const bool full = L.count == TK_K;
-        const int32_t theta = tk_val(__shfl_sync(0xffffffffu, L.e, TK_K - 1));
-        const unsigned long long ck = s_lists[ci * TK_K + lane];
-        const unsigned reach = __ballot_sync(0xffffffffu, ck != 0 && (!full || tk_val(ck) >= theta));
-        const long long cn = n - c * TK_CHUNK < TK_CHUNK ? n - c * TK_CHUNK : TK_CHUNK;
-        const int mode = reach == 0 ? 0 : ((!full || (__popc(reach) == TK_K && cn > TK_K)) ? 2 : 1);
-        if (mode == 1) {
-          // fewer than 32 of the chunk's elements reach theta: all are in its
-          // list; insert them in arrival order
-          const uint32_t myidx = tk_idx(ck);
-          int r = 0;
-          for (int j = 0; j < TK_K; ++j) {
-            const uint32_t oj = __shfl_sync(0xffffffffu, myidx, j);
-            r += ((reach >> j) & 1) && oj < myidx;
-          }
-          unsigned long long mine_sorted = 0;
-          for (int j = 0; j < TK_K; ++j) {
-            const unsigned long long kj = __shfl_sync(0xffffffffu, ck, j);
-            const int rj = __shfl_sync(0xffffffffu, r, j);
-            if (((reach >> j) & 1) && rj == lane) mine_sorted = kj;
-          }
-          const int nc = __popc(reach);
-          for (int i = 0; i < nc; ++i) tk_insert(L, __shfl_sync(0xffffffffu, mine_sorted, i));
+      const int skip = c == 0 ? TK_K : 0;   // chunk 0's first 32 elements are in the list
+      const unsigned long long ck = S.lists[ci * TK_K + lane];
+      // every chunk element reaching theta is in the chunk's list only when
+      // fewer than 32 list entries reach it (an element tying the 32nd key's
+      // value with a later index is otherwise left out)
+      const bool all_in = __popc(__ballot_sync(0xffffffffu, ck != 0 && tk_val(ck) >= L.last)) < TK_K;
+      const unsigned reach = __ballot_sync(
+          0xffffffffu, ck != 0 && (int)(tk_idx(ck) - (uint32_t)(c * TK_CHUNK)) >= skip && tk_val(ck) >= L.last);
+      if (all_in && reach == 0) continue;
+      if (all_in) {
+        // insert them in arrival order (loops over the candidate lanes only:
+        // usually a few per chunk)
+        const uint32_t myidx = tk_idx(ck);
+        int r = 0;
+        for (unsigned m = reach; m; m &= m - 1) r += __shfl_sync(0xffffffffu, myidx, __ffs(m) - 1) < myidx;
+        unsigned long long mine = 0;
+        for (unsigned m = reach; m; m &= m - 1) {
+          const int j = __ffs(m) - 1;
+          const unsigned long long kj = __shfl_sync(0xffffffffu, ck, j);
+          const int rj = __shfl_sync(0xffffffffu, r, j);
+          if (rj == lane) mine = kj;
         }
-        if (lane == 0) s_mode[ci & 1] = mode;   // two slots: a slow reader of chunk ci - 1 is never overtaken
-      }
-      __syncthreads();
-      if (s_mode[ci & 1] != 2) continue;   // uniform: every thread reads it after the barrier
-      // scan: 8 sub-blocks of 256 elements in arrival order, each filtered
-      // against the running theta and its survivors inserted by warp 0
-      for (int sb = 0; sb < TK_CHUNK / TK_THREADS; ++sb) {
-        if (warp == 0 && lane == 0) {
-          s_full = L.count == TK_K ? 1 : 0;
+        const int nc = __popc(reach);
+        for (int i = 0; i < nc; ++i) tk_insert(L, __shfl_sync(0xffffffffu, mine, i));
+      } else {
+        // scan the chunk with the helper warps
+        if (lane == 0) {
+          S.cmd = c;
+          S.skip = skip;
         }
-        if (warp == 0) {
-          const int32_t th = tk_val(__shfl_sync(0xffffffffu, L.e, TK_K - 1));
-          if (lane == 0) s_theta = th;
-        }
-        __syncthreads();
-        const long long e = c * TK_CHUNK + sb * TK_THREADS + tid;
-        bool keep = false;
-        unsigned long long kk = 0;
-        if (e < n) {
-          const int32_t v = vals[e];
-          keep = !s_full || v >= s_theta;
-          kk = tk_key(v, (uint32_t)e);
-        }
-        const unsigned bal = __ballot_sync(0xffffffffu, keep);
-        if (lane == 0) s_wcnt[warp] = __popc(bal);
-        __syncthreads();
-        int off = __popc(bal & ((1u << lane) - 1));
-        for (int w = 0; w < warp; ++w) off += s_wcnt[w];
-        if (keep) s_cand[off] = kk;
-        if (tid == 0) {
-          int tot = 0;
-          for (int w = 0; w < TK_THREADS / 32; ++w) tot += s_wcnt[w];
-          s_ncand = tot;
-        }
-        __syncthreads();
-        if (warp == 0) {
-          const int nc = s_ncand;
-          for (int i = 0; i < nc; ++i) tk_insert(L, s_cand[i]);
-        }
-        __syncthreads();
+        __syncwarp();
+        bar_named(1, TK_THREADS);
+        tk_scan_chunk(S, L, vals, n, c);
       }
     }
+    __syncwarp();   // the next tile overwrites S.lists
   }
-  if (warp == 0) {
-    const bool have = lane < L.count;
-    out->val[lane] = have ? tk_val(L.e) : 0;
-    out->idx[lane] = have ? (int32_t)tk_idx(L.e) : -1;
-    const unsigned long long top = __shfl_sync(0xffffffffu, L.e, 0);
-    if (lane == 0) {
-      out->count = L.count;
-      out->ovf_lit = L.lit ? 1 : 0;
-      out->ovf_disp = L.disp ? 1 : 0;
-      out->amax_idx = L.count ? (int32_t)tk_idx(top) : 0;
-      out->amax_val = L.count ? tk_val(top) : 0;
-      out->e_x = e_x ? *e_x : 0;
-      out->n = (int32_t)n;
-    }
+  if (lane == 0) S.cmd = -1;
+  __syncwarp();
+  bar_named(1, TK_THREADS);   // release the helpers
+  const bool have = lane < L.count;
+  out->val[lane] = have ? tk_val(L.e) : 0;
+  out->idx[lane] = have ? (int32_t)tk_idx(L.e) : -1;
+  const unsigned long long top = __shfl_sync(0xffffffffu, L.e, 0);
+  if (lane == 0) {
+    out->count = L.count;
+    out->ovf_lit = L.lit ? 1 : 0;
+    out->ovf_disp = L.disp ? 1 : 0;
+    out->amax_idx = L.count ? (int32_t)tk_idx(top) : 0;
+    out->amax_val = L.count ? tk_val(top) : 0;
+    out->e_x = e_x ? *e_x : 0;
+    out->n = (int32_t)n;
   }
 }
 
