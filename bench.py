@@ -477,6 +477,7 @@ def time_batched(m, B, ctx_len, steps, warmup, seed, prefill=False):
     (the work of a step does not depend on the cached values)."""
     import torch
     from fable5_llm_b200.batch import BatchModel
+    steps = max(steps, 10)   # a 420-launch graph per step: amortise the first launches
     bm = BatchModel(m, B, max_T=ctx_len + warmup + 2 * steps + 16)
     bm.reset()
     rng = np.random.default_rng(seed + B)
@@ -489,7 +490,6 @@ def time_batched(m, B, ctx_len, steps, warmup, seed, prefill=False):
         bm.step(rng.integers(0, m.geom.vocab, B))
     bm.launch(warmup)
     bm.sync()
-    steps = max(steps, 10)   # a 420-launch graph per step: amortise the first launches
     st = torch.cuda.ExternalStream(bm.stream_handle())
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
@@ -520,7 +520,8 @@ def run_batched(args, ws, rank, local):
     hbm_peak, peak_kind = peaks()
     B, ctx_len = args.batch, args.context
     geom = Geometry(args.layers, args.vocab)
-    m = DecodeModel(geom, max_T=16, device=local, max_pos=ctx_len + args.warmup + 2 * args.steps + 16)
+    # time_batched times at least 10 steps (plus as many e2e steps): RoPE rows for all of them
+    m = DecodeModel(geom, max_T=16, device=local, max_pos=ctx_len + args.warmup + 2 * max(args.steps, 10) + 16)
     m.load_synthetic(args.seed)
     clocks = ClockSampler(local)
     if ws > 1:
