@@ -68,6 +68,8 @@ SIGNATURES = [
     ("f5_bctx_sync", c_int, [c_vp, c_vp, c_vp]),
     ("f5_bctx_stream", c_int, [c_vp, c_vp]),
     ("f5_bctx_time_step", c_int, [c_vp, c_int, c_vp, c_int]),
+    ("f5_bctx_set_logits", c_int, [c_vp, c_int]),
+    ("f5_bctx_topk", c_int, [c_vp, c_vp]),
     ("f5_bctx_read", c_int, [c_vp, c_int, c_int, c_int, c_vp, c_size]),
     ("f5_bctx_write", c_int, [c_vp, c_int, c_int, c_int, c_vp, c_size]),
     ("f5_matvec_y32_host", c_int, [c_vp, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp]),

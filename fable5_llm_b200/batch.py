@@ -92,6 +92,30 @@ class BatchModel:
         L.check(self.lib.f5_bctx_stream(self.h, ctypes.byref(sp)), "f5_bctx_stream")
         return sp.value
 
+    # ---- TOPK-32 capture and per-sequence sampling (sw/chat_seq.py:1776-1928) ----
+    def set_logits(self, on=True):
+        """Store the LM head's y32 logits of every sequence each step."""
+        L.check(self.lib.f5_bctx_set_logits(self.h, int(on)), "f5_bctx_set_logits")
+
+    def logits(self, seq):
+        return self.read(seq, L.BUF_LOGITS)
+
+    def topk(self):
+        """The last step's TOPK-32 capture of every sequence (needs
+        set_logits(True) before the step) -> list of sampling.TopK32Result."""
+        from .sampling import TopK32Result
+        res = (L.TopK32 * self.B)()
+        L.check(self.lib.f5_bctx_topk(self.h, ctypes.byref(res)), "f5_bctx_topk")
+        return [TopK32Result.from_struct(r) for r in res]
+
+    def sample_step(self, tokens, samplers):
+        """One step of every sequence whose next tokens are drawn by
+        samplers[b] (sampling.Sampler) from that sequence's capture list
+        -> (tokens int32[B], per-sequence info)."""
+        self.step(tokens)
+        picks = [s.pick(r.values, r.indices, r.e_x) for s, r in zip(samplers, self.topk())]
+        return np.array([t for t, _ in picks], dtype=np.int32), [i for _, i in picks]
+
     # ---- buffers of one sequence ----
     def _size(self, what):
         g = self.geom
@@ -104,7 +128,7 @@ class BatchModel:
                 L.BUF_DN_CONV: (g.CONV_DIM * 4, np.int16), L.BUF_DN_KH: (g.LNH, np.int32),
                 L.BUF_K8: (g.NKV * self.max_T * g.HD, np.int8), L.BUF_KE: (g.NKV * self.max_T, np.int8),
                 L.BUF_V8: (g.NKV * self.max_T * g.HD, np.int8), L.BUF_VE: (g.NKV * self.max_T, np.int8),
-                L.BUF_KA: (1, np.int32)}[what]
+                L.BUF_KA: (1, np.int32), L.BUF_LOGITS: (g.vocab, np.int32)}[what]
 
     def read(self, seq, what, layer=0):
         n, dt = self._size(what)

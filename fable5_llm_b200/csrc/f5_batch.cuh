@@ -41,6 +41,8 @@ struct BgemmArgs {
   int ptot;
   unsigned long long *key;   // [Bp] argmax keys (argmax segments)
   uint32_t *err;
+  int32_t *y_out;     // argmax segments, optional: y32 of every row, y_out[b * y_bs + row]
+  long long y_bs;
   unsigned long long *trace; // optional globaltimer marks of CTA 0, 10240 words: [0,1024) stage
                              // issued, [1024,2048) stage unpack start, then per group [2048,4096)
                              // unpacked, [4096,6144) MMA issued, [6144,8192) accumulator ready,

@@ -25,6 +25,7 @@
 
 #include "../../include/f5b200.h"
 #include "f5_attn.cuh"
+#include "f5_topk.cuh"
 #include "f5_batch.cuh"
 #include "f5_capi_util.h"
 #include "f5_ctx_priv.h"
@@ -115,6 +116,10 @@ struct f5_bctx {
   size_t p_words = 0;
   unsigned long long *key = nullptr, *stats = nullptr;
   uint32_t *err = nullptr;
+  int32_t *logits = nullptr;   // [B][vocab] y32 of the LM head when enabled (f5_bctx_set_logits)
+  bool want_logits = false;
+  void *tk_ws = nullptr;       // f5_bctx_topk: chunk lists of B logit rows, B results
+  f5_topk32 *tk_out = nullptr;
   StepParams *params = nullptr, *h_params = nullptr;
   cudaGraphExec_t exec = nullptr;
   bool dirty = true;
@@ -225,6 +230,10 @@ cudaError_t bop(f5_bctx *c, const BSeg *sg, int nseg, int K, const GemvPrologue 
   ga.p = c->p;
   ga.ptot = prow;
   ga.key = head ? c->key : nullptr;
+  if (head && c->want_logits) {
+    ga.y_out = c->logits;
+    ga.y_bs = c->m->cfg.vocab;
+  }
   ga.err = c->err;
   if (c->sizing) {
     c->need_p = std::max(c->need_p, (size_t)ga.S * c->Bp * (size_t)prow);
@@ -468,6 +477,7 @@ int bbuf(f5_bctx *c, int what, int layer, int seq, uint8_t **ptr, size_t *bytes)
     case F5_BUF_PROD64: base = (uint8_t *)c->prod64; n = (size_t)NQ * HD * 8; break;
     case F5_BUF_QKVC16: base = (uint8_t *)c->qkvc16; n = (size_t)CONV_DIM * 2; break;
     case F5_BUF_GATES: base = (uint8_t *)c->gates; n = (size_t)2 * LNH * 4; break;
+    case F5_BUF_LOGITS: if (!c->logits) break; base = (uint8_t *)c->logits; n = (size_t)c->m->cfg.vocab * 4; break;
     case F5_BUF_ON16: base = (uint8_t *)c->on16; n = (size_t)LVD * 2; break;
     case F5_BUF_QG16: base = (uint8_t *)c->qg16; n = (size_t)NQ * HD * 4; break;
     case F5_BUF_PROD16: base = (uint8_t *)c->prod16; n = (size_t)FFN * 2; break;
@@ -700,6 +710,39 @@ int f5_bctx_time_step(f5_bctx *c, int reps, double *out, int nout) {
   out[2 * BK_N + 1] = 0;
   for (int k = 0; k < BK_N; ++k) out[2 * BK_N + 1] += ms[k];
   return bfinish(c, "f5_bctx_time_step");
+}
+
+int f5_bctx_set_logits(f5_bctx *c, int on) {
+  if (!c) return set_error(F5_EINVAL, "null batched context");
+  BDevGuard dg(c->device);
+  if (on && !c->logits) {
+    int rc = balloc(c, reinterpret_cast<void **>(&c->logits), (size_t)c->B * c->m->cfg.vocab * 4);
+    if (rc) return rc;
+  }
+  if ((on != 0) != c->want_logits) {
+    c->want_logits = on != 0;
+    c->dirty = true;   // the step graph is recorded again with the LM head's y32 output
+  }
+  return F5_OK;
+}
+
+int f5_bctx_topk(f5_bctx *c, f5_topk32 *out) {
+  if (!c || !out) return set_error(F5_EINVAL, "null argument");
+  if (!c->logits || !c->want_logits)
+    return set_error(F5_ESTATE, "f5_bctx_topk: logits not stored (f5_bctx_set_logits(bctx, 1) before the step)");
+  BDevGuard dg(c->device);
+  const int vocab = c->m->cfg.vocab;
+  int rc;
+  if (!c->tk_ws) {
+    if ((rc = balloc(c, &c->tk_ws, (size_t)c->B * topk32_ws_bytes(vocab)))) return rc;
+    if ((rc = balloc(c, reinterpret_cast<void **>(&c->tk_out), (size_t)c->B * sizeof(f5_topk32)))) return rc;
+  }
+  // the LM head's prologue left each sequence's {e_x, in_f} in xmeta
+  F5_CU(launch_topk32_b(c->logits, vocab, c->B, vocab, c->tk_ws, c->tk_out, c->xmeta, 2, c->st), "f5_bctx_topk");
+  F5_CU(cudaMemcpyAsync(out, c->tk_out, (size_t)c->B * sizeof(f5_topk32), cudaMemcpyDeviceToHost, c->st),
+        "f5_bctx_topk");
+  F5_CU(cudaStreamSynchronize(c->st), "f5_bctx_topk");
+  return F5_OK;
 }
 
 int f5_bctx_stream(f5_bctx *c, void **stream) {

@@ -332,6 +332,7 @@ __global__ void __launch_bounds__(bg_threads(BP), 1) k_bgemm(const __grid_consta
           if (valid && b < a.B) {
             const int32_t y = finish_y32(acc[jj], a.sh, a.err, nullptr);
             atomicMax(&s_key[b], argmax_key(y, row));
+            if (a.y_out) a.y_out[(size_t)b * a.y_bs + row] = y;
           }
         }
       } else if (valid) {

@@ -57,9 +57,12 @@ F5_DEV unsigned long long warp_max_u64(unsigned long long v) {
 }
 
 // chunk lists: ws[c * TK_K + j] = key j (descending), 0 past the chunk's size
-__global__ void __launch_bounds__(TK_THREADS) k_topk_chunks(const int32_t *__restrict__ vals, long long n,
-                                                            unsigned long long *__restrict__ ws) {
+__global__ void __launch_bounds__(TK_THREADS) k_topk_chunks(const int32_t *__restrict__ vals0, long long n,
+                                                            unsigned long long *__restrict__ ws0, long long vals_bs) {
   __shared__ unsigned long long s_cand[TK_THREADS / 32][TK_K];
+  // array blockIdx.y of a batched launch
+  const int32_t *__restrict__ vals = vals0 + (long long)blockIdx.y * vals_bs;
+  unsigned long long *__restrict__ ws = ws0 + (size_t)blockIdx.y * gridDim.x * TK_K;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const long long c0 = (long long)blockIdx.x * TK_CHUNK;
   // each lane holds 8 keys of its warp's 256 elements (0 = no element)
@@ -179,10 +182,17 @@ F5_DEV void tk_scan_chunk(TkShared &S, TkList &L, const int32_t *__restrict__ va
   }
 }
 
-__global__ void __launch_bounds__(TK_THREADS) k_topk_merge(const int32_t *__restrict__ vals, long long n,
-                                                           const unsigned long long *__restrict__ ws,
-                                                           f5_topk32 *__restrict__ out, const int *e_x) {
+__global__ void __launch_bounds__(TK_THREADS) k_topk_merge(const int32_t *__restrict__ vals0, long long n,
+                                                           const unsigned long long *__restrict__ ws0,
+                                                           f5_topk32 *__restrict__ out0, const int *e_x0,
+                                                           long long vals_bs, int ex_bs) {
   __shared__ TkShared S;
+  // array blockIdx.x of a batched launch
+  const int32_t *__restrict__ vals = vals0 + (long long)blockIdx.x * vals_bs;
+  const unsigned long long *__restrict__ ws =
+      ws0 + (size_t)blockIdx.x * (size_t)((n + TK_CHUNK - 1) / TK_CHUNK) * TK_K;
+  f5_topk32 *__restrict__ out = out0 + blockIdx.x;
+  const int *e_x = e_x0 ? e_x0 + (long long)blockIdx.x * ex_bs : nullptr;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const long long nchunks = (n + TK_CHUNK - 1) / TK_CHUNK;
   TkList L;
@@ -283,17 +293,25 @@ size_t topk32_ws_bytes(long long n) {
   return (size_t)(nchunks > 0 ? nchunks : 1) * TK_K * sizeof(unsigned long long);
 }
 
-cudaError_t launch_topk32(const int32_t *vals, long long n, void *ws, f5_topk32 *out, const int *e_x,
-                          cudaStream_t st) {
-  if (n < 0 || n > 0x7FFFFFFFll || (n > 0 && !vals) || !ws || !out) return cudaErrorInvalidValue;
+cudaError_t launch_topk32_b(const int32_t *vals, long long n, int nb, long long vals_bs, void *ws, f5_topk32 *out,
+                            const int *e_x, int ex_bs, cudaStream_t st) {
+  if (n < 0 || n > 0x7FFFFFFFll || nb < 1 || nb > 65535 || (n > 0 && !vals) || !ws || !out)
+    return cudaErrorInvalidValue;
   const long long nchunks = (n + TK_CHUNK - 1) / TK_CHUNK;
   if (nchunks > 0) {
-    k_topk_chunks<<<(unsigned)nchunks, TK_THREADS, 0, st>>>(vals, n, static_cast<unsigned long long *>(ws));
+    k_topk_chunks<<<dim3((unsigned)nchunks, nb), TK_THREADS, 0, st>>>(vals, n, static_cast<unsigned long long *>(ws),
+                                                                       vals_bs);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
-  k_topk_merge<<<1, TK_THREADS, 0, st>>>(vals, n, static_cast<const unsigned long long *>(ws), out, e_x);
+  k_topk_merge<<<nb, TK_THREADS, 0, st>>>(vals, n, static_cast<const unsigned long long *>(ws), out, e_x, vals_bs,
+                                           ex_bs);
   return cudaGetLastError();
+}
+
+cudaError_t launch_topk32(const int32_t *vals, long long n, void *ws, f5_topk32 *out, const int *e_x,
+                          cudaStream_t st) {
+  return launch_topk32_b(vals, n, 1, 0, ws, out, e_x, 0, st);
 }
 
 }  // namespace f5

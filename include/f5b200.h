@@ -358,6 +358,13 @@ int f5_bctx_time_step(f5_bctx *bctx, int reps, double *out, int nout);
 /* sequence seq's copy of an f5_buf buffer (same sizes as f5_ctx_read): the
  * state buffers of a layer, and the activations of the last layer that wrote
  * them (X16, QKV16, Z16, B16, A16, ON16, QG16, K16, V16, PROD64, PROD16) */
+/* also store the LM head's y32 logits of every sequence each step
+ * (F5_BUF_LOGITS, per sequence), as f5_ctx_set_logits does for one */
+int f5_bctx_set_logits(f5_bctx *bctx, int on);
+/* the last step's TOPK-32 capture of every sequence (out: batch entries)
+ * with each sequence's head-input exponent e_x: the candidate sets that
+ * sw/chat_seq.py:1776-1928 Sampler.pick draws from, per sequence */
+int f5_bctx_topk(f5_bctx *bctx, f5_topk32 *out);
 int f5_bctx_read(f5_bctx *bctx, int seq, int what, int layer, void *dst, size_t bytes);
 int f5_bctx_write(f5_bctx *bctx, int seq, int what, int layer, const void *src, size_t bytes);
 

@@ -150,3 +150,47 @@ def test_batch_engine_greedy_loop_and_offsets(model4b):
         assert (int(last[b]), int(mv[b])) == m.sync(), f"sequence {b}"
         assert bm.position(b) == (8, off[b] + 8)
     bm.close()
+
+
+def test_batch_topk_and_sampling(model4b):
+    """Per-sequence TOPK-32 capture of the batched step: each sequence's
+    stored logits equal the single-sequence engine's, its capture equals the
+    oracle's over them and the single engine's capture (e_x included), and
+    entry 0 is the greedy token; a seeded sampled continuation of every
+    sequence is reproducible."""
+    from oracle import topk as OT
+    from fable5_llm_b200 import sampling as S
+    m = model4b
+    B = 5
+    rng = np.random.default_rng(3)
+    toks = rng.integers(0, m.geom.vocab, (B, 3))
+    bm = BatchModel(m, B)
+    bm.set_logits(True)
+    bm.reset()
+    for t in range(3):
+        nt, mv = bm.step(toks[:, t])
+    caps = bm.topk()
+    m.set_logits(True)
+    for b in (0, 2, B - 1):
+        single_run(m, toks[b])
+        lg = bm.logits(b)
+        assert np.array_equal(lg, m.logits()), f"sequence {b} logits"
+        r, rs = caps[b], m.topk()
+        exp = OT.topk32(lg)
+        assert np.array_equal(r.values, exp["val"]) and np.array_equal(r.indices, exp["idx"])
+        assert (r.ovf_lit, r.ovf_disp) == (exp["ovf_lit"], exp["ovf_disp"])
+        assert r.indices[0] == nt[b] and r.values[0] == mv[b]
+        assert np.array_equal(r.values, rs.values) and np.array_equal(r.indices, rs.indices) and r.e_x == rs.e_x
+    m.set_logits(False)
+    runs = []
+    for rep in range(2):
+        bm.reset()
+        samplers = [S.Sampler(temp=0.9, top_k=16, seed=100 + b, logit_exp0=m.head_logit_exp0()) for b in range(B)]
+        cur, seq = toks[:, 0], []
+        for t in range(3):
+            cur, info = bm.sample_step(cur, samplers)
+            assert all(i["mode"] == "sampled" for i in info)
+            seq.append(cur.copy())
+        runs.append(np.stack(seq))
+    assert np.array_equal(runs[0], runs[1])
+    bm.close()
