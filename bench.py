@@ -319,10 +319,10 @@ def run_step(args, ws, rank, local):
         F.connect(m)
         torch.distributed.barrier()
     m.prepare()
-    # context: greedy-decode ctx_len tokens on the device (not timed)
-    m.decode_step(17, 0)
-    if ctx_len > 1:
-        m.decode_launch(ctx_len - 1)
+    # context: ctx_len seeded random token ids fed on the device, one step
+    # each, as the reference prefills (not timed); the timed steps then
+    # continue greedily from the argmax of the last prompt token
+    m.prefill(np.random.default_rng(args.seed).integers(0, m.geom.vocab, ctx_len))
     tok, _ = m.sync()
     st = torch.cuda.ExternalStream(m.stream_handle())
     for _ in range(args.warmup):
@@ -421,7 +421,8 @@ def run_step(args, ws, rank, local):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "strong",
             "vs_baseline": round(toks / FPGA_TOKS, 2), "dtype": "int4xint8->int32/int64",
-            "data": "synthetic (seeded int4 W4 images and integer vectors, Qwen3.5-9B shapes)",
+            "data": f"synthetic (seeded int4 W4 images and integer vectors, Qwen3.5-9B shapes); context prefilled "
+                    f"with {ctx_len} seeded random token ids",
             "config": {"workload": f"full 32-layer integer decode step + 248,320-row LM head argmax at "
                                    f"context {ctx_len}, greedy device-fed, " +
                                    ("one persistent-kernel launch per step" if engine == "persistent"

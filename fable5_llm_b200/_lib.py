@@ -100,6 +100,7 @@ SIGNATURES = [
     ("f5_ctx_trace_step", c_int, [c_vp, c_vp, c_size, c_vp, c_vp]),
     ("f5_decode_step", c_int, [c_vp, c_int, c_int, c_vp, c_vp]),
     ("f5_decode_launch", c_int, [c_vp, c_int, c_vp]),
+    ("f5_decode_prefill", c_int, [c_vp, c_vp, c_int]),
     ("f5_ctx_sync", c_int, [c_vp, c_vp, c_vp]),
     ("f5_ctx_time_step", c_int, [c_vp, c_int, c_vp, c_int]),
     ("f5_layer_step", c_int, [c_vp, c_int, c_vp, c_int, c_int]),

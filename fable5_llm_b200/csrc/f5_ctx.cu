@@ -67,6 +67,9 @@ __global__ void k_step_end(StepParams *p, const unsigned long long *key, const u
 
 __global__ void k_collect_err(StepParams *p, const uint32_t *err) { p->err |= *err; }
 
+// prefill: the input token of the next step comes from the prompt, not the argmax
+__global__ void k_set_token(StepParams *p, const int32_t *toks, int i) { p->tok = toks[i]; }
+
 static cudaError_t launch_pdl(const void *fn, void **args, dim3 grid, dim3 block, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -1095,6 +1098,25 @@ int f5_decode_launch(f5_ctx *c, int n_steps, void *stream_unused) {
   if ((rc = resolve_engine(c, eng))) return rc;
   for (int i = 0; i < n_steps; ++i)
     if ((rc = launch_step(c, eng))) return rc;
+  return F5_OK;
+}
+
+int f5_decode_prefill(f5_ctx *c, const int32_t *tokens, int n) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  if (n < 0 || (n > 0 && !tokens)) return set_error(F5_EINVAL, "f5_decode_prefill: n=%d, tokens %p", n, tokens);
+  if (n > c->cfg.max_T) return set_error(F5_EINVAL, "f5_decode_prefill: %d tokens, KV capacity %d", n, c->cfg.max_T);
+  DevGuard dg(c->device);
+  int eng;
+  if ((rc = resolve_engine(c, eng))) return rc;
+  if (!c->prompt) F5_ALLOC(c, c->prompt, (size_t)c->cfg.max_T * sizeof(int32_t));
+  F5_CU(cudaMemcpyAsync(c->prompt, tokens, (size_t)n * sizeof(int32_t), cudaMemcpyHostToDevice, c->st),
+        "f5_decode_prefill");
+  for (int i = 0; i < n; ++i) {
+    k_set_token<<<1, 1, 0, c->st>>>(c->params, c->prompt, i);
+    F5_CU(cudaGetLastError(), "f5_decode_prefill");
+    if ((rc = launch_step(c, eng))) return rc;
+  }
   return F5_OK;
 }
 

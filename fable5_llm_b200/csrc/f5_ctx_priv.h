@@ -67,6 +67,7 @@ struct f5_ctx {
   bool timing = false;         // bracket every launch with events (f5_ctx_time_step)
   std::vector<Timed> timed;
   int32_t *logits = nullptr;   // [vocab] y32 of the LM head when enabled
+  int32_t *prompt = nullptr;   // [max_T] tokens of f5_decode_prefill
   // TOPK-32 capture (f5_ctx_topk): chunk lists, result, head-prologue operand and {e_x, in_f}
   void *tk_ws = nullptr;
   f5_topk32 *tk_out = nullptr;

@@ -225,6 +225,14 @@ class DecodeModel:
                 "f5_decode_step")
         return nt.value, mv.value
 
+    def prefill(self, tokens):
+        """Feed a prompt: one step per token from the current position, the
+        tokens taken on the device (no host round trip between steps);
+        asynchronous.  sync() then returns the argmax after the last token,
+        and decode_launch continues greedily from it."""
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32).reshape(-1))
+        L.check(self.lib.f5_decode_prefill(self.h, _p(t), int(t.size)), "f5_decode_prefill")
+
     def decode_launch(self, n):
         L.check(self.lib.f5_decode_launch(self.h, int(n), None), "f5_decode_launch")
 

@@ -307,6 +307,13 @@ int f5_decode_step(f5_ctx *ctx, int32_t tok, int32_t pos, int32_t *next_tok, int
 /* n greedy steps on the device without host round trips: each step feeds
  * its argmax to the next (pos and T advance); read the last with f5_ctx_sync */
 int f5_decode_launch(f5_ctx *ctx, int n_steps, void *stream_unused);
+/* Prefill: n steps whose input tokens are tokens[0..n) (host array), from
+ * the context's current position, without a host round trip between steps
+ * (the reference prefills a prompt the same way, one token per step:
+ * sw/chat_client.py:21, ref/fidelity_check.py:423-448 per token).  After
+ * it, the next device-fed step (f5_decode_launch) starts from the argmax of
+ * the last prompt step; f5_ctx_sync returns it.  Asynchronous. */
+int f5_decode_prefill(f5_ctx *ctx, const int32_t *tokens, int n);
 int f5_ctx_sync(f5_ctx *ctx, int32_t *last_tok, int32_t *max_logit);
 
 /* Run `reps` decode steps eagerly with a CUDA event pair around every kernel

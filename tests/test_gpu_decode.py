@@ -266,3 +266,25 @@ def test_full_9b_vs_oracle():
             assert nt == ref_tok and mv == int(y.max())
         _compare_states(m, r, 3)
     m.close()
+
+
+def test_prefill_matches_host_steps(model4, engine):
+    """A device-fed prompt (f5_decode_prefill) leaves the same state, logit
+    and next token as the same tokens fed one host step at a time, and the
+    greedy continuation from it is the same."""
+    m = model4
+    m.set_engine(engine)
+    toks = [17, 901, 4000, 3, 17, 256, 9]
+    m.reset()
+    for t, tok in enumerate(toks):
+        nt, mv = m.decode_step(tok, t)
+    x_ref = m.read(L.BUF_X16)
+    m.decode_launch(3)
+    cont_ref = m.sync()
+    m.reset()
+    m.prefill(toks)
+    assert m.sync() == (nt, mv)
+    assert np.array_equal(m.read(L.BUF_X16), x_ref)
+    assert m.position() == (len(toks), len(toks))
+    m.decode_launch(3)
+    assert m.sync() == cont_ref
