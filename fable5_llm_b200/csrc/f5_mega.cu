@@ -701,14 +701,38 @@ F5_DEV bool c_dn(const MegaArgs &ma, const DnArgs &d, const MegaSmem &S, int &w_
   long long o = 0;
   int sat = 0;
   int16_t *Sg = d.S + (size_t)h * 16384 + (size_t)qd * 4096;
+  const unsigned long long dabs = uabs(delta);
+  if (dabs < (1ull << 24)) {
+    // |delta| < 2^24 (always, for beta <= 2^15): the rank-1 term in 32-bit
+    // integers, rshr(kn * delta, NRM_F) = sign(kn * delta) * (|kn| dh +
+    // ((|kn| dl + 2^(NRM_F-1)) >> NRM_F)) with |delta| = dh 2^NRM_F + dl
+    // (the same split as dn_head_rec); 8 terms of |sn * qn| <= 2^15 * 2896
+    // stay inside int32
+    const int32_t dh = (int32_t)(dabs >> NRM_F), dl = (int32_t)(dabs & ((1u << NRM_F) - 1));
+    const int32_t sdl = delta < 0 ? -1 : 0;
+    int32_t o32 = 0;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int dk = warp * 8 + i;
-    long long sn = (long long)sd[dk * 32 + lane] + rshr((long long)kn[dk] * delta, NRM_F);
-    if (sn > 32767 || sn < -32767) ++sat;   // |Sh| > 32767 (ref/layer_fixed.py:1557)
-    sn = clip16(sn);
-    Sg[dk * 32 + lane] = (int16_t)sn;
-    o += sn * qn[dk];
+    for (int i = 0; i < 8; ++i) {
+      const int dk = warp * 8 + i;
+      const int32_t k = kn[dk], ak = k < 0 ? -k : k, sg = (k >> 31) ^ sdl;
+      const int32_t r = ak * dh + ((ak * dl + (1 << (NRM_F - 1))) >> NRM_F);
+      int32_t sn = (int32_t)sd[dk * 32 + lane] + ((r ^ sg) - sg);
+      sat += (uint32_t)(sn + 32767) > 65534u;   // |Sh| > 32767 (ref/layer_fixed.py:1557)
+      sn = min(max(sn, -32768), 32767);
+      Sg[dk * 32 + lane] = (int16_t)sn;
+      o32 += sn * qn[dk];
+    }
+    o = o32;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int dk = warp * 8 + i;
+      long long sn = (long long)sd[dk * 32 + lane] + rshr((long long)kn[dk] * delta, NRM_F);
+      if (sn > 32767 || sn < -32767) ++sat;   // |Sh| > 32767 (ref/layer_fixed.py:1557)
+      sn = clip16(sn);
+      Sg[dk * 32 + lane] = (int16_t)sn;
+      o += sn * qn[dk];
+    }
   }
   if (d.stats && sat) atomicAdd(d.stats, (unsigned long long)sat);
   part[warp * 32 + lane] = o;
