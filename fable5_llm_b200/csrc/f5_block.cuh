@@ -241,4 +241,22 @@ F5_DEV unsigned long long g_max_ull(const SY &sy, unsigned long long v, unsigned
   return t;
 }
 
+// Reduce four per-lane values over the warp with six shuffles instead of
+// twenty: afterwards every lane of the 8-lane group g = lane >> 3 holds the
+// warp total of v[g].  Integer sums are order-free, so the result equals
+// four separate butterflies.
+F5_DEV int warp_sum4_i32(const int (&v)[4]) {
+  const int lane = threadIdx.x & 31;
+  const bool b4 = lane & 16, b3 = lane & 8;
+  int k0 = b4 ? v[2] : v[0], k1 = b4 ? v[3] : v[1];
+  k0 += __shfl_xor_sync(0xffffffffu, b4 ? v[0] : v[2], 16);
+  k1 += __shfl_xor_sync(0xffffffffu, b4 ? v[1] : v[3], 16);
+  int k = b3 ? k1 : k0;
+  k += __shfl_xor_sync(0xffffffffu, b3 ? k0 : k1, 8);
+  k += __shfl_xor_sync(0xffffffffu, k, 4);
+  k += __shfl_xor_sync(0xffffffffu, k, 2);
+  k += __shfl_xor_sync(0xffffffffu, k, 1);
+  return k;
+}
+
 }  // namespace f5

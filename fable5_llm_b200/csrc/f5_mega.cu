@@ -941,7 +941,7 @@ F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int
   for (int h = 0; h < 4; ++h)
 #pragma unroll
     for (int i = 0; i < 8; ++i) qr[h][i] = q16[h * 256 + 8 * lane + i];
-  long long lmax[4] = {LLONG_MIN, LLONG_MIN, LLONG_MIN, LLONG_MIN};
+  long long lmax = LLONG_MIN;   // of head lane >> 3
   const int len = max(0, g.t1 - g.t0);
   const int nfill = (len + MEGA_SUB - 1) / MEGA_SUB;
   bool bad = false;
@@ -979,15 +979,13 @@ F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int
 #pragma unroll
         for (int h = 0; h < 4; ++h) dot[h] += qr[h][j] * b0 + qr[h][4 + j] * b1;
       }
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-#pragma unroll
-        for (int o = 16; o; o >>= 1) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], o);
-        const long long sv = rshr((long long)dot[h] * 2048, 15);   // SCALE_Q15 = round(2^15/sqrt(256))
-        const long long s = shift_to(sv, QKV_F - kex - 16);
-        lmax[h] = s > lmax[h] ? s : lmax[h];
-        if (lane == h) sc[h * cm + (t - g.t0)] = s;
-      }
+      // lane group lane >> 3 receives head (lane >> 3)'s total
+      const int tot = warp_sum4_i32(dot);
+      // rshr(dot * 2048, 15) (SCALE_Q15 = round(2^15/sqrt(256))) is the same
+      // rational rounded the same way as rshr(dot, 4); |dot| < 2^30
+      const long long s = shift_to(rshr32p(tot, 4), QKV_F - kex - 16);
+      lmax = s > lmax ? s : lmax;
+      if ((lane & 7) == 0) sc[(lane >> 3) * cm + (t - g.t0)] = s;
     }
   }
   if (sy.any(bad)) return false;
@@ -995,9 +993,7 @@ F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int
   // group score max over the kv head's cpg CTAs (marked slots, phase 0)
   unsigned long long *slots = m.slots + (size_t)g.kv * g.cpg * 8;
   const size_t phase_stride = (size_t)a.nkv * g.cpg * 8;
-  if (lane == 0)
-#pragma unroll
-    for (int h = 0; h < 4; ++h) red4[warp * 4 + h] = lmax[h];
+  if ((lane & 7) == 0) red4[warp * 4 + (lane >> 3)] = lmax;
   sy.sync();
   if (tid < 4) {
     long long mx = LLONG_MIN;
