@@ -1004,21 +1004,23 @@ F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int
   MG_MARK(4);
 
   // ---- 3. exp, group sum, reciprocal, probabilities (Q15) ----
-  long long sum[4] = {0, 0, 0, 0};
-#pragma unroll
-  for (int h = 0; h < 4; ++h) {
-    const long long mx = mg_att[h];
-    for (int i = tid; i < len; i += MG_CT) {
-      const long long x = sc[h * cm + i] - mx;
+  // one pass over (token, head): thread t works on head t & 3 (MG_CT is a
+  // multiple of 4), lanes with equal lane & 3 share a head
+  const int hx = tid & 3;
+  long long sum = 0;
+  {
+    const long long mx = mg_att[hx];
+    for (int idx = tid; idx < 4 * len; idx += MG_CT) {
+      const int i = idx >> 2;
+      const long long x = sc[hx * cm + i] - mx;
       const long long es = exp_neg_q(x < 0 ? x : 0);
-      sc[h * cm + i] = es;
-      sum[h] += es;
+      sc[hx * cm + i] = es;
+      sum += es;
     }
-    sum[h] = warp_sum_ll(sum[h]);
   }
-  if (lane == 0)
 #pragma unroll
-    for (int h = 0; h < 4; ++h) red4[warp * 4 + h] = sum[h];
+  for (int o = 16; o >= 4; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (lane < 4) red4[warp * 4 + lane] = sum;
   sy.sync();
   if (tid < 4) {
     long long tot = 0;
@@ -1036,11 +1038,13 @@ F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int
     mg_att[4 + tid] = 30 - re + 15;
   }
   sy.sync();
-#pragma unroll
-  for (int h = 0; h < 4; ++h) {
-    const long long rcp = mg_att[h];
-    const int psh = (int)mg_att[4 + h];
-    for (int i = tid; i < len; i += MG_CT) sc[h * cm + i] = clip(rshr(sc[h * cm + i] * rcp, psh), 0, 1 << 15);
+  {
+    const long long rcp = mg_att[hx];
+    const int psh = (int)mg_att[4 + hx];
+    for (int idx = tid; idx < 4 * len; idx += MG_CT) {
+      const int i = idx >> 2;
+      sc[hx * cm + i] = clip(rshr(sc[hx * cm + i] * rcp, psh), 0, 1 << 15);
+    }
   }
   sy.sync();
 
