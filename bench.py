@@ -424,7 +424,7 @@ def run_step(args, ws, rank, local):
             "data": f"synthetic (seeded int4 W4 images and integer vectors, Qwen3.5-9B shapes); context prefilled "
                     f"with {ctx_len} seeded random token ids",
             "config": {"workload": f"full 32-layer integer decode step + 248,320-row LM head argmax at "
-                                   f"context {ctx_len}, greedy device-fed, " +
+                                   f"context {ctx_len} (prefilled from seeded random ids), greedy device-fed, " +
                                    ("one persistent-kernel launch per step" if engine == "persistent"
                                     else "one CUDA graph per step"),
                        "engine": engine,
