@@ -310,8 +310,11 @@ def run_step(args, ws, rank, local):
     # N > 1: one sequence, every matrix row-sharded over the N GPUs
     # (split_rows); the GEMV epilogues store their output rows into every
     # GPU's buffers (peer stores over NVLink), the vector work is replicated
+    # RoPE rows: this run's positions, and the config-5 summary's (context
+    # 1024, 3 warm-up + 2 x 10 steps) when it runs on this model
+    max_pos = max(ctx_len + args.warmup + 2 * args.steps + 8, 1024 + 3 + 2 * 10 + 16)
     m = DecodeModel(Geometry(args.layers, args.vocab), max_T=ctx_len + args.warmup + 2 * args.steps + 8, device=local,
-                    max_pos=ctx_len + args.warmup + 2 * args.steps + 8, world_size=ws, rank=rank)
+                    max_pos=max_pos, world_size=ws, rank=rank)
     m.load_synthetic(args.seed)
     m.reset()
     if ws > 1:
