@@ -739,8 +739,67 @@ F5_DEV bool c_dn(const MegaArgs &ma, const DnArgs &d, const MegaSmem &S, int &w_
   sy.sync();
   MG_MARK(4);
 
-  // ---- the head's 128 o values: publish this quarter, gather all four ----
   unsigned long long *xsl = d.xslots + (size_t)h * 128 * 2;
+  if (d.norm_mode == 0) {
+    // ---- float gated norm: each CTA outputs its own 32 columns (warp 0, lane
+    // = column), so the four quarters exchange only their max |o| and their
+    // wrapping (numpy int64, order-free) sum of o*o ----
+    bool ok = true;
+    long long ot = 0;
+    unsigned long long om = 0ull, ssu = 0ull;
+    if (warp == 0) {
+#pragma unroll
+      for (int w = 0; w < MG_CONS; ++w) ot += part[w * 32 + lane];
+      ot = rshr(ot, NRM_F);
+      unsigned long long qm = uabs(ot), qs = (unsigned long long)ot * (unsigned long long)ot;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        const unsigned long long u = __shfl_xor_sync(0xffffffffu, qm, o);
+        qm = u > qm ? u : qm;
+        qs += __shfl_xor_sync(0xffffffffu, qs, o);
+      }
+      if (lane == 0) {
+        slot_put(xsl + (size_t)(2 * qd) * 2, (long long)qm);
+        slot_put(xsl + (size_t)(2 * qd + 1) * 2, (long long)qs);
+      }
+      __syncwarp();
+      long long v = 0;
+      if (lane < 8) ok = slot_get(xsl + (size_t)lane * 2, v, ab);   // even lanes: maxima, odd: sums
+      unsigned long long mx = (lane < 8 && (lane & 1) == 0) ? (unsigned long long)v : 0ull;
+      unsigned long long sm = (lane < 8 && (lane & 1)) ? (unsigned long long)v : 0ull;
+#pragma unroll
+      for (int o = 4; o; o >>= 1) {
+        const unsigned long long u = __shfl_xor_sync(0xffffffffu, mx, o);
+        mx = u > mx ? u : mx;
+        sm += __shfl_xor_sync(0xffffffffu, sm, o);
+      }
+      om = __shfl_sync(0xffffffffu, mx, 0);
+      ssu = __shfl_sync(0xffffffffu, sm, 0);
+    }
+    if (sy.any(!ok)) return false;
+    MG_MARK(5);
+    if (warp == 0) {
+      // block-float k_h (ref/layer_fixed.py:470-486), norm scale (:509-546)
+      const int kh_shift = bf_shift(om);
+      const long long o16 = clip16(kh_shift >= 0 ? rshr(ot, kh_shift) : (long long)((unsigned long long)ot << (-kh_shift)));
+      const long long m = dn_norm_scale((long long)ssu, kh_shift, 128);
+      const long long tt = clip16(rshr(o16 * m, 15));
+      const long long nh = clip16(rshr(tt * vzn[64 + lane], 14));
+      const long long zg = clip16(silu_q(vzn[32 + lane] << (12 - QKV_F)));
+      const int32_t ov16 = clip16(rshr(nh * zg, 12));
+      const int col = h * 128 + qd * 32 + lane;
+      if (epoch && d.out_tag_op1)
+        reinterpret_cast<uint32_t *>(d.on16)[col] = tag_word(mk_tag(epoch, d.out_tag_op1), ov16);
+      else
+        d.on16[col] = (int16_t)ov16;
+      if (qd == 0 && lane == 0 && d.kh_out) d.kh_out[h] = kh_shift;
+    }
+    release_scratch(sy, (&mg_bfree));
+    MG_MARK(6);
+    return true;
+  }
+  // ---- eps gated norm: its sum needs k_h first, so the head's 128 o values
+  // are published by quarter and gathered by all four CTAs ----
   if (warp == 0) {
     long long ot = 0;
 #pragma unroll
@@ -752,25 +811,13 @@ F5_DEV bool c_dn(const MegaArgs &ma, const DnArgs &d, const MegaSmem &S, int &w_
   if (tid < 128) ok = slot_get(xsl + (size_t)tid * 2, ov, ab);
   if (sy.any(!ok)) return false;
   MG_MARK(5);
-  // ---- block-float k_h (ref/layer_fixed.py:470-486) and the gated norm
-  // (ref/layer_fixed.py:509-546 or 694-781); identical in the four CTAs ----
-  // float mode: max |o| and the numpy int64 (wrapping, order-free) sum of
-  // o*o in one round; eps mode needs k_h before its sum
-  unsigned long long om, ssu = 0ull;
-  if (d.norm_mode == 0)
-    g_max_sum_ull(sy, tid < 128 ? uabs(ov) : 0ull, (unsigned long long)ov * (unsigned long long)ov,
-                  reinterpret_cast<unsigned long long *>(mg_red), om, ssu);
-  else
-    om = g_max_ull(sy, tid < 128 ? uabs(ov) : 0ull, reinterpret_cast<unsigned long long *>(mg_red));
+  // block-float k_h (ref/layer_fixed.py:470-486), then the EPS-NORM law
+  // (ref/layer_fixed.py:694-781) over the shifted values; identical in the
+  // four CTAs
+  const unsigned long long om = g_max_ull(sy, tid < 128 ? uabs(ov) : 0ull, reinterpret_cast<unsigned long long *>(mg_red));
   const int kh_shift = bf_shift(om);
   const long long o16 = clip16(kh_shift >= 0 ? rshr(ov, kh_shift) : (long long)((unsigned long long)ov << (-kh_shift)));
-  long long m;
-  if (d.norm_mode == 0) {
-    m = dn_norm_scale((long long)ssu, kh_shift, 128);
-  } else {
-    const long long ss = g_sum_ll(sy, o16 * o16, mg_red);
-    m = eps_norm_scale(ss, kh_shift, 7);
-  }
+  const long long m = eps_norm_scale(g_sum_ll(sy, o16 * o16, mg_red), kh_shift, 7);
   if (tid >= qd * 32 && tid < qd * 32 + 32) {
     const int i = tid - qd * 32;
     const long long tt = clip16(rshr(o16 * m, 15));
