@@ -92,32 +92,54 @@ class DecodeModel:
 
     def upload_layer(self, i, qw):
         """One layer in the reference dict layout (ref/layer_fixed.py:1607-1651)."""
-        self.upload_vector(i, L.VEC_LN1, qw["ln1"])
-        self.upload_vector(i, L.VEC_LN2, qw["ln2"])
         for nm, sl in MLP_SLOTS.items():
             self.upload_qmat(i, sl, qw["mlp"][nm])
+        own = (qw["attn"], ATTN_SLOTS) if qw["type"] == "full_attention" else (qw["dn"], DN_SLOTS)
+        for nm, sl in own[1].items():
+            self.upload_qmat(i, sl, own[0][nm])
+        self.upload_layer_vectors(i, qw)
+
+    def upload_layer_vectors(self, i, qw):
+        """The integer vectors of one reference layer dict (norm gains, and
+        conv taps / gate constants / gated-norm gain, or q/k norm gains)."""
+        self.upload_vector(i, L.VEC_LN1, qw["ln1"])
+        self.upload_vector(i, L.VEC_LN2, qw["ln2"])
         if qw["type"] == "full_attention":
             a = qw["attn"]
-            for nm, sl in ATTN_SLOTS.items():
-                self.upload_qmat(i, sl, a[nm])
             self.upload_vector(i, L.VEC_Q_NORM, a["q_norm"])
             self.upload_vector(i, L.VEC_K_NORM, a["k_norm"])
         else:
             d = qw["dn"]
-            for nm, sl in DN_SLOTS.items():
-                self.upload_qmat(i, sl, d[nm])
             self.upload_vector(i, L.VEC_CONV_W, d["conv_w"])
             self.upload_vector(i, L.VEC_DT_BIAS, d["dt_bias_q12"])
             self.upload_vector(i, L.VEC_A, d["A_q15"])
             self.upload_vector(i, L.VEC_NORM_W, d["norm_w_q14"])
 
+    @staticmethod
+    def slot_of(name):
+        """Matrix slot of a reference matrix name ("head" for the LM head)."""
+        return L.S_HEAD if name == "head" else {**DN_SLOTS, **ATTN_SLOTS, **MLP_SLOTS}[name]
+
+    def upload_final_norm(self, ln_f_q12):
+        self.upload_vector(-1, L.VEC_LN_F, ln_f_q12)
+
+    def upload_embedding(self, emb_q):
+        emb = np.ascontiguousarray(emb_q, dtype=np.int16)
+        L.check(self.lib.f5_ctx_upload_embedding(self.h, _p(emb), emb.shape[0], emb.shape[1]), "upload_embedding")
+
     def upload_model(self, layers, emb_q, head, ln_f_q12):
         for i, qw in enumerate(layers):
             self.upload_layer(i, qw)
         self.upload_qmat(-1, L.S_HEAD, head)
-        self.upload_vector(-1, L.VEC_LN_F, ln_f_q12)
-        emb = np.ascontiguousarray(emb_q, dtype=np.int16)
-        L.check(self.lib.f5_ctx_upload_embedding(self.h, _p(emb), emb.shape[0], emb.shape[1]), "upload_embedding")
+        self.upload_final_norm(ln_f_q12)
+        self.upload_embedding(emb_q)
+
+    def load_artifact(self, prefix, layers=None, ln_f_q12=None):
+        """A reference weight artifact (``<prefix>.weights.json``, its
+        ``_w<wid>.bin`` images and ``.emb.bin``), image by image; the layer
+        vectors come from the reference layer dicts (fable5_llm_b200.artifact)."""
+        from . import artifact
+        return artifact.load_artifact(self, prefix, layers, ln_f_q12)
 
     def load_synthetic(self, seed):
         """The seeded synthetic model of fable5_llm_b200.synth, generated on
