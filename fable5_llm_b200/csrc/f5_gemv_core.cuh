@@ -162,6 +162,24 @@ F5_DEV int32_t rms_elem32(int32_t x, int32_t r, int s, int32_t gain) {
   return (int32_t)(t < 0 ? -c : (c > 32767 ? 32767 : c));
 }
 
+// rms_elem32 for 17 <= s <= 47 (every int16 RMSNorm input: s = 30 - e of
+// rsqrt_q is >= 17 for any sum of squares >= 1) in 32-bit integer
+// arithmetic.  With r = rh 2^16 + rl (0 < r < 2^31, rh < 2^15):
+//   vh = |x| rh + ((|x| rl) >> 16) = floor(|x| r / 2^16)  (< 2^31),
+//   q  = (vh + 2^(s-17)) >> (s-16) = rshr(|x| r, s)        (< 2^31, no clamp),
+// exact because 2^(s-1) is a multiple of 2^16 (nested floor division); the
+// gain product |t| = q |gain| saturates clip16 once it reaches 2^29 - 8192,
+// so only its high word's zero test and the low word are needed.
+F5_DEV int32_t rms_elem_s17(int32_t x, uint32_t rh, uint32_t rl, int s, int32_t gain) {
+  const uint32_t ax = (uint32_t)(x < 0 ? -x : x);
+  const uint32_t vh = ax * rh + ((ax * rl) >> 16);
+  const uint32_t q = (vh + (1u << (s - 17))) >> (s - 16);
+  const uint32_t ag = gain < 0 ? 0u - (uint32_t)gain : (uint32_t)gain;
+  const uint32_t lo = q * ag, hi = __umulhi(q, ag);
+  const uint32_t c = (hi != 0u || lo >= (1u << 29) - 8192u) ? 32768u : (lo + 8192u) >> 14;
+  return ((x < 0) != (gain < 0)) ? -(int32_t)c : (int32_t)(c < 32767u ? c : 32767u);
+}
+
 // element j (0..7) of 8 int16 packed in a uint4
 F5_DEV long long get16(const uint4 &u, int j) {
   const uint32_t w = (j >> 1) == 0 ? u.x : ((j >> 1) == 1 ? u.y : ((j >> 1) == 2 ? u.z : u.w));
@@ -321,6 +339,8 @@ F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red,
         // fast path when rsqrt's r and shift are in rms_elem32's domain (always
         // for int16 inputs of H = 4096); the general law otherwise
         const bool fast = r > 0 && r < (1ll << 31) && 30 - e >= 1 && 30 - e <= 62;
+        const bool fast17 = fast && 30 - e >= 17 && 30 - e <= 47;
+        const uint32_t rh = (uint32_t)r >> 16, rl = (uint32_t)r & 0xFFFFu;
 #pragma unroll
         for (int j = 0; j < MAXB; ++j) {
           const int wv[8] = {wl[j][0].x, wl[j][0].y, wl[j][0].z, wl[j][0].w,
@@ -329,7 +349,10 @@ F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red,
 #pragma unroll
           for (int k = 0; k < 8; k += 2) {
             int32_t x0, x1;
-            if (fast) {
+            if (fast17) {
+              x0 = rms_elem_s17(get16i(raw[j], k), rh, rl, 30 - e, wv[k] + add1);
+              x1 = rms_elem_s17(get16i(raw[j], k + 1), rh, rl, 30 - e, wv[k + 1] + add1);
+            } else if (fast) {
               x0 = rms_elem32(get16i(raw[j], k), (int32_t)r, 30 - e, wv[k] + add1);
               x1 = rms_elem32(get16i(raw[j], k + 1), (int32_t)r, 30 - e, wv[k + 1] + add1);
             } else {
