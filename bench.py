@@ -7,7 +7,9 @@
 Workloads (seeded synthetic int4 weights with the 9B shapes):
   step         one full 32-layer fixed-point decode step + LM head + argmax
                (the reference's FxRunner.step, ref/fidelity_check.py:423-448)
-               at a context of --context tokens, replayed as one CUDA graph.
+               at a context of --context tokens: one persistent-kernel launch
+               per step (the default engine; the per-op CUDA-graph engine is
+               reported beside it).
   projections  all 249 projection matvecs of one step (4,091,805,696 B of
                W4 weights) with their fused epilogues.
 
@@ -17,7 +19,9 @@ line.  Under torchrun each rank holds a row shard of every matrix
 (ref/seq_format.py:1177-1189 split_rows) and outputs are all-gathered.
 
 ``--impl reference`` times the CPU oracle port (oracle/, the restatement of
-the reference's numpy law) on this host's cores over the same workload.
+the reference's numpy law) on all of this host's cores over the same
+workload (the reference itself is Python and does not travel to the GPU
+box).
 """
 from __future__ import annotations
 
@@ -134,22 +138,35 @@ def cpu_sample_projections(seconds=12.0, threads=0):
                       f"oracle matvec in {spent:.1f} s, scaled to one token"}
 
 
-def cpu_sample_step(seconds=20.0):
-    """Time the oracle's full decode step (numpy law + C matvec) on the first
-    4 layers of the 9B model for about `seconds` of greedy steps, plus one
-    LM-head matvec; scaled to one 32-layer token."""
+def cpu_sample_step(seconds=20.0, context=2048):
+    """Time the oracle's full decode step (numpy law + C matvec on all host
+    cores) on the first 4 layers of the 9B model (3 DeltaNet + 1 attention,
+    the model's layer mix) at `context` cached tokens, for about `seconds`
+    of greedy steps, plus one LM-head matvec; scaled to one 32-layer token.
+    The attention cache holds `context` seeded random int8 K/V rows (a
+    step's work does not depend on the cached values)."""
     import oracle as O
     from oracle.model import OracleModel
+    cores = os.cpu_count() or 1
+    O.set_threads(cores)
     t_build = time.time()
-    nl, max_T = 4, 2048
+    nl = 4
     geom = O.Geometry(n_layers=nl, vocab=8192)
     m = OracleModel(2026, geom)
-    r = O.OracleRunner(m, max_T=max_T)
+    r = O.OracleRunner(m, max_T=context + 256)
+    rng = np.random.default_rng(7)
+    for c, lt in zip(r.caches, geom.layer_types):
+        if lt == "full_attention":
+            c.k8[:, :context] = rng.integers(-127, 128, c.k8[:, :context].shape)
+            c.v8[:, :context] = rng.integers(-127, 128, c.v8[:, :context].shape)
+            c.ke[:, :context] = rng.integers(-8, 1, c.ke[:, :context].shape)
+            c.ve[:, :context] = rng.integers(-8, 1, c.ve[:, :context].shape)
+            c.T = context
     build_s = time.time() - t_build
     steps, spent, tok = 0, 0.0, 17
-    while spent < seconds and steps < max_T - 1:
+    while spent < seconds and steps < 255:
         t0 = time.perf_counter()
-        tok, _ = r.step(tok, steps)
+        tok, _ = r.step(tok, context + steps)
         spent += time.perf_counter() - t0
         steps += 1
     per_layer_step = spent / steps / nl
@@ -159,10 +176,11 @@ def cpu_sample_step(seconds=20.0):
     head_s = (time.perf_counter() - t0) * (248320 / m.head.N)
     full = per_layer_step * 32 + head_s
     return {"value": round(1.0 / full, 5), "unit": "tok/s", "cores": O.oracle_threads(), "kind": "port",
-            "sample": f"{steps} greedy decode steps (context 0..{steps - 1}) of the first {nl} layers "
-                      f"(3 DeltaNet + 1 attention) of the synthetic 9B model through the oracle "
-                      f"({spent:.1f} s; model build {build_s:.0f} s untimed), scaled to 32 layers, plus "
-                      f"one LM-head matvec scaled to 248,320 rows"}
+            "context": context,
+            "sample": f"{steps} greedy decode steps at context {context}..{context + steps - 1} of the first {nl} "
+                      f"layers (3 DeltaNet + 1 attention) of the synthetic 9B model through the oracle "
+                      f"({spent:.1f} s on {O.oracle_threads()} threads; model build {build_s:.0f} s untimed), "
+                      f"scaled to 32 layers, plus one LM-head matvec scaled to 248,320 rows"}
 
 
 # ---------------------------------------------------------------------------
@@ -201,8 +219,9 @@ def mega_traffic():
                     k, v = ln.split()
                     vals[k] = int(v)
         return {"dram_bytes_per_launch": vals["dram_read_bytes"] + vals["dram_write_bytes"],
-                "source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one k_mega launch, full 9B step "
-                          "(profiles/k_mega_decode_step_traffic.md)"}
+                "source": "read from the committed ncu capture, not measured in this run: "
+                          "dram__bytes_read.sum + dram__bytes_write.sum of one k_mega launch of the full 9B "
+                          "step at context 8 (profiles/k_mega_traffic.txt, profiles/k_mega_decode_step_traffic.md)"}
     except (OSError, ValueError, KeyError):
         return None
 
@@ -327,6 +346,7 @@ def run_step(args, ws, rank, local):
     # continue greedily from the argmax of the last prompt token
     m.prefill(np.random.default_rng(args.seed).integers(0, m.geom.vocab, ctx_len))
     tok, _ = m.sync()
+    prefill_tok = tok
     st = torch.cuda.ExternalStream(m.stream_handle())
     for _ in range(args.warmup):
         m.decode_launch(1)
@@ -354,8 +374,10 @@ def run_step(args, ws, rank, local):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
     tok = last_tok
+    e2e_toks = []
     for i in range(args.steps):
         tok, _ = m.decode_step(tok, pos + i)
+        e2e_toks.append(tok)
     e1.record(st)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
@@ -364,6 +386,20 @@ def run_step(args, ws, rank, local):
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
         e2e_ms = float(tt.item())
     engine = m.engine()
+    # greedy token chain: the argmax after the prompt, after the warm-up and
+    # timed device-fed steps, and every e2e step's token; each token depends
+    # on all earlier ones, so equal digests at 1/2/4/8 GPUs mean equal runs
+    chain = [int(prefill_tok), int(last_tok)] + [int(t) for t in e2e_toks]
+    import hashlib
+    token_digest = hashlib.sha256(np.asarray(chain, dtype=np.int64).tobytes()).hexdigest()[:16]
+    sat = m.stats()
+    if ws > 1:   # row shards: each rank saw the layer-output rows its epilogues own
+        import torch.distributed as tdist
+        mx = torch.tensor([sat["resid_max"]], dtype=torch.int64, device="cuda")
+        cl = torch.tensor([sat["resid_clip"]], dtype=torch.int64, device="cuda")
+        tdist.all_reduce(mx, op=tdist.ReduceOp.MAX)
+        tdist.all_reduce(cl, op=tdist.ReduceOp.SUM)
+        sat["resid_max"], sat["resid_clip"] = int(mx.item()), int(cl.item())
     # in-kernel phase decomposition of one persistent step (device globaltimer)
     phases = None
     if engine == "persistent":
@@ -390,7 +426,7 @@ def run_step(args, ws, rank, local):
                                              (bms * 1e-3) / 1e9, 1)}
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        cpu = cpu_sample_step(seconds=20.0)
+        cpu = cpu_sample_step(seconds=20.0, context=ctx_len)
     if rank == 0:
         toks = 1000.0 / ms   # one sequence, all N GPUs on every token
         step_gbs = WEIGHT_BYTES_9B / (ms * 1e-3) / 1e9
@@ -444,6 +480,13 @@ def run_step(args, ws, rank, local):
                     "d2h_bytes_per_step": 32},
             "gpu_launches": launches * args.steps,
             "clocks": ck, "context_tokens_after": T,
+            "tokens": {"after_prompt": chain[0], "after_timed": chain[1], "e2e": chain[2:],
+                       "digest": token_digest},
+            "saturation": {"dn_state_clipped": sat["dn_sat"], "resid_max": sat["resid_max"],
+                           "resid_clipped": sat["resid_clip"], "steps": T,
+                           "note": "cumulative over every step since reset (prompt, warm-up, timed, e2e); "
+                                   "FxRunner's resid_max / resid_clip (over all ranks' rows) and the "
+                                   "DeltaNet state's sat counter"},
         }
         if batched:
             line["batched_config5"] = {"per_B": batched, "context": 1024,
@@ -725,17 +768,20 @@ def run_reference(args):
     if rank != 0:
         return 0
     if args.workload == "projections":
+        import oracle as O
+        O.set_threads(os.cpu_count() or 1)
         cb = cpu_sample_projections(seconds=max(10.0, 3.0 * args.steps))
         metric = "9B W4A8 projection matvecs per token (token-equivalents/s)"
     else:
-        cb = cpu_sample_step(seconds=max(15.0, 4.0 * args.steps))
+        cb = cpu_sample_step(seconds=max(15.0, 4.0 * args.steps), context=args.context)
         metric = "9B W4A8 decode tok/s"
     line = {"impl": "reference", "metric": metric, "value": cb["value"], "unit": "tok/s",
             "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1000.0 / cb["value"], 3) if cb["value"] else None,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int64", "data": "synthetic (seeded int4 weights, 9B shapes)",
-            "config": {"workload": args.workload, "context": args.context},
+            "config": {"workload": args.workload, "context": args.context,
+                       "same_config": args.workload != "step" or cb.get("context") == args.context},
             "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)

@@ -217,6 +217,7 @@ int f5_matvec_y32_host(const uint8_t *img, int N, int K, int g, int sh, const in
   if (p) F5_TRY(cudaMemcpy(p, d_p, sizeof(int64_t) * N, cudaMemcpyDeviceToHost));
   F5_TRY(cudaMemcpy(&herr, d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost));
   if (herr & DERR_Y32_OVERFLOW) rc = set_error(F5_EOVERFLOW, "y32 overflow -- sh miscomputed (ref/w4a8_ref.py:288)");
+  else if (herr & DERR_TIMEOUT) rc = set_error(F5_ETIMEOUT, "a bounded device wait gave up");
 done:
 #undef F5_TRY
   if (e != cudaSuccess) rc = cuda_status(e, "f5_matvec_y32_host");

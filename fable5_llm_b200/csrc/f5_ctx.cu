@@ -438,6 +438,7 @@ static cudaError_t enqueue_layer(f5_ctx *c, int li, bool pdl) {
   p4.src = c->prod16;
   p4.in_f = RS_F;
   GemvSeg sd = mkseg(l.m[10], c->x16, GM_RESID, RS_F);
+  sd.rstat = c->stats + 1;   // the layer output: FxRunner's resid_max / resid_clip
   return gemv(c, &sd, 1, FFN, p4, nullptr, pdl);
 }
 
@@ -751,7 +752,7 @@ int f5_ctx_create(const f5_config *cfg, int device, f5_ctx **out) {
       (rc = alloc(c, (void **)&c->prod16, FFN * 2)) || (rc = alloc(c, (void **)&c->prod64, NQ * HD * 8)) ||
       (rc = alloc(c, (void **)&c->x8, FFN)) || (rc = alloc(c, (void **)&c->xmeta, 16)) ||
       (rc = alloc(c, (void **)&c->qkvc16, CONV_DIM * 2)) || (rc = alloc(c, (void **)&c->gates, 2 * LNH * 4)) ||
-      (rc = alloc(c, (void **)&c->key, 8)) || (rc = alloc(c, (void **)&c->stats, 8)) ||
+      (rc = alloc(c, (void **)&c->key, 8)) || (rc = alloc(c, (void **)&c->stats, 4 * 8)) ||
       (rc = alloc(c, (void **)&c->err, 4)) || (rc = alloc(c, (void **)&c->params, sizeof(StepParams))))
     return fail(rc);
   if ((rc = cuda_status(cudaMallocHost(&c->h_params, sizeof(StepParams)), "cudaMallocHost"))) return fail(rc);
@@ -896,7 +897,7 @@ int f5_ctx_reset(f5_ctx *c) {
   F5_CU(cudaMemsetAsync(c->params, 0, sizeof(StepParams), c->st), "reset");
   if (c->twin_mem) F5_CU(cudaMemsetAsync(c->twin_mem, 0, c->twin_bytes, c->st), "reset");
   F5_CU(cudaMemsetAsync(c->err, 0, 4, c->st), "reset");
-  F5_CU(cudaMemsetAsync(c->stats, 0, 8, c->st), "reset");
+  F5_CU(cudaMemsetAsync(c->stats, 0, 4 * 8, c->st), "reset");
   F5_CU(cudaStreamSynchronize(c->st), "reset");
   return F5_OK;
 }
@@ -1207,7 +1208,7 @@ int f5_ctx_read(f5_ctx *c, int what, int layer, void *dst, size_t bytes) {
     case F5_BUF_V16: src = c->v16; n = NKV * HD * 2; break;
     case F5_BUF_PROD64: src = c->prod64; n = NQ * HD * 8; break;
     case F5_BUF_PROD16: src = c->prod16; n = FFN * 2; break;
-    case F5_BUF_STATS: src = c->stats; n = 8; break;
+    case F5_BUF_STATS: src = c->stats; n = 4 * 8; break;
     case F5_BUF_DN_S: if (l && !l->attn) { src = l->S; n = (size_t)LNH * LDK * LDV * 2; } break;
     case F5_BUF_DN_CONV: if (l && !l->attn) { src = l->conv; n = (size_t)CONV_DIM * 4 * 2; } break;
     case F5_BUF_DN_KH: if (l && !l->attn) { src = l->kh; n = LNH * 4; } break;

@@ -179,6 +179,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1) k_gemv(const __grid_constant__ 
 
   // ---- deferred epilogues: one unit per consumer thread ----
   unsigned long long best = 0ull;
+  RStat rs;
   for (int i = tid; i < u1 - u0; i += GT_CTHREADS) {
     const int u = u0 + i;
     const GemvSeg &sg = a.seg[seg_of(a, u)];
@@ -186,9 +187,10 @@ __global__ void __launch_bounds__(GT_THREADS, 1) k_gemv(const __grid_constant__ 
     if (sg.mode == GM_SILU_MUL) {
       epilogue_pair(a, sg, row, s_res[2 * i], s_res[2 * i + 1], e_x, in_f);
     } else {
-      epilogue_row(a, sg, row, s_res[i], e_x, in_f, best);
+      epilogue_row(a, sg, row, s_res[i], e_x, in_f, best, 0, sg.rstat ? &rs : nullptr);
     }
   }
+  if (a.nseg == 1 && a.seg[0].rstat) rstat_flush(a.seg[0].rstat, rs);
   if (a.argmax_key) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) {

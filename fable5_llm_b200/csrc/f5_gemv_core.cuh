@@ -489,8 +489,28 @@ F5_DEV int32_t decay_gate(long long v, int32_t dt_bias, int32_t A) {
   const long long dec = rshr(exp_neg_q(g < 0 ? g : 0), 15);
   return (int32_t)(dec > 32767 ? 32767 : dec);
 }
+// Per-thread residual statistics of GM_RESID outputs (GemvSeg::rstat),
+// folded into the global words once per warp by rstat_flush.
+struct RStat {
+  unsigned mx = 0u, n = 0u;
+  F5_DEV void add(int32_t v) {
+    const unsigned m = (unsigned)(v < 0 ? -v : v);
+    mx = m > mx ? m : mx;
+    n += (v >= 32767 || v <= -32768) ? 1u : 0u;
+  }
+};
+// every lane of the warp calls it (lanes without rows contribute zeros)
+F5_DEV void rstat_flush(unsigned long long *p, const RStat &s) {
+  const unsigned mx = __reduce_max_sync(0xffffffffu, s.mx);
+  const unsigned n = __reduce_add_sync(0xffffffffu, s.n);
+  if ((threadIdx.x & 31) == 0) {
+    if (mx) atomicMax(p, (unsigned long long)mx);
+    if (n) atomicAdd(p + 1, (unsigned long long)n);
+  }
+}
+
 F5_DEV void epilogue_row(const GemvArgs &a, const GemvSeg &sg, int row, long long acc16, int e_x,
-                         int in_f, unsigned long long &best, uint32_t epoch = 0) {
+                         int in_f, unsigned long long &best, uint32_t epoch = 0, RStat *rs = nullptr) {
   long long pex;
   const int32_t y = finish_y32(acc16, a.sh, a.err, &pex);
   const int orow = sg.out_row0 + row;
@@ -511,15 +531,19 @@ F5_DEV void epilogue_row(const GemvArgs &a, const GemvSeg &sg, int row, long lon
       else static_cast<int16_t *>(sg.out)[orow] = (int16_t)v;
     } break;
     case GM_TO64: static_cast<int64_t *>(sg.out)[orow] = shift_to(y, sh2); break;
-    case GM_RESID:
+    case GM_RESID: {
+      int32_t nv;
       if (tag) {   // the row's previous word was written by this CTA (same row partition)
         uint32_t *o = static_cast<uint32_t *>(sg.out) + orow;
-        st_tagged(a, o, tag_word(tag, clip16((int64_t)tag_s16(__ldcg(o)) + clip16(shift_to(y, sh2)))));
+        nv = clip16((int64_t)tag_s16(__ldcg(o)) + clip16(shift_to(y, sh2)));
+        st_tagged(a, o, tag_word(tag, nv));
       } else {
         int16_t *o = static_cast<int16_t *>(sg.out) + orow;   // written by other CTAs: read at L2
-        *o = (int16_t)clip16((int64_t)__ldcg(o) + clip16(shift_to(y, sh2)));
+        nv = clip16((int64_t)__ldcg(o) + clip16(shift_to(y, sh2)));
+        *o = (int16_t)nv;
       }
-      break;
+      if (rs) rs->add(nv);
+    } break;
     case GM_CONV: {   // ref/layer_fixed.py:1511-1520 for channel orow
       const long long v = clip16(shift_to(y, sh2));
       if (sg.out) static_cast<int16_t *>(sg.out)[orow] = (int16_t)v;

@@ -105,6 +105,11 @@ struct GemvSeg {
   const int *T;       // GM_CONV: tokens already in the window (ring slot T % 4)
   int tag_op1;        // 0: plain outputs; else tagged words from op tag_op1 - 1 (TO16, RESID,
                       // SILU_MUL: out; CONV, GATE_*: aux_out, and out is skipped when null)
+  // optional (GM_RESID): residual statistics of the layer output, the
+  // reference's FxRunner.resid_max / resid_clip (ref/fidelity_check.py:
+  // 430-431): rstat[0] = max |out| (atomicMax), rstat[1] += the outputs at
+  // the int16 rails (out >= 32767 or out <= -32768)
+  unsigned long long *rstat;
 };
 
 struct GemvArgs {

@@ -434,18 +434,19 @@ F5_DEV void epi_prefetch(const GemvArgs &a, int uu) {
 // back to mg_xres (the CTA wrote them last: BEGIN and every residual op use
 // the same 4096-row partition); everything else is the shared epilogue_row.
 F5_DEV void mega_epilogue_row(const GemvArgs &a, const GemvSeg &sg, int i, int uu, long long acc, int e_x, int in_f,
-                              uint32_t epoch) {
+                              uint32_t epoch, RStat &rs) {
   const int row = uu - sg.unit_begin, orow = sg.out_row0 + row;
   const uint32_t tag = (epoch && sg.tag_op1) ? mk_tag(epoch, sg.tag_op1) : 0u;
   if (!(sg.mode == GM_RESID && tag && i < MG_XRES)) {
     unsigned long long unused = 0ull;
-    epilogue_row(a, sg, row, acc, e_x, in_f, unused, epoch);
+    epilogue_row(a, sg, row, acc, e_x, in_f, unused, epoch, sg.rstat ? &rs : nullptr);
     return;
   }
   const int32_t y = finish_y32(acc, a.sh, a.err, nullptr);
   const long long v = clip16(shift_to(y, (15 - sg.e - a.sh) - e_x + in_f - sg.out_f));
   const int32_t nv = clip16((int64_t)mg_xres[i] + v);
   mg_xres[i] = (int16_t)nv;
+  if (sg.rstat) rs.add(nv);
   st_tagged(a, static_cast<uint32_t *>(sg.out) + orow, tag_word(tag, nv));
 }
 // K = 4096 (every GEMV of the step but the MLP down projection): one row per
@@ -537,12 +538,14 @@ F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const 
     if (lane == 0 && best) atomicMax(a.argmax_key, best);
     return true;
   }
+  RStat rs;
   for (int i = tid; i < u1 - u0; i += MG_CT) {
     const int uu = u0 + i;
     const GemvSeg &sg = a.seg[seg_of(a, uu)];
     if (sg.mode == GM_SILU_MUL) epilogue_pair(a, sg, uu - sg.unit_begin, res[2 * i], res[2 * i + 1], e_x, in_f, epoch);
-    else mega_epilogue_row(a, sg, i, uu, res[i], e_x, in_f, epoch);
+    else mega_epilogue_row(a, sg, i, uu, res[i], e_x, in_f, epoch, rs);
   }
+  if (a.nseg == 1 && a.seg[0].rstat) rstat_flush(a.seg[0].rstat, rs);
   return true;
 }
 
@@ -597,6 +600,7 @@ F5_DEV bool c_gemv_split(const GemvArgs &a, const MegaSmem &S, RingPos &rp, cons
   }
   if (sy.any(bad)) return false;
   MG_MARK(3);
+  RStat rs;
   for (int i = tid; i < u1 - u0; i += MG_CT) {
     const int uu = u0 + i;
     const GemvSeg &sg = a.seg[seg_of(a, uu)];
@@ -604,9 +608,10 @@ F5_DEV bool c_gemv_split(const GemvArgs &a, const MegaSmem &S, RingPos &rp, cons
 #pragma unroll
     for (int p = 0; p < NP; ++p) acc += S.res()[NP * i + p];
     if (i == 0) MG_MARK(4);
-    mega_epilogue_row(a, sg, i, uu, acc, e_x, in_f, epoch);
+    mega_epilogue_row(a, sg, i, uu, acc, e_x, in_f, epoch, rs);
     if (i == 0) MG_MARK(5);
   }
+  if (a.nseg == 1 && a.seg[0].rstat) rstat_flush(a.seg[0].rstat, rs);
   return true;
 }
 

@@ -1,15 +1,15 @@
 // f5_matvec_y32_host_noalloc: the host-buffer matvec without any device
 // allocation.
 //
-// Who needs it: callers that must not call cudaMalloc -- a process that is
-// capturing some stream into a CUDA graph at the time (an allocation in the
-// middle of a capture breaks it), a host whose device memory is owned
-// entirely by another allocator (a framework's caching pool or a fixed
-// arena), and latency-critical loops that cannot take the device-wide
-// synchronisation cudaMalloc / cudaFree imply.  f5_matvec_y32_host allocates
-// and frees its device buffers on every call; this variant stages the image,
-// x8, y32, p and the error word in one fixed array that the library reserves
-// in device memory, so a call only copies and launches.
+// Who needs it: callers that must not call cudaMalloc -- a host whose device
+// memory is owned entirely by another allocator (a framework's caching pool
+// or a fixed arena that has already reserved the GPU's memory, so a
+// cudaMalloc beside it fails or fragments that pool), and latency-critical
+// loops that cannot take the device-wide synchronisation cudaMalloc /
+// cudaFree imply.  f5_matvec_y32_host allocates and frees its device buffers
+// on every call; this variant stages the image, x8, y32, p and the error word
+// in one fixed array that the library reserves in device memory, so a call
+// only copies and launches.
 //
 // Contract:
 //   - the array is F5_NOALLOC_SCRATCH_BYTES (16 MiB); every GPU that loads

@@ -10,13 +10,13 @@ the reference mutates them.  Like the reference's module-global
 ``SEQ_NORM`` (False: float64 host scale; True: integer EPS-NORM).
 
 ``layer_decode_fx`` runs one layer through a single-layer GPU context that
-is cached per quantized dict; the cache state is uploaded before and read
-back after every call, so this entry point is for parity and drop-in use --
-the production path is ``fable5_llm_b200.model.DecodeModel.decode_step``.
+is cached per layer dict (at most ``MAX_LAYER_CTX`` of them, least recently
+used evicted; ``release_layer`` / ``clear_layer_cache`` free them); the
+cache state is uploaded before and read back after every call, so this
+entry point is for parity and drop-in use -- the production path is
+``fable5_llm_b200.model.DecodeModel.decode_step``.
 """
 from __future__ import annotations
-
-import weakref
 
 import numpy as np
 
@@ -125,12 +125,49 @@ def new_cache_fx(layer_type):
             "S": np.zeros((g.LNH, g.LDK, g.LDV), dtype=np.int16)}
 
 
-_CTX = weakref.WeakKeyDictionary() if False else {}
+# GPU contexts of the layer dicts seen by layer_decode_fx, most recently used
+# last.  Each entry holds the dict itself and every array it was uploaded
+# from, so a cached id can never be handed to another dict (the dict stays
+# alive while cached) and a matrix or vector replaced inside the dict is seen
+# as a change.  Arrays modified in place are not detected: call
+# release_layer(qw) (or clear_layer_cache()) after editing one.
+_CTX = {}
+MAX_LAYER_CTX = 40
+
+
+def _leaves(qw):
+    """(path, value) of every array and scalar of a layer dict, in a fixed order."""
+    out = []
+
+    def walk(p, v):
+        if isinstance(v, dict):
+            for k in sorted(v):
+                walk(p + (k,), v[k])
+        else:
+            out.append((p, v))
+    walk((), qw)
+    return out
+
+
+def _same_leaves(a, b):
+    if len(a) != len(b):
+        return False
+    for (pa, va), (pb, vb) in zip(a, b):
+        if pa != pb:
+            return False
+        if isinstance(va, np.ndarray) or isinstance(vb, np.ndarray):
+            if va is not vb:
+                return False
+        elif type(va) is not type(vb) or va != vb:
+            return False
+    return True
 
 
 class _LayerCtx:
     def __init__(self, qw, max_T):
         from .model import DecodeModel
+        self.qw = qw
+        self.leaves = _leaves(qw)
         self.type = qw["type"]
         self.max_T = max_T
         self.mode = SEQ_NORM
@@ -138,14 +175,37 @@ class _LayerCtx:
                              norm_mode="eps" if SEQ_NORM else "float", max_pos=max(max_T, 4096))
         self.m.upload_layer(0, qw)
 
+    def close(self):
+        self.m.close()
+
+
+def release_layer(qw):
+    """Free the GPU context that layer_decode_fx holds for this dict."""
+    c = _CTX.pop(id(qw), None)
+    if c is not None:
+        c.close()
+
+
+def clear_layer_cache():
+    """Free every GPU context that layer_decode_fx holds."""
+    for c in list(_CTX.values()):
+        c.close()
+    _CTX.clear()
+
 
 def _layer_ctx(qw, T):
     key = id(qw)
-    c = _CTX.get(key)
+    c = _CTX.pop(key, None)
     need = max(64, 1 << (T + 1).bit_length())
-    if c is None or c.max_T < T + 1 or c.mode != SEQ_NORM or c.type != qw["type"]:
+    if c is not None and (c.qw is not qw or c.max_T < T + 1 or c.mode != SEQ_NORM or c.type != qw["type"]
+                          or not _same_leaves(c.leaves, _leaves(qw))):
+        c.close()
+        c = None
+    if c is None:
+        while len(_CTX) >= MAX_LAYER_CTX:
+            _CTX.pop(next(iter(_CTX))).close()
         c = _LayerCtx(qw, need)
-        _CTX[key] = c
+    _CTX[key] = c
     return c
 
 

@@ -3,7 +3,8 @@
 ``DecodeModel`` owns an ``f5_ctx`` (include/f5b200.h): the integer
 Qwen3.5-9B weights in HBM in the reference's packed row format, the decode
 state (int8 KV caches, DeltaNet conv windows and int16 states) and the
-decode step recorded as one CUDA graph.  All compute is in the CUDA
+decode step (one persistent cooperative launch per token by default, or
+the per-op kernel chain replayed as a CUDA graph).  All compute is in the CUDA
 library; this module only moves parameters and results.
 """
 from __future__ import annotations
@@ -284,7 +285,7 @@ class DecodeModel:
                  L.BUF_B16: (g.LNH, np.int16), L.BUF_A16: (g.LNH, np.int16), L.BUF_ON16: (g.LVD, np.int16),
                  L.BUF_QG16: (g.NQ * g.HD * 2, np.int16), L.BUF_K16: (g.NKV * g.HD, np.int16),
                  L.BUF_V16: (g.NKV * g.HD, np.int16), L.BUF_PROD64: (g.NQ * g.HD, I64),
-                 L.BUF_PROD16: (g.FFN, np.int16), L.BUF_STATS: (1, np.uint64),
+                 L.BUF_PROD16: (g.FFN, np.int16), L.BUF_STATS: (4, np.uint64),
                  L.BUF_DN_S: (g.LNH * g.LDK * g.LDV, np.int16), L.BUF_DN_CONV: (g.CONV_DIM * 4, np.int16),
                  L.BUF_DN_KH: (g.LNH, np.int32), L.BUF_K8: (g.NKV * self.max_T * g.HD, np.int8),
                  L.BUF_KE: (g.NKV * self.max_T, np.int8), L.BUF_V8: (g.NKV * self.max_T * g.HD, np.int8),
@@ -302,6 +303,15 @@ class DecodeModel:
 
     def logits(self):
         return self.read(L.BUF_LOGITS)
+
+    def stats(self):
+        """Saturation counters since the last reset: the DeltaNet state
+        writes clipped to int16 (the reference's state["sat"] summed over
+        layers), and max |x| / the count of rail values over every layer
+        output (FxRunner.resid_max / resid_clip, ref/fidelity_check.py:
+        416-433)."""
+        s = self.read(L.BUF_STATS)
+        return {"dn_sat": int(s[0]), "resid_max": int(s[1]), "resid_clip": int(s[2])}
 
     # ---- TOPK-32 capture and sampling (sw/chat_seq.py:1776-1928) ----
     def head_logit_exp0(self):

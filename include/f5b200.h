@@ -154,9 +154,9 @@ int f5_matvec_y32_host(const uint8_t *img, int N, int K, int g, int sh,
                        const int8_t *x8, int32_t *y32, int64_t *p);
 
 /* Allocation-free form of f5_matvec_y32_host, for callers that cannot call
- * cudaMalloc (a process capturing a stream into a CUDA graph at the time, a
- * host whose device memory belongs to another allocator, a loop that cannot
- * take cudaMalloc/cudaFree's device synchronisation).  No counterpart in the
+ * cudaMalloc (a host whose device memory belongs to another allocator's
+ * pool or arena, a loop that cannot take cudaMalloc/cudaFree's device
+ * synchronisation).  No counterpart in the
  * reference: it is an extra deployment form of the matvec_y32 drop-in.
  * Stages everything in one fixed device array of F5_NOALLOC_SCRATCH_BYTES
  * that every GPU loading the library holds until exit; larger requests fail
@@ -203,7 +203,12 @@ enum f5_vec { F5_VEC_LN1 = 0, F5_VEC_LN2 = 1, F5_VEC_Q_NORM = 2, F5_VEC_K_NORM =
 /* device buffers readable with f5_ctx_read (debug taps and state) */
 enum f5_buf { F5_BUF_X16 = 0, F5_BUF_QKV16 = 1, F5_BUF_Z16 = 2, F5_BUF_B16 = 3, F5_BUF_A16 = 4,
               F5_BUF_ON16 = 5, F5_BUF_QG16 = 6, F5_BUF_K16 = 7, F5_BUF_V16 = 8,
-              F5_BUF_PROD64 = 9, F5_BUF_PROD16 = 10, F5_BUF_STATS = 11,
+              F5_BUF_PROD64 = 9, F5_BUF_PROD16 = 10,
+              F5_BUF_STATS = 11 /* uint64 [4], cumulative since f5_ctx_reset: [0] DeltaNet state
+                                   writes clipped to int16 (the reference's state["sat"],
+                                   ref/layer_fixed.py:1551,1569), [1] max |x| of every layer
+                                   output, [2] layer-output words at the int16 rails (FxRunner
+                                   resid_max / resid_clip, ref/fidelity_check.py:430-431), [3] 0 */,
               F5_BUF_DN_S = 12 /* int16 [32 heads][4][128 dk][32]: dv = 32 * quarter + i */, F5_BUF_DN_CONV = 13 /* int16 [8192][4] ring */,
               F5_BUF_DN_KH = 14, F5_BUF_K8 = 15, F5_BUF_KE = 16, F5_BUF_V8 = 17, F5_BUF_VE = 18,
               F5_BUF_KA = 19, F5_BUF_LOGITS = 20 /* int32 [vocab], see f5_ctx_set_logits */,

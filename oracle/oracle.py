@@ -358,8 +358,19 @@ def _clib():
     return _CLIB
 
 
+_THREADS = 0   # 0: the OpenMP default (OMP_NUM_THREADS)
+
+
+def set_threads(n):
+    """Thread count of every later C matvec (0: the OpenMP default).  A
+    launcher such as torchrun sets OMP_NUM_THREADS=1; a CPU baseline that
+    wants the host's cores sets them here explicitly."""
+    global _THREADS
+    _THREADS = max(0, int(n))
+
+
 def oracle_threads():
-    return int(_clib().f5o_num_threads())
+    return _THREADS if _THREADS > 0 else int(_clib().f5o_num_threads())
 
 
 def matvec_img(img, N, K, sh, x8, g=G, want_p=False, threads=0):
@@ -374,7 +385,7 @@ def matvec_img(img, N, K, sh, x8, g=G, want_p=False, threads=0):
     p = np.empty(N, dtype=I64) if want_p else None
     rc = _clib().f5o_matvec_rows(
         img.ctypes.data, stride, N, K, g, x8.ctypes.data, int(sh),
-        y.ctypes.data, p.ctypes.data if p is not None else None, int(threads))
+        y.ctypes.data, p.ctypes.data if p is not None else None, int(threads) if threads > 0 else _THREADS)
     if rc != 0:
         raise AssertionError(f"oracle matvec overflow assertion (rc={rc})")
     return (y, p) if want_p else y
@@ -744,6 +755,7 @@ class OracleRunner:
         self.caches = [AttnCache(self.max_T, self.geom) if t == "full_attention"
                        else DNCache(self.geom) for t in self.geom.layer_types]
         self.layer_out = []
+        self.resid_max = 0
         self.resid_clip = 0
 
     def step_logits(self, tok, pos):
@@ -753,7 +765,8 @@ class OracleRunner:
         for i, qw in enumerate(m.layers):
             x = layer_decode_fx(x, qw, self.caches[i], pos, self.geom, self.norm_mode)
             self.layer_out.append(x.copy())
-            self.resid_clip += int(((x >= 32767) | (x <= -32768)).sum())
+            self.resid_max = max(self.resid_max, int(np.abs(x).max()))      # ref/fidelity_check.py:430
+            self.resid_clip += int(((x >= 32767) | (x <= -32768)).sum())   # :431
         xn = rmsnorm_fx(x, m.ln_f_q12, RS_F, False)
         x8, _ = dyn_quant_i8(xn)
         h = m.head

@@ -1,8 +1,8 @@
 #!/usr/bin/env python3
 """Generate the weight-artifact fixtures with the UNMODIFIED reference writer.
 
-Run in a container that has the reference checkout (default
-``/root/reference``; override with F5_REFERENCE); the GPU box never runs it.
+Run where the reference checkout exists, with the environment variable
+F5_REFERENCE set to its root directory; the GPU box never runs it.
 It registers a few small seeded W4 matrices (g = 128 and g = 64, K = 256 ..
 4096) on the reference's ``Mach`` and calls its ``dump_weights``
 (ref/gen_layer_script.py:1555-1670) with ``emb_row_bytes`` and ``rs_f`` as
@@ -22,7 +22,9 @@ import sys
 
 import numpy as np
 
-REF = os.environ.get("F5_REFERENCE", "/root/reference")
+REF = os.environ.get("F5_REFERENCE")
+if not REF or not os.path.isdir(os.path.join(REF, "ref")):
+    sys.exit("set F5_REFERENCE to the root of the reference checkout (the directory holding ref/)")
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "artifact")
 os.environ["FABLE5_MODEL"] = "9b"

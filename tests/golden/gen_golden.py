@@ -1,8 +1,8 @@
 #!/usr/bin/env python3
 """Generate the committed golden fixtures from the UNMODIFIED reference.
 
-Run in a container that has the reference checkout (default
-``/root/reference``; override with F5_REFERENCE); the GPU box never runs it.
+Run where the reference checkout exists, with the environment variable
+F5_REFERENCE set to its root directory; the GPU box never runs it.
 It reads the reference's own committed golden vectors (tb/vec_s1..s4 matvec
 vectors, tb/vectors/s1..s4 unit-block vectors, the LUT ROM images) and runs
 the reference's Python model (ref/w4a8_ref.py, ref/fixedpoint.py,
@@ -10,7 +10,8 @@ ref/layer_fixed.py) with FABLE5_MODEL=9b on seeded inputs, storing inputs and
 outputs as small .npz files next to this script.
 
     python tests/golden/gen_golden.py            # unit + layer + reduced model
-    python tests/golden/gen_golden.py --full     # + full 32-layer 9B model step
+    python tests/golden/gen_golden.py --full     # + full 32-layer 9B model steps
+    python tests/golden/gen_golden.py --only model32   # only those
 
 Large exhaustive domains (e.g. silu over the whole 21-bit port) are stored as
 sha256 digests of the int64 output plus a strided sample.
@@ -25,7 +26,9 @@ import time
 
 import numpy as np
 
-REF = os.environ.get("F5_REFERENCE", "/root/reference")
+REF = os.environ.get("F5_REFERENCE")
+if not REF or not os.path.isdir(os.path.join(REF, "ref")):
+    sys.exit("set F5_REFERENCE to the root of the reference checkout (the directory holding ref/)")
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 os.environ["FABLE5_MODEL"] = "9b"
@@ -324,17 +327,20 @@ def run_model(g, toks, tag):
             f"{tag}_ymax": np.array(ymax, dtype=I64), f"{tag}_layer_x": np.stack(layer_x)}
 
 
-def gen_model(full=False):
-    out = {}
+def gen_model():
     g = Geom(4, 4096)
-    out.update(run_model(g, [17, 901, 4000, 3, 17, 256], "m4"))
+    out = run_model(g, [17, 901, 4000, 3, 17, 256], "m4")
     np.savez_compressed(os.path.join(HERE, "ref_model4.npz"), **out)
     print("ref_model4.npz")
-    if full:
-        g = Geom(32, 248320)
-        out = run_model(g, [1234, 248319], "m32")
-        np.savez_compressed(os.path.join(HERE, "ref_model32.npz"), **out)
-        print("ref_model32.npz")
+
+
+def gen_model32():
+    """The full 32-layer 9B model with the 248,320-row head for three host
+    tokens (about four minutes per step through the reference)."""
+    g = Geom(32, 248320)
+    out = run_model(g, [1234, 248319, 77], "m32")
+    np.savez_compressed(os.path.join(HERE, "ref_model32.npz"), **out)
+    print("ref_model32.npz")
 
 
 def main():
@@ -342,7 +348,7 @@ def main():
     ap.add_argument("--full", action="store_true")
     ap.add_argument("--only", default="")
     a = ap.parse_args()
-    parts = a.only.split(",") if a.only else ["tb", "prims", "layers", "model"]
+    parts = a.only.split(",") if a.only else ["tb", "prims", "layers", "model"] + (["model32"] if a.full else [])
     if "tb" in parts:
         gen_tb_matvec()
         gen_tb_layer()
@@ -351,7 +357,9 @@ def main():
     if "layers" in parts:
         gen_layers()
     if "model" in parts:
-        gen_model(a.full)
+        gen_model()
+    if "model32" in parts:
+        gen_model32()
 
 
 if __name__ == "__main__":

@@ -3,8 +3,8 @@
 generator (``tb/scripts/gen_topk_cases.py``, the numpy reference of the
 RUNG-4 TOPK-32 block).
 
-Run in a container that has the reference checkout (default
-``/root/reference``; override with F5_REFERENCE); the GPU box never runs it.
+Run where the reference checkout exists, with the environment variable
+F5_REFERENCE set to its root directory; the GPU box never runs it.
 The reference script is run as a subprocess with a fixed seed and writes its
 own text format (``topk_cases.txt``: per case a header line ``name nwords
 ncmds count count ovf_lit ovf_disp am_idx am_val(hex) nelem``, the scratch
@@ -23,7 +23,9 @@ import tempfile
 
 import numpy as np
 
-REF = os.environ.get("F5_REFERENCE", "/root/reference")
+REF = os.environ.get("F5_REFERENCE")
+if not REF or not os.path.isdir(os.path.join(REF, "ref")):
+    sys.exit("set F5_REFERENCE to the root of the reference checkout (the directory holding ref/)")
 HERE = os.path.dirname(os.path.abspath(__file__))
 SEED = 20261202
 

@@ -55,6 +55,7 @@ def test_dn_layer_vs_reference(golden, model4, model4_eps, mode):
     st = m.get_dn_state(0, T)
     assert digest(st["S"]) == str(d[f"dn_{mode}_S_digest"])
     assert np.array_equal(st["conv"], d[f"dn_{mode}_conv"])
+    assert m.stats()["dn_sat"] == int(d[f"dn_{mode}_sat"])   # the reference's state["sat"]
 
 
 def test_attn_layer_vs_reference(golden, model4):

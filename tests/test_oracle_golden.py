@@ -1,6 +1,7 @@
 """Pin the CPU oracle against the reference's own golden vectors and against
 outputs of the unmodified reference (tests/golden/gen_golden.py)."""
 import hashlib
+import os
 
 import numpy as np
 import pytest
@@ -226,3 +227,23 @@ def test_oracle_model4_vs_reference(golden, oracle_model4):
         assert nt == int(d["m4_out"][t]) and int(y.max()) == int(d["m4_ymax"][t])
         for i, x in enumerate(r.layer_out):
             assert np.array_equal(x, d["m4_layer_x"][t][i].astype(I64)), (t, i)
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden",
+                                                    "ref_model32.npz")), reason="no ref_model32 fixture")
+def test_oracle_model32_vs_reference(golden):
+    """The full 32-layer 9B model with the 248,320-row head: the unmodified
+    reference's FxRunner-sequence run (three steps from context 0) pins the
+    oracle's tokens, max logits, every layer's output and the residual
+    saturation counters (ref/fidelity_check.py:416-433)."""
+    from oracle.model import OracleModel
+    d = golden("ref_model32")
+    r = O.OracleRunner(OracleModel(2026, O.GEOM_9B), max_T=8)
+    for t, tok in enumerate(d["m32_in"]):
+        nt, y = r.step(int(tok), t)
+        assert nt == int(d["m32_out"][t]) and int(y.max()) == int(d["m32_ymax"][t])
+        for i, x in enumerate(r.layer_out):
+            assert np.array_equal(x, d["m32_layer_x"][t][i].astype(I64)), (t, i)
+    x = d["m32_layer_x"].astype(I64)
+    assert r.resid_max == int(np.abs(x).max())
+    assert r.resid_clip == int(((x >= 32767) | (x <= -32768)).sum())

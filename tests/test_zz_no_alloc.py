@@ -1,9 +1,8 @@
 """The allocation-free matvec entry point.
 
-f5_matvec_y32_host_noalloc serves callers that cannot call cudaMalloc (a
-process capturing a stream into a CUDA graph at the time, device memory
-owned by another allocator, loops that cannot take the synchronisation of
-cudaMalloc/cudaFree).  It stages its buffers in one fixed device array the
+f5_matvec_y32_host_noalloc serves callers that cannot call cudaMalloc
+(device memory owned by another allocator's pool or arena, loops that cannot
+take the device synchronisation of cudaMalloc/cudaFree).  It stages its buffers in one fixed device array the
 library reserves at load time.  This test calls it through the C ABI twice
 in a row with different inputs and requires exactly the results of the
 allocating entry point f5_matvec_y32_host (bit-exact: the integer law has no
