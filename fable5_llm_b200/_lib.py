@@ -104,6 +104,9 @@ SIGNATURES = [
     ("f5_ctx_sync", c_int, [c_vp, c_vp, c_vp]),
     ("f5_ctx_time_step", c_int, [c_vp, c_int, c_vp, c_int]),
     ("f5_layer_step", c_int, [c_vp, c_int, c_vp, c_int, c_int]),
+    ("f5_state_bytes", c_size, [c_vp, c_int, c_int]),
+    ("f5_state_save", c_int, [c_vp, c_int, c_vp, c_size]),
+    ("f5_state_load", c_int, [c_vp, c_int, c_vp, c_size, c_int]),
     ("f5_ctx_read", c_int, [c_vp, c_int, c_int, c_vp, c_size]),
     ("f5_ctx_write", c_int, [c_vp, c_int, c_int, c_vp, c_size]),
 ]

@@ -1255,3 +1255,127 @@ int f5_ctx_write(f5_ctx *c, int what, int layer, const void *src, size_t bytes) 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Reference-layout state images (ref/layer_fixed.py:1654-1666 new_cache_fx,
+// the caches the reference's layer_decode_fx mutates).  DeltaNet layer:
+// S int16 [LNH][LDK][LDV] then the conv window int64 [CONV_DIM][3], oldest
+// first; attention layer at T tokens: k8 int8 [T][NKV][HD], ke int8
+// [T][NKV], v8 int8 [T][NKV][HD], ve int8 [T][NKV] -- the reference's
+// cache["k"][t][h] = (k8, ke) lists flattened in that order.
+// ---------------------------------------------------------------------------
+namespace {
+size_t state_bytes_of(const f5_ctx *c, int layer, int T) {
+  if (layer < 0 || layer >= (int)c->L.size() || T < 0) return 0;
+  if (!c->L[layer].attn) return (size_t)LNH * LDK * LDV * 2 + (size_t)CONV_DIM * 3 * 8;
+  return (size_t)T * NKV * (HD + 1) * 2;
+}
+}  // namespace
+
+size_t f5_state_bytes(f5_ctx *c, int layer, int T) {
+  if (!c) return 0;
+  return state_bytes_of(c, layer, T);
+}
+
+int f5_state_save(f5_ctx *c, int layer, void *dst, size_t bytes) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  if (!dst) return set_error(F5_EINVAL, "f5_state_save: null destination");
+  if (layer < 0 || layer >= (int)c->L.size()) return set_error(F5_EINVAL, "f5_state_save: layer %d", layer);
+  DevGuard dg(c->device);
+  F5_CU(cudaMemcpyAsync(c->h_params, c->params, sizeof(StepParams), cudaMemcpyDeviceToHost, c->st), "f5_state_save");
+  F5_CU(cudaStreamSynchronize(c->st), "f5_state_save");
+  const int T = c->h_params->T;
+  const size_t need = state_bytes_of(c, layer, T);
+  if (bytes != need) return set_error(F5_EINVAL, "f5_state_save: layer %d at T=%d needs %zu bytes, got %zu", layer, T, need, bytes);
+  const Layer &l = c->L[layer];
+  uint8_t *out = static_cast<uint8_t *>(dst);
+  if (!l.attn) {
+    std::vector<int16_t> S((size_t)LNH * LDK * LDV), ring((size_t)CONV_DIM * 4);
+    F5_CU(cudaMemcpyAsync(S.data(), l.S, S.size() * 2, cudaMemcpyDeviceToHost, c->st), "f5_state_save");
+    F5_CU(cudaMemcpyAsync(ring.data(), l.conv, ring.size() * 2, cudaMemcpyDeviceToHost, c->st), "f5_state_save");
+    F5_CU(cudaStreamSynchronize(c->st), "f5_state_save");
+    int16_t *so = reinterpret_cast<int16_t *>(out);
+    // device [head][dv / 32][dk][dv % 32] -> reference [head][dk][dv]
+    for (int h = 0; h < LNH; ++h)
+      for (int q = 0; q < LDV / 32; ++q)
+        for (int k = 0; k < LDK; ++k)
+          for (int i = 0; i < 32; ++i)
+            so[((size_t)h * LDK + k) * LDV + q * 32 + i] = S[(((size_t)h * (LDV / 32) + q) * LDK + k) * 32 + i];
+    int64_t *co = reinterpret_cast<int64_t *>(out + (size_t)LNH * LDK * LDV * 2);
+    // ring slot T % 4 takes this step's input; the other three, oldest first
+    for (int ch = 0; ch < CONV_DIM; ++ch)
+      for (int j = 0; j < 3; ++j) co[(size_t)ch * 3 + j] = ring[(size_t)ch * 4 + ((T - 3 + j) & 3)];
+    return F5_OK;
+  }
+  const size_t mt = (size_t)c->cfg.max_T;
+  std::vector<int8_t> k8(NKV * mt * HD), ke(NKV * mt), v8(NKV * mt * HD), ve(NKV * mt);
+  F5_CU(cudaMemcpyAsync(k8.data(), l.k8, k8.size(), cudaMemcpyDeviceToHost, c->st), "f5_state_save");
+  F5_CU(cudaMemcpyAsync(ke.data(), l.ke, ke.size(), cudaMemcpyDeviceToHost, c->st), "f5_state_save");
+  F5_CU(cudaMemcpyAsync(v8.data(), l.v8, v8.size(), cudaMemcpyDeviceToHost, c->st), "f5_state_save");
+  F5_CU(cudaMemcpyAsync(ve.data(), l.ve, ve.size(), cudaMemcpyDeviceToHost, c->st), "f5_state_save");
+  F5_CU(cudaStreamSynchronize(c->st), "f5_state_save");
+  int8_t *o = reinterpret_cast<int8_t *>(out);
+  const size_t rows = (size_t)T * NKV;
+  for (int t = 0; t < T; ++t)
+    for (int h = 0; h < NKV; ++h) {
+      const size_t r = (size_t)t * NKV + h, dr = (size_t)h * mt + t;
+      memcpy(o + r * HD, k8.data() + dr * HD, HD);
+      o[rows * HD + r] = ke[dr];
+      memcpy(o + rows * (HD + 1) + r * HD, v8.data() + dr * HD, HD);
+      o[rows * (2 * HD + 1) + r] = ve[dr];
+    }
+  return F5_OK;
+}
+
+int f5_state_load(f5_ctx *c, int layer, const void *src, size_t bytes, int T) {
+  int rc = check_ctx(c);
+  if (rc) return rc;
+  if (!src) return set_error(F5_EINVAL, "f5_state_load: null source");
+  if (layer < 0 || layer >= (int)c->L.size()) return set_error(F5_EINVAL, "f5_state_load: layer %d", layer);
+  if (T < 0 || T > c->cfg.max_T) return set_error(F5_EINVAL, "f5_state_load: T=%d outside [0, max_T]", T);
+  const size_t need = state_bytes_of(c, layer, T);
+  if (bytes != need) return set_error(F5_EINVAL, "f5_state_load: layer %d at T=%d needs %zu bytes, got %zu", layer, T, need, bytes);
+  DevGuard dg(c->device);
+  const Layer &l = c->L[layer];
+  const uint8_t *in = static_cast<const uint8_t *>(src);
+  if (!l.attn) {
+    std::vector<int16_t> S((size_t)LNH * LDK * LDV), ring((size_t)CONV_DIM * 4, 0);
+    const int16_t *si = reinterpret_cast<const int16_t *>(in);
+    for (int h = 0; h < LNH; ++h)
+      for (int q = 0; q < LDV / 32; ++q)
+        for (int k = 0; k < LDK; ++k)
+          for (int i = 0; i < 32; ++i)
+            S[(((size_t)h * (LDV / 32) + q) * LDK + k) * 32 + i] = si[((size_t)h * LDK + k) * LDV + q * 32 + i];
+    const int64_t *ci = reinterpret_cast<const int64_t *>(in + (size_t)LNH * LDK * LDV * 2);
+    for (int ch = 0; ch < CONV_DIM; ++ch)
+      for (int j = 0; j < 3; ++j) {
+        const int64_t v = ci[(size_t)ch * 3 + j];
+        if (v < -32768 || v > 32767)
+          return set_error(F5_EINVAL, "f5_state_load: conv window value %lld of channel %d is not int16", (long long)v, ch);
+        ring[(size_t)ch * 4 + ((T - 3 + j) & 3)] = (int16_t)v;
+      }
+    F5_CU(cudaMemcpyAsync(l.S, S.data(), S.size() * 2, cudaMemcpyHostToDevice, c->st), "f5_state_load");
+    F5_CU(cudaMemcpyAsync(l.conv, ring.data(), ring.size() * 2, cudaMemcpyHostToDevice, c->st), "f5_state_load");
+    F5_CU(cudaStreamSynchronize(c->st), "f5_state_load");
+    return F5_OK;
+  }
+  const size_t mt = (size_t)c->cfg.max_T;
+  std::vector<int8_t> k8(NKV * mt * HD, 0), ke(NKV * mt, 0), v8(NKV * mt * HD, 0), ve(NKV * mt, 0);
+  const int8_t *i8 = reinterpret_cast<const int8_t *>(in);
+  const size_t rows = (size_t)T * NKV;
+  for (int t = 0; t < T; ++t)
+    for (int h = 0; h < NKV; ++h) {
+      const size_t r = (size_t)t * NKV + h, dr = (size_t)h * mt + t;
+      memcpy(k8.data() + dr * HD, i8 + r * HD, HD);
+      ke[dr] = i8[rows * HD + r];
+      memcpy(v8.data() + dr * HD, i8 + rows * (HD + 1) + r * HD, HD);
+      ve[dr] = i8[rows * (2 * HD + 1) + r];
+    }
+  F5_CU(cudaMemcpyAsync(l.k8, k8.data(), k8.size(), cudaMemcpyHostToDevice, c->st), "f5_state_load");
+  F5_CU(cudaMemcpyAsync(l.ke, ke.data(), ke.size(), cudaMemcpyHostToDevice, c->st), "f5_state_load");
+  F5_CU(cudaMemcpyAsync(l.v8, v8.data(), v8.size(), cudaMemcpyHostToDevice, c->st), "f5_state_load");
+  F5_CU(cudaMemcpyAsync(l.ve, ve.data(), ve.size(), cudaMemcpyHostToDevice, c->st), "f5_state_load");
+  F5_CU(cudaStreamSynchronize(c->st), "f5_state_load");
+  return F5_OK;
+}

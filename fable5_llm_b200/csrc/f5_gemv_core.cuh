@@ -31,6 +31,25 @@ F5_DEV void st_tagged(const GemvArgs &a, uint32_t *p, uint32_t w) {
   for (int r = 0; r < a.nrank; ++r) *reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(p) + a.peer_delta[r]) = w;
 }
 
+// L2 loads the compiler must issue on every call (poll loops re-read them;
+// a plain __ldcg could be hoisted out of the loop)
+F5_DEV uint4 ld_cg_poll(const uint4 *p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p)
+               : "memory");
+  return v;
+}
+F5_DEV uint2 ld_cg_poll(const uint2 *p) {
+  uint2 v;
+  asm volatile("ld.global.cg.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
+F5_DEV uint32_t ld_cg_poll(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.global.cg.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Bounded poll until the n words at p (n = 1, 2 or 8; 16-byte aligned for 8)
 // all carry `tag`; reads at L2.  Gives up after 1 s (or once the kernel's
 // abort flag is up, polled every ~20 us), then raises DERR_TIMEOUT and the
@@ -40,14 +59,14 @@ F5_DEV bool ld_tagged(const uint32_t *p, uint32_t tag, uint32_t (&w)[N], unsigne
   unsigned long long t0 = 0, tpoll = 0;
   for (uint32_t it = 0;; ++it) {
     if (N == 8) {
-      const uint4 a = __ldcg(reinterpret_cast<const uint4 *>(p)), b = __ldcg(reinterpret_cast<const uint4 *>(p) + 1);
+      const uint4 a = ld_cg_poll(reinterpret_cast<const uint4 *>(p)), b = ld_cg_poll(reinterpret_cast<const uint4 *>(p) + 1);
       w[0] = a.x; w[1 % N] = a.y; w[2 % N] = a.z; w[3 % N] = a.w;
       w[4 % N] = b.x; w[5 % N] = b.y; w[6 % N] = b.z; w[7 % N] = b.w;
     } else if (N == 2) {
-      const uint2 a = __ldcg(reinterpret_cast<const uint2 *>(p));
+      const uint2 a = ld_cg_poll(reinterpret_cast<const uint2 *>(p));
       w[0] = a.x; w[1 % N] = a.y;
     } else {
-      w[0] = __ldcg(p);
+      w[0] = ld_cg_poll(p);
     }
     bool ok = true;
 #pragma unroll
@@ -282,6 +301,24 @@ F5_DEV long long row_dot4096(const uint8_t *row, int lane, const uint2 (&xr)[4][
 }
 
 
+// two K = 4096 rows at once: independent chains the scheduler interleaves
+F5_DEV void row_dot4096x2(const uint8_t *row0, const uint8_t *row1, int lane, const uint2 (&xr)[4][4],
+                          long long &out0, long long &out1) {
+  long long a0 = 0, a1 = 0;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int boff = c * 512 + lane * 16;
+    const uint4 w0 = *reinterpret_cast<const uint4 *>(row0 + boff);
+    const uint4 w1 = *reinterpret_cast<const uint4 *>(row1 + boff);
+    const uint32_t m0 = *reinterpret_cast<const uint16_t *>(row0 + 2048 + 2 * (boff >> 6));
+    const uint32_t m1 = *reinterpret_cast<const uint16_t *>(row1 + 2048 + 2 * (boff >> 6));
+    a0 += (long long)m0 * dot32(w0, xr[c][0], xr[c][1], xr[c][2], xr[c][3]);
+    a1 += (long long)m1 * dot32(w1, xr[c][0], xr[c][1], xr[c][2], xr[c][3]);
+  }
+  out0 = a0;
+  out1 = a1;
+}
+
 // Redundant per-CTA computation of the GEMV's quantized input (see GemvPro).
 // Every value is read from global memory once and held in registers across
 // the reduction passes (MAXB 8-element blocks per thread).
@@ -289,7 +326,7 @@ F5_DEV long long row_dot4096(const uint8_t *row, int lane, const uint2 (&xr)[4][
 // (persistent kernel) and each thread polls its words until they are ready.
 template <int MAXB, class SY>
 F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red, long long *s_r, int *s_meta,
-                     uint32_t epoch = 0) {
+                     uint32_t epoch = 0, const int32_t *gains_smem = nullptr) {
   const int tid = sy.tid(), BT = sy.n(), K = a.K, nblk = K >> 3;
   const GemvPrologue &P = a.pro;
   const bool store = (P.xq_out.x8 != nullptr) && blockIdx.x == 0;
@@ -298,18 +335,20 @@ F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red,
   if (P.mode == PRO_RMSNORM || P.mode == PRO_DYNQ8) {
     const int16_t *src = static_cast<const int16_t *>(P.src);
     uint4 raw[MAXB];
+    if (in_tag) {
 #pragma unroll
-    for (int j = 0; j < MAXB; ++j) {
-      const int b = tid + j * BT;
-      if (b >= nblk) {
-        raw[j] = make_uint4(0, 0, 0, 0);
-      } else if (in_tag) {
-        uint32_t w[8];
-        ld_tagged<8>(static_cast<const uint32_t *>(P.src) + 8 * b, in_tag, w, a.abort_flag, a.err);
+      for (int j = 0; j < MAXB; ++j) {
+        const int b = tid + j * BT;
+        uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (b < nblk) ld_tagged<8>(static_cast<const uint32_t *>(P.src) + 8 * b, in_tag, w, a.abort_flag, a.err);
         raw[j] = make_uint4((w[0] & 0xFFFFu) | (w[1] << 16), (w[2] & 0xFFFFu) | (w[3] << 16),
                             (w[4] & 0xFFFFu) | (w[5] << 16), (w[6] & 0xFFFFu) | (w[7] << 16));
-      } else {
-        raw[j] = __ldcg(reinterpret_cast<const uint4 *>(src + 8 * b));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < MAXB; ++j) {
+        const int b = tid + j * BT;
+        raw[j] = b < nblk ? __ldcg(reinterpret_cast<const uint4 *>(src + 8 * b)) : make_uint4(0, 0, 0, 0);
       }
     }
     if constexpr (MAXB <= 2) {
@@ -318,9 +357,17 @@ F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red,
 #pragma unroll
         for (int j = 0; j < MAXB; ++j) {
           const int b = tid + j * BT;
-          // gains streamed at L2 (__ldcg): L1 stays with the LUTs
-          wl[j][0] = b < nblk ? __ldcg(reinterpret_cast<const int4 *>(P.w + 8 * b)) : make_int4(0, 0, 0, 0);
-          wl[j][1] = b < nblk ? __ldcg(reinterpret_cast<const int4 *>(P.w + 8 * b + 4)) : make_int4(0, 0, 0, 0);
+          // gains from the caller's shared-memory copy, else streamed at L2 (__ldcg)
+          const int32_t *gw = gains_smem ? gains_smem : P.w;
+          if (b >= nblk) {
+            wl[j][0] = wl[j][1] = make_int4(0, 0, 0, 0);
+          } else if (gains_smem) {
+            wl[j][0] = *reinterpret_cast<const int4 *>(gw + 8 * b);
+            wl[j][1] = *reinterpret_cast<const int4 *>(gw + 8 * b + 4);
+          } else {
+            wl[j][0] = __ldcg(reinterpret_cast<const int4 *>(gw + 8 * b));
+            wl[j][1] = __ldcg(reinterpret_cast<const int4 *>(gw + 8 * b + 4));
+          }
         }
         long long ss = 0;   // < 16 * 2^30 per thread
 #pragma unroll
@@ -509,8 +556,11 @@ F5_DEV void rstat_flush(unsigned long long *p, const RStat &s) {
   }
 }
 
+// T_known >= 0: the step's token count, known to the caller (GM_CONV then
+// skips reading *sg.T)
 F5_DEV void epilogue_row(const GemvArgs &a, const GemvSeg &sg, int row, long long acc16, int e_x,
-                         int in_f, unsigned long long &best, uint32_t epoch = 0, RStat *rs = nullptr) {
+                         int in_f, unsigned long long &best, uint32_t epoch = 0, RStat *rs = nullptr,
+                         int T_known = -1) {
   long long pex;
   const int32_t y = finish_y32(acc16, a.sh, a.err, &pex);
   const int orow = sg.out_row0 + row;
@@ -551,7 +601,7 @@ F5_DEV void epilogue_row(const GemvArgs &a, const GemvSeg &sg, int row, long lon
       // cached loads: the ring word is touched only by this row's epilogue
       // (this step's write below, the next step's read in a later launch)
       const int4 cw = *reinterpret_cast<const int4 *>(static_cast<const int32_t *>(sg.aux1) + (size_t)orow * 4);
-      const int T = *sg.T;
+      const int T = T_known >= 0 ? T_known : *sg.T;
       const uint2 rw = *reinterpret_cast<const uint2 *>(ring);   // 4 int16 slots
       const int32_t qc = conv_silu(v, rw, cw, T);
       if (tag) st_tagged(a, static_cast<uint32_t *>(sg.aux_out) + orow, tag_word(tag, qc));

@@ -18,6 +18,17 @@ static __device__ const int32_t f5_lut_exp2[F5_LUT_EXP2_N] = F5_LUT_EXP2_INIT;
 static __device__ const int32_t f5_lut_sigmoid[F5_LUT_SIGMOID_N] = F5_LUT_SIGMOID_INIT;
 static __device__ const int32_t f5_lut_softplus[F5_LUT_SOFTPLUS_N] = F5_LUT_SOFTPLUS_INIT;
 
+// The arrays the lookups below read.  A translation unit whose kernels keep
+// their own copy of the tables (the persistent decode kernel holds them in
+// shared memory) defines these names before including this header.
+#ifndef F5_LUT_RSQRT
+#define F5_LUT_RSQRT f5_lut_rsqrt
+#define F5_LUT_RECIP f5_lut_recip
+#define F5_LUT_EXP2 f5_lut_exp2
+#define F5_LUT_SIGMOID f5_lut_sigmoid
+#define F5_LUT_SOFTPLUS f5_lut_softplus
+#endif
+
 namespace f5 {
 
 // fixed-point formats of the 9B operating point (ref/layer_fixed.py:103-147,404)
@@ -92,7 +103,7 @@ F5_DEV void rsqrt_q(uint64_t v, int P, int64_t &r_out, int &e_out) {
   const uint64_t m = s >= 0 ? (v >> s) : (v << (-s));
   const int E = s - P + 30;
   const int idx = m < (1ull << 31) ? (int)((m >> 22) & 0xFF) : (256 | (int)((m >> 23) & 0xFF));
-  int64_t r = (int64_t)f5_lut_rsqrt[idx] << 15;
+  int64_t r = (int64_t)F5_LUT_RSQRT[idx] << 15;
   const int64_t mi = (int64_t)m;
 #pragma unroll
   for (int it = 0; it < 2; ++it) {
@@ -111,7 +122,7 @@ F5_DEV void recip_q(uint64_t v, int P, int64_t &r_out, int &e_out) {
   const uint64_t m = sh >= 0 ? (v >> sh) : (v << (-sh));
   int64_t idx = ((int64_t)m - (1ll << 30)) >> 22;
   if (idx > 255) idx = 255;
-  int64_t r = (int64_t)f5_lut_recip[idx] << 15;
+  int64_t r = (int64_t)F5_LUT_RECIP[idx] << 15;
   const int64_t mi = (int64_t)m;
 #pragma unroll
   for (int it = 0; it < 2; ++it) {
@@ -125,7 +136,7 @@ F5_DEV void recip_q(uint64_t v, int P, int64_t &r_out, int &e_out) {
 // ref/fixedpoint.py:99-106 exp2_frac_q16, f in [0, 2^16)
 F5_DEV int64_t exp2_frac_q16(int64_t f) {
   const int i = (int)(f >> 8), lo = (int)(f & 0xFF);
-  const int64_t a = f5_lut_exp2[i], b = f5_lut_exp2[i + 1];
+  const int64_t a = F5_LUT_EXP2[i], b = F5_LUT_EXP2[i + 1];
   return a + (((b - a) * lo + 128) >> 8);
 }
 
@@ -144,7 +155,7 @@ F5_DEV int64_t sigmoid_q(int64_t x) {
   const int64_t xc = clip(x, -(16 << 12), (16 << 12) - 1);
   const int u = (int)(xc + (16 << 12));
   const int i = u >> 9, lo = u & 0x1FF;
-  const int64_t a = f5_lut_sigmoid[i], b = f5_lut_sigmoid[i + 1];
+  const int64_t a = F5_LUT_SIGMOID[i], b = F5_LUT_SIGMOID[i + 1];
   return a + (((b - a) * lo + 256) >> 9);
 }
 
@@ -154,7 +165,7 @@ F5_DEV int64_t softplus_q(int64_t x) {
   if (x < -(16 << 12)) return 0;
   const int u = (int)(x + (16 << 12));
   const int i = u >> 9, lo = u & 0x1FF;
-  const int64_t a = f5_lut_softplus[i], b = f5_lut_softplus[i + 1];
+  const int64_t a = F5_LUT_SOFTPLUS[i], b = F5_LUT_SOFTPLUS[i + 1];
   return a + (((b - a) * lo + 256) >> 9);
 }
 

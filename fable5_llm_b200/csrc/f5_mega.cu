@@ -35,11 +35,22 @@
 
 #include <cuda_runtime.h>
 
+#include "f5_luts.h"
 namespace f5 {
 // this op's trace row (consumer thread 0 only), null when not tracing;
 // declared ahead of the shared cores so their phase marks can reach it
 __shared__ unsigned long long *mg_tr;
+// The integer LUTs in shared memory (copied from the global tables at
+// launch): every lookup of the step's prologues, epilogues and cores is a
+// shared-memory read, never an L1 miss behind the weight stream.
+__shared__ int32_t mg_lut_rsqrt[F5_LUT_RSQRT_N], mg_lut_recip[F5_LUT_RECIP_N], mg_lut_exp2[F5_LUT_EXP2_N],
+    mg_lut_sigmoid[F5_LUT_SIGMOID_N], mg_lut_softplus[F5_LUT_SOFTPLUS_N];
 }  // namespace f5
+#define F5_LUT_RSQRT mg_lut_rsqrt
+#define F5_LUT_RECIP mg_lut_recip
+#define F5_LUT_EXP2 mg_lut_exp2
+#define F5_LUT_SIGMOID mg_lut_sigmoid
+#define F5_LUT_SOFTPLUS mg_lut_softplus
 #define F5_PRO_MARK(k)                                     \
   do {                                                     \
     if (threadIdx.x == 0 && mg_tr) mg_tr[(k)] = gtimer();  \
@@ -56,6 +67,7 @@ constexpr int MG_CT = MG_CONS * 32;
 constexpr int MG_NS_MAX = 6;
 constexpr int MG_XS = 12 * 4 * 32 * 8;          // x8 of K <= 12288 in the lane-major layout
 constexpr int MG_RESB = MEGA_RES * 8;
+constexpr int MG_GAINB = 4096 * 4;              // the RMSNorm gains of one K = 4096 prologue
 constexpr unsigned long long MG_WAIT_NS = 1000000000ull;   // 1 s: a safety net only
 using CSync = NamedSync<1, MG_CT>;
 
@@ -119,6 +131,7 @@ F5_DEV bool mwait(uint64_t *b, uint32_t parity, const Abort &ab) {
     }
   }
 }
+
 
 // Counter barrier over `target` CTAs (consumer groups).  One thread's
 // release add / acquire polls, bracketed by the group's named barrier, order
@@ -191,7 +204,9 @@ F5_DEV void release_scratch(const CSync &sy, uint64_t *bfree) {
   }
 }
 
-F5_DEV int part_lo(int total, int G, int b) { return (int)((long long)total * b / G); }
+// first unit of CTA b when `total` units split over G CTAs; total * G < 2^31
+// here (<= 248,320 rows x the SM count), so 32-bit arithmetic is exact
+F5_DEV int part_lo(int total, int G, int b) { return (int)((unsigned)total * (unsigned)b / (unsigned)G); }
 
 // ---------------------------------------------------------------------------
 // attention geometry (identical in producer and consumers)
@@ -232,16 +247,17 @@ F5_DEV void att_issue(uint8_t *dst_rows, uint8_t *dst_e, const int8_t *rows, con
 // Shared memory at namespace scope: every address below is a compile-time
 // constant (no pointer kept in registers); the dynamic region's layout
 // depends only on the ring depth ns (a launch parameter):
-//   [ns x MEGA_STAGE ring][MG_XS x8 layout][MG_RESB row results][scratch]
+//   [ns x MEGA_STAGE ring][MG_XS x8 layout][MG_RESB row results][MG_GAINB gains][scratch]
 extern __shared__ __align__(128) uint8_t mg_dyn[];
 __shared__ __align__(8) uint64_t mg_full[MG_NS_MAX], mg_empty[MG_NS_MAX];
 __shared__ __align__(8) uint64_t mg_bsd, mg_bsk, mg_bsv, mg_bfree, mg_bpd[2];
+__shared__ __align__(8) uint64_t mg_gfull, mg_gfree;   // the gains buffer: filled by the producer, freed by the prologue
 __shared__ __align__(16) MegaOp mg_cop[2], mg_pop[2];   // op i's descriptor in [i & 1]
 __shared__ long long mg_red[64];
 __shared__ long long mg_r, mg_gate[4], mg_att[8];
 __shared__ long long mg_gat[64];   // group_gather's per-warp partials (apart from mg_red: no reuse race)
 __shared__ int mg_meta[4], mg_e[2];
-__shared__ int mg_cnt[6];   // issued fills: [0] ring, [1] sd, [2] sk, [3] sv (producer), [4] sk, [5] sv (consumers)
+__shared__ int mg_cnt[7];   // issued fills: [0] ring, [1] sd, [2] sk, [3] sv (producer), [4] sk, [5] sv (consumers), [6] gains
 __shared__ volatile int mg_abort;
 __shared__ int mg_last;
 __shared__ __align__(16) MegaOp mg_fop;   // the L2 prefetcher's descriptor buffer
@@ -260,7 +276,8 @@ struct MegaSmem {
   F5_DEV uint8_t *ring() const { return mg_dyn; }
   F5_DEV uint2 *xs() const { return reinterpret_cast<uint2 *>(mg_dyn + ns * MEGA_STAGE); }
   F5_DEV long long *res() const { return reinterpret_cast<long long *>(mg_dyn + ns * MEGA_STAGE + MG_XS); }
-  F5_DEV uint8_t *scr() const { return mg_dyn + ns * MEGA_STAGE + MG_XS + MG_RESB; }
+  F5_DEV int32_t *gains() const { return reinterpret_cast<int32_t *>(mg_dyn + ns * MEGA_STAGE + MG_XS + MG_RESB); }
+  F5_DEV uint8_t *scr() const { return mg_dyn + ns * MEGA_STAGE + MG_XS + MG_RESB + MG_GAINB; }
 };
 
 // position in the stage ring: stage s, lap parity ph (flips each wrap)
@@ -288,7 +305,7 @@ F5_DEV void issue_desc(const MegaArgs &ma, const MegaSmem &S, int oi) {
 
 F5_DEV void producer(const MegaArgs &ma, const MegaSmem &S, int T, int pos, const Abort &ab) {
   const int G = gridDim.x, b = blockIdx.x, ns = S.ns;
-  int issued = 0, n_scr = 0;
+  int issued = 0, n_scr = 0, n_gain = 0;
   RingPos rp;
   bool bad = false;
   int desc_pending = -1;   // descriptor copy in flight (drained before exit)
@@ -305,6 +322,12 @@ F5_DEV void producer(const MegaArgs &ma, const MegaSmem &S, int T, int pos, cons
     const int kind = op.kind;
     if (kind == MK_GEMV) {
       const GemvArgs &a = op.g;
+      if (a.pro.mode == PRO_RMSNORM) {   // the prologue's gains, ahead of the op's rows
+        if (n_gain > 0 && !mwait(&mg_gfree, (n_gain - 1) & 1, ab)) { bad = true; break; }
+        mbar_expect_tx(&mg_gfull, MG_GAINB);
+        bulk_g2s(S.gains(), a.pro.w, MG_GAINB, &mg_gfull);
+        mg_cnt[6] = ++n_gain;
+      }
       int u = part_lo(a.total_units, G, b);
       const int u1 = part_lo(a.total_units, G, b + 1);
       Chunk ch;
@@ -434,12 +457,12 @@ F5_DEV void epi_prefetch(const GemvArgs &a, int uu) {
 // back to mg_xres (the CTA wrote them last: BEGIN and every residual op use
 // the same 4096-row partition); everything else is the shared epilogue_row.
 F5_DEV void mega_epilogue_row(const GemvArgs &a, const GemvSeg &sg, int i, int uu, long long acc, int e_x, int in_f,
-                              uint32_t epoch, RStat &rs) {
+                              uint32_t epoch, RStat &rs, int T) {
   const int row = uu - sg.unit_begin, orow = sg.out_row0 + row;
   const uint32_t tag = (epoch && sg.tag_op1) ? mk_tag(epoch, sg.tag_op1) : 0u;
   if (!(sg.mode == GM_RESID && tag && i < MG_XRES)) {
     unsigned long long unused = 0ull;
-    epilogue_row(a, sg, row, acc, e_x, in_f, unused, epoch, sg.rstat ? &rs : nullptr);
+    epilogue_row(a, sg, row, acc, e_x, in_f, unused, epoch, sg.rstat ? &rs : nullptr, T);
     return;
   }
   const int32_t y = finish_y32(acc, a.sh, a.err, nullptr);
@@ -457,12 +480,24 @@ F5_DEV void mega_epilogue_row(const GemvArgs &a, const GemvSeg &sg, int i, int u
 // sum uses two redux.sync adds, and the LM head's argmax epilogue is batched
 // -- lane k % 32 of a warp holds the warp's k-th row sum, and every 32 rows
 // all lanes turn their rows into (y32, row) keys at once.
-F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const Abort &ab, uint32_t epoch) {
+F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const Abort &ab, uint32_t epoch,
+                       int &w_g, int T) {
   const CSync sy;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, b = blockIdx.x, ns = S.ns;
-  prologue<1>(sy, a, S.xs(), mg_red, (&mg_r), mg_meta, epoch);
-  sy.sync();
+  // RMSNorm gains: the producer's copy in shared memory (in place long before)
+  const bool rms = a.pro.mode == PRO_RMSNORM;
+  bool got = true;
+  if (rms) {
+    got = mwait(&mg_gfull, w_g & 1, ab);
+    ++w_g;
+  }
+  prologue<1>(sy, a, S.xs(), mg_red, (&mg_r), mg_meta, epoch, rms ? S.gains() : nullptr);
+  if (sy.any(!got)) return false;
+  if (rms && tid == 0) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the gains reads before the next fill
+    mbar_arrive(&mg_gfree);
+  }
   MG_MARK(2);
   const int e_x = mg_meta[0], in_f = mg_meta[1];
   uint2 xr[4][4];
@@ -491,6 +526,58 @@ F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const 
   };
   bool bad = false;
   int u = u0;
+  if (!argmax) {
+    // Two groups of eight warps take the op's stages in turn (chunk j goes to
+    // group j % 2); a stage holds <= 16 rows (rows_per_stage <= 16) and warp
+    // w of the group reduces rows w and w + 8 together, so every wait,
+    // arrival and loop step is shared by two rows.  Each warp arrives with
+    // count 2, keeping the empty barrier's 16 arrivals per stage.
+    const int grp = warp >> 3, wl = warp & 7;
+    int j = 0;
+    while (u < u1 && !bad) {
+      const int si = seg_of(a, u);
+      const GemvSeg &sg = a.seg[si];
+      const int seg_hi = min(u1, si + 1 < a.nseg ? a.seg[si + 1].unit_begin : a.total_units);
+      const bool pair = sg.mode == GM_SILU_MUL;
+      const int ru = pair ? (a.rows_per_stage >> 1) : a.rows_per_stage;
+      while (u < seg_hi) {
+        const int n = min(ru, seg_hi - u);
+        if ((j & 1) == grp) {
+          if (mg_abort || !mwait(&mg_full[rp.s], rp.ph, ab)) {
+            mg_abort = 1;
+            bad = true;
+            break;
+          }
+          const int nrows = pair ? 2 * n : n;
+          const uint8_t *st = S.ring() + rp.s * MEGA_STAGE;
+          const int cbase = u - u0;
+          const int r1 = wl + 8;
+          // result slot of stage row r: paired stages hold n gate rows, then n up rows
+          const int i0 = pair ? 2 * (cbase + wl) : cbase + wl;   // wl < n whenever r1 < nrows
+          if (r1 < nrows) {
+            long long p0, p1;
+            row_dot4096x2(st + wl * stride, st + r1 * stride, lane, xr, p0, p1);
+            const long long s0 = warp_sum_row(p0), s1 = warp_sum_row(p1);
+            const int i1 = pair ? (r1 < n ? 2 * (cbase + r1) : 2 * (cbase + r1 - n) + 1) : cbase + r1;
+            if (lane == 0) {
+              res[i0] = s0;
+              res[i1] = s1;
+            }
+          } else if (wl < nrows) {
+            const long long s0 = warp_sum_row(row_dot4096(st + wl * stride, lane, xr));
+            const int ix = pair ? (wl < n ? 2 * (cbase + wl) : 2 * (cbase + wl - n) + 1) : cbase + wl;
+            if (lane == 0) res[ix] = s0;
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cnt(&mg_empty[rp.s], 2);
+        }
+        rp.next(ns);
+        u += n;
+        ++j;
+      }
+    }
+    u = u1;
+  }
   while (u < u1 && !bad) {
     const int si = seg_of(a, u);
     const GemvSeg &sg = a.seg[si];
@@ -543,7 +630,7 @@ F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const 
     const int uu = u0 + i;
     const GemvSeg &sg = a.seg[seg_of(a, uu)];
     if (sg.mode == GM_SILU_MUL) epilogue_pair(a, sg, uu - sg.unit_begin, res[2 * i], res[2 * i + 1], e_x, in_f, epoch);
-    else mega_epilogue_row(a, sg, i, uu, res[i], e_x, in_f, epoch, rs);
+    else mega_epilogue_row(a, sg, i, uu, res[i], e_x, in_f, epoch, rs, T);
   }
   if (a.nseg == 1 && a.seg[0].rstat) rstat_flush(a.seg[0].rstat, rs);
   return true;
@@ -555,7 +642,7 @@ F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const 
 // registers.  The partial sums are exact integers; the deferred epilogue adds
 // the NP partials of a row (order-free) before the group-scale law's shift.
 template <int NP>
-F5_DEV bool c_gemv_split(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const Abort &ab, uint32_t epoch) {
+F5_DEV bool c_gemv_split(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const Abort &ab, uint32_t epoch, int T) {
   const CSync sy;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, b = blockIdx.x, ns = S.ns;
@@ -608,7 +695,7 @@ F5_DEV bool c_gemv_split(const GemvArgs &a, const MegaSmem &S, RingPos &rp, cons
 #pragma unroll
     for (int p = 0; p < NP; ++p) acc += S.res()[NP * i + p];
     if (i == 0) MG_MARK(4);
-    mega_epilogue_row(a, sg, i, uu, acc, e_x, in_f, epoch, rs);
+    mega_epilogue_row(a, sg, i, uu, acc, e_x, in_f, epoch, rs, T);
     if (i == 0) MG_MARK(5);
   }
   if (a.nseg == 1 && a.seg[0].rstat) rstat_flush(a.seg[0].rstat, rs);
@@ -1204,7 +1291,7 @@ F5_DEV void consumers(const MegaArgs &ma, const MegaSmem &S, int tok, int T, int
                       uint32_t epoch) {
   const CSync sy;
   RingPos rp;
-  int w_sd = 0, w_sk = 0, w_sv = 0;
+  int w_sd = 0, w_sk = 0, w_sv = 0, w_g = 0;
   unsigned long long *tr = ma.trace ? ma.trace + (size_t)blockIdx.x * ma.nops * MEGA_TRACE_SLOTS : nullptr;
   stage_desc(ma, S, 0);
   for (int oi = 0; oi < ma.nops; ++oi) {
@@ -1218,14 +1305,13 @@ F5_DEV void consumers(const MegaArgs &ma, const MegaSmem &S, int tok, int T, int
     if (bar >= 0 && !counter_barrier(sy, &ma.bars[bar], gridDim.x, ab)) return;
     if (threadIdx.x == 0) mg_tr = tr ? tr + (size_t)oi * MEGA_TRACE_SLOTS : nullptr;
     if (oi + 1 < ma.nops) stage_desc(ma, S, oi + 1);
-    if (threadIdx.x >= 64 && threadIdx.x < 64 + 51) lut_prefetch_l1(threadIdx.x - 64);
     const MegaOp &op = mg_cop[oi & 1];
     if (tr && threadIdx.x == 0) tr[(size_t)oi * MEGA_TRACE_SLOTS] = gtimer();
     bool ok = true;
     switch (op.kind) {
       case MK_BEGIN: c_begin(ma, op.b, tok, epoch); break;
       case MK_GEMV:
-        ok = op.g.K > 4096 ? c_gemv_split<3>(op.g, S, rp, ab, epoch) : c_gemv4096(op.g, S, rp, ab, epoch);
+        ok = op.g.K > 4096 ? c_gemv_split<3>(op.g, S, rp, ab, epoch, T) : c_gemv4096(op.g, S, rp, ab, epoch, w_g, T);
         break;
       case MK_DN: ok = c_dn(ma, op.d, S, w_sd, ab, epoch); break;
       case MK_ATTN: ok = c_attn(ma, op.at, S, T, pos, w_sk, w_sv, ab, epoch); break;
@@ -1257,13 +1343,20 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega(const __grid_constant_
     mbar_init(&mg_bfree, 1);
     mbar_init(&mg_bpd[0], 1);
     mbar_init(&mg_bpd[1], 1);
-    for (int i = 0; i < 6; ++i) mg_cnt[i] = 0;
+    mbar_init(&mg_gfull, 1);
+    mbar_init(&mg_gfree, 1);
+    for (int i = 0; i < 7; ++i) mg_cnt[i] = 0;
     mg_abort = 0;
     mg_last = 0;
     mg_tr = nullptr;
     mg_issued = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  for (int i = tid; i < F5_LUT_RSQRT_N; i += MEGA_THREADS) mg_lut_rsqrt[i] = f5_lut_rsqrt[i];
+  for (int i = tid; i < F5_LUT_RECIP_N; i += MEGA_THREADS) mg_lut_recip[i] = f5_lut_recip[i];
+  for (int i = tid; i < F5_LUT_EXP2_N; i += MEGA_THREADS) mg_lut_exp2[i] = f5_lut_exp2[i];
+  for (int i = tid; i < F5_LUT_SIGMOID_N; i += MEGA_THREADS) mg_lut_sigmoid[i] = f5_lut_sigmoid[i];
+  for (int i = tid; i < F5_LUT_SOFTPLUS_N; i += MEGA_THREADS) mg_lut_softplus[i] = f5_lut_softplus[i];
   // step parameters: written by the host or by the previous launch only
   const volatile StepParams *vp = ma.params;
   const int tok = vp->tok, T = vp->T, pos = vp->pos;
@@ -1289,6 +1382,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega(const __grid_constant_
       mbar_wait(&mg_full[s], (last / ns) & 1, MG_WAIT_NS);
     }
     if (mg_cnt[1]) mbar_wait(&mg_bsd, (mg_cnt[1] - 1) & 1, MG_WAIT_NS);
+    if (mg_cnt[6]) mbar_wait(&mg_gfull, (mg_cnt[6] - 1) & 1, MG_WAIT_NS);
     const int nk = mg_cnt[2] + mg_cnt[4], nv = mg_cnt[3] + mg_cnt[5];
     if (nk) mbar_wait(&mg_bsk, (nk - 1) & 1, MG_WAIT_NS);
     if (nv) mbar_wait(&mg_bsv, (nv - 1) & 1, MG_WAIT_NS);
@@ -1360,7 +1454,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega(const __grid_constant_
 static size_t mega_smem_bytes(int ns, int chunk_max) {
   size_t scr = (size_t)AT_SC + (size_t)4 * chunk_max * 8;
   if (scr < (size_t)DN_END) scr = DN_END;
-  return (size_t)ns * MEGA_STAGE + MG_XS + MG_RESB + scr;
+  return (size_t)ns * MEGA_STAGE + MG_XS + MG_RESB + MG_GAINB + scr;
 }
 
 cudaError_t mega_config(int chunk_max, int *grid, size_t *smem, int *ns) {
@@ -1377,7 +1471,12 @@ cudaError_t mega_config(int chunk_max, int *grid, size_t *smem, int *ns) {
   while (n >= 3 && mega_smem_bytes(n, chunk_max) + fa.sharedSizeBytes > (size_t)optin) --n;
   if (n < 3) return cudaErrorInvalidValue;
   const size_t bytes = mega_smem_bytes(n, chunk_max);
-  if ((e = cudaFuncSetAttribute(k_mega, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes))) return e;
+  // the limit is a property of the kernel, shared by every context of the
+  // process: raise it to what any configuration may use, never lower it
+  // below another context's launch size
+  if ((e = cudaFuncSetAttribute(k_mega, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)((size_t)optin - fa.sharedSizeBytes))))
+    return e;
   int per_sm = 0;
   if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_mega, MEGA_THREADS, bytes))) return e;
   if (per_sm < 1) return cudaErrorInvalidConfiguration;

@@ -19,6 +19,9 @@ F5_DEV void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
 F5_DEV void mbar_arrive(uint64_t *b) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
+F5_DEV void mbar_arrive_cnt(uint64_t *b, uint32_t cnt) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(cnt) : "memory");
+}
 F5_DEV unsigned long long gtimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

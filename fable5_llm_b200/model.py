@@ -339,61 +339,96 @@ class DecodeModel:
         return sampler.pick(r.values, r.indices, r.e_x)
 
     # ---- reference-layout state I/O (ref/layer_fixed.py:1654-1666) ----
+    def state_image(self, layer):
+        """The layer's state in the reference cache layout (f5_state_save),
+        at the context's current T, as raw bytes."""
+        T, _ = self.position()
+        n = self.lib.f5_state_bytes(self.h, int(layer), T)
+        buf = np.empty(n, dtype=np.uint8)
+        L.check(self.lib.f5_state_save(self.h, int(layer), _p(buf), n), f"state_save({layer})")
+        return buf
+
+    def load_state_image(self, layer, img, T):
+        img = np.ascontiguousarray(img, dtype=np.uint8).reshape(-1)
+        L.check(self.lib.f5_state_load(self.h, int(layer), _p(img), img.size, int(T)), f"state_load({layer})")
+
     def get_dn_state(self, layer, T):
-        """-> {"conv": int64[CONV_DIM, 3] oldest first, "S": int16[LNH, LDK, LDV]}"""
+        """-> {"conv": int64[CONV_DIM, 3] oldest first, "S": int16[LNH, LDK, LDV]}
+        at T tokens (the reference's DeltaNet cache dict)."""
         g = self.geom
-        ring = self.read(L.BUF_DN_CONV, layer).reshape(g.CONV_DIM, 4).astype(I64)
-        conv = np.stack([ring[:, (T - 3 + j) & 3] for j in range(3)], axis=1)
-        # device layout [head][dv // 32][dk][dv % 32] -> reference [head][dk][dv]
-        S = self.read(L.BUF_DN_S, layer).reshape(g.LNH, g.LDV // 32, g.LDK, 32).transpose(0, 2, 1, 3)
-        return {"conv": conv, "S": np.ascontiguousarray(S).reshape(g.LNH, g.LDK, g.LDV)}
+        T0, pos = self.position()
+        if T != T0:
+            self.set_position(T, pos)
+        try:
+            img = self.state_image(layer)
+        finally:
+            if T != T0:
+                self.set_position(T0, pos)
+        ns = g.LNH * g.LDK * g.LDV * 2
+        return {"S": img[:ns].view(np.int16).reshape(g.LNH, g.LDK, g.LDV).copy(),
+                "conv": img[ns:].view(I64).reshape(g.CONV_DIM, 3).copy()}
 
     def set_dn_state(self, layer, T, cache):
         g = self.geom
-        ring = np.zeros((g.CONV_DIM, 4), dtype=np.int16)
-        conv = np.asarray(cache["conv"], dtype=I64)
-        assert (np.abs(conv) <= 32768).all(), "conv window holds clip16 values"
-        for j in range(3):
-            ring[:, (T - 3 + j) & 3] = conv[:, j]
-        self.write(L.BUF_DN_CONV, layer, ring)
-        S = np.asarray(cache["S"], dtype=np.int16).reshape(g.LNH, g.LDK, g.LDV // 32, 32).transpose(0, 2, 1, 3)
-        self.write(L.BUF_DN_S, layer, np.ascontiguousarray(S))
+        S = np.ascontiguousarray(np.asarray(cache["S"]).astype(np.int16)).reshape(-1).view(np.uint8)
+        conv = np.ascontiguousarray(np.asarray(cache["conv"], dtype=I64)).reshape(-1).view(np.uint8)
+        assert S.size == g.LNH * g.LDK * g.LDV * 2 and conv.size == g.CONV_DIM * 3 * 8
+        self.load_state_image(layer, np.concatenate([S, conv]), T)
+
+    def _kv_arrays(self, layer, T):
+        g = self.geom
+        T0, pos = self.position()
+        if T != T0:
+            self.set_position(T, pos)
+        try:
+            img = self.state_image(layer).view(np.int8)
+        finally:
+            if T != T0:
+                self.set_position(T0, pos)
+        n = T * g.NKV
+        k8 = img[:n * g.HD].reshape(T, g.NKV, g.HD)
+        ke = img[n * g.HD:n * (g.HD + 1)].reshape(T, g.NKV)
+        v8 = img[n * (g.HD + 1):n * (2 * g.HD + 1)].reshape(T, g.NKV, g.HD)
+        ve = img[n * (2 * g.HD + 1):].reshape(T, g.NKV)
+        return k8, ke, v8, ve
 
     def get_kv(self, layer, T):
         """-> {"k": [[(k8, ke)] * NKV] * T, "v": ...} (ref/layer_fixed.py:1400-1401)"""
         g = self.geom
-        k8 = self.read(L.BUF_K8, layer).reshape(g.NKV, self.max_T, g.HD)
-        ke = self.read(L.BUF_KE, layer).reshape(g.NKV, self.max_T)
-        v8 = self.read(L.BUF_V8, layer).reshape(g.NKV, self.max_T, g.HD)
-        ve = self.read(L.BUF_VE, layer).reshape(g.NKV, self.max_T)
-        return {"k": [[(k8[h, t].copy(), int(ke[h, t])) for h in range(g.NKV)] for t in range(T)],
-                "v": [[(v8[h, t].copy(), int(ve[h, t])) for h in range(g.NKV)] for t in range(T)]}
+        k8, ke, v8, ve = self._kv_arrays(layer, T)
+        return {"k": [[(k8[t, h].copy(), int(ke[t, h])) for h in range(g.NKV)] for t in range(T)],
+                "v": [[(v8[t, h].copy(), int(ve[t, h])) for h in range(g.NKV)] for t in range(T)]}
 
     def set_kv(self, layer, cache):
         g = self.geom
         T = len(cache["k"])
         assert T <= self.max_T
-        k8 = np.zeros((g.NKV, self.max_T, g.HD), dtype=np.int8)
+        k8 = np.zeros((T, g.NKV, g.HD), dtype=np.int8)
         v8 = np.zeros_like(k8)
-        ke = np.zeros((g.NKV, self.max_T), dtype=np.int8)
+        ke = np.zeros((T, g.NKV), dtype=np.int8)
         ve = np.zeros_like(ke)
         for t in range(T):
             for h in range(g.NKV):
-                k8[h, t], ke[h, t] = cache["k"][t][h]
-                v8[h, t], ve[h, t] = cache["v"][t][h]
-        for buf, a in ((L.BUF_K8, k8), (L.BUF_KE, ke), (L.BUF_V8, v8), (L.BUF_VE, ve)):
-            self.write(buf, layer, a)
+                k8[t, h], ke[t, h] = cache["k"][t][h]
+                v8[t, h], ve[t, h] = cache["v"][t][h]
+        self.load_state_image(layer, np.concatenate([a.reshape(-1).view(np.uint8) for a in (k8, ke, v8, ve)]), T)
         return T
 
-    def save_state(self, path, T):
-        """Per-sequence state (.npz) in the reference's cache layout arrays."""
-        out = {"T": np.array(T)}
+    def save_state(self, path, T=None):
+        """Every layer's state in the reference cache layout (.npz of the
+        f5_state_save images: per DeltaNet layer S [32,128,128] int16 and
+        conv [8192,3] int64; per attention layer k8/v8 [T,4,256] int8 and
+        ke/ve [T,4] int8), plus T and pos."""
+        T0, pos = self.position()
+        if T is not None and T != T0:
+            raise ValueError(f"save_state: the context holds {T0} tokens, not {T}")
+        out = {"T": np.array(T0), "pos": np.array(pos)}
         for i, lt in enumerate(self.geom.layer_types):
             if lt == "full_attention":
-                for nm, buf in (("k8", L.BUF_K8), ("ke", L.BUF_KE), ("v8", L.BUF_V8), ("ve", L.BUF_VE)):
-                    out[f"l{i}_{nm}"] = self.read(buf, i)
+                for nm, a in zip(("k8", "ke", "v8", "ve"), self._kv_arrays(i, T0)):
+                    out[f"l{i}_{nm}"] = a
             else:
-                st = self.get_dn_state(i, T)
+                st = self.get_dn_state(i, T0)
                 out[f"l{i}_conv"], out[f"l{i}_S"] = st["conv"], st["S"]
         np.savez(path, **out)
 
@@ -402,9 +437,12 @@ class DecodeModel:
         T = int(d["T"])
         for i, lt in enumerate(self.geom.layer_types):
             if lt == "full_attention":
-                for nm, buf in (("k8", L.BUF_K8), ("ke", L.BUF_KE), ("v8", L.BUF_V8), ("ve", L.BUF_VE)):
-                    self.write(buf, i, d[f"l{i}_{nm}"])
+                self.load_state_image(i, np.concatenate([np.ascontiguousarray(d[f"l{i}_{nm}"], dtype=np.int8)
+                                                         .reshape(-1).view(np.uint8)
+                                                         for nm in ("k8", "ke", "v8", "ve")]), T)
             else:
                 self.set_dn_state(i, T, {"conv": d[f"l{i}_conv"], "S": d[f"l{i}_S"]})
+        if pos is None:
+            pos = int(d["pos"]) if "pos" in d else T
         self.set_position(T, T if pos is None else pos)
         return T

@@ -332,6 +332,21 @@ int f5_ctx_time_step(f5_ctx *ctx, int reps, double *out, int nout);
  * cache is updated in place (KV slot T / conv window / state). */
 int f5_layer_step(f5_ctx *ctx, int layer, int16_t *x16_inout, int T, int pos);
 
+/* State I/O in the reference's cache layout (ref/layer_fixed.py:1654-1666
+ * new_cache_fx, the caches layer_decode_fx mutates, :1400-1401 and
+ * :1522-1569), one layer at a time:
+ *   DeltaNet layer: S int16 [32][128][128] (head, dk, dv), then the conv
+ *     window int64 [8192][3], oldest first (cache["S"], cache["conv"]);
+ *   attention layer at T tokens: k8 int8 [T][4][256], ke int8 [T][4],
+ *     v8 int8 [T][4][256], ve int8 [T][4] (cache["k"][t][h] = (k8, ke),
+ *     cache["v"][t][h] = (v8, ve)).
+ * f5_state_bytes: image size (0 for a bad layer); f5_state_save: the layer's
+ * image at the context's current T; f5_state_load: write the layer's state
+ * from an image of T tokens (then set T / pos with f5_ctx_set_position). */
+size_t f5_state_bytes(f5_ctx *ctx, int layer, int T);
+int f5_state_save(f5_ctx *ctx, int layer, void *dst, size_t bytes);
+int f5_state_load(f5_ctx *ctx, int layer, const void *src, size_t bytes, int T);
+
 /* raw device buffer copies (enum f5_buf); bytes must equal the buffer size */
 int f5_ctx_read(f5_ctx *ctx, int what, int layer, void *dst, size_t bytes);
 int f5_ctx_write(f5_ctx *ctx, int what, int layer, const void *src, size_t bytes);

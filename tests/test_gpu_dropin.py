@@ -206,3 +206,40 @@ def test_fxrunner_vs_reference(golden, om4):
     y = r.step(int(d["m4_in"][0]), 0)
     assert int(np.argmax(y)) == int(d["m4_out"][0])
     r.model.close()
+
+
+def test_state_images_reference_layout(om4):
+    """f5_state_save / f5_state_load images are the reference cache layout:
+    after a few steps they equal the oracle's caches byte for byte, and a
+    context loaded from them continues identically."""
+    from fable5_llm_b200.model import DecodeModel
+    from fable5_llm_b200.config import Geometry
+    g = O.Geometry(4, 4096)
+    m = DecodeModel(Geometry(4, 4096), max_T=64)
+    m.load_synthetic(SEED)
+    m.reset()
+    orr = O.OracleRunner(om4, max_T=64)
+    tok = 33
+    for t in range(5):
+        tok, _ = m.decode_step(tok, t)
+        orr.step(33 if t == 0 else prev, t)
+        prev = tok
+    imgs = [m.state_image(i) for i in range(4)]
+    for i, lt in enumerate(g.layer_types):
+        c = orr.caches[i]
+        if lt == "full_attention":
+            T = 5
+            ref = np.concatenate([c.k8[:, :T].transpose(1, 0, 2).reshape(-1), c.ke[:, :T].T.reshape(-1),
+                                  c.v8[:, :T].transpose(1, 0, 2).reshape(-1), c.ve[:, :T].T.reshape(-1)])
+            assert np.array_equal(imgs[i].view(np.int8), ref.astype(np.int8))
+        else:
+            ref = np.concatenate([c.S.astype(np.int16).reshape(-1).view(np.uint8),
+                                  c.conv.astype(I64).reshape(-1).view(np.uint8)])
+            assert np.array_equal(imgs[i], ref)
+    nxt = m.decode_step(tok, 5)
+    m.reset()
+    for i in range(4):
+        m.load_state_image(i, imgs[i], 5)
+    m.set_position(5, 5)
+    assert m.decode_step(tok, 5) == nxt
+    m.close()
