@@ -91,6 +91,52 @@ F5_DEV bool ld_tagged(const uint32_t *p, uint32_t tag, uint32_t (&w)[N], unsigne
   }
 }
 
+// ld_tagged over N independent words: every still-pending word is loaded
+// in the same round, so a thread waits one L2 round trip per poll instead of
+// one per word.  Words with act[i] false are skipped (w[i] = 0).
+template <int N>
+F5_DEV bool ld_tagged_multi(const uint32_t *const (&p)[N], const bool (&act)[N], uint32_t tag, uint32_t (&w)[N],
+                            unsigned *abortf, uint32_t *err) {
+  bool done[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    done[i] = !act[i];
+    w[i] = 0;
+  }
+  unsigned long long t0 = 0, tpoll = 0;
+  for (uint32_t it = 0;; ++it) {
+    uint32_t v[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = done[i] ? 0u : ld_cg_poll(p[i]);
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      if (!done[i] && (v[i] >> 16) == tag) {
+        w[i] = v[i];
+        done[i] = true;
+      }
+      ok &= done[i];
+    }
+    if (ok) return true;
+    if ((it & 7) == 7) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t0 == 0) {
+        t0 = t;
+        tpoll = t + 20000;
+      } else if (t >= tpoll) {
+        if (abortf && *reinterpret_cast<volatile unsigned *>(abortf)) return false;
+        if (t - t0 > 1000000000ull) {
+          atomicOr(err, DERR_TIMEOUT);
+          if (abortf) atomicExch(abortf, 1u);
+          return false;
+        }
+        tpoll = t + 20000;
+      }
+    }
+  }
+}
+
 F5_DEV uint4 ld_stream16(const uint8_t *p) {
   uint4 v;
   asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"

@@ -741,7 +741,30 @@ F5_DEV bool c_dn(const MegaArgs &ma, const DnArgs &d, const MegaSmem &S, int &w_
   // ---- every input in one round of loads (tagged: each polled until ready) ----
   const uint32_t itag = (epoch && d.in_tag_op1) ? mk_tag(epoch, d.in_tag_op1) : 0u;
   long long qv = 0, kv = 0;
-  if (tid < 128) {
+  if (itag && tid <= 160) {   // each thread's two tagged words polled together
+    const uint32_t *c32 = reinterpret_cast<const uint32_t *>(d.qkvc);
+    const int i = tid - 128, dv = qd * 32 + i;
+    const uint32_t *const pw[2] = {
+        tid < 128 ? c32 + kh * 128 + tid
+                  : (tid < 160 ? c32 + 2 * d.lkd + h * 128 + dv : reinterpret_cast<const uint32_t *>(d.beta) + h),
+        tid < 128 ? c32 + d.lkd + kh * 128 + tid
+                  : (tid < 160 ? reinterpret_cast<const uint32_t *>(d.z16) + h * 128 + dv
+                               : reinterpret_cast<const uint32_t *>(d.decay) + h)};
+    const bool act[2] = {true, true};
+    uint32_t w2[2];
+    ld_tagged_multi<2>(pw, act, itag, w2, ab.flag, ab.err);
+    if (tid < 128) {
+      qv = tag_s16(w2[0]);
+      kv = tag_s16(w2[1]);
+    } else if (tid < 160) {
+      vzn[i] = tag_s16(w2[0]);
+      vzn[32 + i] = tag_s16(w2[1]);
+      vzn[64 + i] = __ldcg(d.norm_w + dv);
+    } else {
+      mg_gate[0] = (long long)(w2[0] & 0xFFFFu);
+      mg_gate[1] = (long long)(w2[1] & 0xFFFFu);
+    }
+  } else if (tid < 128) {
     qv = ld_in16(d.qkvc, kh * 128 + tid, itag, ab);
     kv = ld_in16(d.qkvc, d.lkd + kh * 128 + tid, itag, ab);
   } else if (tid < 160) {
@@ -1037,11 +1060,33 @@ F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int
 
   // ---- 0. every operand in one round of loads ----
   const uint32_t itag = (epoch && m.in_tag_op1) ? mk_tag(epoch, m.in_tag_op1) : 0u;
-  const long long qx0 = ld_in16(a.qg16, hq * 512 + e, itag, ab), qx1 = ld_in16(a.qg16, hq * 512 + e + 128, itag, ab);
-  const long long kx0 = k_act ? ld_in16(a.k16, g.kv * 256 + e, itag, ab) : 0;
-  const long long kx1 = k_act ? ld_in16(a.k16, g.kv * 256 + e + 128, itag, ab) : 0;
-  const long long v0 = k_act ? ld_in16(a.v16, g.kv * 256 + e, itag, ab) : 0;
-  const long long v1 = k_act ? ld_in16(a.v16, g.kv * 256 + e + 128, itag, ab) : 0;
+  long long qx0, qx1, kx0 = 0, kx1 = 0, v0 = 0, v1 = 0;
+  if (itag) {   // the six tagged words polled together (one L2 round trip per poll)
+    const uint32_t *q32 = reinterpret_cast<const uint32_t *>(a.qg16), *k32 = reinterpret_cast<const uint32_t *>(a.k16),
+                   *v32 = reinterpret_cast<const uint32_t *>(a.v16);
+    const uint32_t *const pw[6] = {q32 + hq * 512 + e, q32 + hq * 512 + e + 128, k32 + g.kv * 256 + e,
+                                   k32 + g.kv * 256 + e + 128, v32 + g.kv * 256 + e, v32 + g.kv * 256 + e + 128};
+    const bool act[6] = {true, true, k_act, k_act, k_act, k_act};
+    uint32_t w6[6];
+    ld_tagged_multi<6>(pw, act, itag, w6, ab.flag, ab.err);
+    qx0 = tag_s16(w6[0]);
+    qx1 = tag_s16(w6[1]);
+    if (k_act) {
+      kx0 = tag_s16(w6[2]);
+      kx1 = tag_s16(w6[3]);
+      v0 = tag_s16(w6[4]);
+      v1 = tag_s16(w6[5]);
+    }
+  } else {
+    qx0 = __ldcg(a.qg16 + hq * 512 + e);
+    qx1 = __ldcg(a.qg16 + hq * 512 + e + 128);
+    if (k_act) {
+      kx0 = __ldcg(a.k16 + g.kv * 256 + e);
+      kx1 = __ldcg(a.k16 + g.kv * 256 + e + 128);
+      v0 = __ldcg(a.v16 + g.kv * 256 + e);
+      v1 = __ldcg(a.v16 + g.kv * 256 + e + 128);
+    }
+  }
   const long long qw0 = __ldcg(a.q_norm + e), qw1 = __ldcg(a.q_norm + e + 128);
   const long long kw0 = __ldcg(a.k_norm + e), kw1 = __ldcg(a.k_norm + e + 128);
   const long long cosv = e < a.rot ? __ldcg(cs + e) : 0, sinv = e < a.rot ? __ldcg(cs + 64 + e) : 0;
