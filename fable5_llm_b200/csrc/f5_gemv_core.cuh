@@ -521,7 +521,9 @@ F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red,
     for (int j = 0; j < MAXB; ++j)
 #pragma unroll
       for (int k = 0; k < 8; ++k) { const unsigned long long m = uabs(v[j][k]); mx = m > mx ? m : mx; }
+    F5_PRO_MARK(4);
     mx = g_max_ull(sy, mx, reinterpret_cast<unsigned long long *>(red));
+    F5_PRO_MARK(6);
     int ka = bf_shift(mx);
     if (ka < 0) ka = 0;                      // attn_o_shift clamp (ref/layer_fixed.py:489-506)
     unsigned long long mg = 0;
@@ -534,6 +536,7 @@ F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red,
         mg = m > mg ? m : mg;
       }
     mg = g_max_ull(sy, mg, reinterpret_cast<unsigned long long *>(red));
+    F5_PRO_MARK(5);
     const int ex = dynq8_e(mg);
 #pragma unroll
     for (int j = 0; j < MAXB; ++j) {

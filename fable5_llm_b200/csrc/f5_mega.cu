@@ -133,6 +133,35 @@ F5_DEV bool mwait(uint64_t *b, uint32_t parity, const Abort &ab) {
 }
 
 
+// The producer's waits (a slot, the scratch or the gains buffer to be freed
+// by the consumers): the producer lane shares a sub-partition with four
+// consumer warps, so between tries it sleeps instead of spinning and takes
+// no issue slots from them; a refill issued up to ~0.1 us late is hidden by
+// the HBM latency it waits on anyway.
+F5_DEV bool pwait(uint64_t *b, uint32_t parity, const Abort &ab) {
+  const uint32_t addr = smem_u32(b);
+  unsigned long long t0 = 0, tpoll = 0;
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok) : "r"(addr), "r"(parity) : "memory");
+    if (ok) return true;
+    __nanosleep(64);
+    if ((it & 15) == 15) {
+      const unsigned long long t = gtimer();
+      if (t0 == 0) {
+        t0 = t;
+        tpoll = t + MG_POLL_NS;
+      } else if (t >= tpoll) {
+        if (ab.raised()) return false;
+        if (t - t0 > MG_WAIT_NS) { ab.raise(); return false; }
+        tpoll = t + MG_POLL_NS;
+      }
+    }
+  }
+}
+
 // Counter barrier over `target` CTAs (consumer groups).  One thread's
 // release add / acquire polls, bracketed by the group's named barrier, order
 // every consumer thread's prior global writes before any later read in the
@@ -312,7 +341,7 @@ F5_DEV void producer(const MegaArgs &ma, const MegaSmem &S, int T, int pos, cons
   issue_desc(ma, S, 0);
   desc_pending = 0;
   for (int oi = 0; oi < ma.nops && !bad; ++oi) {
-    if (!mwait(&mg_bpd[oi & 1], (oi >> 1) & 1, ab)) { bad = true; break; }
+    if (!pwait(&mg_bpd[oi & 1], (oi >> 1) & 1, ab)) { bad = true; break; }
     desc_pending = -1;
     if (oi + 1 < ma.nops) {
       issue_desc(ma, S, oi + 1);
@@ -323,7 +352,7 @@ F5_DEV void producer(const MegaArgs &ma, const MegaSmem &S, int T, int pos, cons
     if (kind == MK_GEMV) {
       const GemvArgs &a = op.g;
       if (a.pro.mode == PRO_RMSNORM) {   // the prologue's gains, ahead of the op's rows
-        if (n_gain > 0 && !mwait(&mg_gfree, (n_gain - 1) & 1, ab)) { bad = true; break; }
+        if (n_gain > 0 && !pwait(&mg_gfree, (n_gain - 1) & 1, ab)) { bad = true; break; }
         mbar_expect_tx(&mg_gfull, MG_GAINB);
         bulk_g2s(S.gains(), a.pro.w, MG_GAINB, &mg_gfull);
         mg_cnt[6] = ++n_gain;
@@ -333,7 +362,7 @@ F5_DEV void producer(const MegaArgs &ma, const MegaSmem &S, int T, int pos, cons
       Chunk ch;
       while (next_chunk(a, u, u1, ch)) {
         const int s = rp.s;
-        if (rp.lap > 0 && !mwait(&mg_empty[s], rp.ph ^ 1u, ab)) { bad = true; break; }
+        if (rp.lap > 0 && !pwait(&mg_empty[s], rp.ph ^ 1u, ab)) { bad = true; break; }
         const GemvSeg &sg = a.seg[ch.seg];
         const uint32_t nb = (uint32_t)ch.n * a.stride;
         const bool pair = sg.mode == GM_SILU_MUL;
@@ -347,7 +376,7 @@ F5_DEV void producer(const MegaArgs &ma, const MegaSmem &S, int T, int pos, cons
       }
     } else if (kind == MK_DN) {
       if (b < 4 * ma.dn_heads) {   // head b / 4, column quarter b % 4: one contiguous 8 KB block
-        if (n_scr > 0 && !mwait((&mg_bfree), (n_scr - 1) & 1, ab)) { bad = true; break; }
+        if (n_scr > 0 && !pwait((&mg_bfree), (n_scr - 1) & 1, ab)) { bad = true; break; }
         mbar_expect_tx((&mg_bsd), 8192);
         bulk_g2s(S.scr() + DN_SD, op.d.S + (size_t)(b >> 2) * 16384 + (size_t)(b & 3) * 4096, 8192, (&mg_bsd));
         mg_cnt[1] += 1;
@@ -357,7 +386,7 @@ F5_DEV void producer(const MegaArgs &ma, const MegaSmem &S, int T, int pos, cons
       const AttnArgs &a = op.at.a;
       const AttGeo g = att_geo(a, T, pos, G, b);
       if (g.kv < a.nkv) {
-        if (n_scr > 0 && !mwait((&mg_bfree), (n_scr - 1) & 1, ab)) { bad = true; break; }
+        if (n_scr > 0 && !pwait((&mg_bfree), (n_scr - 1) & 1, ab)) { bad = true; break; }
         int sb;
         const int n = att_fill_rows(g, 0, sb);
         if (n > 0) {
@@ -741,6 +770,7 @@ F5_DEV bool c_dn(const MegaArgs &ma, const DnArgs &d, const MegaSmem &S, int &w_
   // ---- every input in one round of loads (tagged: each polled until ready) ----
   const uint32_t itag = (epoch && d.in_tag_op1) ? mk_tag(epoch, d.in_tag_op1) : 0u;
   long long qv = 0, kv = 0;
+  const long long nw_pre = (tid >= 128 && tid < 160) ? __ldcg(d.norm_w + qd * 32 + tid - 128) : 0;
   if (itag && tid <= 160) {   // each thread's two tagged words polled together
     const uint32_t *c32 = reinterpret_cast<const uint32_t *>(d.qkvc);
     const int i = tid - 128, dv = qd * 32 + i;
@@ -759,7 +789,7 @@ F5_DEV bool c_dn(const MegaArgs &ma, const DnArgs &d, const MegaSmem &S, int &w_
     } else if (tid < 160) {
       vzn[i] = tag_s16(w2[0]);
       vzn[32 + i] = tag_s16(w2[1]);
-      vzn[64 + i] = __ldcg(d.norm_w + dv);
+      vzn[64 + i] = nw_pre;
     } else {
       mg_gate[0] = (long long)(w2[0] & 0xFFFFu);
       mg_gate[1] = (long long)(w2[1] & 0xFFFFu);
@@ -1058,7 +1088,11 @@ F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int
   const size_t kvrow = (size_t)g.kv * a.max_T;
   const bool k_act = hs == 0;
 
-  // ---- 0. every operand in one round of loads ----
+  // ---- 0. every operand in one round of loads: the constants first (their
+  // L2 round trip overlaps the wait for the tagged inputs) ----
+  const long long qw0 = __ldcg(a.q_norm + e), qw1 = __ldcg(a.q_norm + e + 128);
+  const long long kw0 = __ldcg(a.k_norm + e), kw1 = __ldcg(a.k_norm + e + 128);
+  const long long cosv = e < a.rot ? __ldcg(cs + e) : 0, sinv = e < a.rot ? __ldcg(cs + 64 + e) : 0;
   const uint32_t itag = (epoch && m.in_tag_op1) ? mk_tag(epoch, m.in_tag_op1) : 0u;
   long long qx0, qx1, kx0 = 0, kx1 = 0, v0 = 0, v1 = 0;
   if (itag) {   // the six tagged words polled together (one L2 round trip per poll)
@@ -1087,9 +1121,6 @@ F5_DEV bool c_attn(const MegaArgs &ma, const MegaAttn &m, const MegaSmem &S, int
       v1 = __ldcg(a.v16 + g.kv * 256 + e + 128);
     }
   }
-  const long long qw0 = __ldcg(a.q_norm + e), qw1 = __ldcg(a.q_norm + e + 128);
-  const long long kw0 = __ldcg(a.k_norm + e), kw1 = __ldcg(a.k_norm + e + 128);
-  const long long cosv = e < a.rot ? __ldcg(cs + e) : 0, sinv = e < a.rot ? __ldcg(cs + 64 + e) : 0;
 
   // ---- 1. q / k norm + rope; kv_quant of the new k and v ----
   long long kn0, kn1;
