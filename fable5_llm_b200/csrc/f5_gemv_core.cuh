@@ -569,11 +569,15 @@ F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red,
 // ---------------------------------------------------------------------------
 // conv4 + SiLU of one channel (ref/layer_fixed.py:1511-1520): ring word rw
 // holds the 4 int16 slots, cw the 4 weights, v this step's pre-conv input
+// ring slot k (0..3) of the four int16 slots packed in rw, selected in
+// registers (a dynamically indexed local array would live in local memory)
+F5_DEV long long ring_slot(uint2 rw, int k) {
+  const uint32_t w = (k & 2) ? rw.y : rw.x;
+  return (long long)(int16_t)((k & 1) ? (w >> 16) : (w & 0xFFFFu));
+}
 F5_DEV int32_t conv_silu(long long v, uint2 rw, int4 cw, int T) {
-  const int16_t r4[4] = {(int16_t)(rw.x & 0xFFFFu), (int16_t)(rw.x >> 16), (int16_t)(rw.y & 0xFFFFu),
-                         (int16_t)(rw.y >> 16)};
-  const long long acc = (long long)r4[(T + 1) & 3] * cw.x + (long long)r4[(T + 2) & 3] * cw.y +
-                        (long long)r4[(T + 3) & 3] * cw.z + v * cw.w;
+  const long long acc = ring_slot(rw, (T + 1) & 3) * cw.x + ring_slot(rw, (T + 2) & 3) * cw.y +
+                        ring_slot(rw, (T + 3) & 3) * cw.z + v * cw.w;
   const long long pre = clip(rshr(acc, RS_F + CW_F - 12), -(1 << 20), (1 << 20) - 1);
   const long long co = clip16(silu_q(pre));
   return (int32_t)rshr(co, 12 - QKV_F);
