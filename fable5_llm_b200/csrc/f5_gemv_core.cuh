@@ -137,6 +137,50 @@ F5_DEV bool ld_tagged_multi(const uint32_t *const (&p)[N], const bool (&act)[N],
   }
 }
 
+// ld_tagged over MAXB 8-word blocks (block j at p[j], 16-byte aligned):
+// all blocks are loaded in the same round, so a thread waits one L2 round
+// trip per poll instead of one per block.  Blocks with act[j]
+// false are skipped; raw[j] receives block j's eight int16 values.
+template <int MAXB>
+F5_DEV bool ld_tagged_blocks(const uint32_t *const (&p)[MAXB], const bool (&act)[MAXB], uint32_t tag,
+                             uint4 (&raw)[MAXB], unsigned *abortf, uint32_t *err) {
+  unsigned long long t0 = 0, tpoll = 0;
+  for (uint32_t it = 0;; ++it) {
+    bool ok = true;
+#pragma unroll
+    for (int j = 0; j < MAXB; ++j) {
+      const uint4 lo = ld_cg_poll(reinterpret_cast<const uint4 *>(p[j]));
+      const uint4 hi = ld_cg_poll(reinterpret_cast<const uint4 *>(p[j]) + 1);
+      const uint32_t t8 = ((lo.x >> 16) ^ tag) | ((lo.y >> 16) ^ tag) | ((lo.z >> 16) ^ tag) | ((lo.w >> 16) ^ tag) |
+                          ((hi.x >> 16) ^ tag) | ((hi.y >> 16) ^ tag) | ((hi.z >> 16) ^ tag) | ((hi.w >> 16) ^ tag);
+      ok &= !act[j] || t8 == 0u;
+      raw[j] = act[j] ? make_uint4((lo.x & 0xFFFFu) | (lo.y << 16), (lo.z & 0xFFFFu) | (lo.w << 16),
+                                   (hi.x & 0xFFFFu) | (hi.y << 16), (hi.z & 0xFFFFu) | (hi.w << 16))
+                      : make_uint4(0, 0, 0, 0);
+    }
+    if (ok) return true;
+    // back off between rounds: every CTA polling all its blocks at full rate
+    // floods L2 with loads of the lines the last writers are storing to
+    __nanosleep(100);
+    if ((it & 7) == 7) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t0 == 0) {
+        t0 = t;
+        tpoll = t + 20000;
+      } else if (t >= tpoll) {
+        if (abortf && *reinterpret_cast<volatile unsigned *>(abortf)) return false;
+        if (t - t0 > 1000000000ull) {
+          atomicOr(err, DERR_TIMEOUT);
+          if (abortf) atomicExch(abortf, 1u);
+          return false;
+        }
+        tpoll = t + 20000;
+      }
+    }
+  }
+}
+
 F5_DEV uint4 ld_stream16(const uint8_t *p) {
   uint4 v;
   asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -381,7 +425,17 @@ F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red,
   if (P.mode == PRO_RMSNORM || P.mode == PRO_DYNQ8) {
     const int16_t *src = static_cast<const int16_t *>(P.src);
     uint4 raw[MAXB];
-    if (in_tag) {
+    if (in_tag && MAXB > 1) {   // several blocks per thread: polled together
+      const uint32_t *pb[MAXB];
+      bool act[MAXB];
+#pragma unroll
+      for (int j = 0; j < MAXB; ++j) {
+        const int b = tid + j * BT;
+        act[j] = b < nblk;
+        pb[j] = static_cast<const uint32_t *>(P.src) + 8 * (act[j] ? b : 0);
+      }
+      ld_tagged_blocks<MAXB>(pb, act, in_tag, raw, a.abort_flag, a.err);
+    } else if (in_tag) {
 #pragma unroll
       for (int j = 0; j < MAXB; ++j) {
         const int b = tid + j * BT;
