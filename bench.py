@@ -319,6 +319,114 @@ class ProjectionsWork:
                 events[j][1].record()
 
 
+def time_configs(args, hbm_peak):
+    """Configs 1-3 of the survey's measurement table on this GPU, through the
+    same GEMV kernel the per-op engine runs (CUDA events, device-resident
+    inputs): config 1 = one 12288 x 4096 matvec (8 seeded copies used in
+    turn, 208 MB > L2), config 2 = all 249 projection matvecs of a step
+    (CUDA graph, 4.09 GB > L2), config 3 = the 248,320-row LM head with the
+    fused first-max argmax (524 MB > L2)."""
+    import torch
+    from fable5_llm_b200 import _lib as L
+    from fable5_llm_b200 import ops, synth
+    out = {}
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(args.seed)
+    # config 1
+    N, K = 12288, 4096
+    stride = 2112
+    copies = [torch.empty(N * stride, dtype=torch.uint8, device=dev) for _ in range(8)]
+    for i, c in enumerate(copies):
+        ops.synth_w4(c, N, K, 128, 0, synth.stream_key(args.seed, 1000 + i, synth.STREAM_W),
+                     synth.stream_key(args.seed, 1000 + i, synth.STREAM_M), 0)
+    x8 = ops.to_dev(rng.integers(-127, 128, K).astype(np.int8))
+    y = torch.empty(N, dtype=torch.int32, device=dev)
+    segs = [ops.seg(c, y, N, L.GM_Y32) for c in copies]
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    # the 8 matvecs replayed as one CUDA graph (launch-bound otherwise)
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        for i in range(16):
+            ops.gemv([segs[i % 8]], K, 128, 7, x8, err=err)
+    torch.cuda.current_stream().wait_stream(st)
+    torch.cuda.synchronize()
+    g1 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g1):
+        for i in range(8):
+            ops.gemv([segs[i]], K, 128, 7, x8, err=err)
+    for _ in range(3):
+        g1.replay()
+    reps = 1000
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps // 8):
+        g1.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    del g1
+    gbs = N * stride / (us * 1e-6) / 1e9
+    out["config1_matvec_12288x4096"] = {"us_per_matvec": round(us, 2), "gbs": round(gbs, 1),
+                                        "frac": round(gbs / hbm_peak, 4), "algorithmic_bytes": N * stride,
+                                        "launches": reps, "note": "8 seeded copies in turn (208 MB > L2), replayed as a CUDA graph of 8 launches"}
+    del copies, segs
+    # config 3: LM head + argmax
+    N = 248320
+    head = torch.empty(N * stride, dtype=torch.uint8, device=dev)
+    ops.synth_w4(head, N, K, 128, 0, synth.stream_key(args.seed, 2000, synth.STREAM_W),
+                 synth.stream_key(args.seed, 2000, synth.STREAM_M), 0)
+    key = torch.zeros(1, dtype=torch.int64, device=dev)
+    hseg = [ops.seg(head, None, N, L.GM_ARGMAX)]
+    for _ in range(3):
+        key.zero_()
+        ops.gemv(hseg, K, 128, 7, x8, argmax=key, err=err)
+    reps = 20
+    e0.record()
+    for _ in range(reps):
+        key.zero_()
+        ops.gemv(hseg, K, 128, 7, x8, argmax=key, err=err)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    gbs = N * stride / (us * 1e-6) / 1e9
+    out["config3_lm_head_argmax"] = {"us_per_head": round(us, 1), "gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4),
+                                     "algorithmic_bytes": N * stride, "launches": 2 * reps,
+                                     "note": "GEMV with the fused first-max argmax key (plus a key reset per call)"}
+    del head
+    # config 2: all projections of a step
+    work = ProjectionsWork(args, 1, 0)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            work.step()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        work.step()
+    for _ in range(3):
+        g.replay()
+    reps = 10
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    gbs = work.bytes_per_step / (ms * 1e-3) / 1e9
+    out["config2_all_projections"] = {"ms_per_step": round(ms, 3), "token_equivalents_per_s": round(1000.0 / ms, 1),
+                                      "gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4),
+                                      "algorithmic_bytes": work.bytes_per_step,
+                                      "launches_per_step": work.launches_per_step,
+                                      "note": "249 matvecs with their fused epilogues, grouped as the decode step "
+                                              "issues them, one CUDA graph per step"}
+    del work, g
+    torch.cuda.synchronize()
+    return out
+
+
 def run_step(args, ws, rank, local):
     """The headline workload: the full decode step replayed as a CUDA graph."""
     import torch
@@ -419,11 +527,14 @@ def run_step(args, ws, rank, local):
     batched = None
     if ws == 1 and args.layers == 32 and not args.no_batched:
         batched = {}
-        for B in (8, 32, 64):
+        for B in (1, 8, 32, 64):
             bms, _, _ = time_batched(m, B, 1024, 10, 3, args.seed)
             batched[f"B{B}"] = {"tok_s": round(B * 1000.0 / bms, 1), "ms_per_step": round(bms, 3),
                                 "gbs": round((WEIGHT_BYTES_9B + B * batched_state_bytes(m.geom, 1024)) /
                                              (bms * 1e-3) / 1e9, 1)}
+    configs = None
+    if ws == 1 and args.layers == 32 and not args.no_batched:
+        configs = time_configs(args, hbm_peak)
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         cpu = cpu_sample_step(seconds=20.0, context=ctx_len)
@@ -488,6 +599,8 @@ def run_step(args, ws, rank, local):
                                    "FxRunner's resid_max / resid_clip (over all ranks' rows) and the "
                                    "DeltaNet state's sat counter"},
         }
+        if configs:
+            line["configs_1_2_3"] = configs
         if batched:
             line["batched_config5"] = {"per_B": batched, "context": 1024,
                                        "note": "B independent sequences, tcgen05 W4A8 GEMMs; caches zero-filled "
