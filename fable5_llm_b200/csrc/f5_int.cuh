@@ -39,16 +39,16 @@ constexpr int64_t EPS_M = 1099512;   // round(1e-6 * 2^40), ref/layer_fixed.py:6
 constexpr int EPS_Q = 40;
 
 // ref/w4a8_ref.py:90-99 rshift_round: round half away from zero; s<0 = exact <<.
+// For s > 0 it is computed branch-free as floor((v + 2^(s-1) - [v < 0]) / 2^s)
+// (an arithmetic shift): for v < 0, -floor((-v + 2^(s-1)) / 2^s) =
+// floor((v - 2^(s-1)) / 2^s + 1 - 2^-s) = floor((v + 2^(s-1) - 1) / 2^s).
 F5_DEV int64_t rshr(int64_t v, int s) {
-  if (s == 0) return v;
-  if (s < 0) return (int64_t)((uint64_t)v << (-s));
-  const int64_t add = (int64_t)1 << (s - 1);
-  return v >= 0 ? (v + add) >> s : -((-v + add) >> s);
+  if (s <= 0) return s == 0 ? v : (int64_t)((uint64_t)v << (-s));
+  return (v + ((int64_t)1 << (s - 1)) - (int64_t)(v < 0)) >> s;
 }
 // 32-bit form for operands known to fit (|v| + 2^(s-1) < 2^31), 0 < s < 31.
 F5_DEV int32_t rshr32p(int32_t v, int s) {
-  const int32_t add = 1 << (s - 1);
-  return v >= 0 ? (v + add) >> s : -((-v + add) >> s);
+  return (v + (1 << (s - 1)) - (int32_t)(v < 0)) >> s;
 }
 F5_DEV int64_t clip(int64_t v, int64_t lo, int64_t hi) { return v < lo ? lo : (v > hi ? hi : v); }
 F5_DEV int32_t clip16(int64_t v) { return (int32_t)clip(v, -32768, 32767); }  // ref/layer_fixed.py:809
