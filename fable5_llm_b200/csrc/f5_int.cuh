@@ -134,10 +134,11 @@ F5_DEV void recip_q(uint64_t v, int P, int64_t &r_out, int &e_out) {
 }
 
 // ref/fixedpoint.py:99-106 exp2_frac_q16, f in [0, 2^16)
+// (table entries < 2^18, lo < 2^8: the interpolation fits 32-bit integers)
 F5_DEV int64_t exp2_frac_q16(int64_t f) {
   const int i = (int)(f >> 8), lo = (int)(f & 0xFF);
-  const int64_t a = F5_LUT_EXP2[i], b = F5_LUT_EXP2[i + 1];
-  return a + (((b - a) * lo + 128) >> 8);
+  const int32_t a = F5_LUT_EXP2[i], b = F5_LUT_EXP2[i + 1];
+  return (int64_t)(a + (((b - a) * lo + 128) >> 8));
 }
 
 // ref/fixedpoint.py:109-121 exp_neg_q: x <= 0 in Q16 -> Q30.  |x| < 2^45.
@@ -151,12 +152,13 @@ F5_DEV int64_t exp_neg_q(int64_t x) {
 }
 
 // ref/fixedpoint.py:135-147 sigmoid_q: Q12 -> Q15, PWL over [-16, 16)
+// (entries <= 32767, lo < 2^9: the interpolation fits 32-bit integers)
 F5_DEV int64_t sigmoid_q(int64_t x) {
-  const int64_t xc = clip(x, -(16 << 12), (16 << 12) - 1);
-  const int u = (int)(xc + (16 << 12));
+  const int32_t xc = (int32_t)clip(x, -(16 << 12), (16 << 12) - 1);
+  const int u = xc + (16 << 12);
   const int i = u >> 9, lo = u & 0x1FF;
-  const int64_t a = F5_LUT_SIGMOID[i], b = F5_LUT_SIGMOID[i + 1];
-  return a + (((b - a) * lo + 256) >> 9);
+  const int32_t a = F5_LUT_SIGMOID[i], b = F5_LUT_SIGMOID[i + 1];
+  return (int64_t)(a + (((b - a) * lo + 256) >> 9));
 }
 
 // ref/fixedpoint.py:150-165 softplus_q: Q12 -> Q12
@@ -165,12 +167,18 @@ F5_DEV int64_t softplus_q(int64_t x) {
   if (x < -(16 << 12)) return 0;
   const int u = (int)(x + (16 << 12));
   const int i = u >> 9, lo = u & 0x1FF;
-  const int64_t a = F5_LUT_SOFTPLUS[i], b = F5_LUT_SOFTPLUS[i + 1];
-  return a + (((b - a) * lo + 256) >> 9);
+  const int32_t a = F5_LUT_SOFTPLUS[i], b = F5_LUT_SOFTPLUS[i + 1];   // < 2^17: 32-bit interpolation
+  return (int64_t)(a + (((b - a) * lo + 256) >> 9));
 }
 
 // ref/fixedpoint.py:168-171 silu_q = rshr(x * sigmoid_q(x), 15)
-F5_DEV int64_t silu_q(int64_t x) { return rshr(x * sigmoid_q(x), 15); }
+// x * sigmoid_q(x) as one 32 x 32 -> 64-bit multiply whenever x fits int32
+// (always on the decode path: |x| <= 2^21)
+F5_DEV int64_t silu_q(int64_t x) {
+  const int64_t sg = sigmoid_q(x);
+  const int64_t p = (x == (int64_t)(int32_t)x) ? (int64_t)(int32_t)x * (int32_t)sg : x * sg;
+  return rshr(p, 15);
+}
 
 // ref/layer_fixed.py:1224-1236 second shift of matvec_to, either direction
 F5_DEV int64_t shift_to(int64_t y32, int sh2) { return sh2 >= 0 ? rshr(y32, sh2) : (int64_t)((uint64_t)y32 << (-sh2)); }
