@@ -54,6 +54,8 @@ SIGNATURES = [
     ("f5_prim_dev", c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp]),
     ("f5_synth_w4_dev", c_int, [c_vp, c_ll, c_int, c_int, c_ll, c_u64, c_u64, c_int, c_vp]),
     ("f5_synth_emb_dev", c_int, [c_vp, c_ll, c_int, c_ll, c_u64, c_vp]),
+    ("f5_quant_w4_scales", c_int, [c_vp, c_int, c_int, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp]),
+    ("f5_quant_w4_pack", c_int, [c_vp, c_int, c_int, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp]),
     ("f5_batch_matvec_ws_bytes", c_size, [c_int, c_int, c_int]),
     ("f5_batch_trace", c_int, [c_int, c_vp, c_size]),
     ("f5_batch_matvec_y32_dev", c_int, [c_vp, c_int, c_int, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp,

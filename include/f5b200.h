@@ -123,6 +123,30 @@ int f5_synth_w4_dev(uint8_t *d_img, long long nrows, int K, int g, long long row
 int f5_synth_emb_dev(int16_t *d_emb, long long nrows, int H, long long row0,
                      uint64_t key_e, void *stream);
 
+/* Checkpoint quantization of one float matrix d_w [N][K] (device; float32,
+ * or float64 when w_f64 is nonzero) into
+ * the W4 row format, on the GPU, bit-identical to the reference's host
+ * quantizers (g = 128):
+ *   1. f5_quant_w4_scales: every group's scale s into d_best_s [N][K/128]
+ *      (double) and the bit pattern of max(s) into *d_smax_bits.  nalpha > 0:
+ *      the MSE grid search of quant_linear_mse (ref/layer_fixed.py:981-1030)
+ *      over the caller's alpha[] (numpy linspace(amin, 1, nalpha)),
+ *      d_salience (nullable) = its per-channel error weights [K]
+ *      (_salience_weights, ref/layer_fixed.py:943-978); nalpha = 0: the
+ *      max|W|/7 rule of quantize_weights (ref/w4a8_ref.py:154-180).
+ *   2. the caller sets e = ceil(log2(max s)) + 1 (ref/w4a8_ref.py:171; host
+ *      libm, like the reference);
+ *   3. f5_quant_w4_pack: m, eff and the codes; d_img [N][row stride]
+ *      receives pack_ddr_rows' bytes (ref/w4a8_ref.py:349-370); d_w4 [N][K]
+ *      and d_m [N][K/128] (both nullable) the unpacked w4 / m arrays.
+ * sh is the fixed rule of final_shift (ref/w4a8_ref.py:177-179). */
+int f5_quant_w4_scales(const void *d_w, int w_f64, int N, int K, int g, const double *alpha,
+                       int nalpha, const double *d_salience, double *d_best_s,
+                       uint64_t *d_smax_bits, void *stream);
+int f5_quant_w4_pack(const void *d_w, int w_f64, int N, int K, int g, const double *d_best_s,
+                     int e_shared, uint8_t *d_img, int8_t *d_w4, uint16_t *d_m,
+                     void *stream);
+
 /* Batched ref/w4a8_ref.py:254-289 matvec_y32 on the tensor cores (tcgen05
  * int8 MMA, int32 TMEM accumulators): y32[b][row] for B quantized inputs
  * d_x8 [B][K] against one packed image (d_w, 256-byte aligned), the way B
