@@ -66,6 +66,7 @@ SIGNATURES = [
     ("f5_bctx_set_position", c_int, [c_vp, c_int, c_int, c_int]),
     ("f5_bctx_get_position", c_int, [c_vp, c_int, c_vp, c_vp]),
     ("f5_bctx_step", c_int, [c_vp, c_vp, c_vp, c_vp]),
+    ("f5_bctx_prefill", c_int, [c_vp, c_int, c_vp, c_int, c_vp, c_vp]),
     ("f5_bctx_launch", c_int, [c_vp, c_int]),
     ("f5_bctx_sync", c_int, [c_vp, c_vp, c_vp]),
     ("f5_bctx_stream", c_int, [c_vp, c_vp]),

@@ -65,6 +65,17 @@ class BatchModel:
         L.check(self.lib.f5_bctx_step(self.h, _p(tok), _p(nt), _p(mv)), "f5_bctx_step")
         return nt, mv
 
+    def prefill(self, seq, tokens):
+        """Ingest a prompt into sequence seq layer-major (f5_bctx_prefill)
+        -> (the argmax after its last token, that token's y32 logit); the
+        state equals len(tokens) decode steps' and the next step of seq is
+        fed that argmax."""
+        tok = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32).reshape(-1))
+        nt, mv = ctypes.c_int32(), ctypes.c_int32()
+        L.check(self.lib.f5_bctx_prefill(self.h, int(seq), _p(tok), int(tok.size), ctypes.byref(nt),
+                                         ctypes.byref(mv)), "f5_bctx_prefill")
+        return int(nt.value), int(mv.value)
+
     def launch(self, n):
         """Enqueue n greedy steps (each sequence fed its own argmax)."""
         L.check(self.lib.f5_bctx_launch(self.h, int(n)), "f5_bctx_launch")

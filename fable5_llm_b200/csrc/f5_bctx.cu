@@ -30,6 +30,7 @@
 #include "f5_capi_util.h"
 #include "f5_ctx_priv.h"
 #include "f5_dn.cuh"
+#include "f5_gemv_core.cuh"
 #include "f5_int.cuh"
 
 namespace f5 {
@@ -65,6 +66,31 @@ __global__ void k_bstep_end(StepParams *p, const unsigned long long *key, const 
     p[b].T += 1;
     p[b].steps += 1;
   }
+}
+
+// Causal conv4 + SiLU of one prompt chunk's pre-conv projections, token by
+// token (ref/layer_fixed.py:1511-1520): channel ch of token t reads the
+// ring's three previous inputs, and its own input then replaces the oldest
+// slot -- the GM_CONV epilogue of C consecutive decode steps.  One thread
+// per channel, the 4-slot ring held in registers across the chunk.
+__global__ void k_conv_seq(const int16_t *pre, int16_t *out, int16_t *ring, const int32_t *cw, int C,
+                           const StepParams *pp, int nch) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+  if (ch >= nch) return;
+  const int T0 = pp[0].T;
+  uint2 rw = *reinterpret_cast<const uint2 *>(ring + (size_t)ch * 4);
+  const int4 w = *reinterpret_cast<const int4 *>(cw + (size_t)ch * 4);
+  for (int t = 0; t < C; ++t) {
+    const int T = T0 + t;
+    const long long v = pre[(size_t)t * nch + ch];
+    out[(size_t)t * nch + ch] = (int16_t)conv_silu(v, rw, w, T);
+    const uint32_t hv = (uint32_t)(uint16_t)(int16_t)v;
+    uint32_t &word = (T & 2) ? rw.y : rw.x;
+    word = (T & 1) ? ((word & 0x0000FFFFu) | (hv << 16)) : ((word & 0xFFFF0000u) | hv);
+  }
+  *reinterpret_cast<uint2 *>(ring + (size_t)ch * 4) = rw;
 }
 
 namespace {
@@ -121,6 +147,8 @@ struct f5_bctx {
   void *tk_ws = nullptr;       // f5_bctx_topk: chunk lists of B logit rows, B results
   f5_topk32 *tk_out = nullptr;
   StepParams *params = nullptr, *h_params = nullptr;
+  StepParams *pparams = nullptr;   // f5_bctx_prefill: one entry per token of the chunk (T, pos, tok)
+  int ncol = 0;                    // GEMM columns of the next ops (0: B); prefill chunks set it
   cudaGraphExec_t exec = nullptr;
   bool dirty = true;
   bool pdl = true;             // programmatic dependent launch between the step's kernels
@@ -224,7 +252,8 @@ cudaError_t bop(f5_bctx *c, const BSeg *sg, int nseg, int K, const GemvPrologue 
   ga.stride = sg[0].m->stride;
   ga.sh = sg[0].m->sh;
   ga.S = bgemm_splits(tiles, NG, sm_count(), head);
-  ga.B = c->B;
+  const int ncol = c->ncol > 0 ? c->ncol : c->B;
+  ga.B = ncol;
   ga.Bp = c->Bp;
   ga.xt = c->xt;
   ga.p = c->p;
@@ -245,7 +274,7 @@ cudaError_t bop(f5_bctx *c, const BSeg *sg, int nseg, int K, const GemvPrologue 
   pa.src2_bs = src2_bs;
   pa.K = K;
   pa.NG = NG;
-  pa.B = c->B;
+  pa.B = ncol;
   pa.Bp = c->Bp;
   pa.xmeta = c->xmeta;
   pa.xt = c->xt;
@@ -268,7 +297,7 @@ cudaError_t bop(f5_bctx *c, const BSeg *sg, int nseg, int K, const GemvPrologue 
   ea.g.sh = ga.sh;
   ea.g.err = c->err;
   ea.S = ga.S;
-  ea.B = c->B;
+  ea.B = ncol;
   ea.Bp = c->Bp;
   ea.ptot = prow;
   ea.p = c->p;
@@ -497,6 +526,157 @@ int bbuf(f5_bctx *c, int what, int layer, int seq, uint8_t **ptr, size_t *bytes)
   return F5_OK;
 }
 
+// One chunk of layer-major prompt ingestion for sequence `seq`: the C
+// tokens in pparams[0..C) (tok, T = T0 + t, pos = pos0 + t) are the C
+// columns of every projection GEMM, while the conv window, the DeltaNet
+// recurrence and the KV appends -- the parts that carry state from one token
+// to the next -- run token by token in order.  Every value therefore equals
+// what C sequential decode steps of that sequence compute.  `last`: the LM
+// head runs too and pparams[t].next_tok receives each column's argmax.
+cudaError_t enqueue_prefill_chunk(f5_bctx *c, int seq, int C, bool last) {
+  cudaError_t e;
+  c->ncol = C;
+  {
+    StepParams *p = c->pparams;
+    const int16_t *emb = c->m->emb;
+    int vocab = c->m->cfg.vocab, hd = H;
+    int16_t *x = c->x16;
+    unsigned long long *k = c->key;
+    void *args[] = {&p, &emb, &vocab, &hd, &x, &k};
+    if ((e = launch_pdl_b((const void *)k_bstep_begin, args, dim3(C), dim3(256), c->st, c->pdl))) return e;
+  }
+  const long long xbs = (long long)H * 2;
+  for (int li = 0; li < (int)c->L.size(); ++li) {
+    const Layer &l = c->m->L[li];
+    BLayer &s = c->L[li];
+    GemvPrologue pro = {};
+    pro.mode = PRO_RMSNORM;
+    pro.src = c->x16;
+    pro.w = l.ln1;
+    pro.in_f = RS_F;
+    pro.one_plus = 1;
+    if (!l.attn) {
+      BSeg sg[4];
+      sg[0].m = &l.m[0]; sg[0].mode = GM_TO16; sg[0].out_f = RS_F;     // pre-conv inputs, convolved below
+      sg[0].out = c->qkv16; sg[0].out_bs = (long long)CONV_DIM * 2;
+      sg[1].m = &l.m[1]; sg[1].mode = GM_TO16; sg[1].out_f = QKV_F; sg[1].out = c->z16; sg[1].out_bs = (long long)LVD * 2;
+      sg[2].m = &l.m[2]; sg[2].mode = GM_GATE_B; sg[2].out_f = 12; sg[2].out = c->b16; sg[2].out_bs = (long long)LNH * 2;
+      sg[2].aux_out = c->gates; sg[2].aux_bs = (long long)2 * LNH * 4;
+      sg[3].m = &l.m[3]; sg[3].mode = GM_GATE_A; sg[3].out_f = 12; sg[3].out = c->a16; sg[3].out_bs = (long long)LNH * 2;
+      sg[3].aux_out = c->gates + LNH; sg[3].aux_bs = (long long)2 * LNH * 4;
+      sg[3].aux0 = l.dt_bias; sg[3].aux1 = l.A;
+      if ((e = bop(c, sg, 4, H, pro, xbs, 0, false))) return e;
+      {
+        const int16_t *pre = c->qkv16;
+        int16_t *out = c->qkvc16;
+        int16_t *ring = s.conv + (size_t)seq * CONV_DIM * 4;
+        const int32_t *cw = l.conv_w;
+        int Cc = C, nch = CONV_DIM;
+        const StepParams *pp = c->pparams;
+        void *args[] = {&pre, &out, &ring, &cw, &Cc, &pp, &nch};
+        if ((e = launch_pdl_b((const void *)k_conv_seq, args, dim3(CONV_DIM / 256), dim3(256), c->st, c->pdl)))
+          return e;
+      }
+      DnBatch bs;
+      bs.qkvc = CONV_DIM; bs.gates = 2 * LNH; bs.z = LVD; bs.S = (long long)LNH * LDK * LDV; bs.on = LVD; bs.kh = LNH;
+      for (int t = 0; t < C; ++t) {
+        DnArgs d = {};
+        d.qkvc = c->qkvc16 + (size_t)t * CONV_DIM;
+        d.beta = c->gates + (size_t)t * 2 * LNH;
+        d.decay = d.beta + LNH;
+        d.z16 = c->z16 + (size_t)t * LVD;
+        d.norm_w = l.norm_w;
+        d.S = s.S + (size_t)seq * LNH * LDK * LDV;
+        d.on16 = c->on16 + (size_t)t * LVD;
+        d.kh_out = s.kh + (size_t)seq * LNH;
+        d.stats = c->stats;
+        d.err = c->err;
+        d.lkd = LKD; d.vrep = LNH / LNKH; d.norm_mode = c->m->cfg.norm_mode;
+        // no programmatic early launch: the kernel copies its head's state
+        // before its dependency wait, and here the previous launch (the
+        // previous token) writes that state
+        if ((e = launch_dn_step_b(d, bs, LNH, 1, c->st, false))) return e;
+      }
+      GemvPrologue p2 = {};
+      p2.mode = PRO_DYNQ8;
+      p2.src = c->on16;
+      p2.in_f = DN_NORM_F;
+      BSeg so;
+      so.m = &l.m[4]; so.mode = GM_RESID; so.out_f = RS_F; so.out = c->x16; so.out_bs = xbs;
+      if ((e = bop(c, &so, 1, LVD, p2, (long long)LVD * 2, 0, false))) return e;
+    } else {
+      BSeg sg[3];
+      sg[0].m = &l.m[0]; sg[0].out = c->qg16; sg[0].out_bs = (long long)NQ * HD * 2 * 2;
+      sg[1].m = &l.m[1]; sg[1].out = c->k16; sg[1].out_bs = (long long)NKV * HD * 2;
+      sg[2].m = &l.m[2]; sg[2].out = c->v16; sg[2].out_bs = (long long)NKV * HD * 2;
+      for (BSeg &x : sg) { x.mode = GM_TO16; x.out_f = QKV_F; }
+      if ((e = bop(c, sg, 3, H, pro, xbs, 0, false))) return e;
+      AttnBatch bs;
+      bs.qg = (long long)NQ * HD * 2; bs.kv16 = (long long)NKV * HD;
+      bs.cache = (long long)NKV * c->max_T * HD; bs.cache_e = (long long)NKV * c->max_T;
+      bs.prod = (long long)NQ * HD; bs.params = (long long)PARAM_INTS;
+      const size_t cs = (size_t)seq * NKV * c->max_T;
+      for (int t = 0; t < C; ++t) {
+        AttnArgs at = {};
+        at.qg16 = c->qg16 + (size_t)t * NQ * HD * 2;
+        at.k16 = c->k16 + (size_t)t * NKV * HD;
+        at.v16 = c->v16 + (size_t)t * NKV * HD;
+        at.q_norm = l.q_norm; at.k_norm = l.k_norm; at.rope = c->m->rope;
+        at.k8 = s.k8 + cs * HD; at.ke = s.ke + cs; at.v8 = s.v8 + cs * HD; at.ve = s.ve + cs;
+        at.prod = c->prod64 + (size_t)t * NQ * HD;
+        at.T = &c->pparams[t].T; at.pos = &c->pparams[t].pos; at.err = c->err;
+        at.max_T = c->max_T; at.max_pos = c->m->rope_npos; at.nq = NQ; at.nkv = NKV; at.rot = ROT;
+        // no programmatic early launch: the kernel copies its cached K rows
+        // before its dependency wait, and the previous token appended one
+        if ((e = launch_attn_b(at, bs, 1, c->st, false))) return e;
+      }
+      GemvPrologue p2 = {};
+      p2.mode = PRO_ATTN_GATE;
+      p2.src = c->prod64;
+      BSeg so;
+      so.m = &l.m[3]; so.mode = GM_RESID; so.out_f = RS_F; so.out = c->x16; so.out_bs = xbs;
+      if ((e = bop(c, &so, 1, NQ * HD, p2, (long long)NQ * HD * 8, 0, false))) return e;
+    }
+    GemvPrologue p3 = {};
+    p3.mode = PRO_RMSNORM;
+    p3.src = c->x16;
+    p3.w = l.ln2;
+    p3.in_f = RS_F;
+    p3.one_plus = 1;
+    BSeg gu;
+    gu.m = &l.m[8]; gu.m2 = &l.m[9]; gu.mode = GM_SILU_MUL; gu.out_f = 12; gu.out_f2 = RS_F;
+    gu.out = c->prod16; gu.out_bs = (long long)FFN * 2;
+    if ((e = bop(c, &gu, 1, H, p3, xbs, 0, false))) return e;
+    GemvPrologue p4 = {};
+    p4.mode = PRO_DYNQ8;
+    p4.src = c->prod16;
+    p4.in_f = RS_F;
+    BSeg sd;
+    sd.m = &l.m[10]; sd.mode = GM_RESID; sd.out_f = RS_F; sd.out = c->x16; sd.out_bs = xbs;
+    if ((e = bop(c, &sd, 1, FFN, p4, (long long)FFN * 2, 0, false))) return e;
+  }
+  if (last) {
+    GemvPrologue pf = {};
+    pf.mode = PRO_RMSNORM;
+    pf.src = c->x16;
+    pf.w = c->m->ln_f;
+    pf.in_f = RS_F;
+    pf.one_plus = 0;
+    BSeg sh;
+    sh.m = &c->m->head;
+    sh.mode = GM_ARGMAX;
+    if ((e = bop(c, &sh, 1, H, pf, (long long)H * 2, 0, true))) return e;
+    StepParams *p = c->pparams;
+    const unsigned long long *k = c->key;
+    const uint32_t *er = c->err;
+    int B = C, adv = 0;
+    void *args[] = {&p, &k, &er, &B, &adv};
+    if ((e = launch_pdl_b((const void *)k_bstep_end, args, dim3(1), dim3(64), c->st, c->pdl))) return e;
+  }
+  c->ncol = 0;
+  return cudaSuccess;
+}
+
 }  // namespace
 }  // namespace f5
 
@@ -563,6 +743,7 @@ int f5_bctx_create(f5_ctx *m, int batch, int max_T, f5_bctx **out) {
   BA(c->stats, 8);
   BA(c->err, 4);
   BA(c->params, B * sizeof(StepParams));
+  BA(c->pparams, B * sizeof(StepParams));
   if (cudaMallocHost(&c->h_params, B * sizeof(StepParams)) != cudaSuccess)
     return fail(set_error(F5_ENOMEM, "pinned params"));
   memset(c->h_params, 0, B * sizeof(StepParams));
@@ -657,6 +838,58 @@ int f5_bctx_step(f5_bctx *c, const int32_t *tok, int32_t *next_tok, int32_t *max
     if (max_logit) max_logit[b] = c->h_params[b].max_val;
   }
   return rc;
+}
+
+int f5_bctx_prefill(f5_bctx *c, int seq, const int32_t *tokens, int n, int32_t *next_tok, int32_t *max_logit) {
+  if (!c || !tokens || n < 1) return set_error(F5_EINVAL, "f5_bctx_prefill: bad argument");
+  if (seq < 0 || seq >= c->B) return set_error(F5_EINVAL, "f5_bctx_prefill: sequence %d outside [0, %d)", seq, c->B);
+  BDevGuard dg(c->device);
+  const int vocab = c->m->cfg.vocab;
+  for (int i = 0; i < n; ++i)
+    if (tokens[i] < 0 || tokens[i] >= vocab) return set_error(F5_EINVAL, "f5_bctx_prefill: token %d out of range", i);
+  F5_CU(cudaStreamSynchronize(c->st), "f5_bctx_prefill");
+  F5_CU(cudaMemcpy(c->h_params, c->params, sizeof(StepParams) * c->B, cudaMemcpyDeviceToHost), "f5_bctx_prefill");
+  const int T0 = c->h_params[seq].T, pos0 = c->h_params[seq].pos;
+  if (T0 + n > c->max_T) return set_error(F5_ESTATE, "f5_bctx_prefill: %d + %d tokens exceed max_T %d", T0, n, c->max_T);
+  if (pos0 + n > c->m->rope_npos) return set_error(F5_ESTATE, "f5_bctx_prefill: positions past the RoPE table");
+  std::vector<StepParams> pp(c->B);
+  F5_CU(cudaMemsetAsync(c->err, 0, 4, c->st), "f5_bctx_prefill");
+  int done = 0;
+  StepParams lastp = {};
+  while (done < n) {
+    const int C = std::min(c->B, n - done);
+    for (int t = 0; t < C; ++t) {
+      pp[t] = StepParams{};
+      pp[t].tok = tokens[done + t];
+      pp[t].T = T0 + done + t;
+      pp[t].pos = pos0 + done + t;
+    }
+    F5_CU(cudaMemcpyAsync(c->pparams, pp.data(), sizeof(StepParams) * C, cudaMemcpyHostToDevice, c->st),
+          "f5_bctx_prefill");
+    const bool last = done + C == n;
+    cudaError_t e = enqueue_prefill_chunk(c, seq, C, last);
+    c->ncol = 0;
+    if (e != cudaSuccess) return cuda_status(e, "f5_bctx_prefill");
+    // pp is reused by the next chunk's copy: wait for this chunk first
+    F5_CU(cudaStreamSynchronize(c->st), "f5_bctx_prefill");
+    if (last) F5_CU(cudaMemcpy(&lastp, c->pparams + (C - 1), sizeof(lastp), cudaMemcpyDeviceToHost), "f5_bctx_prefill");
+    done += C;
+  }
+  uint32_t herr = 0;
+  F5_CU(cudaMemcpy(&herr, c->err, 4, cudaMemcpyDeviceToHost), "f5_bctx_prefill");
+  c->h_params[seq].T = T0 + n;
+  c->h_params[seq].pos = pos0 + n;
+  c->h_params[seq].next_tok = lastp.next_tok;
+  c->h_params[seq].max_val = lastp.max_val;
+  c->h_params[seq].tok = lastp.next_tok;
+  F5_CU(cudaMemcpy(c->params, c->h_params, sizeof(StepParams) * c->B, cudaMemcpyHostToDevice), "f5_bctx_prefill");
+  if (next_tok) *next_tok = lastp.next_tok;
+  if (max_logit) *max_logit = lastp.max_val;
+  if ((herr | lastp.err) & DERR_TIMEOUT) return set_error(F5_ETIMEOUT, "f5_bctx_prefill: a bounded device wait expired");
+  if ((herr | lastp.err) & DERR_Y32_OVERFLOW) return set_error(F5_EOVERFLOW, "f5_bctx_prefill: |y32| >= 2^31");
+  if ((herr | lastp.err) & DERR_KV_FULL) return set_error(F5_ESTATE, "f5_bctx_prefill: KV cache full (max_T)");
+  if ((herr | lastp.err) & DERR_RANGE) return set_error(F5_EINVAL, "f5_bctx_prefill: input out of range");
+  return F5_OK;
 }
 
 int f5_bctx_launch(f5_bctx *c, int n_steps) {

@@ -396,6 +396,18 @@ int f5_bctx_get_position(f5_bctx *bctx, int seq, int *T, int *pos);
 /* one step of every sequence: tok[B] in, next_tok[B] / max_logit[B] out
  * (nullable); advances each sequence's T and pos by one */
 int f5_bctx_step(f5_bctx *bctx, const int32_t *tok, int32_t *next_tok, int32_t *max_logit);
+/* Layer-major prompt ingestion into sequence seq: the n prompt tokens go
+ * through the model in chunks of up to `batch` tokens, each chunk's tokens
+ * being the columns of every projection GEMM (one read of every weight
+ * image per chunk instead of one per token), while the conv windows, the
+ * DeltaNet recurrences and the KV appends run token by token in order.  The
+ * sequence's state, T and pos end exactly as n decode steps leave them
+ * (sw/chat_client.py:21 feeds a prompt one step at a time); next_tok /
+ * max_logit (nullable) receive the argmax after the last prompt token, and
+ * the sequence's next step input is set to it.  Other sequences are not
+ * touched. */
+int f5_bctx_prefill(f5_bctx *bctx, int seq, const int32_t *tokens, int n, int32_t *next_tok,
+                    int32_t *max_logit);
 /* enqueue n greedy steps (each sequence fed its own argmax), no host sync */
 int f5_bctx_launch(f5_bctx *bctx, int n_steps);
 int f5_bctx_sync(f5_bctx *bctx, int32_t *last_tok, int32_t *max_logit);
