@@ -579,23 +579,23 @@ cudaError_t enqueue_prefill_chunk(f5_bctx *c, int seq, int C, bool last) {
       }
       DnBatch bs;
       bs.qkvc = CONV_DIM; bs.gates = 2 * LNH; bs.z = LVD; bs.S = (long long)LNH * LDK * LDV; bs.on = LVD; bs.kh = LNH;
-      for (int t = 0; t < C; ++t) {
+      {
         DnArgs d = {};
-        d.qkvc = c->qkvc16 + (size_t)t * CONV_DIM;
-        d.beta = c->gates + (size_t)t * 2 * LNH;
-        d.decay = d.beta + LNH;
-        d.z16 = c->z16 + (size_t)t * LVD;
+        d.qkvc = c->qkvc16;
+        d.beta = c->gates;
+        d.decay = c->gates + LNH;
+        d.z16 = c->z16;
         d.norm_w = l.norm_w;
         d.S = s.S + (size_t)seq * LNH * LDK * LDV;
-        d.on16 = c->on16 + (size_t)t * LVD;
+        d.on16 = c->on16;
         d.kh_out = s.kh + (size_t)seq * LNH;
         d.stats = c->stats;
         d.err = c->err;
         d.lkd = LKD; d.vrep = LNH / LNKH; d.norm_mode = c->m->cfg.norm_mode;
-        // no programmatic early launch: the kernel copies its head's state
-        // before its dependency wait, and here the previous launch (the
-        // previous token) writes that state
-        if ((e = launch_dn_step_b(d, bs, LNH, 1, c->st, false))) return e;
+        // all C tokens in one launch, the state kept in shared memory
+        // between them (no programmatic early launch: the state is read
+        // right after the previous kernels)
+        if ((e = launch_dn_scan(d, bs, LNH, C, c->st))) return e;
       }
       GemvPrologue p2 = {};
       p2.mode = PRO_DYNQ8;

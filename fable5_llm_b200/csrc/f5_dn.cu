@@ -84,6 +84,69 @@ __global__ void __launch_bounds__(128 * NQ) k_dn_step(const __grid_constant__ Dn
   dn_head_rec<BlockSync, NQ>(sy, a, h, sm, qkv, zn);
 }
 
+// ntok consecutive tokens of ONE sequence (layer-major prompt prefill): the
+// head's state is copied in once and stays in shared memory from token to
+// token (dn_head_rec<KEEP>), token k's inputs / outputs at k times the
+// DnBatch strides; S in HBM holds the state after every token.  One CTA per
+// value head, as k_dn_step.
+template <int NQ>
+__global__ void __launch_bounds__(128 * NQ) k_dn_scan(const __grid_constant__ DnArgs a0, const DnBatch bs, int ntok) {
+  __shared__ __align__(128) int16_t s_sd[128 * 128];
+  __shared__ int4 s_kq[128];
+  __shared__ long long s_part[NQ > 1 ? NQ * 128 : 1];
+  __shared__ long long red[32];
+  __shared__ long long s_gate[4];
+  __shared__ int s_e[2];
+  __shared__ __align__(8) uint64_t bar_s;
+
+  const int h = blockIdx.x, t = threadIdx.x;
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (t == 0) {
+    mbar_init(&bar_s, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_expect_tx(&bar_s, 128 * 128 * 2);
+    bulk_g2s(s_sd, a0.S + (size_t)h * 128 * 128, 128 * 128 * 2, &bar_s);
+  }
+  __syncthreads();   // the barrier is initialised before any thread waits on it
+  const DnSmem sm = {s_sd, s_kq, NQ > 1 ? s_part : nullptr, red, s_gate, s_e};
+  const BlockSync sy;
+  const bool got = mbar_wait(&bar_s, 0, 2000000000ull);
+  if (sy.any(!got)) {
+    if (t == 0) atomicOr(a0.err, DERR_TIMEOUT);
+    if (!got) mbar_wait(&bar_s, 0, 2000000000ull);
+    return;
+  }
+  for (int k = 0; k < ntok; ++k) {
+    DnArgs a;
+    a.qkvc = a0.qkvc + k * bs.qkvc;
+    a.beta = a0.beta + k * bs.gates;
+    a.decay = a0.decay + k * bs.gates;
+    a.z16 = a0.z16 + k * bs.z;
+    a.norm_w = a0.norm_w;
+    a.S = a0.S;
+    a.xslots = a0.xslots;
+    a.in_tag_op1 = a0.in_tag_op1;
+    a.out_tag_op1 = a0.out_tag_op1;
+    a.on16 = a0.on16 + k * bs.on;
+    a.kh_out = a0.kh_out;
+    a.stats = a0.stats;
+    a.err = a0.err;
+    a.lkd = a0.lkd;
+    a.vrep = a0.vrep;
+    a.norm_mode = a0.norm_mode;
+    sy.sync();   // the previous token's readers of the shared scratch are done
+    long long qkv[3], zn[2];
+    dn_head_pre<BlockSync, NQ>(sy, a, h, sm, qkv, zn);
+    dn_head_rec<BlockSync, NQ, true>(sy, a, h, sm, qkv, zn);
+  }
+}
+
+cudaError_t launch_dn_scan(const DnArgs &a, const DnBatch &bs, int nheads, int ntok, cudaStream_t st) {
+  k_dn_scan<2><<<nheads, 256, 0, st>>>(a, bs, ntok);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_dn_step(const DnArgs &a, int nheads, cudaStream_t st, bool pdl) {
   return launch_dn_step_b(a, DnBatch{}, nheads, 1, st, pdl);
 }

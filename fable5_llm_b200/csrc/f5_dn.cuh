@@ -34,5 +34,8 @@ struct DnBatch {
 
 cudaError_t launch_dn_step(const DnArgs &a, int nheads, cudaStream_t st, bool pdl);
 cudaError_t launch_dn_step_b(const DnArgs &a, const DnBatch &bs, int nheads, int B, cudaStream_t st, bool pdl);
+// ntok consecutive tokens of one sequence (token k's inputs / outputs at k
+// times bs's strides; one state)
+cudaError_t launch_dn_scan(const DnArgs &a, const DnBatch &bs, int nheads, int ntok, cudaStream_t st);
 
 }  // namespace f5

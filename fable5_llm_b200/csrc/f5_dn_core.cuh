@@ -72,8 +72,10 @@ F5_DEV void dn_head_pre(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, 
 }
 
 // recurrence, block-float shift, gated norm, x silu(z)  (ref/layer_fixed.py:
-// 1545-1580).  sm.sd must hold the head's state.
-template <class SY, int NQ>
+// 1545-1580).  sm.sd must hold the head's state.  KEEP: the new state also
+// stays in sm.sd (each thread rewrites the entries it read), for a next
+// token of the same sequence.
+template <class SY, int NQ, bool KEEP = false>
 F5_DEV void dn_head_rec(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, const long long (&qkv)[3],
                         const long long (&zn)[2]) {
   const int t = sy.tid(), dv = t & 127, q = t >> 7;
@@ -128,6 +130,7 @@ F5_DEV void dn_head_rec(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, 
         sat += (uint32_t)(sn + 32767) > 65534u;   // |Sh| > 32767 (ref/layer_fixed.py:1557)
         sn = min(max(sn, -32768), 32767);
         S[sidx(dk, dv)] = (int16_t)sn;
+        if (KEEP) sm.sd[sidx(dk, dv)] = (int16_t)sn;
         oc += sn * kq.w;
       }
       o += oc;
@@ -140,6 +143,7 @@ F5_DEV void dn_head_rec(const SY &sy, const DnArgs &a, int h, const DnSmem &sm, 
       if (sn > 32767 || sn < -32767) ++sat;   // |Sh| > 32767 (ref/layer_fixed.py:1557)
       sn = clip16(sn);
       S[sidx(dk, dv)] = (int16_t)sn;
+      if (KEEP) sm.sd[sidx(dk, dv)] = (int16_t)sn;
       o += sn * kq.w;
     }
   }
