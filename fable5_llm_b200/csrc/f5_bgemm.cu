@@ -156,8 +156,8 @@ __global__ void __launch_bounds__(bg_threads(BP), 1) k_bgemm(const __grid_consta
         if (lane == 0) {
           // rows past the image read as zeros
           mbar_expect_tx(&full[s], (uint32_t)STAGE);
-          tma_load_2d(dst, &a.tmap[si], g * 64, r0, &full[s]);
-          tma_load_2d(dst + BG_WBYTES / 2, &a.tmap[si], g * 64 + 128, r0, &full[s]);
+          tma_load_2d_stream(dst, &a.tmap[si], g * 64, r0, &full[s]);
+          tma_load_2d_stream(dst + BG_WBYTES / 2, &a.tmap[si], g * 64 + 128, r0, &full[s]);
           bulk_g2s(dst + BG_WBYTES, a.xt + (size_t)g * BP * 128, XBYTES, &full[s]);
         }
         __syncwarp();

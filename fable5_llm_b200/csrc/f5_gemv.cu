@@ -86,8 +86,8 @@ __global__ void __launch_bounds__(GT_THREADS, 1) k_gemv(const __grid_constant__ 
       uint8_t *dst = smem + pi * stage_bytes;
       const bool pair = sg.mode == GM_SILU_MUL;
       mbar_expect_tx(&bar_full[pi], pair ? 2 * nb : nb);
-      bulk_g2s(dst, sg.w + (size_t)ch.r0 * a.stride, nb, &bar_full[pi]);
-      if (pair) bulk_g2s(dst + nb, sg.w2 + (size_t)ch.r0 * a.stride, nb, &bar_full[pi]);
+      bulk_g2s_stream(dst, sg.w + (size_t)ch.r0 * a.stride, nb, &bar_full[pi]);
+      if (pair) bulk_g2s_stream(dst + nb, sg.w2 + (size_t)ch.r0 * a.stride, nb, &bar_full[pi]);
       ++pi;
     }
   }
@@ -132,8 +132,8 @@ __global__ void __launch_bounds__(GT_THREADS, 1) k_gemv(const __grid_constant__ 
         uint8_t *dst = smem + s * stage_bytes;
         const bool pair = sg.mode == GM_SILU_MUL;
         mbar_expect_tx(&bar_full[s], pair ? 2 * nb : nb);
-        bulk_g2s(dst, sg.w + (size_t)ch.r0 * a.stride, nb, &bar_full[s]);
-        if (pair) bulk_g2s(dst + nb, sg.w2 + (size_t)ch.r0 * a.stride, nb, &bar_full[s]);
+        bulk_g2s_stream(dst, sg.w + (size_t)ch.r0 * a.stride, nb, &bar_full[s]);
+        if (pair) bulk_g2s_stream(dst + nb, sg.w2 + (size_t)ch.r0 * a.stride, nb, &bar_full[s]);
         ++issued;
       }
       // never leave the CTA with copies in flight: drain every issued stage

@@ -368,8 +368,8 @@ F5_DEV void producer(const MegaArgs &ma, const MegaSmem &S, int T, int pos, cons
         const bool pair = sg.mode == GM_SILU_MUL;
         uint8_t *dst = S.ring() + (size_t)s * MEGA_STAGE;
         mbar_expect_tx(&mg_full[s], pair ? 2 * nb : nb);
-        bulk_g2s(dst, sg.w + (size_t)ch.r0 * a.stride, nb, &mg_full[s]);
-        if (pair) bulk_g2s(dst + nb, sg.w2 + (size_t)ch.r0 * a.stride, nb, &mg_full[s]);
+        bulk_g2s_stream(dst, sg.w + (size_t)ch.r0 * a.stride, nb, &mg_full[s]);
+        if (pair) bulk_g2s_stream(dst + nb, sg.w2 + (size_t)ch.r0 * a.stride, nb, &mg_full[s]);
         mg_cnt[0] = ++issued;
         mg_issued = mg_issued + (pair ? 2 * nb : nb);
         rp.next(ns);
