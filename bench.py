@@ -221,7 +221,7 @@ def mega_traffic():
         return {"dram_bytes_per_launch": vals["dram_read_bytes"] + vals["dram_write_bytes"],
                 "source": "read from the committed ncu capture, not measured in this run: "
                           "dram__bytes_read.sum + dram__bytes_write.sum of one k_mega launch of the full 9B "
-                          "step at context 8 (profiles/k_mega_traffic.txt, profiles/k_mega_decode_step_traffic.md)"}
+                          "step at context 2051 (profiles/k_mega_traffic.txt, profiles/k_mega_decode_step_traffic.md)"}
     except (OSError, ValueError, KeyError):
         return None
 
