@@ -5,10 +5,13 @@ Run where the reference checkout exists, with the environment variable
 F5_REFERENCE set to its root directory; the GPU box never runs it.
 
 1. ref/gen_token_script.py writes a 9B-geometry token stream with the SEQ
-   emitter on (FABLE5_MODEL=9b SEQ_EMIT=1 SEQ_PROFILE=epsnorm): seed 1,
-   3 tokens, vocab 8192, the legacy 2-layer stack (one DeltaNet + one
-   full-attention layer).  Its weight images (265 MB), embedding (64 MB)
-   and state images (2 x 155 MB) stay outside the repository.
+   emitter on (FABLE5_MODEL=9b SEQ_EMIT=1 SEQ_PROFILE=epsnorm), vocab 8192:
+   by default seed 1, 3 tokens, the legacy 2-layer stack (one DeltaNet +
+   one full-attention layer, "tok9"); --seed 2 --ntok 4 --nlayers 4 --name
+   tok9l4 gives the config's first four layers (3 DeltaNet + 1 attention,
+   per-layer banked state, residual projections scaled by 1/sqrt(8)).  The
+   weight images (265-450 MB), embedding (64 MB) and state images
+   (2 x 155 MB) stay outside the repository.
 2. ref/seq_model.py --gate replays the .txt script and the .seq stream and
    must print "SEQ GATE: PASS" (tokens, banked state, state region and
    scratch bit-identical).
@@ -19,12 +22,13 @@ F5_REFERENCE set to its root directory; the GPU box never runs it.
    final state image decoded by fable5_llm_b200.state_region (pinning that
    layout restatement).
 
-Written: tests/golden/seq9b/tok9.{seq,seq.json,seqdata.bin,weights.json}
+Written: tests/golden/seq9b/<name>.{seq,seq.json,seqdata.bin,weights.json}
 (the stream, its blob and metadata, the weight manifest: ~80 KB) and
-tests/golden/seq9b_ref.npz (tokens, layer outputs, the quantized vectors,
-and the sha256 of every weight image, the embedding and both state images).
+tests/golden/seq9b_ref.npz (<name>_ref.npz for other names: tokens, layer
+outputs, the quantized vectors, and the sha256 of every weight image, the
+embedding and both state images).
 
-    python tests/golden/gen_seq_golden.py [--artifact PREFIX]
+    python tests/golden/gen_seq_golden.py [--artifact PREFIX] [--seed S --ntok N --nlayers L --name NAME]
 """
 from __future__ import annotations
 
@@ -48,6 +52,7 @@ os.environ["FABLE5_MODEL"] = "9b"
 sys.dont_write_bytecode = True
 SEED, NTOK, VOCAB, NLAYERS = 1, 3, 8192, 2
 NAME = "tok9"
+LEGACY_TYPES = ["linear_attention", "full_attention"]
 
 
 def sha_file(path):
@@ -73,6 +78,16 @@ def gate(prefix):
         sys.exit("the reference SEQ gate did not pass")
 
 
+def layer_types(nlayers):
+    """ref/gen_token_script.py:90-100: the legacy pair at 2 layers, else
+    the config's first nlayers types."""
+    if nlayers == 2:
+        return list(LEGACY_TYPES)
+    import json
+    cfg = json.load(open(os.path.join(REF, "ref", "qwen3_5_9b_config.json")))
+    return cfg["text_config"]["layer_types"][:nlayers]
+
+
 def rebuild_and_step(prefix):
     sys.path.insert(0, os.path.join(REF, "ref"))
     sys.path.insert(0, REPO)
@@ -85,8 +100,9 @@ def rebuild_and_step(prefix):
     from fable5_llm_b200.state_region import StateRegion, slots
 
     rng = np.random.default_rng(SEED)
-    types = ["linear_attention", "full_attention"]
-    layers = [LF.quant_layer(LR.init_layer_weights(rng, lt, out_scale=1.0)) for lt in types]
+    types = layer_types(NLAYERS)
+    out_scale = 1.0 if NLAYERS == 2 else 1.0 / np.sqrt(2.0 * NLAYERS)
+    layers = [LF.quant_layer(LR.init_layer_weights(rng, lt, out_scale=out_scale)) for lt in types]
     ln_f = np.asarray(np.clip(np.round(rng.normal(0, 0.5, LR.H) * (1 << 14)), -32768, 32767), dtype=np.int64)
     _hw = rng.normal(0, 1.0, (VOCAB, LR.H)) / np.sqrt(LR.H)
     head = LF.quant_linear(_hw)
@@ -126,18 +142,28 @@ def rebuild_and_step(prefix):
             assert np.array_equal(win, c["conv"]), "conv window"
             assert np.array_equal(taps, layers[i]["dn"]["conv_w"]), "conv taps"
     print("final state image == layer_decode_fx caches (S, conv taps + window, K/V rows + exponents)")
-    dn, at = layers[0]["dn"], layers[1]["attn"]
-    vec = {"l0_ln1": layers[0]["ln1"], "l0_ln2": layers[0]["ln2"], "l0_conv_w": dn["conv_w"],
-           "l0_dt_bias_q12": dn["dt_bias_q12"], "l0_A_q15": dn["A_q15"], "l0_norm_w_q14": dn["norm_w_q14"],
-           "l1_ln1": layers[1]["ln1"], "l1_ln2": layers[1]["ln2"], "l1_q_norm": at["q_norm"],
-           "l1_k_norm": at["k_norm"], "ln_f": ln_f}
+    vec = {"ln_f": ln_f}
+    for i, qw in enumerate(layers):
+        vec[f"l{i}_ln1"], vec[f"l{i}_ln2"] = qw["ln1"], qw["ln2"]
+        if qw["type"] == "full_attention":
+            vec[f"l{i}_q_norm"], vec[f"l{i}_k_norm"] = qw["attn"]["q_norm"], qw["attn"]["k_norm"]
+        else:
+            d = qw["dn"]
+            vec[f"l{i}_conv_w"], vec[f"l{i}_dt_bias_q12"] = d["conv_w"], d["dt_bias_q12"]
+            vec[f"l{i}_A_q15"], vec[f"l{i}_norm_w_q14"] = d["A_q15"], d["norm_w_q14"]
     return toks, np.array(outs, dtype=np.int16), vec
 
 
 def main():
+    global SEED, NTOK, NLAYERS, NAME
     ap = argparse.ArgumentParser()
     ap.add_argument("--artifact", help="reuse an artifact written by step 1 (its prefix)")
+    ap.add_argument("--seed", type=int, default=SEED)
+    ap.add_argument("--ntok", type=int, default=NTOK)
+    ap.add_argument("--nlayers", type=int, default=NLAYERS)
+    ap.add_argument("--name", default=NAME)
     a = ap.parse_args()
+    SEED, NTOK, NLAYERS, NAME = a.seed, a.ntok, a.nlayers, a.name
     td = None
     if a.artifact:
         prefix = a.artifact
@@ -154,11 +180,12 @@ def main():
     man = json.load(open(prefix + ".weights.json"))
     wids = sorted(int(k) for k in man if k.isdigit())
     digests = np.array([sha_file(os.path.join(os.path.dirname(prefix), man[str(w)]["file"])) for w in wids])
-    np.savez_compressed(os.path.join(HERE, "seq9b_ref.npz"), tokens=np.array(toks), layer_out=outs,
+    ref_name = "seq9b_ref.npz" if NAME == "tok9" else f"{NAME}_ref.npz"
+    np.savez_compressed(os.path.join(HERE, ref_name), tokens=np.array(toks), layer_out=outs,
                         image_sha256=digests, emb_sha256=np.array(sha_file(prefix + ".emb.bin")),
                         state_sha256=np.array(sha_file(prefix + ".state.bin")),
                         state_final_sha256=np.array(sha_file(prefix + ".state_final.bin")),
-                        seed=np.array(SEED), vocab=np.array(VOCAB), **vec)
+                        seed=np.array(SEED), vocab=np.array(VOCAB), nlayers=np.array(NLAYERS), **vec)
     print("tokens", toks, "->", dst)
     if td:
         shutil.rmtree(td)

@@ -24,27 +24,32 @@ import numpy as np
 import pytest
 
 import oracle as O
-from fable5_llm_b200 import _lib as L
 from fable5_llm_b200 import quant as Q
 from fable5_llm_b200.artifact import wid_plan
-from fable5_llm_b200.seq_harness import ATTN_NAMES, DN_NAMES, SeqHarness
+from fable5_llm_b200.seq_harness import ATTN_NAMES, DN_NAMES, SeqHarness, layer_types_of
 from fable5_llm_b200.seq_stream import SeqArtifact
 from fable5_llm_b200.seq_weights import DDRWeights
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-PREFIX = os.path.join(HERE, "golden", "seq9b", "tok9")
 sys.path.insert(0, os.path.join(HERE, "golden"))
 import seq_model_gen as GEN  # noqa: E402
 
 pytestmark = [pytest.mark.gpu, pytest.mark.slow]
 
+# (stream name, reference fixture) of every committed SEQ artifact: the
+# legacy DeltaNet + attention pair, and the config's first four layers
+ARTIFACTS = [(n, f) for n, f in (("tok9", "seq9b_ref"), ("tok9l4", "tok9l4_ref"))
+             if os.path.exists(os.path.join(HERE, "golden", "seq9b", n + ".seq"))]
 
-@pytest.fixture(scope="module")
-def rebuilt(golden):
+
+@pytest.fixture(scope="module", params=ARTIFACTS, ids=[a[0] for a in ARTIFACTS])
+def rebuilt(request, golden):
     """(artifact, reference fixture, vectors per layer, {wid: (device image, e)}, model)."""
-    d = golden("seq9b_ref")
-    art = SeqArtifact.load(PREFIX)
-    m = GEN.token_model(int(d["seed"]), vocab=int(d["vocab"]))
+    name, fx = request.param
+    d = golden(fx)
+    art = SeqArtifact.load(os.path.join(HERE, "golden", "seq9b", name))
+    types, _ = layer_types_of(art.meta["weights"])
+    m = GEN.token_model(int(d["seed"]), types, vocab=int(d["vocab"]))
     images, vecs, wid = {}, [], 0
     for wf in m["layers"]:
         vecs.append(Q.layer_vectors(wf))
@@ -106,7 +111,9 @@ def test_seq_decode_on_the_gpu(rebuilt, norm_mode):
 
 @pytest.mark.skipif(not os.environ.get("F5_SEQ_ARTIFACT"), reason="F5_SEQ_ARTIFACT (a full artifact prefix) not set")
 def test_seq_decode_from_the_artifact_files(rebuilt):
-    _, d, vecs, _, m = rebuilt
+    ref_art, d, vecs, _, m = rebuilt
+    if os.path.basename(os.environ["F5_SEQ_ARTIFACT"]) != os.path.basename(ref_art.prefix):
+        pytest.skip("F5_SEQ_ARTIFACT names another stream")
     art = SeqArtifact.load(os.environ["F5_SEQ_ARTIFACT"])
     h = SeqHarness(art, vecs, m["ln_f_q14"])
     try:

@@ -23,6 +23,24 @@ PREFIX = os.path.join(HERE, "golden", "seq9b", "tok9")
 sys.path.insert(0, os.path.join(HERE, "golden"))
 import seq_model_gen as GEN  # noqa: E402
 
+# (stream name, reference fixture) of every committed SEQ artifact
+ARTIFACTS = [(n, f) for n, f in (("tok9", "seq9b_ref"), ("tok9l4", "tok9l4_ref"))
+             if os.path.exists(os.path.join(HERE, "golden", "seq9b", n + ".seq"))]
+
+
+def ref_layers(d, types):
+    """The reference's per-layer vectors from a fixture, as layer dicts."""
+    out = []
+    for i, lt in enumerate(types):
+        qw = {"ln1": d[f"l{i}_ln1"], "ln2": d[f"l{i}_ln2"], "type": lt}
+        if lt == "full_attention":
+            qw["attn"] = {"q_norm": d[f"l{i}_q_norm"], "k_norm": d[f"l{i}_k_norm"]}
+        else:
+            qw["dn"] = {"dt_bias_q12": d[f"l{i}_dt_bias_q12"], "A_q15": d[f"l{i}_A_q15"],
+                        "norm_w_q14": d[f"l{i}_norm_w_q14"], "conv_w": d[f"l{i}_conv_w"]}
+        out.append(qw)
+    return out
+
 
 @pytest.fixture(scope="module")
 def art():
@@ -78,17 +96,33 @@ def test_layer_types_from_the_weight_plan(art):
     assert layer_types_of(art.meta["weights"]) == (["linear_attention", "full_attention"], 8192)
 
 
-def test_stream_constants_are_the_reference_vectors(art, golden):
-    d = golden("seq9b_ref")
-    layers = [{"ln1": d["l0_ln1"], "ln2": d["l0_ln2"],
-               "dn": {"dt_bias_q12": d["l0_dt_bias_q12"], "A_q15": d["l0_A_q15"],
-                      "norm_w_q14": d["l0_norm_w_q14"], "conv_w": d["l0_conv_w"]}},
-              {"ln1": d["l1_ln1"], "ln2": d["l1_ln2"], "attn": {"q_norm": d["l1_q_norm"], "k_norm": d["l1_k_norm"]}}]
-    h = SeqHarness(art, layers, d["ln_f"], emb_q=np.zeros((1, 1)), images={})
+@pytest.mark.parametrize("name,fx", ARTIFACTS)
+def test_stream_constants_are_the_reference_vectors(name, fx, golden):
+    d = golden(fx)
+    a = SeqArtifact.load(os.path.join(HERE, "golden", "seq9b", name))
+    types, _ = layer_types_of(a.meta["weights"])
+    layers = ref_layers(d, types)
+    h = SeqHarness(a, layers, d["ln_f"], emb_q=np.zeros((1, 1)), images={})
     h.check_constants()
-    layers[1]["attn"]["q_norm"] = d["l1_q_norm"] + 1
+    ia = types.index("full_attention")
+    layers[ia]["attn"]["q_norm"] = layers[ia]["attn"]["q_norm"] + 1
     with pytest.raises(AssertionError):
         h.check_constants()
+
+
+@pytest.mark.parametrize("name,fx", ARTIFACTS)
+def test_every_artifact_reads_and_resolves(name, fx, golden):
+    a = SeqArtifact.load(os.path.join(HERE, "golden", "seq9b", name))
+    d = golden(fx)
+    assert a.histogram() == a.meta["opcode_histogram"]
+    assert a.expect_tokens == [int(t) for t in d["tokens"]]
+    plan = a.weight_plan
+    rows = {}
+    for _, wid, r0, n, sh, ng in a.check_mvgo_plan():
+        rows.setdefault(wid, set()).update(range(r0, r0 + n))
+    assert sorted(rows) == sorted(plan) and all(len(rows[w]) == plan[w]["nrows"] for w in rows)
+    types, vocab = layer_types_of(a.meta["weights"])
+    assert len(types) == (int(d["nlayers"]) if "nlayers" in d else 2)
 
 
 def test_state_region_round_trip(art):
@@ -116,18 +150,22 @@ def test_state_region_round_trip(art):
 
 
 @pytest.mark.slow
-def test_seed_restatement_matches_the_reference_generator(art, golden):
-    """The float model rebuilt from seed 1 gives the reference's quantized
-    vectors, embedding table (sha256) and prompt token."""
-    d = golden("seq9b_ref")
-    m = GEN.token_model(int(d["seed"]), vocab=int(d["vocab"]))
-    v0, v1 = Q.layer_vectors(m["layers"][0]), Q.layer_vectors(m["layers"][1])
-    for got, key in ((v0["ln1"], "l0_ln1"), (v0["ln2"], "l0_ln2"), (v0["dn"]["conv_w"], "l0_conv_w"),
-                     (v0["dn"]["dt_bias_q12"], "l0_dt_bias_q12"), (v0["dn"]["A_q15"], "l0_A_q15"),
-                     (v0["dn"]["norm_w_q14"], "l0_norm_w_q14"), (v1["ln1"], "l1_ln1"), (v1["ln2"], "l1_ln2"),
-                     (v1["attn"]["q_norm"], "l1_q_norm"), (v1["attn"]["k_norm"], "l1_k_norm"),
-                     (m["ln_f_q14"], "ln_f")):
-        assert np.array_equal(got, d[key]), key
+@pytest.mark.parametrize("name,fx", ARTIFACTS)
+def test_seed_restatement_matches_the_reference_generator(name, fx, golden):
+    """The float model rebuilt from the generator's seed gives the
+    reference's quantized vectors, embedding table (sha256) and prompt."""
+    d = golden(fx)
+    a = SeqArtifact.load(os.path.join(HERE, "golden", "seq9b", name))
+    types, vocab = layer_types_of(a.meta["weights"])
+    m = GEN.token_model(int(d["seed"]), types, vocab=int(d["vocab"]))
+    ref = ref_layers(d, types)
+    for i, wf in enumerate(m["layers"]):
+        v = Q.layer_vectors(wf)
+        assert np.array_equal(v["ln1"], ref[i]["ln1"]) and np.array_equal(v["ln2"], ref[i]["ln2"]), f"layer {i}"
+        sub = "attn" if wf["type"] == "full_attention" else "dn"
+        for k, want in ref[i][sub].items():
+            assert np.array_equal(v[sub][k], want), f"layer {i} {k}"
+    assert np.array_equal(m["ln_f_q14"], d["ln_f"])
     emb = np.ascontiguousarray(m["emb_q"].astype("<i2"))
     assert hashlib.sha256(emb.tobytes()).hexdigest() == str(d["emb_sha256"])
-    assert [m["prompt"]] == art.prompt
+    assert [m["prompt"]] == a.prompt
