@@ -298,6 +298,29 @@ F5_DEV int32_t get16i(const uint4 &u, int j) {
   const uint32_t w = (j >> 1) == 0 ? u.x : ((j >> 1) == 1 ? u.y : ((j >> 1) == 2 ? u.z : u.w));
   return (int32_t)(int16_t)((j & 1) ? (w >> 16) : (w & 0xFFFFu));
 }
+// rmsnorm_fx of one 8-element block outside rms_elem_s17's domain (the
+// 32-bit law for 1 <= s <= 62, else the 64-bit law).  Kept out of line:
+// the decode step never takes it (int16 inputs always give 17 <= s <= 47),
+// and as inlined code it only enlarged the persistent kernel's instruction
+// footprint (measured 0.6 % of the step).
+static __device__ __noinline__ uint4 rms_block_slow(uint4 raw, int4 w0, int4 w1, long long r, int e, int add1) {
+  const int wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  const bool fast = r > 0 && r < (1ll << 31) && 30 - e >= 1 && 30 - e <= 62;
+  uint32_t pk[4];
+  for (int k = 0; k < 8; k += 2) {
+    int32_t x0, x1;
+    if (fast) {
+      x0 = rms_elem32(get16i(raw, k), (int32_t)r, 30 - e, wv[k] + add1);
+      x1 = rms_elem32(get16i(raw, k + 1), (int32_t)r, 30 - e, wv[k + 1] + add1);
+    } else {
+      x0 = (int32_t)rms_elem(get16(raw, k), r, e, (long long)wv[k] + add1);
+      x1 = (int32_t)rms_elem(get16(raw, k + 1), r, e, (long long)wv[k + 1] + add1);
+    }
+    pk[k >> 1] = ((uint32_t)x0 & 0xFFFFu) | ((uint32_t)x1 << 16);
+  }
+  return make_uint4(pk[0], pk[1], pk[2], pk[3]);
+}
+
 // the int8 values q[0..7] of block b into the lane-major even/odd layout
 F5_DEV void put8i(uint2 *xs, int b, const int32_t q[8]) {
   const uint32_t ev = __byte_perm(__byte_perm(q[0], q[2], 0x0040), __byte_perm(q[4], q[6], 0x0040), 0x5410);
@@ -485,27 +508,21 @@ F5_DEV void prologue(const SY &sy, const GemvArgs &a, uint2 *xs, long long *red,
         const int add1 = P.one_plus ? (1 << 14) : 0;
         // fast path when rsqrt's r and shift are in rms_elem32's domain (always
         // for int16 inputs of H = 4096); the general law otherwise
-        const bool fast = r > 0 && r < (1ll << 31) && 30 - e >= 1 && 30 - e <= 62;
-        const bool fast17 = fast && 30 - e >= 17 && 30 - e <= 47;
+        const bool fast17 = r > 0 && r < (1ll << 31) && 30 - e >= 17 && 30 - e <= 47;
         const uint32_t rh = (uint32_t)r >> 16, rl = (uint32_t)r & 0xFFFFu;
 #pragma unroll
         for (int j = 0; j < MAXB; ++j) {
+          if (!fast17) {
+            raw[j] = rms_block_slow(raw[j], wl[j][0], wl[j][1], r, e, add1);
+            continue;
+          }
           const int wv[8] = {wl[j][0].x, wl[j][0].y, wl[j][0].z, wl[j][0].w,
                              wl[j][1].x, wl[j][1].y, wl[j][1].z, wl[j][1].w};
           uint32_t pk[4];
 #pragma unroll
           for (int k = 0; k < 8; k += 2) {
-            int32_t x0, x1;
-            if (fast17) {
-              x0 = rms_elem_s17(get16i(raw[j], k), rh, rl, 30 - e, wv[k] + add1);
-              x1 = rms_elem_s17(get16i(raw[j], k + 1), rh, rl, 30 - e, wv[k + 1] + add1);
-            } else if (fast) {
-              x0 = rms_elem32(get16i(raw[j], k), (int32_t)r, 30 - e, wv[k] + add1);
-              x1 = rms_elem32(get16i(raw[j], k + 1), (int32_t)r, 30 - e, wv[k + 1] + add1);
-            } else {
-              x0 = (int32_t)rms_elem(get16(raw[j], k), r, e, (long long)wv[k] + add1);
-              x1 = (int32_t)rms_elem(get16(raw[j], k + 1), r, e, (long long)wv[k + 1] + add1);
-            }
+            const int32_t x0 = rms_elem_s17(get16i(raw[j], k), rh, rl, 30 - e, wv[k] + add1);
+            const int32_t x1 = rms_elem_s17(get16i(raw[j], k + 1), rh, rl, 30 - e, wv[k + 1] + add1);
             pk[k >> 1] = ((uint32_t)x0 & 0xFFFFu) | ((uint32_t)x1 << 16);
           }
           raw[j] = make_uint4(pk[0], pk[1], pk[2], pk[3]);   // normalised, int16
