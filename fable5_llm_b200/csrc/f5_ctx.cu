@@ -651,12 +651,6 @@ static int build_mega(f5_ctx *c, bool &unsupported) {
   m.rank = c->cfg.rank;
   for (int r = 0; r < F5_MAX_RANKS; ++r) m.peer_delta[r] = c->peer_delta[r];
   m.xkey = c->xkey;
-  // L2 prefetch lead per CTA: off by default (a sweep of 128 KB - 1 MB
-  // leads measured no gain: the TMA ring refills from L2 barely faster than
-  // from HBM); F5_MEGA_PREFETCH_KB sets it for experiments
-  long long pf_kb = 0;
-  if (const char *ev = getenv("F5_MEGA_PREFETCH_KB")) pf_kb = atoll(ev);
-  m.pf_bytes = pf_kb * 1024;
   c->mega_dirty = false;
   return F5_OK;
 }

@@ -681,7 +681,11 @@ F5_DEV void rstat_flush(unsigned long long *p, const RStat &s) {
 }
 
 // T_known >= 0: the step's token count, known to the caller (GM_CONV then
-// skips reading *sg.T)
+// skips reading *sg.T).  PERSIST: the persistent kernel's copy, without the
+// GM_Y32 / GM_TO64 cases that its step program never emits (an unexpected
+// mode raises DERR_RANGE): every line of code in that one-function kernel
+// costs instruction-cache room between its phases.
+template <bool PERSIST = false>
 F5_DEV void epilogue_row(const GemvArgs &a, const GemvSeg &sg, int row, long long acc16, int e_x,
                          int in_f, unsigned long long &best, uint32_t epoch = 0, RStat *rs = nullptr,
                          int T_known = -1) {
@@ -698,13 +702,19 @@ F5_DEV void epilogue_row(const GemvArgs &a, const GemvSeg &sg, int row, long lon
   const int sh2 = (15 - sg.e - a.sh) - e_x + in_f - sg.out_f;
   const uint32_t tag = (epoch && sg.tag_op1) ? mk_tag(epoch, sg.tag_op1) : 0u;
   switch (sg.mode) {
-    case GM_Y32: static_cast<int32_t *>(sg.out)[orow] = y; break;
+    case GM_Y32:
+      if constexpr (PERSIST) atomicOr(a.err, DERR_RANGE);
+      else static_cast<int32_t *>(sg.out)[orow] = y;
+      break;
     case GM_TO16: {
       const int32_t v = clip16(shift_to(y, sh2));
       if (tag) st_tagged(a, static_cast<uint32_t *>(sg.out) + orow, tag_word(tag, v));
       else static_cast<int16_t *>(sg.out)[orow] = (int16_t)v;
     } break;
-    case GM_TO64: static_cast<int64_t *>(sg.out)[orow] = shift_to(y, sh2); break;
+    case GM_TO64:
+      if constexpr (PERSIST) atomicOr(a.err, DERR_RANGE);
+      else static_cast<int64_t *>(sg.out)[orow] = shift_to(y, sh2);
+      break;
     case GM_RESID: {
       int32_t nv;
       if (tag) {   // the row's previous word was written by this CTA (same row partition)

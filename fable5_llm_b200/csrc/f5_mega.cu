@@ -13,12 +13,9 @@
 //    fills and HBM stays busy.  It also prefetches the CTA's DeltaNet head
 //    state and its attention K / V rows into a scratch region, gated by a
 //    scratch-free mbarrier the consumers arrive on after each use.
-//  * an L2-prefetch warp (warp 17) walks the same op list ahead of the
-//    producer and issues cp.async.bulk.prefetch.L2 over the rows the CTA will
-//    stream next, at most MegaArgs::pf_bytes ahead of the producer's issued
-//    bytes, so HBM keeps streaming into L2 while the smem ring is full and
-//    the consumers sit in a barrier, a prologue or a DeltaNet / attention
-//    core; the ring's TMA fills then read those rows from L2.
+//  * warp 17 has no role (an L2-prefetch warp that ran ahead of the
+//    producer measured slower at every lead and was removed: the kernel is a
+//    single function whose code size shows in its instruction-fetch stalls).
 //  * consumers (warps 0-15, named barrier 1) run the ops in order, separated
 //    by grid barriers (global counters, bounded spins): GEMV prologue /
 //    row dot products / epilogues (f5_gemv_core.cuh), the DeltaNet head core
@@ -289,8 +286,6 @@ __shared__ int mg_meta[4], mg_e[2];
 __shared__ int mg_cnt[7];   // issued fills: [0] ring, [1] sd, [2] sk, [3] sv (producer), [4] sk, [5] sv (consumers), [6] gains
 __shared__ volatile int mg_abort;
 __shared__ int mg_last;
-__shared__ __align__(16) MegaOp mg_fop;   // the L2 prefetcher's descriptor buffer
-__shared__ volatile long long mg_issued;  // weight bytes the producer has issued (its only writer)
 constexpr int MG_XRES = 64;
 __shared__ int16_t mg_xres[MG_XRES];      // this CTA's rows of the residual (4096-row partition)
 
@@ -371,7 +366,6 @@ F5_DEV void producer(const MegaArgs &ma, const MegaSmem &S, int T, int pos, cons
         bulk_g2s_stream(dst, sg.w + (size_t)ch.r0 * a.stride, nb, &mg_full[s]);
         if (pair) bulk_g2s_stream(dst + nb, sg.w2 + (size_t)ch.r0 * a.stride, nb, &mg_full[s]);
         mg_cnt[0] = ++issued;
-        mg_issued = mg_issued + (pair ? 2 * nb : nb);
         rp.next(ns);
       }
     } else if (kind == MK_DN) {
@@ -401,62 +395,6 @@ F5_DEV void producer(const MegaArgs &ma, const MegaSmem &S, int T, int pos, cons
     }
   }
   if (desc_pending >= 0) mbar_wait(&mg_bpd[desc_pending & 1], (desc_pending >> 1) & 1, MG_WAIT_NS);
-}
-
-// ---------------------------------------------------------------------------
-// L2 prefetcher (warp 17): advisory only -- nothing waits on a prefetch, so
-// it stops at the first sign of trouble and never delays the step's exit
-// ---------------------------------------------------------------------------
-constexpr uint32_t MG_PF_PIECE = 32768;
-
-F5_DEV bool pf_throttle(long long pf, long long lead, const Abort &ab) {
-  unsigned long long t0 = 0;
-  for (uint32_t it = 0; pf - mg_issued > lead; ++it) {
-    __nanosleep(128);
-    if ((it & 63) == 63) {
-      if (ab.raised()) return false;
-      const unsigned long long t = gtimer();
-      if (t0 == 0) t0 = t;
-      else if (t - t0 > MG_WAIT_NS) return false;
-    }
-  }
-  return true;
-}
-
-F5_DEV void prefetcher(const MegaArgs &ma, const Abort &ab) {
-  const int lane = threadIdx.x & 31, G = gridDim.x, b = blockIdx.x;
-  const long long lead = ma.pf_bytes;
-  if (lead <= 0) return;
-  long long pf = 0;
-  for (int oi = 0; oi < ma.nops; ++oi) {
-    __syncwarp();
-    if (lane < (int)(sizeof(MegaOp) / 16))
-      reinterpret_cast<uint4 *>(&mg_fop)[lane] = __ldcg(reinterpret_cast<const uint4 *>(ma.ops + oi) + lane);
-    __syncwarp();
-    if (mg_fop.kind != MK_GEMV) continue;
-    int stop = 0;
-    if (lane == 0) {
-      const GemvArgs &a = mg_fop.g;
-      const int u0 = part_lo(a.total_units, G, b), u1 = part_lo(a.total_units, G, b + 1);
-      for (int si = 0; si < a.nseg && !stop; ++si) {
-        const GemvSeg &sg = a.seg[si];
-        const int sb = sg.unit_begin, se = si + 1 < a.nseg ? a.seg[si + 1].unit_begin : a.total_units;
-        const int lo = max(u0, sb), hi = min(u1, se);
-        if (lo >= hi) continue;
-        const size_t off = (size_t)(lo - sb) * a.stride, len = (size_t)(hi - lo) * a.stride;
-        for (int k = 0; k < (sg.mode == GM_SILU_MUL ? 2 : 1) && !stop; ++k) {
-          const uint8_t *base = (k ? sg.w2 : sg.w) + off;
-          for (size_t p = 0; p < len; p += MG_PF_PIECE) {
-            const uint32_t n = (uint32_t)min((size_t)MG_PF_PIECE, len - p);
-            if (!pf_throttle(pf, lead, ab)) { stop = 1; break; }
-            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + p), "r"(n) : "memory");
-            pf += n;
-          }
-        }
-      }
-    }
-    if (__shfl_sync(0xffffffffu, stop, 0)) return;
-  }
 }
 
 // ---------------------------------------------------------------------------
@@ -491,7 +429,7 @@ F5_DEV void mega_epilogue_row(const GemvArgs &a, const GemvSeg &sg, int i, int u
   const uint32_t tag = (epoch && sg.tag_op1) ? mk_tag(epoch, sg.tag_op1) : 0u;
   if (!(sg.mode == GM_RESID && tag && i < MG_XRES)) {
     unsigned long long unused = 0ull;
-    epilogue_row(a, sg, row, acc, e_x, in_f, unused, epoch, sg.rstat ? &rs : nullptr, T);
+    epilogue_row<true>(a, sg, row, acc, e_x, in_f, unused, epoch, sg.rstat ? &rs : nullptr, T);
     return;
   }
   const int32_t y = finish_y32(acc, a.sh, a.err, nullptr);
@@ -1425,7 +1363,6 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega(const __grid_constant_
     mg_abort = 0;
     mg_last = 0;
     mg_tr = nullptr;
-    mg_issued = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   for (int i = tid; i < F5_LUT_RSQRT_N; i += MEGA_THREADS) mg_lut_rsqrt[i] = f5_lut_rsqrt[i];
@@ -1441,9 +1378,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega(const __grid_constant_
 
   if (warp == MG_CONS) {
     if (lane == 0) producer(ma, S, T, pos, ab);
-  } else if (warp == MG_CONS + 1) {
-    prefetcher(ma, ab);
-  } else {
+  } else if (warp < MG_CONS) {
     consumers(ma, S, tok, T, pos, ab, epoch);
   }
   __syncwarp();   // reconverge each warp (the producer lane joins its warp) before the CTA barrier

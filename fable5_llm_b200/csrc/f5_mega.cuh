@@ -62,7 +62,6 @@ struct MegaArgs {
   int dn_heads;     // CTAs [0, dn_heads) run one DeltaNet value head each
   int ns;           // ring stages (from mega_config)
   unsigned long long *trace;   // optional [G][nops][MEGA_TRACE_SLOTS] globaltimer marks
-  long long pf_bytes;          // L2 prefetch lead per CTA in weight bytes (0: off)
   // row-sharded across nrank GPUs: the LM head's argmax keys are exchanged
   // through xkey ([F5_MAX_RANKS][2] marked words, in the twin allocation,
   // peers at + peer_delta[r])
