@@ -452,8 +452,11 @@ def run_step(args, ws, rank, local):
     # context: ctx_len seeded random token ids fed on the device, one step
     # each, as the reference prefills (not timed); the timed steps then
     # continue greedily from the argmax of the last prompt token
-    m.prefill(np.random.default_rng(args.seed).integers(0, m.geom.vocab, ctx_len))
+    prompt = np.random.default_rng(args.seed).integers(0, m.geom.vocab, ctx_len)
+    pf0 = time.time()
+    m.prefill(prompt)
     tok, _ = m.sync()
+    prefill_s = time.time() - pf0
     prefill_tok = tok
     st = torch.cuda.ExternalStream(m.stream_handle())
     for _ in range(args.warmup):
@@ -532,6 +535,12 @@ def run_step(args, ws, rank, local):
             batched[f"B{B}"] = {"tok_s": round(B * 1000.0 / bms, 1), "ms_per_step": round(bms, 3),
                                 "gbs": round((WEIGHT_BYTES_9B + B * batched_state_bytes(m.geom, 1024)) /
                                              (bms * 1e-3) / 1e9, 1)}
+    # the same prompt ingested layer-major (f5_bctx_prefill: 64-token chunks as
+    # the GEMM columns) into one sequence of a batched context: its time, and
+    # that it ends on the same next token as the step-by-step fill above
+    prefill_lm = None
+    if ws == 1 and args.layers == 32 and not args.no_batched and ctx_len >= 64:
+        prefill_lm = time_layer_major_prefill(m, prompt, int(prefill_tok), prefill_s)
     configs = None
     if ws == 1 and args.layers == 32 and not args.no_batched:
         configs = time_configs(args, hbm_peak)
@@ -601,6 +610,8 @@ def run_step(args, ws, rank, local):
         }
         if configs:
             line["configs_1_2_3"] = configs
+        if prefill_lm:
+            line["prefill"] = prefill_lm
         if batched:
             line["batched_config5"] = {"per_B": batched, "context": 1024,
                                        "note": "B independent sequences, tcgen05 W4A8 GEMMs; caches zero-filled "
@@ -628,6 +639,29 @@ def batched_launches(geom):
     (prologue, GEMM, epilogue) + the DeltaNet / attention core, the LM head
     (prologue, GEMM with the argmax), end."""
     return 2 + geom.n_layers * 13 + 2
+
+
+def time_layer_major_prefill(m, prompt, step_tok, step_s):
+    """The prompt through f5_bctx_prefill (wall time around the call, which
+    synchronises) beside its step-by-step fill through the decode engine."""
+    import torch
+    from fable5_llm_b200.batch import BatchModel
+    n = len(prompt)
+    bm = BatchModel(m, 64, max_T=n + 16)
+    bm.reset()
+    bm.prefill(0, prompt[:64])   # first-call set-up outside the timing
+    bm.reset()
+    torch.cuda.synchronize()
+    t0 = time.time()
+    nt, _ = bm.prefill(0, prompt)
+    dt = time.time() - t0
+    bm.close()
+    return {"tokens": n, "layer_major_ms": round(dt * 1e3, 1), "layer_major_tok_s": round(n / dt, 1),
+            "decode_steps_ms": round(step_s * 1e3, 1), "decode_steps_tok_s": round(n / step_s, 1),
+            "same_next_token": bool(nt == step_tok),
+            "note": "layer-major: 64-token chunks of one sequence as the columns of every projection GEMM "
+                    "(f5_bctx_prefill); decode steps: one persistent step per prompt token (f5_decode_prefill, "
+                    "the reference's one-token-per-step prefill); wall time, host synchronised"}
 
 
 def time_batched(m, B, ctx_len, steps, warmup, seed, prefill=False):
