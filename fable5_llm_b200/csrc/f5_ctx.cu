@@ -1056,7 +1056,7 @@ int f5_ctx_trace_step(f5_ctx *c, uint64_t *out, size_t cap, int *grid, int *nops
   MegaArgs m = c->margs;
   m.trace = d;
   cudaError_t e = cudaMemsetAsync(d, 0, n * 8, c->st);
-  if (e == cudaSuccess) e = launch_mega(m, c->mega_grid, c->mega_smem, c->st);
+  if (e == cudaSuccess) e = launch_mega_traced(m, c->mega_grid, c->mega_smem, c->st);
   if (e == cudaSuccess) e = cudaMemcpyAsync(out, d, n * 8, cudaMemcpyDeviceToHost, c->st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(c->st);
   cudaFree(d);

@@ -33,10 +33,19 @@
 #include <cuda_runtime.h>
 
 #include "f5_luts.h"
+// F5_MEGA_TRACE selects the instance this translation unit builds: 0 the
+// step kernel k_mega, whose code holds no trace marks (the kernel's speed
+// follows its code size), 1 the traced copy k_mega_traced that
+// f5_mega_trace.cu compiles from this same source for f5_ctx_trace_step.
+#ifndef F5_MEGA_TRACE
+#define F5_MEGA_TRACE 0
+#endif
 namespace f5 {
+#if F5_MEGA_TRACE
 // this op's trace row (consumer thread 0 only), null when not tracing;
 // declared ahead of the shared cores so their phase marks can reach it
 __shared__ unsigned long long *mg_tr;
+#endif
 // The integer LUTs in shared memory (copied from the global tables at
 // launch): every lookup of the step's prologues, epilogues and cores is a
 // shared-memory read, never an L1 miss behind the weight stream.
@@ -48,10 +57,12 @@ __shared__ int32_t mg_lut_rsqrt[F5_LUT_RSQRT_N], mg_lut_recip[F5_LUT_RECIP_N], m
 #define F5_LUT_EXP2 mg_lut_exp2
 #define F5_LUT_SIGMOID mg_lut_sigmoid
 #define F5_LUT_SOFTPLUS mg_lut_softplus
+#if F5_MEGA_TRACE
 #define F5_PRO_MARK(k)                                     \
   do {                                                     \
     if (threadIdx.x == 0 && mg_tr) mg_tr[(k)] = gtimer();  \
   } while (0)
+#endif
 
 #include "f5_dn_core.cuh"
 #include "f5_gemv_core.cuh"
@@ -290,10 +301,16 @@ constexpr int MG_XRES = 64;
 __shared__ int16_t mg_xres[MG_XRES];      // this CTA's rows of the residual (4096-row partition)
 
 // trace marker k (2..7) of the current op: consumer thread 0 only
+#if F5_MEGA_TRACE
 #define MG_MARK(k)                                                   \
   do {                                                               \
     if (threadIdx.x == 0 && mg_tr) mg_tr[(k)] = gtimer();            \
   } while (0)
+#else
+#define MG_MARK(k) \
+  do {             \
+  } while (0)
+#endif
 
 struct MegaSmem {
   int ns;
@@ -1306,7 +1323,7 @@ F5_DEV void consumers(const MegaArgs &ma, const MegaSmem &S, int tok, int T, int
   const CSync sy;
   RingPos rp;
   int w_sd = 0, w_sk = 0, w_sv = 0, w_g = 0;
-  unsigned long long *tr = ma.trace ? ma.trace + (size_t)blockIdx.x * ma.nops * MEGA_TRACE_SLOTS : nullptr;
+  unsigned long long *tr = F5_MEGA_TRACE && ma.trace ? ma.trace + (size_t)blockIdx.x * ma.nops * MEGA_TRACE_SLOTS : nullptr;
   stage_desc(ma, S, 0);
   for (int oi = 0; oi < ma.nops; ++oi) {
     // The sync publishes op oi's staged descriptor and retires every reader
@@ -1317,7 +1334,9 @@ F5_DEV void consumers(const MegaArgs &ma, const MegaSmem &S, int tok, int T, int
     sy.sync();
     const int bar = mg_cop[oi & 1].bar;
     if (bar >= 0 && !counter_barrier(sy, &ma.bars[bar], gridDim.x, ab)) return;
+#if F5_MEGA_TRACE
     if (threadIdx.x == 0) mg_tr = tr ? tr + (size_t)oi * MEGA_TRACE_SLOTS : nullptr;
+#endif
     if (oi + 1 < ma.nops) stage_desc(ma, S, oi + 1);
     const MegaOp &op = mg_cop[oi & 1];
     if (tr && threadIdx.x == 0) tr[(size_t)oi * MEGA_TRACE_SLOTS] = gtimer();
@@ -1339,7 +1358,12 @@ F5_DEV void consumers(const MegaArgs &ma, const MegaSmem &S, int tok, int T, int
   }
 }
 
-__global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega(const __grid_constant__ MegaArgs ma) {
+#if F5_MEGA_TRACE
+#define F5_MEGA_KERNEL k_mega_traced
+#else
+#define F5_MEGA_KERNEL k_mega
+#endif
+__global__ void __launch_bounds__(MEGA_THREADS, 1) F5_MEGA_KERNEL(const __grid_constant__ MegaArgs ma) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ns = ma.ns;
   MegaSmem S;
@@ -1362,7 +1386,9 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega(const __grid_constant_
     for (int i = 0; i < 7; ++i) mg_cnt[i] = 0;
     mg_abort = 0;
     mg_last = 0;
+#if F5_MEGA_TRACE
     mg_tr = nullptr;
+#endif
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   for (int i = tid; i < F5_LUT_RSQRT_N; i += MEGA_THREADS) mg_lut_rsqrt[i] = f5_lut_rsqrt[i];
@@ -1462,6 +1488,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_mega(const __grid_constant_
   for (int i = tid; i < ma.nbars; i += MEGA_THREADS) ma.bars[i] = 0u;
 }
 
+#if !F5_MEGA_TRACE
 static size_t mega_smem_bytes(int ns, int chunk_max) {
   size_t scr = (size_t)AT_SC + (size_t)4 * chunk_max * 8;
   if (scr < (size_t)DN_END) scr = DN_END;
@@ -1510,5 +1537,34 @@ cudaError_t launch_mega(const MegaArgs &a, int grid, size_t smem, cudaStream_t s
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, k_mega, a);
 }
+
+#else
+// The traced instance: same grid, shared memory and cooperative launch as
+// the step kernel (its dynamic shared-memory limit raised on each call:
+// tracing is a diagnostic, and the limit is per device).
+cudaError_t launch_mega_traced(const MegaArgs &a, int grid, size_t smem, cudaStream_t st) {
+  int dev = 0, optin = 0;
+  cudaFuncAttributes fa;
+  cudaError_t e;
+  if ((e = cudaGetDevice(&dev))) return e;
+  if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev))) return e;
+  if ((e = cudaFuncGetAttributes(&fa, k_mega_traced))) return e;
+  if (smem + fa.sharedSizeBytes > (size_t)optin) return cudaErrorInvalidValue;
+  if ((e = cudaFuncSetAttribute(k_mega_traced, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)((size_t)optin - fa.sharedSizeBytes))))
+    return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(MEGA_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_mega_traced, a);
+}
+#endif
 
 }  // namespace f5

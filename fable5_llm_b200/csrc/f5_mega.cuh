@@ -61,7 +61,7 @@ struct MegaArgs {
   int advance;      // feed the argmax back as the next token (greedy loop)
   int dn_heads;     // CTAs [0, dn_heads) run one DeltaNet value head each
   int ns;           // ring stages (from mega_config)
-  unsigned long long *trace;   // optional [G][nops][MEGA_TRACE_SLOTS] globaltimer marks
+  unsigned long long *trace;   // [G][nops][MEGA_TRACE_SLOTS] globaltimer marks (traced instance only)
   // row-sharded across nrank GPUs: the LM head's argmax keys are exchanged
   // through xkey ([F5_MAX_RANKS][2] marked words, in the twin allocation,
   // peers at + peer_delta[r])
@@ -70,7 +70,7 @@ struct MegaArgs {
   unsigned long long *xkey;
 };
 
-constexpr int MEGA_THREADS = 576;       // 16 consumer warps + producer warp + L2-prefetch warp
+constexpr int MEGA_THREADS = 576;       // 16 consumer warps + producer warp + warp 17 (no role)
 constexpr int MEGA_STAGE = 33792;       // ring stage: 16 rows of K=4096, 5 of K=12288
 constexpr int MEGA_RES = 256;           // deferred per-CTA row results
 constexpr int MEGA_SUB = 64;            // attention tokens per K/V shared-memory fill
@@ -89,5 +89,8 @@ inline int mega_rows_per_stage(int stride) {
 // for a given attention token chunk bound; error if it cannot be resident.
 cudaError_t mega_config(int chunk_max, int *grid, size_t *smem, int *ns);
 cudaError_t launch_mega(const MegaArgs &a, int grid, size_t smem, cudaStream_t st);
+// The same step with per-op globaltimer marks written to a.trace (the traced
+// instance, f5_mega_trace.cu); grid and smem from mega_config.
+cudaError_t launch_mega_traced(const MegaArgs &a, int grid, size_t smem, cudaStream_t st);
 
 }  // namespace f5

@@ -146,6 +146,28 @@ def test_greedy_device_loop_matches_host_steps(model4, engine):
     assert m.position() == (6, 6)
 
 
+def test_traced_step_is_a_greedy_step(model4):
+    """The traced instance of the persistent kernel (f5_ctx_trace_step, the
+    same source with its marks compiled in) runs the same greedy step as the
+    step kernel, and every CTA's op marks are present and ordered."""
+    m = model4
+    m.set_engine("persistent")
+    m.reset()
+    toks, tok = [], 17
+    for t in range(6):
+        tok, _ = m.decode_step(tok, t)
+        toks.append(tok)
+    m.reset()
+    m.decode_step(17, 0)
+    t, kinds = m.trace_step()
+    m.decode_launch(4)
+    last, _ = m.sync()
+    assert last == toks[-1]
+    assert m.position() == (6, 6)
+    assert t.shape[1] == len(kinds)
+    assert (t[:, :, 0] >= 0).all() and (t[:, :, 1] >= t[:, :, 0]).all()
+
+
 def test_state_save_load_roundtrip(model4, tmp_path):
     m = model4
     m.reset()
