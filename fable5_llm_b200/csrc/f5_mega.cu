@@ -511,13 +511,16 @@ F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const 
   bool bad = false;
   int u = u0;
   if (!argmax) {
-    // Two groups of eight warps take the op's stages in turn (chunk j goes to
-    // group j % 2); a stage holds <= 16 rows (rows_per_stage <= 16) and warp
-    // w of the group reduces rows w and w + 8 together, so every wait,
-    // arrival and loop step is shared by two rows.  Each warp arrives with
-    // count 2, keeping the empty barrier's 16 arrivals per stage.
+    // Two groups of eight warps share the op's stages: stage s always goes
+    // to group s % 2, so each group waits on its own stages' full barriers
+    // lap after lap and a parity wait can never alias an earlier lap (with
+    // chunk j going to group j % 2 and an odd ring depth, a stage alternated
+    // between the groups and a group could pass the wait on a phase still
+    // pending for the other).  A stage holds <= 16 rows (rows_per_stage <=
+    // 16) and warp w of the group reduces rows w and w + 8 together, so every
+    // wait, arrival and loop step is shared by two rows.  Each warp arrives
+    // with count 2, keeping the empty barrier's 16 arrivals per stage.
     const int grp = warp >> 3, wl = warp & 7;
-    int j = 0;
     while (u < u1 && !bad) {
       const int si = seg_of(a, u);
       const GemvSeg &sg = a.seg[si];
@@ -526,7 +529,7 @@ F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const 
       const int ru = pair ? (a.rows_per_stage >> 1) : a.rows_per_stage;
       while (u < seg_hi) {
         const int n = min(ru, seg_hi - u);
-        if ((j & 1) == grp) {
+        if ((rp.s & 1) == grp) {
           if (mg_abort || !mwait(&mg_full[rp.s], rp.ph, ab)) {
             mg_abort = 1;
             bad = true;
@@ -557,7 +560,6 @@ F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const 
         }
         rp.next(ns);
         u += n;
-        ++j;
       }
     }
     u = u1;
