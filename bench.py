@@ -65,21 +65,40 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.f = None
+        self.n0 = 0
+
+    def _rows(self):
+        try:
+            with open(self.f.name) as fh:
+                return fh.read().count("\n")
+        except OSError:
+            return 0
 
     def start(self):
+        """Start sampling every 20 ms and return once the first sample is
+        written (nvidia-smi takes a while to start), so that a timed region
+        of a few tens of milliseconds is sampled too."""
         try:
             self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        t_end = time.time() + 5.0
+        while self._rows() == 0 and time.time() < t_end and self.proc.poll() is None:
+            time.sleep(0.01)
+        self.n0 = self._rows()
 
     def stop(self):
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.25)
+        # at least two samples taken after the timed region began
+        t_end = time.time() + 2.0
+        while self._rows() < self.n0 + 2 and time.time() < t_end and self.proc.poll() is None:
+            time.sleep(0.01)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -87,6 +106,7 @@ class ClockSampler:
             self.proc.kill()
         self.f.flush()
         rows = [l.strip().split(", ") for l in open(self.f.name) if l.strip()]
+        rows = rows[self.n0:] or rows   # the samples from the timed region on
         os.unlink(self.f.name)
         sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
@@ -428,7 +448,8 @@ def time_configs(args, hbm_peak):
 
 
 def run_step(args, ws, rank, local):
-    """The headline workload: the full decode step replayed as a CUDA graph."""
+    """The headline workload: the full decode step, one persistent-kernel
+    launch per step (the per-op CUDA-graph engine is timed beside it)."""
     import torch
     from fable5_llm_b200.config import Geometry
     from fable5_llm_b200.model import DecodeModel
@@ -596,7 +617,9 @@ def run_step(args, ws, rank, local):
                        "launches_per_step": launches},
             "roofline": roof,
             "cpu_baseline": cpu,
-            "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 32,
+            # per f5_decode_step: tok and pos in (8 B), the 32-byte step
+            # parameter block (next token, its logit, error bits) back
+            "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 32},
             "gpu_launches": launches * args.steps,
             "clocks": ck, "context_tokens_after": T,

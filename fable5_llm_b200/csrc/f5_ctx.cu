@@ -13,6 +13,7 @@
 // Both are built by the same enqueue_step walk (the persistent program is
 // the walk in "emit" mode), so they run the same descriptors.
 #include <algorithm>
+#include <cstddef>
 #include <cstdlib>
 #include <cstring>
 #include <string>
@@ -1070,12 +1071,16 @@ int f5_decode_step(f5_ctx *c, int32_t tok, int32_t pos, int32_t *next_tok, int32
   DevGuard dg(c->device);
   int eng;
   if ((rc = resolve_engine(c, eng))) return rc;
-  F5_CU(cudaMemcpyAsync(c->h_params, c->params, sizeof(StepParams), cudaMemcpyDeviceToHost, c->st), "decode step");
-  F5_CU(cudaStreamSynchronize(c->st), "decode step");
+  // Only the step's inputs travel: tok and pos, the first two words of the
+  // parameter block, from the pinned host copy (no read-back of the block
+  // first: T and the launch counter stay the device's own words); then the
+  // error words are cleared.  finish_host's read-back rewrites the host copy
+  // after the step, on the same stream.
+  static_assert(offsetof(StepParams, tok) == 0 && offsetof(StepParams, pos) == sizeof(int32_t), "tok, pos first");
   c->h_params->tok = tok;
   c->h_params->pos = pos;
-  c->h_params->err = 0;
-  F5_CU(cudaMemcpyAsync(c->params, c->h_params, sizeof(StepParams), cudaMemcpyHostToDevice, c->st), "decode step");
+  F5_CU(cudaMemcpyAsync(c->params, c->h_params, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, c->st), "decode step");
+  F5_CU(cudaMemsetAsync(&c->params->err, 0, sizeof(uint32_t), c->st), "decode step");
   F5_CU(cudaMemsetAsync(c->err, 0, 4, c->st), "decode step");
   if ((rc = launch_step(c, eng))) return rc;
   if ((rc = finish_host(c, "f5_decode_step"))) return rc;
