@@ -469,6 +469,12 @@ F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const 
   const CSync sy;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, b = blockIdx.x, ns = S.ns;
+  // the op's row partition and epilogue operands first: none depends on the
+  // input vector, so this runs while the prologue's inputs are still in flight
+  const int u0 = part_lo(a.total_units, G, b), u1 = part_lo(a.total_units, G, b + 1);
+  const int stride = a.stride, sh = a.sh;
+  const bool argmax = a.seg[0].mode == GM_ARGMAX;
+  if (!argmax && tid < u1 - u0) epi_prefetch(a, u0 + tid);
   // RMSNorm gains: the producer's copy in shared memory (in place long before)
   const bool rms = a.pro.mode == PRO_RMSNORM;
   bool got = true;
@@ -489,10 +495,6 @@ F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const 
   for (int c = 0; c < 4; ++c)
 #pragma unroll
     for (int j = 0; j < 4; ++j) xr[c][j] = S.xs()[((c << 2) + j) * 32 + lane];
-  const int u0 = part_lo(a.total_units, G, b), u1 = part_lo(a.total_units, G, b + 1);
-  const int stride = a.stride, sh = a.sh;
-  const bool argmax = a.seg[0].mode == GM_ARGMAX;
-  if (!argmax && tid < u1 - u0) epi_prefetch(a, u0 + tid);
   long long *res = S.res();
   int32_t *logits = static_cast<int32_t *>(a.seg[0].out);   // argmax: optional y32 of every row
   unsigned long long best = 0ull;
@@ -632,6 +634,8 @@ F5_DEV bool c_gemv_split(const GemvArgs &a, const MegaSmem &S, RingPos &rp, cons
   const CSync sy;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, b = blockIdx.x, ns = S.ns;
+  const int K2 = a.K >> 1;
+  const int u0 = part_lo(a.total_units, G, b), u1 = part_lo(a.total_units, G, b + 1);
   prologue<(NP * 4 * 128 + MG_CT - 1) / MG_CT>(sy, a, S.xs(), mg_red, (&mg_r), mg_meta, epoch);
   sy.sync();
   MG_MARK(2);
@@ -642,8 +646,6 @@ F5_DEV bool c_gemv_split(const GemvArgs &a, const MegaSmem &S, RingPos &rp, cons
   for (int c = 0; c < 4; ++c)
 #pragma unroll
     for (int j = 0; j < 4; ++j) xr[c][j] = S.xs()[(((part * 4 + c) << 2) + j) * 32 + lane];
-  const int K2 = a.K >> 1;
-  const int u0 = part_lo(a.total_units, G, b), u1 = part_lo(a.total_units, G, b + 1);
   bool bad = false;
   int u = u0;
   Chunk ch;
