@@ -456,6 +456,26 @@ F5_DEV void mega_epilogue_row(const GemvArgs &a, const GemvSeg &sg, int i, int u
   if (sg.rstat) rs.add(nv);
   st_tagged(a, static_cast<uint32_t *>(sg.out) + orow, tag_word(tag, nv));
 }
+// The split-K GEMV's epilogue: the step program emits it only for the MLP
+// down projection, a tagged residual add whose rows (<= 4096 / 128 per CTA)
+// all sit in mg_xres; anything else raises DERR_RANGE.  Only this law is
+// compiled into the split loop: the kernel is one function whose speed
+// follows its code size.
+F5_DEV void mega_epilogue_resid(const GemvArgs &a, const GemvSeg &sg, int i, int uu, long long acc, int e_x,
+                                int in_f, uint32_t epoch, RStat &rs) {
+  const int orow = sg.out_row0 + (uu - sg.unit_begin);
+  const uint32_t tag = (epoch && sg.tag_op1) ? mk_tag(epoch, sg.tag_op1) : 0u;
+  if (!(sg.mode == GM_RESID && tag && i < MG_XRES)) {
+    atomicOr(a.err, DERR_RANGE);
+    return;
+  }
+  const int32_t y = finish_y32(acc, a.sh, a.err, nullptr);
+  const long long v = clip16(shift_to(y, (15 - sg.e - a.sh) - e_x + in_f - sg.out_f));
+  const int32_t nv = clip16((int64_t)mg_xres[i] + v);
+  mg_xres[i] = (int16_t)nv;
+  if (sg.rstat) rs.add(nv);
+  st_tagged(a, static_cast<uint32_t *>(sg.out) + orow, tag_word(tag, nv));
+}
 // K = 4096 (every GEMV of the step but the MLP down projection): one row per
 // consumer warp per 16-row stage.  The consumer loop is issue-bound, so it is
 // kept to the row's own arithmetic: chunks are walked segment by segment
@@ -630,7 +650,7 @@ F5_DEV bool c_gemv4096(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const 
 // registers.  The partial sums are exact integers; the deferred epilogue adds
 // the NP partials of a row (order-free) before the group-scale law's shift.
 template <int NP>
-F5_DEV bool c_gemv_split(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const Abort &ab, uint32_t epoch, int T) {
+F5_DEV bool c_gemv_split(const GemvArgs &a, const MegaSmem &S, RingPos &rp, const Abort &ab, uint32_t epoch) {
   const CSync sy;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, b = blockIdx.x, ns = S.ns;
@@ -683,7 +703,7 @@ F5_DEV bool c_gemv_split(const GemvArgs &a, const MegaSmem &S, RingPos &rp, cons
 #pragma unroll
     for (int p = 0; p < NP; ++p) acc += S.res()[NP * i + p];
     if (i == 0) MG_MARK(4);
-    mega_epilogue_row(a, sg, i, uu, acc, e_x, in_f, epoch, rs, T);
+    mega_epilogue_resid(a, sg, i, uu, acc, e_x, in_f, epoch, rs);
     if (i == 0) MG_MARK(5);
   }
   if (a.nseg == 1 && a.seg[0].rstat) rstat_flush(a.seg[0].rstat, rs);
@@ -1348,7 +1368,7 @@ F5_DEV void consumers(const MegaArgs &ma, const MegaSmem &S, int tok, int T, int
     switch (op.kind) {
       case MK_BEGIN: c_begin(ma, op.b, tok, epoch); break;
       case MK_GEMV:
-        ok = op.g.K > 4096 ? c_gemv_split<3>(op.g, S, rp, ab, epoch, T) : c_gemv4096(op.g, S, rp, ab, epoch, w_g, T);
+        ok = op.g.K > 4096 ? c_gemv_split<3>(op.g, S, rp, ab, epoch) : c_gemv4096(op.g, S, rp, ab, epoch, w_g, T);
         break;
       case MK_DN: ok = c_dn(ma, op.d, S, w_sd, ab, epoch); break;
       case MK_ATTN: ok = c_attn(ma, op.at, S, T, pos, w_sk, w_sv, ab, epoch); break;
