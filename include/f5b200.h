@@ -325,7 +325,10 @@ int f5_ctx_attach_peers(f5_ctx *ctx, const void *handles, int n);
  * globaltimer (ns) at 8 marks of each op: out[(cta * nops + op) * 8 + k],
  * k = 0 start (after the grid barrier), 1 end, 2..6 op phases, 7 arrival at
  * the next grid barrier (0 where a CTA has no such phase).  With out == NULL
- * only *grid and *nops are returned; otherwise cap >= grid * nops * 8. */
+ * only *grid and *nops are returned; otherwise cap >= grid * nops * 8.
+ * The step runs on a separately compiled instance of the persistent kernel
+ * that carries the marks (the step kernel itself has none): same program and
+ * results, a few percent slower. */
 int f5_ctx_trace_step(f5_ctx *ctx, uint64_t *out, size_t cap, int *grid, int *nops);
 
 /* One full model step from a host token id: embedding row, every layer,
